@@ -1,0 +1,225 @@
+/*
+ * mlxcat_cuda.h -- C ABI of the B200 (sm_100a) n-gram speculative-decode path.
+ *
+ * A Swift shim (SwiftPM system-library target) keeps the Swift surface of
+ * mlxcat's ContinuousBatchGenerator / BatchKVCache / Scheduler / TokenSampler
+ * and calls these entry points in place of the MLX graph.  Plain pointers and
+ * sizes only; every call returns 0 on success or a negative MLXCAT_E* code
+ * (message: mlxcat_last_error / mlxcat_op_last_error).  Calls on one context
+ * must be serialised by the caller (the reference runs them on the Scheduler
+ * actor, Sources/MLXCat/TrackB/Scheduler.swift:13).  No CPU fallback exists:
+ * without a CUDA device every compute call fails with MLXCAT_E_CUDA.
+ *
+ * Reference paths below are inside the mlxcat project.
+ */
+#ifndef MLXCAT_CUDA_H
+#define MLXCAT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define MLXCAT_API __attribute__((visibility("default")))
+#else
+#define MLXCAT_API
+#endif
+
+#define MLXCAT_OK 0
+#define MLXCAT_E_INVALID (-1)   /* bad argument / shape                    */
+#define MLXCAT_E_CUDA (-2)      /* CUDA runtime error or no device         */
+#define MLXCAT_E_OOM (-3)       /* device allocation failed                */
+#define MLXCAT_E_STATE (-4)     /* call out of order (e.g. no weights)     */
+
+#define MLXCAT_MODEL_TRANSFORMER 0   /* Llama / Qwen3 dense, MLX affine q4 g64   */
+#define MLXCAT_MODEL_TABLE 1         /* next-token table (the reference's fake
+                                        LanguageModel test doubles)            */
+
+#define MLXCAT_ACCEPT_COMPAT 0  /* BatchGenerator.swift:906-940 semantics   */
+#define MLXCAT_ACCEPT_PREFIX 1  /* batched prefix match / rejection sampling */
+
+#define MLXCAT_MAX_PROPOSAL 8   /* k upper bound                           */
+#define MLXCAT_MAX_EOS 8
+
+/* Model description.  Replaces the model half of mlx-swift-lm's
+ * LanguageModel as injected through LanguageModelBox (Scheduler.swift:5-11,
+ * 68-89). */
+typedef struct {
+    int32_t kind;                 /* MLXCAT_MODEL_*                         */
+    int32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab;
+    int32_t tie_embeddings;       /* lm_head = embedding table              */
+    int32_t qk_norm;              /* Qwen3 per-head q/k RMSNorm             */
+    float rms_eps, rope_theta;
+    int32_t group_size, bits;     /* must be 64 and 4 (MLX affine q4 g64)   */
+} mlxcat_model_config;
+
+/* SamplingParameters subset on the path (Sampling.swift:139-217). */
+typedef struct {
+    float temperature;            /* 0 = greedy                             */
+    float top_p;                  /* (0,1) enables the nucleus filter       */
+    uint64_t seed;                /* per-request RNG seed                   */
+    int32_t has_seed;             /* request carried its own seed           */
+    int32_t eos[MLXCAT_MAX_EOS];
+    int32_t n_eos;
+    int32_t trigger;              /* tool-call start token, -1 if none      */
+} mlxcat_sampling;
+
+/* SpeculativeDecodingConfiguration (BatchGenerator.swift:10-29) plus mode. */
+typedef struct {
+    int32_t mode;                 /* MLXCAT_ACCEPT_*                        */
+    int32_t enabled;
+    int32_t max_proposal;         /* k, 0..MLXCAT_MAX_PROPOSAL              */
+    int32_t max_suffix;           /* n, >= 1                                */
+    int32_t min_context;          /* >= 2                                   */
+} mlxcat_spec_config;
+
+/* SpeculativeDecodingStats (BatchGenerator.swift:31-38). */
+typedef struct {
+    int64_t proposed, accepted, proposal_batches, rejected_batches;
+} mlxcat_stats;
+
+typedef struct mlxcat_ctx mlxcat_ctx;
+typedef struct mlxcat_cache mlxcat_cache;
+
+/* ---- context -------------------------------------------------------------
+ * replaces: model construction + MLX device stream (NativeModelEngine.swift:44-54) */
+MLXCAT_API int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx **out);
+MLXCAT_API int mlxcat_ctx_destroy(mlxcat_ctx *ctx);
+MLXCAT_API const char *mlxcat_last_error(const mlxcat_ctx *ctx);
+/* the context's CUDA stream (cudaStream_t), for callers that time or order work */
+MLXCAT_API int mlxcat_ctx_stream(mlxcat_ctx *ctx, void **stream);
+MLXCAT_API int mlxcat_ctx_synchronize(mlxcat_ctx *ctx);
+/* number of kernel launches issued by the context (graph replays count their nodes) */
+MLXCAT_API int64_t mlxcat_ctx_launch_count(const mlxcat_ctx *ctx);
+
+/* ---- weights ---------------------------------------------------------------
+ * replaces: MLX QuantizedLinear / QuantizedEmbedding parameter loading.
+ * tensor ids: layer*16 + {0 q,1 k,2 v,3 o,4 gate,5 up,6 down},
+ * 0xFFFF0000 embedding, 0xFFFF0001 lm_head (untied only). */
+MLXCAT_API int mlxcat_weights_synth(mlxcat_ctx *ctx, uint64_t seed, float stddev);
+MLXCAT_API int mlxcat_weights_set_q4(mlxcat_ctx *ctx, uint32_t tensor_id, const uint32_t *wq,
+                          const uint16_t *scales, const uint16_t *biases);
+MLXCAT_API int mlxcat_weights_get_q4(mlxcat_ctx *ctx, uint32_t tensor_id, uint32_t *wq, uint16_t *scales,
+                          uint16_t *biases);
+MLXCAT_API int mlxcat_weights_set_table(mlxcat_ctx *ctx, const int32_t *next_token, int32_t vocab);
+/* bytes of q4 weights one forward streams (packed words + scales + biases) */
+MLXCAT_API int64_t mlxcat_weights_bytes(const mlxcat_ctx *ctx);
+
+/* ---- cache: BatchKVCache + per-row generator state --------------------------
+ * replaces: BatchKVCache (BatchCache.swift:37-89) and the per-row arrays of
+ * ContinuousBatchGenerator (BatchGenerator.swift:144-215) on the device.
+ * Layout: K and V fp16 [layer][row][kv_head][max_len][head_dim], right-ragged
+ * with one length per row. */
+MLXCAT_API int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxcat_cache **out);
+MLXCAT_API int mlxcat_cache_destroy(mlxcat_cache *cache);
+/* admission: prefill prompt into `row`, sample the first token (generation
+ * index 0).  Scheduler.completeAdmission + generator.insert
+ * (Scheduler.swift:599-668, BatchGenerator.swift:380-460).  Requires
+ * len + max_new_tokens + MLXCAT_MAX_PROPOSAL + 1 <= max_len. */
+MLXCAT_API int mlxcat_cache_insert_row(mlxcat_cache *cache, int32_t row, const int32_t *prompt, int32_t len,
+                            int32_t max_new_tokens, const mlxcat_sampling *sampling,
+                            int32_t *first_token);
+/* generator.remove(uid:) */
+MLXCAT_API int mlxcat_cache_remove_row(mlxcat_cache *cache, int32_t row);
+/* BatchKVCache.trim(n) (BatchCache.swift:403-424): every row loses
+ * min(n, its length); *trimmed = min(n, longest row) */
+MLXCAT_API int mlxcat_cache_trim(mlxcat_cache *cache, int32_t n, int32_t *trimmed);
+/* per-row KV lengths (BatchKVCache.offset / ropeOffset) */
+MLXCAT_API int mlxcat_cache_lengths(mlxcat_cache *cache, int32_t *out_rows);
+/* speculativeTokenHistory[row] (BatchGenerator.swift:452-456, 1012-1014) */
+MLXCAT_API int mlxcat_cache_history(mlxcat_cache *cache, int32_t row, int32_t *out, int32_t cap,
+                         int32_t *len);
+/* BatchKVCache.extract(row) state: fp16 [n_kv][len][head_dim] for one layer */
+MLXCAT_API int mlxcat_cache_extract_row(mlxcat_cache *cache, int32_t row, int32_t layer, uint16_t *k_out,
+                             uint16_t *v_out);
+MLXCAT_API int mlxcat_cache_active(mlxcat_cache *cache, int32_t *out_rows);
+
+/* ---- hot path ----------------------------------------------------------------
+ * mlxcat_draft: proposeSuffixTokens for every row (BatchGenerator.swift:982-1010)
+ *   with the gate and limit of :877-892, :957-975.
+ *   drafts: [max_rows][k] (unused slots repeat the current token), counts: [max_rows].
+ * mlxcat_verify_forward: the (k+1)-token verify forward of :897-904 for every
+ *   row on the tokens [current, drafts...]; KV appended at each row's length;
+ *   logits [max_rows][k+1][vocab] fp32 (NULL to skip the copy).  Lengths are
+ *   NOT advanced (mlxcat_accept does that).
+ * mlxcat_accept: the acceptance loop + rollback of :906-954 on the logits of
+ *   the last verify forward; tokens [max_rows][k+1], counts [max_rows].
+ * mlxcat_spec_step: draft -> verify -> accept fused on the device, one host
+ *   synchronisation per step (replays a CUDA graph per configuration).
+ *   With spec->enabled == 0 it is one ordinary decode step. */
+MLXCAT_API int mlxcat_draft(mlxcat_cache *cache, const mlxcat_spec_config *spec, int32_t *drafts,
+                 int32_t *counts);
+MLXCAT_API int mlxcat_verify_forward(mlxcat_cache *cache, const mlxcat_spec_config *spec, float *logits);
+MLXCAT_API int mlxcat_accept(mlxcat_cache *cache, const mlxcat_spec_config *spec, int32_t *out_tokens,
+                  int32_t *out_counts, int32_t *out_finished, mlxcat_stats *stats);
+MLXCAT_API int mlxcat_spec_step(mlxcat_cache *cache, const mlxcat_spec_config *spec, int32_t *out_tokens,
+                     int32_t *out_counts, int32_t *out_finished, mlxcat_stats *stats);
+/* device time (ms) of the verify forward inside the last mlxcat_spec_step */
+MLXCAT_API int mlxcat_last_verify_ms(mlxcat_cache *cache, float *ms);
+
+/* ---- device-pointer operators ------------------------------------------------
+ * Stream-ordered kernels on caller-owned device memory (fp16 passed as
+ * uint16_t).  `stream` is a cudaStream_t (NULL = legacy default stream).
+ * Operators that need scratch take a caller-owned device workspace whose size
+ * the matching *_workspace query returns. */
+MLXCAT_API const char *mlxcat_op_last_error(void);
+
+/* quantizedMatmul (mlx-swift, called by QuantizedLinear): y[M][N] fp32 =
+ * x[M][K] fp16 . dequant(W)^T, W MLX affine q4 g64. */
+MLXCAT_API size_t mlxcat_op_q4_linear_workspace(int32_t N, int32_t K, int32_t M);
+MLXCAT_API int mlxcat_op_q4_linear(const uint32_t *wq, const uint16_t *scales, const uint16_t *biases,
+                        int32_t N, int32_t K, const uint16_t *x, int32_t M, float *y,
+                        void *workspace, size_t workspace_bytes, void *stream);
+
+/* MLXFast.scaledDotProductAttention with the causal mask of CausalMask.swift:4-28
+ * on a right-ragged cache.  q [M][n_heads][head_dim] fp16; token m belongs
+ * to row trow[m] at position tpos[m] and sees keys 0..tpos[m]; tokens come in
+ * groups of `qg` consecutive positions of one row.  out [M][n_heads*head_dim]. */
+MLXCAT_API size_t mlxcat_op_attention_workspace(int32_t M, int32_t qg, int32_t n_heads, int32_t n_kv_heads,
+                                     int32_t head_dim, int32_t max_len);
+MLXCAT_API int mlxcat_op_attention(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                        int32_t max_len, const int32_t *trow, const int32_t *tpos, int32_t M,
+                        int32_t qg, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                        uint16_t *out, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Seeded N(0, stddev) weights quantised to MLX affine q4 g64 (bit-identical
+ * with the CPU restatement). */
+MLXCAT_API int mlxcat_op_synth_q4(uint64_t seed, uint32_t tensor_id, float stddev, int32_t N, int32_t K,
+                       uint32_t *wq, uint16_t *scales, uint16_t *biases, void *stream);
+
+/* Per-row generator state on the device, for the drafter / acceptance
+ * operators.  All arrays have `rows` entries (eos: rows x MLXCAT_MAX_EOS). */
+typedef struct {
+    int32_t *hist;                /* [rows][hist_cap]                        */
+    int32_t hist_cap;
+    int32_t rows;
+    int32_t *hist_len, *kv_len, *n_gen, *max_new, *active;
+    float *temperature, *top_p;
+    uint64_t *seed;
+    int32_t *has_seed, *eos, *n_eos, *trigger;
+} mlxcat_rows;
+
+/* proposeSuffixTokens + gate for every row: vtok [rows][k+1] = current token
+ * then drafts (padding repeats the current token), count [rows], and the
+ * verify tokens' row / position descriptors trow, tpos [rows*(k+1)]. */
+MLXCAT_API int mlxcat_op_draft(const mlxcat_rows *rows, const mlxcat_spec_config *spec, int32_t *vtok,
+                    int32_t *count, int32_t *trow, int32_t *tpos, void *stream);
+
+/* Acceptance + rollback on given logits [rows][k+1][vocab] fp32 (greedy rows
+ * by argmax, temperature rows by rejection sampling).  Updates the row state
+ * in place; tokens [rows][k+1], n [rows], finished [rows]; stats[4] device
+ * uint64 counters (proposed, accepted, proposal_batches, rejected_batches)
+ * are incremented. */
+MLXCAT_API size_t mlxcat_op_accept_workspace(int32_t rows, int32_t k);
+MLXCAT_API int mlxcat_op_accept(const mlxcat_rows *rows, const mlxcat_spec_config *spec, const int32_t *vtok,
+                     const int32_t *count, const float *logits, int32_t vocab, int32_t *tokens,
+                     int32_t *n, int32_t *finished, uint64_t *stats, void *workspace,
+                     size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

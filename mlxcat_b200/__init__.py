@@ -1,0 +1,23 @@
+"""mlxcat_b200 -- B200-native (sm_100a) n-gram speculative-decode path of mlxcat.
+
+The compute lives in ``libmlxcat_cuda.so`` (CUDA kernels + C ABI, see
+``include/mlxcat_cuda.h``); this package is the host-side mirror of the
+reference's Swift surface over that ABI.  Importing it loads the library and
+fails loudly when it is missing: there is no CPU fallback.
+"""
+from . import _abi
+from ._abi import MlxcatError, lib
+
+lib()
+
+from .engine import (  # noqa: E402
+    CONFIGS, LLAMA3_8B, QWEN3_4B, TINY, BatchKVCache, ContinuousBatchGenerator, Context,
+    FinishReason, ModelConfig, Request, Response, SamplingParameters, Scheduler,
+    SpeculativeDecodingConfiguration, SpeculativeDecodingStats,
+)
+
+__all__ = [
+    "BatchKVCache", "CONFIGS", "ContinuousBatchGenerator", "Context", "FinishReason", "LLAMA3_8B",
+    "MlxcatError", "ModelConfig", "QWEN3_4B", "Request", "Response", "SamplingParameters",
+    "Scheduler", "SpeculativeDecodingConfiguration", "SpeculativeDecodingStats", "TINY", "lib",
+]

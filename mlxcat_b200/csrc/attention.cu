@@ -1,0 +1,332 @@
+// attention.cu -- GQA decode attention for the verify forward.
+//
+// Replaces MLXFast.scaledDotProductAttention with the additive causal mask of
+// BatchCache.swift:379-400 / CausalMask.swift:4-28 on the (k+1)-token verify
+// step.  The cache is right-ragged: row r holds positions [0, len_r) and the
+// mask comes from the per-token position alone (query at position p sees keys
+// 0..p), so no left padding and no zeroed slots are ever read.
+//
+// Work item = (token group, kv head, key split, key half).  A token group is
+// the qg consecutive verify tokens of one row; all G = Hq/Hkv query heads of
+// the kv head and all qg tokens form the MMA M dimension (qg*G <= 16*QT), so
+// every K/V tile fetched from HBM is used by every query of the group.
+// K/V tiles of 64 keys are double-buffered in shared memory with cp.async;
+// each of the two warps per query tile takes 32 keys of a tile (its own online
+// softmax).  Partials (m, l, O) go to scratch; attention_combine merges them.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mlxcat {
+
+namespace {
+
+constexpr int KB = 64;   // keys per staged block
+
+__device__ __forceinline__ void mma16816(float *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t *d, uint32_t a) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]) : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t *d, uint32_t a) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]) : "r"(a));
+}
+__device__ __forceinline__ void cp16(uint32_t s, const void *g, int bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(g), "r"(bytes));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+template <int QT, int D>
+__global__ void __launch_bounds__(QT * 64)
+attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
+            const __half *__restrict__ vc, int max_len, const int32_t *__restrict__ trow,
+            const int32_t *__restrict__ tpos, int M, int qg, int Hq, int Hkv, int key_chunk,
+            int splits, float scale_log2, float *__restrict__ o_part, float *__restrict__ ml_part) {
+    constexpr int QROWS = QT * 16;
+    constexpr int PITCH = D + 8;               // halves
+    constexpr int NTHREADS = QT * 64;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __half *qs = reinterpret_cast<__half *>(smem);                 // [QROWS][PITCH]
+    __half *ks = qs + QROWS * PITCH;                                // [2][KB][PITCH]
+    __half *vs = ks + 2 * KB * PITCH;                               // [2][KB][PITCH]
+
+    const int grp = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+    const int G = Hq / Hkv;
+    const int t0 = grp * qg;
+    const int ntok = min(qg, M - t0);
+    const int NQ = ntok * G;
+    const int row = trow[t0], pos0 = tpos[t0];
+    const int kend = pos0 + ntok;
+    const int kb = s * key_chunk, ke = min(kend, kb + key_chunk);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int mt = warp >> 1, kh = warp & 1;
+    const int g = lane >> 2, t = lane & 3;
+
+    const size_t item = (((size_t)grp * Hkv + h) * splits + s) * 2 + kh;
+    float *op = o_part + item * QROWS * D;
+    float *mlp = ml_part + item * QROWS * 2;
+
+    if (kb >= ke) {
+        for (int i = threadIdx.x; i < QROWS * 2; i += NTHREADS) {
+            const size_t it0 = (((size_t)grp * Hkv + h) * splits + s) * 2;
+            ml_part[it0 * QROWS * 2 + i] = (i & 1) ? 0.f : -INFINITY;
+            ml_part[(it0 + 1) * QROWS * 2 + i] = (i & 1) ? 0.f : -INFINITY;
+        }
+        return;
+    }
+
+    const __half *kbase = kc + ((size_t)row * Hkv + h) * max_len * D;
+    const __half *vbase = vc + ((size_t)row * Hkv + h) * max_len * D;
+    const uint32_t qs_a = (uint32_t)__cvta_generic_to_shared(qs);
+    const uint32_t ks_a = (uint32_t)__cvta_generic_to_shared(ks);
+    const uint32_t vs_a = (uint32_t)__cvta_generic_to_shared(vs);
+
+    // stage Q: row qi = j*G + gh -> token t0+j, head h*G+gh
+    for (int v = threadIdx.x; v < QROWS * (D / 8); v += NTHREADS) {
+        const int qi = v / (D / 8), c8 = v - qi * (D / 8);
+        const int j = qi / G, gh = qi - j * G;
+        const bool ok = qi < NQ;
+        const __half *src = qbuf + ((size_t)(ok ? t0 + j : t0) * Hq + h * G + (ok ? gh : 0)) * D + c8 * 8;
+        cp16(qs_a + (uint32_t)(qi * PITCH + c8 * 8) * 2, src, ok ? 16 : 0);
+    }
+    auto stage_kv = [&](int blk, int buf) {
+        const int key0 = kb + blk * KB;
+        for (int v = threadIdx.x; v < KB * (D / 8); v += NTHREADS) {
+            const int kr = v / (D / 8), c8 = v - kr * (D / 8);
+            const int key = key0 + kr;
+            const bool ok = key < ke;
+            const size_t off = (size_t)(ok ? key : kb) * D + c8 * 8;
+            const uint32_t so = (uint32_t)((buf * KB + kr) * PITCH + c8 * 8) * 2;
+            cp16(ks_a + so, kbase + off, ok ? 16 : 0);
+            cp16(vs_a + so, vbase + off, ok ? 16 : 0);
+        }
+    };
+    const int nblk = (ke - kb + KB - 1) / KB;
+    stage_kv(0, 0);
+    cp_commit();
+
+    uint32_t qf[D / 16][4];
+    float o[D / 8][4];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+    // query row -> allowed key limit (inclusive): pos0 + token index
+    const int qrow0 = mt * 16 + g, qrow1 = qrow0 + 8;
+    const int lim0 = qrow0 < NQ ? pos0 + qrow0 / G : -1;
+    const int lim1 = qrow1 < NQ ? pos0 + qrow1 / G : -1;
+
+    for (int b = 0; b < nblk; ++b) {
+        if (b + 1 < nblk) stage_kv(b + 1, (b + 1) & 1);
+        cp_commit();
+        cp_wait<1>();
+        __syncthreads();
+        if (b == 0) {
+#pragma unroll
+            for (int ks16 = 0; ks16 < D / 16; ++ks16) {
+                const int mi = lane >> 3, rr = lane & 7;
+                const int qr = mt * 16 + (mi & 1) * 8 + rr;
+                ldsm_x4(qf[ks16], qs_a + (uint32_t)(qr * PITCH + ks16 * 16 + (mi >> 1) * 8) * 2);
+            }
+        }
+        const int buf = b & 1;
+        const int key_base = kb + b * KB + kh * 32;
+        // S = Q K^T over 32 keys (4 n8 tiles)
+        float sc[4][4];
+#pragma unroll
+        for (int n = 0; n < 4; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+        for (int ks16 = 0; ks16 < D / 16; ++ks16) {
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int mi = lane >> 3, rr = lane & 7;
+                const int kr = kh * 32 + u * 16 + (mi >> 1) * 8 + rr;
+                uint32_t bb[4];
+                ldsm_x4(bb, ks_a + (uint32_t)((buf * KB + kr) * PITCH + ks16 * 16 + (mi & 1) * 8) * 2);
+                mma16816(sc[2 * u], qf[ks16], bb[0], bb[1]);
+                mma16816(sc[2 * u + 1], qf[ks16], bb[2], bb[3]);
+            }
+        }
+        // mask + online softmax (scores in log2 units)
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int key = key_base + n * 8 + 2 * t + (c & 1);
+                const int lim = c < 2 ? lim0 : lim1;
+                const float v = (key <= lim && key < ke) ? sc[n][c] * scale_log2 : -INFINITY;
+                sc[n][c] = v;
+                mx[c >> 1] = fmaxf(mx[c >> 1], v);
+            }
+        }
+        float alpha[2];
+#pragma unroll
+        for (int rI = 0; rI < 2; ++rI) {
+            mx[rI] = fmaxf(mx[rI], __shfl_xor_sync(0xffffffffu, mx[rI], 1));
+            mx[rI] = fmaxf(mx[rI], __shfl_xor_sync(0xffffffffu, mx[rI], 2));
+            const float mn = fmaxf(m_r[rI], mx[rI]);
+            alpha[rI] = (mn == -INFINITY) ? 0.f : exp2f(m_r[rI] - mn);
+            m_r[rI] = mn;
+            l_r[rI] *= alpha[rI];
+        }
+        uint32_t pa[2][4];
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+            float p[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float mref = m_r[c >> 1];
+                p[c] = (mref == -INFINITY) ? 0.f : exp2f(sc[n][c] - mref);
+                l_r[c >> 1] += p[c];
+            }
+            const int u = n >> 1;
+            if ((n & 1) == 0) { pa[u][0] = pack_h2(p[0], p[1]); pa[u][1] = pack_h2(p[2], p[3]); }
+            else { pa[u][2] = pack_h2(p[0], p[1]); pa[u][3] = pack_h2(p[2], p[3]); }
+        }
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) {
+            o[i][0] *= alpha[0]; o[i][1] *= alpha[0];
+            o[i][2] *= alpha[1]; o[i][3] *= alpha[1];
+        }
+        // O += P V
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+#pragma unroll
+            for (int dv = 0; dv < D / 16; ++dv) {
+                const int mi = lane >> 3, rr = lane & 7;
+                const int kr = kh * 32 + u * 16 + (mi & 1) * 8 + rr;
+                uint32_t bb[4];
+                ldsm_x4_t(bb, vs_a + (uint32_t)((buf * KB + kr) * PITCH + dv * 16 + (mi >> 1) * 8) * 2);
+                mma16816(o[2 * dv], pa[u], bb[0], bb[1]);
+                mma16816(o[2 * dv + 1], pa[u], bb[2], bb[3]);
+            }
+        }
+        __syncthreads();
+    }
+    cp_wait<0>();
+
+#pragma unroll
+    for (int rI = 0; rI < 2; ++rI) {
+        l_r[rI] += __shfl_xor_sync(0xffffffffu, l_r[rI], 1);
+        l_r[rI] += __shfl_xor_sync(0xffffffffu, l_r[rI], 2);
+    }
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+        const int d = i * 8 + 2 * t;
+        *reinterpret_cast<float2 *>(op + (size_t)qrow0 * D + d) = make_float2(o[i][0], o[i][1]);
+        *reinterpret_cast<float2 *>(op + (size_t)qrow1 * D + d) = make_float2(o[i][2], o[i][3]);
+    }
+    if (t == 0) {
+        mlp[qrow0 * 2] = m_r[0]; mlp[qrow0 * 2 + 1] = l_r[0];
+        mlp[qrow1 * 2] = m_r[1]; mlp[qrow1 * 2 + 1] = l_r[1];
+    }
+}
+
+// merge 2*splits partials per (group, kv head); one thread per (query, d)
+template <int QT>
+__global__ void attn_combine_kernel(const float *__restrict__ o_part, const float *__restrict__ ml_part,
+                                    int M, int qg, int Hq, int Hkv, int D, int splits,
+                                    __half *__restrict__ out, int permuted) {
+    constexpr int QROWS = QT * 16;
+    const int grp = blockIdx.x, h = blockIdx.y;
+    const int G = Hq / Hkv;
+    const int t0 = grp * qg;
+    const int ntok = min(qg, M - t0);
+    const int NQ = ntok * G;
+    const int P = splits * 2;
+    const size_t it0 = ((size_t)grp * Hkv + h) * P;
+    const int KO = Hq * D;
+    for (int v = threadIdx.x; v < NQ * D; v += blockDim.x) {
+        const int qi = v / D, d = v - qi * D;
+        float mmax = -INFINITY;
+        for (int p = 0; p < P; ++p) mmax = fmaxf(mmax, ml_part[((it0 + p) * QROWS + qi) * 2]);
+        float num = 0.f, den = 0.f;
+        if (mmax != -INFINITY) {
+            for (int p = 0; p < P; ++p) {
+                const float mp = ml_part[((it0 + p) * QROWS + qi) * 2];
+                if (mp == -INFINITY) continue;
+                const float w = exp2f(mp - mmax);
+                den += w * ml_part[((it0 + p) * QROWS + qi) * 2 + 1];
+                num += w * o_part[((it0 + p) * QROWS + qi) * D + d];
+            }
+        }
+        const float r = den > 0.f ? num / den : 0.f;
+        const int j = qi / G, gh = qi - j * G;
+        const int k = (h * G + gh) * D + d;
+        out[(size_t)(t0 + j) * KO + (permuted ? xperm(k) : k)] = __float2half_rn(r);
+    }
+}
+
+template <int QT, int D>
+cudaError_t launch_attn(const __half *qbuf, KVLayer kv, const int32_t *trow, const int32_t *tpos,
+                        int M, int qg, int Hq, int Hkv, int key_chunk, int splits,
+                        AttnScratch sc, __half *out, bool permuted, cudaStream_t st) {
+    constexpr int PITCH = D + 8;
+    const size_t smem = (size_t)(QT * 16 + 4 * KB) * PITCH * 2;
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(attn_kernel<QT, D>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr[dev & 63] = true;
+    }
+    const int groups = (M + qg - 1) / qg;
+    dim3 grid(groups, Hkv, splits);
+    const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+    attn_kernel<QT, D><<<grid, QT * 64, smem, st>>>(qbuf, kv.k, kv.v, kv.max_len, trow, tpos, M, qg,
+                                                    Hq, Hkv, key_chunk, splits, scale_log2, sc.o, sc.ml);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    dim3 g2(groups, Hkv);
+    attn_combine_kernel<QT><<<g2, 256, 0, st>>>(sc.o, sc.ml, M, qg, Hq, Hkv, D, splits, out, permuted ? 1 : 0);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+int attention_qrows(int qg, int n_heads, int n_kv) {
+    const int nq = qg * (n_heads / n_kv);
+    return nq <= 16 ? 16 : (nq <= 32 ? 32 : 64);
+}
+
+int attention_max_splits(int max_len, int key_chunk) { return (max_len + key_chunk - 1) / key_chunk; }
+
+size_t attention_scratch_items(int groups, int n_kv, int splits) {
+    return (size_t)groups * n_kv * splits * 2;
+}
+
+cudaError_t attention(const __half *qbuf, KVLayer kv, const int32_t *trow, const int32_t *tpos,
+                      int M, int qg, int n_heads, int n_kv, int D, int key_chunk, int splits,
+                      AttnScratch scratch, __half *out, bool permuted_out, cudaStream_t st) {
+    if (key_chunk % KB || n_heads % n_kv) return cudaErrorInvalidValue;
+    const int nq = qg * (n_heads / n_kv);
+    const int groups = (M + qg - 1) / qg;
+    if (attention_scratch_items(groups, n_kv, splits) > scratch.items) return cudaErrorInvalidValue;
+    if (D == 128) {
+        if (nq <= 16) return launch_attn<1, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, st);
+        if (nq <= 32) return launch_attn<2, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, st);
+        if (nq <= 64) return launch_attn<4, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, st);
+    } else if (D == 64) {
+        if (nq <= 16) return launch_attn<1, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, st);
+        if (nq <= 32) return launch_attn<2, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, st);
+        if (nq <= 64) return launch_attn<4, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace mlxcat

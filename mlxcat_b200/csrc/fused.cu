@@ -1,0 +1,277 @@
+// fused.cu -- per-token kernels between the q4 linears of the verify forward:
+// embedding + RMSNorm, split-K reduction + residual + RMSNorm, q/k/v epilogue
+// (per-head q/k RMSNorm, RoPE, KV append), SwiGLU, argmax, and the table
+// model used as the reference's fake LanguageModel.
+//
+// Model math follows mlx-swift-lm's Llama / Qwen3 blocks as used on the
+// verify forward (BatchGenerator.swift:900-904): pre-norm residual blocks,
+// rotate-half RoPE, GQA, SwiGLU.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mlxcat {
+
+namespace {
+
+constexpr int TPB = 256;
+
+__device__ __forceinline__ float block_sum(float v, float *sh) {
+    v = warp_sum(v);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    float r = 0.f;
+    const int nw = blockDim.x >> 5;
+    for (int i = 0; i < nw; ++i) r += sh[i];
+    return r;
+}
+
+__global__ void embed_norm_kernel(const uint32_t *__restrict__ wq, const __half *__restrict__ sc,
+                                  const __half *__restrict__ bi, int H, const int32_t *tok,
+                                  const float *__restrict__ nw, float eps, float *__restrict__ h,
+                                  __half *__restrict__ xn) {
+    __shared__ float sh[32];
+    const int m = blockIdx.x;
+    const int t = tok[m];
+    const uint32_t *row = wq + (size_t)t * (H / 8);
+    float *hm = h + (size_t)m * H;
+    float ss = 0.f;
+    for (int w = threadIdx.x; w < H / 8; w += blockDim.x) {
+        const uint32_t word = row[w];
+        const int grp = (w * 8) / MLXCAT_GS;
+        const float s = __half2float(sc[(size_t)t * (H / MLXCAT_GS) + grp]);
+        const float b = __half2float(bi[(size_t)t * (H / MLXCAT_GS) + grp]);
+        for (int i = 0; i < 8; ++i) {
+            const float v = s * (float)((word >> (4 * i)) & 0xfu) + b;
+            hm[w * 8 + i] = v;
+            ss += v * v;
+        }
+    }
+    ss = block_sum(ss, sh);
+    const float r = 1.0f / sqrtf(ss / (float)H + eps);
+    for (int w = threadIdx.x; w < H / 8; w += blockDim.x)
+        for (int i = 0; i < 8; ++i) {
+            const int k = w * 8 + i;
+            xn[(size_t)m * H + xperm(k)] = __float2half_rn(hm[k] * r * nw[k]);
+        }
+}
+
+__global__ void residual_norm_kernel(const float *__restrict__ part, int splits, int M, int H,
+                                     const float *__restrict__ nw, float eps,
+                                     float *__restrict__ h, __half *__restrict__ xn) {
+    __shared__ float sh[32];
+    const int m = blockIdx.x;
+    float *hm = h + (size_t)m * H;
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < H; k += blockDim.x) {
+        float v = hm[k];
+        float a = 0.f;
+        for (int s = 0; s < splits; ++s) a += part[((size_t)s * M + m) * H + k];
+        v += a;
+        hm[k] = v;
+        ss += v * v;
+    }
+    if (!xn) return;
+    ss = block_sum(ss, sh);
+    const float r = 1.0f / sqrtf(ss / (float)H + eps);
+    for (int k = threadIdx.x; k < H; k += blockDim.x)
+        xn[(size_t)m * H + xperm(k)] = __float2half_rn(hm[k] * r * nw[k]);
+}
+
+// one warp per head; lanes own rotate-half pairs (i, i + D/2)
+__global__ void qkv_epilogue_kernel(const float *__restrict__ part, int splits, int M,
+                                    int n_heads, int n_kv, int D, const float *__restrict__ q_norm,
+                                    const float *__restrict__ k_norm, float eps,
+                                    const float *__restrict__ inv_freq, const int32_t *trow,
+                                    const int32_t *tpos, __half *__restrict__ qbuf,
+                                    __half *__restrict__ kc, __half *__restrict__ vc,
+                                    int max_len) {
+    const int m = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int N = (n_heads + 2 * n_kv) * D;
+    const int row = trow[m], pos = tpos[m];
+    const int half = D / 2;
+    const int PP = 4;  // pairs per lane (D <= 256)
+    for (int hh = warp; hh < n_heads + 2 * n_kv; hh += nwarps) {
+        const bool is_q = hh < n_heads, is_k = !is_q && hh < n_heads + n_kv;
+        const int base = hh * D;
+        float a[PP], b[PP];
+        float ss = 0.f;
+#pragma unroll
+        for (int p = 0; p < PP; ++p) {
+            const int i = lane + 32 * p;
+            a[p] = b[p] = 0.f;
+            if (i < half) {
+                for (int s = 0; s < splits; ++s) {
+                    a[p] += part[((size_t)s * M + m) * N + base + i];
+                    b[p] += part[((size_t)s * M + m) * N + base + i + half];
+                }
+                ss += a[p] * a[p] + b[p] * b[p];
+            }
+        }
+        if (is_q || is_k) {
+            const float *nw = is_q ? q_norm : k_norm;
+            float r = 1.f;
+            if (nw) {
+                ss = warp_sum(ss);
+                r = 1.0f / sqrtf(ss / (float)D + eps);
+            }
+#pragma unroll
+            for (int p = 0; p < PP; ++p) {
+                const int i = lane + 32 * p;
+                if (i < half) {
+                    float x0 = a[p], x1 = b[p];
+                    if (nw) { x0 = x0 * r * nw[i]; x1 = x1 * r * nw[i + half]; }
+                    const float ang = __fmul_rn((float)pos, inv_freq[i]);
+                    float sn, cs;
+                    sincosf(ang, &sn, &cs);
+                    a[p] = x0 * cs - x1 * sn;
+                    b[p] = x0 * sn + x1 * cs;
+                }
+            }
+        }
+        __half *dst;
+        if (is_q) {
+            dst = qbuf + ((size_t)m * n_heads + hh) * D;
+        } else {
+            const int kvh = is_k ? hh - n_heads : hh - n_heads - n_kv;
+            __half *cache = is_k ? kc : vc;
+            dst = cache + (((size_t)row * n_kv + kvh) * max_len + pos) * D;
+        }
+#pragma unroll
+        for (int p = 0; p < PP; ++p) {
+            const int i = lane + 32 * p;
+            if (i < half) {
+                dst[i] = __float2half_rn(a[p]);
+                dst[i + half] = __float2half_rn(b[p]);
+            }
+        }
+    }
+}
+
+__global__ void swiglu_kernel(const float *__restrict__ part, int splits, int M, int I,
+                              __half *__restrict__ xn) {
+    const int m = blockIdx.y;
+    const int N = 2 * I;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < I; i += gridDim.x * blockDim.x) {
+        float gg = 0.f, uu = 0.f;
+        for (int s = 0; s < splits; ++s) {
+            gg += part[((size_t)s * M + m) * N + i];
+            uu += part[((size_t)s * M + m) * N + I + i];
+        }
+        const float a = gg / (1.0f + expf(-gg)) * uu;
+        xn[(size_t)m * I + xperm(i)] = __float2half_rn(a);
+    }
+}
+
+__global__ void reduce_splits_kernel(const float *__restrict__ part, int splits, size_t n,
+                                     float *__restrict__ y) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+        float a = 0.f;
+        for (int s = 0; s < splits; ++s) a += part[(size_t)s * n + i];
+        y[i] = a;
+    }
+}
+
+__global__ void permute_kernel(const __half *__restrict__ x, __half *__restrict__ y, int M, int K) {
+    const size_t n = (size_t)M * K;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const int m = (int)(i / K), k = (int)(i - (size_t)m * K);
+        y[(size_t)m * K + xperm(k)] = x[i];
+    }
+}
+
+// max value, lowest index on ties (MLX argMax returns the first maximum)
+__global__ void argmax_kernel(const float *__restrict__ logits, int V, int32_t *out) {
+    __shared__ unsigned long long sh[32];
+    const int m = blockIdx.x;
+    const float *l = logits + (size_t)m * V;
+    unsigned long long best = 0;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const unsigned long long key =
+            ((unsigned long long)float_key(l[i]) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
+        best = key > best ? key : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+        best = v > best ? v : best;
+    }
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) sh[w] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long b = 0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) b = sh[i] > b ? sh[i] : b;
+        out[m] = (int32_t)(0xffffffffu - (uint32_t)(b & 0xffffffffull));
+    }
+}
+
+__global__ void table_logits_kernel(const int32_t *next, const int32_t *tok, int V, float *logits) {
+    const int m = blockIdx.y;
+    const int nt = next[tok[m]];
+    for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < V; v += gridDim.x * blockDim.x)
+        logits[(size_t)m * V + v] = v == nt ? 20.0f : -20.0f;
+}
+
+}  // namespace
+
+cudaError_t embed_norm(const Q4Weight &embed, const int32_t *tok, int M, const float *norm_w,
+                       float eps, float *h, __half *xn, cudaStream_t st) {
+    embed_norm_kernel<<<M, TPB, 0, st>>>(embed.wq, embed.scales, embed.biases, embed.K, tok,
+                                         norm_w, eps, h, xn);
+    return cudaGetLastError();
+}
+
+cudaError_t residual_norm(const float *part, int splits, int M, int H, const float *norm_w,
+                          float eps, float *h, __half *xn, cudaStream_t st) {
+    residual_norm_kernel<<<M, TPB, 0, st>>>(part, splits, M, H, norm_w, eps, h, xn);
+    return cudaGetLastError();
+}
+
+cudaError_t qkv_epilogue(const float *part, int splits, int M, int n_heads, int n_kv, int D,
+                         const float *q_norm, const float *k_norm, float eps,
+                         const float *inv_freq, const int32_t *trow, const int32_t *tpos,
+                         __half *qbuf, KVLayer kv, cudaStream_t st) {
+    if (D > 256 || (D & 1)) return cudaErrorInvalidValue;
+    qkv_epilogue_kernel<<<M, TPB, 0, st>>>(part, splits, M, n_heads, n_kv, D, q_norm, k_norm, eps,
+                                           inv_freq, trow, tpos, qbuf, kv.k, kv.v, kv.max_len);
+    return cudaGetLastError();
+}
+
+cudaError_t swiglu(const float *part, int splits, int M, int I, __half *xn, cudaStream_t st) {
+    dim3 grid((I + TPB - 1) / TPB, M);
+    swiglu_kernel<<<grid, TPB, 0, st>>>(part, splits, M, I, xn);
+    return cudaGetLastError();
+}
+
+cudaError_t permute_activations(const __half *x, __half *x_perm, int M, int K, cudaStream_t st) {
+    if (K % 128) return cudaErrorInvalidValue;
+    const size_t n = (size_t)M * K;
+    const int blocks = (int)((n + TPB - 1) / TPB < 4096 ? (n + TPB - 1) / TPB : 4096);
+    permute_kernel<<<blocks > 0 ? blocks : 1, TPB, 0, st>>>(x, x_perm, M, K);
+    return cudaGetLastError();
+}
+
+cudaError_t reduce_splits(const float *part, int splits, size_t n, float *y, cudaStream_t st) {
+    const size_t b = (n + TPB - 1) / TPB;
+    reduce_splits_kernel<<<(unsigned)(b < 4096 ? (b ? b : 1) : 4096), TPB, 0, st>>>(part, splits, n, y);
+    return cudaGetLastError();
+}
+
+cudaError_t argmax_rows(const float *logits, int M, int V, int32_t *out, cudaStream_t st) {
+    argmax_kernel<<<M, 1024, 0, st>>>(logits, V, out);
+    return cudaGetLastError();
+}
+
+cudaError_t table_logits(const int32_t *next, const int32_t *tok, int M, int V, float *logits,
+                         cudaStream_t st) {
+    dim3 grid((V + TPB - 1) / TPB < 64 ? (V + TPB - 1) / TPB : 64, M);
+    table_logits_kernel<<<grid, TPB, 0, st>>>(next, tok, V, logits);
+    return cudaGetLastError();
+}
+
+}  // namespace mlxcat

@@ -1,0 +1,133 @@
+// kernels.h -- internal launch interface of the mlxcat_b200 CUDA kernels.
+// Everything here is device-pointer based and stream ordered; the C ABI in
+// include/mlxcat_cuda.h sits on top.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mlxcat {
+
+// One MLX affine-q4 matrix [N][K]: packed words, fp16 scales and biases.
+struct Q4Weight {
+    const uint32_t *wq = nullptr;
+    const __half *scales = nullptr;
+    const __half *biases = nullptr;
+    int N = 0, K = 0;
+};
+
+// ---- weight synthesis (seeded N(0, std) then affine q4, bit-exact with the
+//      CPU restatement) ------------------------------------------------------
+cudaError_t synth_q4(uint64_t seed, uint32_t tensor_id, float stddev, int N, int K,
+                     uint32_t *wq, __half *scales, __half *biases, int row_offset,
+                     cudaStream_t st);
+
+// ---- q4 linear (small-M path): out[s][M][N] fp32 partials over split s ----
+int q4_linear_splits(int N, int K, int M, int sm_count);
+int q4_linear_real_splits(int K, int splits);
+cudaError_t q4_linear(const Q4Weight &w, const __half *x_perm, int M, int ldx, int splits,
+                      float *out, cudaStream_t st);
+
+// ---- activation layout helpers --------------------------------------------
+cudaError_t permute_activations(const __half *x, __half *x_perm, int M, int K, cudaStream_t st);
+// y[i] = sum_s part[s][i] for i < n (fixed split order)
+cudaError_t reduce_splits(const float *part, int splits, size_t n, float *y, cudaStream_t st);
+
+// ---- per-token fused kernels ------------------------------------------------
+// h = dequant(embed[tok]);  xn = rmsnorm(h) * w   (xn permuted fp16)
+cudaError_t embed_norm(const Q4Weight &embed, const int32_t *tok, int M, const float *norm_w,
+                       float eps, float *h, __half *xn, cudaStream_t st);
+// h += sum_s part[s];  xn = rmsnorm(h) * w
+cudaError_t residual_norm(const float *part, int splits, int M, int H, const float *norm_w,
+                          float eps, float *h, __half *xn, cudaStream_t st);
+// q/k/v from partials; optional per-head q/k RMSNorm; RoPE; q -> qbuf,
+// k/v -> cache at (row, pos)
+struct KVLayer {
+    __half *k = nullptr, *v = nullptr;   // [rows][n_kv][max_len][D]
+    int max_len = 0;
+};
+cudaError_t qkv_epilogue(const float *part, int splits, int M, int n_heads, int n_kv, int D,
+                         const float *q_norm, const float *k_norm, float eps,
+                         const float *inv_freq, const int32_t *trow, const int32_t *tpos,
+                         __half *qbuf, KVLayer kv, cudaStream_t st);
+// xn[m][i] = silu(g) * u from partials [.., 2I] (gate rows first)
+cudaError_t swiglu(const float *part, int splits, int M, int I, __half *xn, cudaStream_t st);
+
+// ---- decode attention (split-K over keys, GQA) -----------------------------
+// Tokens come in groups of `qg` consecutive positions of one row (the verify
+// tokens of a row, or a slice of a prompt).  Output fp16, permuted, [M][Hq*D].
+struct AttnScratch {
+    float *o = nullptr;     // [groups*n_kv*splits][QMAX][D]
+    float *ml = nullptr;    // [groups*n_kv*splits][QMAX][2]
+    size_t items = 0;
+};
+int attention_max_splits(int max_len, int key_chunk);
+size_t attention_scratch_items(int groups, int n_kv, int splits);
+int attention_qrows(int qg, int n_heads, int n_kv);
+cudaError_t attention(const __half *qbuf, KVLayer kv, const int32_t *trow, const int32_t *tpos,
+                      int M, int qg, int n_heads, int n_kv, int D, int key_chunk, int splits,
+                      AttnScratch scratch, __half *out, bool permuted_out, cudaStream_t st);
+
+// ---- lm head / sampling ----------------------------------------------------
+cudaError_t argmax_rows(const float *logits, int M, int V, int32_t *out, cudaStream_t st);
+
+// ---- drafter ----------------------------------------------------------------
+struct RowState {
+    int32_t *hist;        // [rows][hist_cap]
+    int32_t *hist_len;    // [rows]
+    int32_t *kv_len;      // [rows]
+    int32_t *n_gen;       // [rows]
+    int32_t *max_new;     // [rows]
+    int32_t *active;      // [rows]
+    float *temperature;   // [rows]
+    float *top_p;         // [rows]
+    uint64_t *seed;       // [rows]
+    int32_t *has_seed;    // [rows]
+    int32_t *eos;         // [rows][8]
+    int32_t *n_eos;       // [rows]
+    int32_t *trigger;     // [rows]
+    int hist_cap;
+    int rows;
+};
+struct SpecParams {
+    int mode, enabled, k, n, min_ctx;
+};
+// vtok[r][0..k]: current token then drafts (padding repeats the current
+// token); count[r]; tokens' row/position descriptors for the forward.
+cudaError_t draft(const RowState &rs, const SpecParams &sp, int32_t *vtok, int32_t *count,
+                  int32_t *trow, int32_t *tpos, cudaStream_t st);
+
+// greedy acceptance + in-place rollback (history append, kv_len, n_gen,
+// finish).  amax: [rows][k+1] argmax per verify position.
+struct StepOut {
+    int32_t *tokens;        // [rows][k+1]
+    int32_t *n;             // [rows]
+    int32_t *finished;      // [rows]
+    unsigned long long *stats;  // [4] proposed, accepted, proposal_batches, rejected
+};
+cudaError_t accept_greedy(const RowState &rs, const SpecParams &sp, const int32_t *vtok,
+                          const int32_t *count, const int32_t *amax, StepOut out,
+                          cudaStream_t st);
+// sampling rows (temperature > 0): single-draft rejection sampling from the
+// row's seeded uniforms; greedy rows are left to accept_greedy.
+struct SampleScratch {
+    float *m;                 // [rows*(k+1)]
+    uint32_t *thr;            // [rows*(k+1)] top-p threshold key
+    unsigned long long *S;    // [rows*(k+1)]
+    unsigned long long *Pd;   // [rows*(k+1)]
+};
+cudaError_t accept_sampled(const RowState &rs, const SpecParams &sp, const int32_t *vtok,
+                           const int32_t *count, const float *logits, int V, SampleScratch sc,
+                           StepOut out, cudaStream_t st);
+
+// first token after prefill: greedy or sampled at generation index 0
+cudaError_t sample_first(const RowState &rs, int row, const float *logits, int V,
+                         const int32_t *amax, SampleScratch sc, int32_t *out_token,
+                         cudaStream_t st);
+
+// table model (the reference's fake LanguageModel): logits +20 at next[tok]
+cudaError_t table_logits(const int32_t *next, const int32_t *tok, int M, int V, float *logits,
+                         cudaStream_t st);
+
+}  // namespace mlxcat

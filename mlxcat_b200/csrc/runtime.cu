@@ -1,0 +1,1023 @@
+// runtime.cu -- context, weights, cache and the speculative step behind the
+// C ABI (include/mlxcat_cuda.h).
+//
+// The host side mirrors ContinuousBatchGenerator.speculativeNext
+// (BatchGenerator.swift:875-955) with every row of the batch speculating at
+// once: draft (device) -> verify forward over rows x (k+1) tokens (device) ->
+// acceptance + in-place rollback (device) -> one device-to-host copy of the
+// emitted tokens.  The whole step is captured once per configuration into a
+// CUDA graph and replayed.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/mlxcat_cuda.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace mlxcat;
+
+namespace {
+
+constexpr int PREFILL_CHUNK = 128;   // prompt tokens per prefill forward
+constexpr int PREFILL_QG = 8;        // prompt tokens per attention group
+constexpr int KEY_CHUNK = 256;       // keys per attention split
+
+thread_local std::string g_op_err;
+
+struct DevLin {
+    uint32_t *wq = nullptr;
+    __half *s = nullptr, *b = nullptr;
+    int N = 0, K = 0;
+    Q4Weight view() const {
+        Q4Weight w;
+        w.wq = wq; w.scales = s; w.biases = b; w.N = N; w.K = K;
+        return w;
+    }
+    size_t bytes() const { return (size_t)N * K / 2 + (size_t)N * (K / 64) * 4; }
+};
+
+}  // namespace
+
+struct mlxcat_ctx {
+    mlxcat_model_config cfg{};
+    int device = 0, sm_count = 148;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    std::vector<void *> allocs;
+    DevLin embed, lm_head;
+    std::vector<DevLin> qkv, o, gu, down;
+    float *norms = nullptr;     // attn[L][H], mlp[L][H], final[H], qn[L][D], kn[L][D]
+    float *inv_freq = nullptr;
+    int32_t *table = nullptr;
+    bool have_weights = false;
+    int64_t launches = 0;
+
+    const float *attn_norm(int l) const { return norms + (size_t)l * cfg.hidden; }
+    const float *mlp_norm(int l) const { return norms + (size_t)(cfg.n_layers + l) * cfg.hidden; }
+    const float *final_norm() const { return norms + (size_t)2 * cfg.n_layers * cfg.hidden; }
+    const float *q_norm(int l) const {
+        return cfg.qk_norm ? norms + (size_t)(2 * cfg.n_layers + 1) * cfg.hidden + (size_t)l * cfg.head_dim
+                           : nullptr;
+    }
+    const float *k_norm(int l) const {
+        return cfg.qk_norm ? norms + (size_t)(2 * cfg.n_layers + 1) * cfg.hidden +
+                                 (size_t)(cfg.n_layers + l) * cfg.head_dim
+                           : nullptr;
+    }
+};
+
+struct mlxcat_cache {
+    mlxcat_ctx *ctx = nullptr;
+    int rows = 0, max_len = 0, hist_cap = 0;
+    std::vector<void *> allocs;
+    __half *k = nullptr, *v = nullptr;
+    // device row state
+    int32_t *hist = nullptr, *hist_len = nullptr, *kv_len = nullptr, *n_gen = nullptr,
+            *max_new = nullptr, *active = nullptr, *has_seed = nullptr, *eos = nullptr,
+            *n_eos = nullptr, *trigger = nullptr;
+    float *temperature = nullptr, *top_p = nullptr;
+    uint64_t *seed = nullptr;
+    std::vector<float> host_temp;
+    // step buffers
+    int m_cap = 0;
+    int32_t *vtok = nullptr, *count = nullptr, *trow = nullptr, *tpos = nullptr, *amax = nullptr,
+            *out_tok = nullptr, *out_n = nullptr, *out_fin = nullptr, *first_tok = nullptr,
+            *ptok = nullptr;
+    unsigned long long *stats = nullptr;
+    float *h = nullptr, *part = nullptr, *logits = nullptr;
+    __half *xn = nullptr, *qbuf = nullptr;
+    size_t part_floats = 0;
+    AttnScratch attn;
+    int attn_splits = 1;
+    SampleScratch samp{};
+    // pinned host mirrors
+    int32_t *h_tok = nullptr, *h_n = nullptr, *h_fin = nullptr;
+    unsigned long long *h_stats = nullptr;
+    // graph of the speculative step
+    cudaGraphExec_t graph = nullptr;
+    mlxcat_spec_config gkey{};
+    bool gsampled = false;
+    int64_t graph_launches = 0;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    int last_k = -1;
+
+    RowState rs() const {
+        RowState r;
+        r.hist = hist; r.hist_len = hist_len; r.kv_len = kv_len; r.n_gen = n_gen;
+        r.max_new = max_new; r.active = active; r.temperature = temperature; r.top_p = top_p;
+        r.seed = seed; r.has_seed = has_seed; r.eos = eos; r.n_eos = n_eos; r.trigger = trigger;
+        r.hist_cap = hist_cap; r.rows = rows;
+        return r;
+    }
+    KVLayer layer(int l) const {
+        const mlxcat_model_config &c = ctx->cfg;
+        KVLayer kv;
+        const size_t per = (size_t)rows * c.n_kv_heads * max_len * c.head_dim;
+        kv.k = k + (size_t)l * per;
+        kv.v = v + (size_t)l * per;
+        kv.max_len = max_len;
+        return kv;
+    }
+};
+
+namespace {
+
+int set_err(mlxcat_ctx *ctx, int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->err = buf;
+    return code;
+}
+
+int op_err(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_op_err = buf;
+    return code;
+}
+
+#define CK(ctx_, expr)                                                                      \
+    do {                                                                                    \
+        cudaError_t e_ = (expr);                                                            \
+        if (e_ != cudaSuccess)                                                              \
+            return set_err((ctx_), e_ == cudaErrorMemoryAllocation ? MLXCAT_E_OOM : MLXCAT_E_CUDA, \
+                           "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__); \
+    } while (0)
+
+#define LK(ctx_, expr)                                                                      \
+    do {                                                                                    \
+        (ctx_)->launches++;                                                                 \
+        CK(ctx_, expr);                                                                     \
+    } while (0)
+
+template <typename T>
+cudaError_t dalloc(std::vector<void *> &list, T **p, size_t n) {
+    void *q = nullptr;
+    cudaError_t e = cudaMalloc(&q, std::max<size_t>(n, 1) * sizeof(T));
+    if (e != cudaSuccess) return e;
+    list.push_back(q);
+    *p = static_cast<T *>(q);
+    return cudaSuccess;
+}
+
+bool valid_config(const mlxcat_model_config *c, std::string &why) {
+    if (c->kind == MLXCAT_MODEL_TABLE) {
+        if (c->vocab <= 0) { why = "vocab must be positive"; return false; }
+        return true;
+    }
+    if (c->kind != MLXCAT_MODEL_TRANSFORMER) { why = "unknown model kind"; return false; }
+    if (c->group_size != 64 || c->bits != 4) { why = "only MLX affine q4 group 64 is supported"; return false; }
+    if (c->n_layers <= 0 || c->hidden <= 0 || c->n_heads <= 0 || c->n_kv_heads <= 0 ||
+        c->head_dim <= 0 || c->intermediate <= 0 || c->vocab <= 0) {
+        why = "dimensions must be positive";
+        return false;
+    }
+    if (c->n_heads % c->n_kv_heads) { why = "n_heads must be a multiple of n_kv_heads"; return false; }
+    if (c->head_dim != 64 && c->head_dim != 128) { why = "head_dim must be 64 or 128"; return false; }
+    const int qkv = (c->n_heads + 2 * c->n_kv_heads) * c->head_dim;
+    const int dims[] = {c->hidden, c->intermediate, c->n_heads * c->head_dim, qkv, 2 * c->intermediate, c->vocab};
+    for (int d : dims)
+        if (d % 128) { why = "hidden, intermediate, q/kv widths and vocab must be multiples of 128"; return false; }
+    return true;
+}
+
+int splits_for(const mlxcat_ctx *ctx, int N, int K, int M) {
+    return q4_linear_real_splits(K, q4_linear_splits(N, K, M, ctx->sm_count));
+}
+
+// ---------------------------------------------------------------------------
+// forward over M tokens (tok/trow/tpos on device); logits for tokens
+// [lg_from, M) into c->logits (rows in that order); lg_from = M: no logits
+// ---------------------------------------------------------------------------
+int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *trow,
+            const int32_t *tpos, int lg_from) {
+    mlxcat_ctx *ctx = c->ctx;
+    const mlxcat_model_config &cf = ctx->cfg;
+    cudaStream_t st = ctx->stream;
+    if (cf.kind == MLXCAT_MODEL_TABLE) {
+        if (lg_from < M) LK(ctx, table_logits(ctx->table, tok + lg_from, M - lg_from, cf.vocab, c->logits, st));
+        return MLXCAT_OK;
+    }
+    const int H = cf.hidden, D = cf.head_dim, Hq = cf.n_heads, Hkv = cf.n_kv_heads,
+              I = cf.intermediate, L = cf.n_layers;
+    const float eps = cf.rms_eps;
+    LK(ctx, embed_norm(ctx->embed.view(), tok, M, ctx->attn_norm(0), eps, c->h, c->xn, st));
+    for (int l = 0; l < L; ++l) {
+        const KVLayer kv = c->layer(l);
+        int sp = splits_for(ctx, ctx->qkv[l].N, H, M);
+        LK(ctx, q4_linear(ctx->qkv[l].view(), c->xn, M, H, q4_linear_splits(ctx->qkv[l].N, H, M, ctx->sm_count), c->part, st));
+        LK(ctx, qkv_epilogue(c->part, sp, M, Hq, Hkv, D, ctx->q_norm(l), ctx->k_norm(l), eps,
+                             ctx->inv_freq, trow, tpos, c->qbuf, kv, st));
+        ctx->launches++;  // attention is two kernels
+        LK(ctx, attention(c->qbuf, kv, trow, tpos, M, qg, Hq, Hkv, D, KEY_CHUNK, c->attn_splits,
+                          c->attn, c->xn, true, st));
+        sp = splits_for(ctx, H, Hq * D, M);
+        LK(ctx, q4_linear(ctx->o[l].view(), c->xn, M, Hq * D, q4_linear_splits(H, Hq * D, M, ctx->sm_count), c->part, st));
+        LK(ctx, residual_norm(c->part, sp, M, H, ctx->mlp_norm(l), eps, c->h, c->xn, st));
+        sp = splits_for(ctx, 2 * I, H, M);
+        LK(ctx, q4_linear(ctx->gu[l].view(), c->xn, M, H, q4_linear_splits(2 * I, H, M, ctx->sm_count), c->part, st));
+        LK(ctx, swiglu(c->part, sp, M, I, c->xn, st));
+        sp = splits_for(ctx, H, I, M);
+        LK(ctx, q4_linear(ctx->down[l].view(), c->xn, M, I, q4_linear_splits(H, I, M, ctx->sm_count), c->part, st));
+        LK(ctx, residual_norm(c->part, sp, M, H, l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(),
+                              eps, c->h, c->xn, st));
+    }
+    if (lg_from < M) {
+        const DevLin &head = cf.tie_embeddings ? ctx->embed : ctx->lm_head;
+        LK(ctx, q4_linear(head.view(), c->xn + (size_t)lg_from * H, M - lg_from, H, 1, c->logits, st));
+    }
+    return MLXCAT_OK;
+}
+
+int check_weights(mlxcat_ctx *ctx) {
+    if (!ctx->have_weights) return set_err(ctx, MLXCAT_E_STATE, "weights not loaded");
+    return MLXCAT_OK;
+}
+
+int validate_spec(mlxcat_ctx *ctx, const mlxcat_spec_config *s) {
+    if (!s) return set_err(ctx, MLXCAT_E_INVALID, "spec config is NULL");
+    if (s->max_proposal < 0 || s->max_proposal > MLXCAT_MAX_PROPOSAL)
+        return set_err(ctx, MLXCAT_E_INVALID, "max_proposal must be in [0, %d]", MLXCAT_MAX_PROPOSAL);
+    if (s->max_suffix < 1 || s->min_context < 2 || (s->mode != 0 && s->mode != 1))
+        return set_err(ctx, MLXCAT_E_INVALID, "bad spec config");
+    return MLXCAT_OK;
+}
+
+SpecParams params_of(const mlxcat_spec_config *s) {
+    SpecParams p;
+    p.mode = s->mode;
+    p.enabled = s->enabled;
+    p.k = s->enabled ? s->max_proposal : 0;
+    p.n = s->max_suffix;
+    p.min_ctx = s->min_context;
+    return p;
+}
+
+StepOut step_out(mlxcat_cache *c) {
+    StepOut o;
+    o.tokens = c->out_tok; o.n = c->out_n; o.finished = c->out_fin; o.stats = c->stats;
+    return o;
+}
+
+bool any_sampled(const mlxcat_cache *c) {
+    for (float t : c->host_temp)
+        if (t != 0.0f) return true;
+    return false;
+}
+
+// draft -> verify -> accept, enqueued on the context stream
+int enqueue_step(mlxcat_cache *c, const SpecParams &sp, bool sampled, bool timed) {
+    mlxcat_ctx *ctx = c->ctx;
+    cudaStream_t st = ctx->stream;
+    const int K1 = sp.k + 1, M = c->rows * K1;
+    LK(ctx, draft(c->rs(), sp, c->vtok, c->count, c->trow, c->tpos, st));
+    if (timed) CK(ctx, cudaEventRecord(c->ev0, st));
+    int rc = forward(c, M, K1, c->vtok, c->trow, c->tpos, 0);
+    if (rc) return rc;
+    if (timed) CK(ctx, cudaEventRecord(c->ev1, st));
+    LK(ctx, argmax_rows(c->logits, M, ctx->cfg.vocab, c->amax, st));
+    LK(ctx, accept_greedy(c->rs(), sp, c->vtok, c->count, c->amax, step_out(c), st));
+    if (sampled) {
+        ctx->launches++;
+        LK(ctx, accept_sampled(c->rs(), sp, c->vtok, c->count, c->logits, ctx->cfg.vocab, c->samp,
+                               step_out(c), st));
+    }
+    CK(ctx, cudaMemcpyAsync(c->h_tok, c->out_tok, sizeof(int32_t) * M, cudaMemcpyDeviceToHost, st));
+    CK(ctx, cudaMemcpyAsync(c->h_n, c->out_n, sizeof(int32_t) * c->rows, cudaMemcpyDeviceToHost, st));
+    CK(ctx, cudaMemcpyAsync(c->h_fin, c->out_fin, sizeof(int32_t) * c->rows, cudaMemcpyDeviceToHost, st));
+    CK(ctx, cudaMemcpyAsync(c->h_stats, c->stats, sizeof(unsigned long long) * 4, cudaMemcpyDeviceToHost, st));
+    return MLXCAT_OK;
+}
+
+void copy_out(mlxcat_cache *c, int K1, int32_t *out_tokens, int32_t *out_counts, int32_t *out_fin,
+              mlxcat_stats *stats) {
+    if (out_tokens) memcpy(out_tokens, c->h_tok, sizeof(int32_t) * c->rows * K1);
+    if (out_counts) memcpy(out_counts, c->h_n, sizeof(int32_t) * c->rows);
+    if (out_fin) memcpy(out_fin, c->h_fin, sizeof(int32_t) * c->rows);
+    if (stats) {
+        stats->proposed = (int64_t)c->h_stats[0];
+        stats->accepted = (int64_t)c->h_stats[1];
+        stats->proposal_batches = (int64_t)c->h_stats[2];
+        stats->rejected_batches = (int64_t)c->h_stats[3];
+    }
+    for (int r = 0; r < c->rows; ++r)
+        if (c->h_fin[r]) c->host_temp[r] = 0.0f;
+}
+
+void drop_graph(mlxcat_cache *c) {
+    if (c->graph) cudaGraphExecDestroy(c->graph);
+    c->graph = nullptr;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+const char *mlxcat_last_error(const mlxcat_ctx *ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+const char *mlxcat_op_last_error(void) { return g_op_err.c_str(); }
+
+int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx **out) {
+    if (!cfg || !out) return op_err(MLXCAT_E_INVALID, "null argument");
+    *out = nullptr;
+    std::string why;
+    if (!valid_config(cfg, why)) return op_err(MLXCAT_E_INVALID, "%s", why.c_str());
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess || ndev == 0)
+        return op_err(MLXCAT_E_CUDA, "no CUDA device: %s", cudaGetErrorString(e));
+    if (device < 0 || device >= ndev) return op_err(MLXCAT_E_INVALID, "device %d out of range", device);
+    mlxcat_ctx *ctx = new mlxcat_ctx();
+    ctx->cfg = *cfg;
+    ctx->device = device;
+    auto fail = [&](int code) {
+        g_op_err = ctx->err;
+        mlxcat_ctx_destroy(ctx);
+        return code;
+    };
+    if (cudaSetDevice(device) != cudaSuccess) { set_err(ctx, MLXCAT_E_CUDA, "cudaSetDevice failed"); return fail(MLXCAT_E_CUDA); }
+    cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+    if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        set_err(ctx, MLXCAT_E_CUDA, "stream creation failed");
+        return fail(MLXCAT_E_CUDA);
+    }
+    const mlxcat_model_config &c = *cfg;
+    int rc = MLXCAT_OK;
+    auto alloc_lin = [&](DevLin &w, int N, int K) {
+        w.N = N; w.K = K;
+        if (dalloc(ctx->allocs, &w.wq, (size_t)N * K / 8) != cudaSuccess ||
+            dalloc(ctx->allocs, &w.s, (size_t)N * K / 64) != cudaSuccess ||
+            dalloc(ctx->allocs, &w.b, (size_t)N * K / 64) != cudaSuccess)
+            rc = set_err(ctx, MLXCAT_E_OOM, "weight allocation failed (%d x %d)", N, K);
+    };
+    if (c.kind == MLXCAT_MODEL_TABLE) {
+        if (dalloc(ctx->allocs, &ctx->table, (size_t)c.vocab) != cudaSuccess)
+            rc = set_err(ctx, MLXCAT_E_OOM, "table allocation failed");
+    } else {
+        const int H = c.hidden, D = c.head_dim, L = c.n_layers;
+        alloc_lin(ctx->embed, c.vocab, H);
+        if (!c.tie_embeddings) alloc_lin(ctx->lm_head, c.vocab, H);
+        ctx->qkv.resize(L); ctx->o.resize(L); ctx->gu.resize(L); ctx->down.resize(L);
+        for (int l = 0; l < L && rc == MLXCAT_OK; ++l) {
+            alloc_lin(ctx->qkv[l], (c.n_heads + 2 * c.n_kv_heads) * D, H);
+            alloc_lin(ctx->o[l], H, c.n_heads * D);
+            alloc_lin(ctx->gu[l], 2 * c.intermediate, H);
+            alloc_lin(ctx->down[l], H, c.intermediate);
+        }
+        const size_t nn = (size_t)(2 * L + 1) * H + (size_t)2 * L * D;
+        if (rc == MLXCAT_OK && dalloc(ctx->allocs, &ctx->norms, nn) != cudaSuccess)
+            rc = set_err(ctx, MLXCAT_E_OOM, "norm allocation failed");
+        if (rc == MLXCAT_OK && dalloc(ctx->allocs, &ctx->inv_freq, (size_t)D / 2) != cudaSuccess)
+            rc = set_err(ctx, MLXCAT_E_OOM, "rope table allocation failed");
+        if (rc == MLXCAT_OK) {
+            // RMSNorm weights: ones (random-init checkpoints carry unit norms)
+            std::vector<float> ones(nn, 1.0f);
+            std::vector<float> inv(D / 2);
+            for (int i = 0; i < D / 2; ++i)
+                inv[i] = (float)(1.0 / pow((double)c.rope_theta, (2.0 * i) / (double)D));
+            if (cudaMemcpy(ctx->norms, ones.data(), nn * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+                cudaMemcpy(ctx->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+                rc = set_err(ctx, MLXCAT_E_CUDA, "norm / rope upload failed");
+        }
+    }
+    if (rc != MLXCAT_OK) return fail(rc);
+    *out = ctx;
+    return MLXCAT_OK;
+}
+
+int mlxcat_ctx_destroy(mlxcat_ctx *ctx) {
+    if (!ctx) return MLXCAT_OK;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    for (void *p : ctx->allocs) cudaFree(p);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return MLXCAT_OK;
+}
+
+int mlxcat_ctx_stream(mlxcat_ctx *ctx, void **stream) {
+    if (!ctx || !stream) return MLXCAT_E_INVALID;
+    *stream = (void *)ctx->stream;
+    return MLXCAT_OK;
+}
+
+int mlxcat_ctx_synchronize(mlxcat_ctx *ctx) {
+    if (!ctx) return MLXCAT_E_INVALID;
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    return MLXCAT_OK;
+}
+
+int64_t mlxcat_ctx_launch_count(const mlxcat_ctx *ctx) { return ctx ? ctx->launches : -1; }
+
+static DevLin *lin_for(mlxcat_ctx *ctx, uint32_t id, int *row_off, int *rows) {
+    const mlxcat_model_config &c = ctx->cfg;
+    if (c.kind != MLXCAT_MODEL_TRANSFORMER) return nullptr;
+    if (id == 0xFFFF0000u) { *row_off = 0; *rows = c.vocab; return &ctx->embed; }
+    if (id == 0xFFFF0001u) {
+        if (c.tie_embeddings) return nullptr;
+        *row_off = 0; *rows = c.vocab; return &ctx->lm_head;
+    }
+    const int l = (int)(id / 16u), kind = (int)(id % 16u);
+    if (l >= c.n_layers) return nullptr;
+    const int D = c.head_dim, qd = c.n_heads * D, kvd = c.n_kv_heads * D;
+    switch (kind) {
+    case 0: *row_off = 0; *rows = qd; return &ctx->qkv[l];
+    case 1: *row_off = qd; *rows = kvd; return &ctx->qkv[l];
+    case 2: *row_off = qd + kvd; *rows = kvd; return &ctx->qkv[l];
+    case 3: *row_off = 0; *rows = c.hidden; return &ctx->o[l];
+    case 4: *row_off = 0; *rows = c.intermediate; return &ctx->gu[l];
+    case 5: *row_off = c.intermediate; *rows = c.intermediate; return &ctx->gu[l];
+    case 6: *row_off = 0; *rows = c.hidden; return &ctx->down[l];
+    default: return nullptr;
+    }
+}
+
+int mlxcat_weights_synth(mlxcat_ctx *ctx, uint64_t seed, float stddev) {
+    if (!ctx) return MLXCAT_E_INVALID;
+    const mlxcat_model_config &c = ctx->cfg;
+    if (c.kind != MLXCAT_MODEL_TRANSFORMER) return set_err(ctx, MLXCAT_E_INVALID, "synth needs a transformer model");
+    CK(ctx, cudaSetDevice(ctx->device));
+    std::vector<uint32_t> ids = {0xFFFF0000u};
+    if (!c.tie_embeddings) ids.push_back(0xFFFF0001u);
+    for (int l = 0; l < c.n_layers; ++l)
+        for (int k = 0; k < 7; ++k) ids.push_back((uint32_t)l * 16u + (uint32_t)k);
+    for (uint32_t id : ids) {
+        int off = 0, rows = 0;
+        DevLin *w = lin_for(ctx, id, &off, &rows);
+        LK(ctx, synth_q4(seed, id, stddev, rows, w->K, w->wq, w->s, w->b, off, ctx->stream));
+    }
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    ctx->have_weights = true;
+    return MLXCAT_OK;
+}
+
+int mlxcat_weights_set_q4(mlxcat_ctx *ctx, uint32_t id, const uint32_t *wq, const uint16_t *scales,
+                          const uint16_t *biases) {
+    if (!ctx || !wq || !scales || !biases) return MLXCAT_E_INVALID;
+    int off = 0, rows = 0;
+    DevLin *w = lin_for(ctx, id, &off, &rows);
+    if (!w) return set_err(ctx, MLXCAT_E_INVALID, "unknown tensor id 0x%x", id);
+    CK(ctx, cudaSetDevice(ctx->device));
+    const int K = w->K;
+    CK(ctx, cudaMemcpy(w->wq + (size_t)off * (K / 8), wq, (size_t)rows * (K / 8) * 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(w->s + (size_t)off * (K / 64), scales, (size_t)rows * (K / 64) * 2, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(w->b + (size_t)off * (K / 64), biases, (size_t)rows * (K / 64) * 2, cudaMemcpyHostToDevice));
+    ctx->have_weights = true;
+    return MLXCAT_OK;
+}
+
+int mlxcat_weights_get_q4(mlxcat_ctx *ctx, uint32_t id, uint32_t *wq, uint16_t *scales, uint16_t *biases) {
+    if (!ctx) return MLXCAT_E_INVALID;
+    int off = 0, rows = 0;
+    DevLin *w = lin_for(ctx, id, &off, &rows);
+    if (!w) return set_err(ctx, MLXCAT_E_INVALID, "unknown tensor id 0x%x", id);
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    const int K = w->K;
+    if (wq) CK(ctx, cudaMemcpy(wq, w->wq + (size_t)off * (K / 8), (size_t)rows * (K / 8) * 4, cudaMemcpyDeviceToHost));
+    if (scales) CK(ctx, cudaMemcpy(scales, w->s + (size_t)off * (K / 64), (size_t)rows * (K / 64) * 2, cudaMemcpyDeviceToHost));
+    if (biases) CK(ctx, cudaMemcpy(biases, w->b + (size_t)off * (K / 64), (size_t)rows * (K / 64) * 2, cudaMemcpyDeviceToHost));
+    return MLXCAT_OK;
+}
+
+int mlxcat_weights_set_table(mlxcat_ctx *ctx, const int32_t *next, int32_t vocab) {
+    if (!ctx || !next) return MLXCAT_E_INVALID;
+    if (ctx->cfg.kind != MLXCAT_MODEL_TABLE || vocab != ctx->cfg.vocab)
+        return set_err(ctx, MLXCAT_E_INVALID, "table model of vocab %d expected", ctx->cfg.vocab);
+    for (int i = 0; i < vocab; ++i)
+        if (next[i] < 0 || next[i] >= vocab) return set_err(ctx, MLXCAT_E_INVALID, "table entry out of range");
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaMemcpy(ctx->table, next, sizeof(int32_t) * vocab, cudaMemcpyHostToDevice));
+    ctx->have_weights = true;
+    return MLXCAT_OK;
+}
+
+int64_t mlxcat_weights_bytes(const mlxcat_ctx *ctx) {
+    if (!ctx || ctx->cfg.kind != MLXCAT_MODEL_TRANSFORMER) return 0;
+    size_t b = ctx->cfg.tie_embeddings ? ctx->embed.bytes() : ctx->lm_head.bytes();
+    for (int l = 0; l < ctx->cfg.n_layers; ++l)
+        b += ctx->qkv[l].bytes() + ctx->o[l].bytes() + ctx->gu[l].bytes() + ctx->down[l].bytes();
+    return (int64_t)b;
+}
+
+int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxcat_cache **out) {
+    if (!ctx || !out || max_rows <= 0 || max_len <= MLXCAT_MAX_PROPOSAL + 2)
+        return set_err(ctx, MLXCAT_E_INVALID, "bad cache shape");
+    *out = nullptr;
+    CK(ctx, cudaSetDevice(ctx->device));
+    const mlxcat_model_config &cf = ctx->cfg;
+    mlxcat_cache *c = new mlxcat_cache();
+    c->ctx = ctx;
+    c->rows = max_rows;
+    c->max_len = max_len;
+    c->hist_cap = max_len + 1;
+    c->host_temp.assign(max_rows, 0.0f);
+    auto &A = c->allocs;
+    int rc = MLXCAT_OK;
+    auto chk = [&](cudaError_t e) {
+        if (e != cudaSuccess && rc == MLXCAT_OK)
+            rc = set_err(ctx, e == cudaErrorMemoryAllocation ? MLXCAT_E_OOM : MLXCAT_E_CUDA,
+                         "cache allocation: %s", cudaGetErrorString(e));
+    };
+    const bool tr = cf.kind == MLXCAT_MODEL_TRANSFORMER;
+    const int R = max_rows;
+    c->m_cap = std::max(R * (MLXCAT_MAX_PROPOSAL + 1), PREFILL_CHUNK);
+    const int Mc = c->m_cap;
+    if (tr) {
+        const size_t kvn = (size_t)cf.n_layers * R * cf.n_kv_heads * max_len * cf.head_dim;
+        chk(dalloc(A, &c->k, kvn));
+        chk(dalloc(A, &c->v, kvn));
+    }
+    chk(dalloc(A, &c->hist, (size_t)R * c->hist_cap));
+    chk(dalloc(A, &c->hist_len, R)); chk(dalloc(A, &c->kv_len, R)); chk(dalloc(A, &c->n_gen, R));
+    chk(dalloc(A, &c->max_new, R)); chk(dalloc(A, &c->active, R)); chk(dalloc(A, &c->has_seed, R));
+    chk(dalloc(A, &c->eos, (size_t)R * MLXCAT_MAX_EOS)); chk(dalloc(A, &c->n_eos, R));
+    chk(dalloc(A, &c->trigger, R)); chk(dalloc(A, &c->temperature, R)); chk(dalloc(A, &c->top_p, R));
+    chk(dalloc(A, &c->seed, R));
+    chk(dalloc(A, &c->vtok, Mc)); chk(dalloc(A, &c->count, R)); chk(dalloc(A, &c->trow, Mc));
+    chk(dalloc(A, &c->tpos, Mc)); chk(dalloc(A, &c->amax, Mc)); chk(dalloc(A, &c->out_tok, Mc));
+    chk(dalloc(A, &c->out_n, R)); chk(dalloc(A, &c->out_fin, R)); chk(dalloc(A, &c->first_tok, 1));
+    chk(dalloc(A, &c->ptok, Mc)); chk(dalloc(A, &c->stats, 4));
+    chk(dalloc(A, &c->logits, (size_t)Mc * cf.vocab));
+    const int KS = Mc;   // sampling scratch slots (rows*(k+1))
+    chk(dalloc(A, &c->samp.m, KS)); chk(dalloc(A, &c->samp.thr, KS));
+    chk(dalloc(A, &c->samp.S, KS)); chk(dalloc(A, &c->samp.Pd, KS));
+    if (tr) {
+        const int H = cf.hidden, I = cf.intermediate, D = cf.head_dim;
+        const int Hq = cf.n_heads, Hkv = cf.n_kv_heads;
+        const int xw = std::max(std::max(H, I), Hq * D);
+        chk(dalloc(A, &c->h, (size_t)Mc * H));
+        chk(dalloc(A, &c->xn, (size_t)Mc * xw));
+        chk(dalloc(A, &c->qbuf, (size_t)Mc * Hq * D));
+        // split-K partials: max over the linears and every token count
+        size_t pf = 0;
+        const int NK[4][2] = {{(Hq + 2 * Hkv) * D, H}, {H, Hq * D}, {2 * I, H}, {H, I}};
+        for (int m = 1; m <= Mc; ++m)
+            for (auto &nk : NK) pf = std::max(pf, (size_t)splits_for(ctx, nk[0], nk[1], m) * m * nk[0]);
+        c->part_floats = pf;
+        chk(dalloc(A, &c->part, pf));
+        // attention scratch
+        c->attn_splits = attention_max_splits(max_len, KEY_CHUNK);
+        int groups = std::max(R, (PREFILL_CHUNK + PREFILL_QG - 1) / PREFILL_QG);
+        int qrows = 16;
+        for (int k = 0; k <= MLXCAT_MAX_PROPOSAL; ++k) qrows = std::max(qrows, attention_qrows(k + 1, Hq, Hkv));
+        qrows = std::max(qrows, attention_qrows(PREFILL_QG, Hq, Hkv));
+        groups = std::max(groups, R);
+        const size_t items = attention_scratch_items(groups, Hkv, c->attn_splits);
+        c->attn.items = items;
+        chk(dalloc(A, &c->attn.o, items * qrows * D));
+        chk(dalloc(A, &c->attn.ml, items * qrows * 2));
+    }
+    chk(cudaMallocHost((void **)&c->h_tok, sizeof(int32_t) * Mc));
+    chk(cudaMallocHost((void **)&c->h_n, sizeof(int32_t) * R));
+    chk(cudaMallocHost((void **)&c->h_fin, sizeof(int32_t) * R));
+    chk(cudaMallocHost((void **)&c->h_stats, sizeof(unsigned long long) * 4));
+    chk(cudaEventCreate(&c->ev0));
+    chk(cudaEventCreate(&c->ev1));
+    if (rc == MLXCAT_OK) {
+        chk(cudaMemset(c->active, 0, sizeof(int32_t) * R));
+        chk(cudaMemset(c->hist_len, 0, sizeof(int32_t) * R));
+        chk(cudaMemset(c->kv_len, 0, sizeof(int32_t) * R));
+        chk(cudaMemset(c->n_gen, 0, sizeof(int32_t) * R));
+        chk(cudaMemset(c->max_new, 0, sizeof(int32_t) * R));
+        chk(cudaMemset(c->temperature, 0, sizeof(float) * R));
+        chk(cudaMemset(c->top_p, 0, sizeof(float) * R));
+        chk(cudaMemset(c->has_seed, 0, sizeof(int32_t) * R));
+        chk(cudaMemset(c->n_eos, 0, sizeof(int32_t) * R));
+        chk(cudaMemset(c->seed, 0, sizeof(uint64_t) * R));
+        chk(cudaMemset(c->stats, 0, sizeof(unsigned long long) * 4));
+        std::vector<int32_t> neg(R, -1);
+        chk(cudaMemcpy(c->trigger, neg.data(), sizeof(int32_t) * R, cudaMemcpyHostToDevice));
+    }
+    if (rc != MLXCAT_OK) {
+        mlxcat_cache_destroy(c);
+        return rc;
+    }
+    *out = c;
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_destroy(mlxcat_cache *c) {
+    if (!c) return MLXCAT_OK;
+    cudaSetDevice(c->ctx->device);
+    cudaStreamSynchronize(c->ctx->stream);
+    drop_graph(c);
+    for (void *p : c->allocs) cudaFree(p);
+    if (c->h_tok) cudaFreeHost(c->h_tok);
+    if (c->h_n) cudaFreeHost(c->h_n);
+    if (c->h_fin) cudaFreeHost(c->h_fin);
+    if (c->h_stats) cudaFreeHost(c->h_stats);
+    if (c->ev0) cudaEventDestroy(c->ev0);
+    if (c->ev1) cudaEventDestroy(c->ev1);
+    delete c;
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_insert_row(mlxcat_cache *c, int32_t row, const int32_t *prompt, int32_t len,
+                            int32_t max_new_tokens, const mlxcat_sampling *sp, int32_t *first_token) {
+    if (!c) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    if (row < 0 || row >= c->rows || !prompt || len < 1 || max_new_tokens < 1 || !sp)
+        return set_err(ctx, MLXCAT_E_INVALID, "bad insert arguments");
+    if ((int64_t)len + max_new_tokens + MLXCAT_MAX_PROPOSAL + 1 > c->max_len)
+        return set_err(ctx, MLXCAT_E_INVALID, "prompt %d + max_new %d exceeds cache length %d", len,
+                       max_new_tokens, c->max_len);
+    if (sp->n_eos < 0 || sp->n_eos > MLXCAT_MAX_EOS) return set_err(ctx, MLXCAT_E_INVALID, "too many EOS ids");
+    if (sp->temperature < 0.0f) return set_err(ctx, MLXCAT_E_INVALID, "negative temperature");
+    for (int i = 0; i < len; ++i)
+        if (prompt[i] < 0 || prompt[i] >= ctx->cfg.vocab) return set_err(ctx, MLXCAT_E_INVALID, "prompt token out of range");
+    int rc = check_weights(ctx);
+    if (rc) return rc;
+    CK(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    CK(ctx, cudaStreamSynchronize(st));
+    // row state (host -> device)
+    const int32_t zero = 0, one = 1;
+    const int32_t eos_pad[MLXCAT_MAX_EOS] = {sp->eos[0], sp->eos[1], sp->eos[2], sp->eos[3],
+                                             sp->eos[4], sp->eos[5], sp->eos[6], sp->eos[7]};
+    CK(ctx, cudaMemcpy(c->hist + (size_t)row * c->hist_cap, prompt, sizeof(int32_t) * len, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->hist_len + row, &len, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->kv_len + row, &len, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->n_gen + row, &zero, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->max_new + row, &max_new_tokens, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->active + row, &one, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->temperature + row, &sp->temperature, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->top_p + row, &sp->top_p, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->seed + row, &sp->seed, 8, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->has_seed + row, &sp->has_seed, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->eos + (size_t)row * MLXCAT_MAX_EOS, eos_pad, sizeof eos_pad, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->n_eos + row, &sp->n_eos, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->trigger + row, &sp->trigger, 4, cudaMemcpyHostToDevice));
+    c->host_temp[row] = sp->temperature;
+    // prefill in chunks; logits only for the last prompt token
+    std::vector<int32_t> rr(PREFILL_CHUNK, row), pp(PREFILL_CHUNK);
+    for (int s0 = 0; s0 < len; s0 += PREFILL_CHUNK) {
+        const int n = std::min(PREFILL_CHUNK, len - s0);
+        for (int i = 0; i < n; ++i) pp[i] = s0 + i;
+        CK(ctx, cudaMemcpyAsync(c->ptok, prompt + s0, 4 * n, cudaMemcpyHostToDevice, st));
+        CK(ctx, cudaMemcpyAsync(c->trow, rr.data(), 4 * n, cudaMemcpyHostToDevice, st));
+        CK(ctx, cudaMemcpyAsync(c->tpos, pp.data(), 4 * n, cudaMemcpyHostToDevice, st));
+        const bool last = s0 + n == len;
+        rc = forward(c, n, PREFILL_QG, c->ptok, c->trow, c->tpos, last ? n - 1 : n);
+        if (rc) return rc;
+        CK(ctx, cudaStreamSynchronize(st));   // host staging vectors are reused
+    }
+    LK(ctx, argmax_rows(c->logits, 1, ctx->cfg.vocab, c->amax, st));
+    LK(ctx, sample_first(c->rs(), row, c->logits, ctx->cfg.vocab, c->amax, c->samp, c->first_tok, st));
+    int32_t t0 = 0;
+    CK(ctx, cudaMemcpyAsync(&t0, c->first_tok, 4, cudaMemcpyDeviceToHost, st));
+    CK(ctx, cudaStreamSynchronize(st));
+    if (first_token) *first_token = t0;
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_remove_row(mlxcat_cache *c, int32_t row) {
+    if (!c || row < 0 || row >= c->rows) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    const int32_t zero = 0;
+    CK(ctx, cudaMemcpy(c->active + row, &zero, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->kv_len + row, &zero, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->hist_len + row, &zero, 4, cudaMemcpyHostToDevice));
+    c->host_temp[row] = 0.0f;
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_trim(mlxcat_cache *c, int32_t n, int32_t *trimmed) {
+    if (!c || n < 0) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    std::vector<int32_t> len(c->rows);
+    CK(ctx, cudaMemcpy(len.data(), c->kv_len, 4 * c->rows, cudaMemcpyDeviceToHost));
+    int idx = 0;
+    for (int x : len) idx = std::max(idx, x);
+    const int t = std::min(n, idx);
+    for (int &x : len) x -= std::min(t, x);
+    CK(ctx, cudaMemcpy(c->kv_len, len.data(), 4 * c->rows, cudaMemcpyHostToDevice));
+    if (trimmed) *trimmed = t;
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_lengths(mlxcat_cache *c, int32_t *out) {
+    if (!c || !out) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    CK(ctx, cudaMemcpy(out, c->kv_len, 4 * c->rows, cudaMemcpyDeviceToHost));
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_active(mlxcat_cache *c, int32_t *out) {
+    if (!c || !out) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    CK(ctx, cudaMemcpy(out, c->active, 4 * c->rows, cudaMemcpyDeviceToHost));
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_history(mlxcat_cache *c, int32_t row, int32_t *out, int32_t cap, int32_t *len) {
+    if (!c || row < 0 || row >= c->rows) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    int32_t L = 0;
+    CK(ctx, cudaMemcpy(&L, c->hist_len + row, 4, cudaMemcpyDeviceToHost));
+    if (len) *len = L;
+    if (out && cap > 0)
+        CK(ctx, cudaMemcpy(out, c->hist + (size_t)row * c->hist_cap, 4 * (size_t)std::min(L, cap),
+                           cudaMemcpyDeviceToHost));
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_extract_row(mlxcat_cache *c, int32_t row, int32_t layer, uint16_t *k_out,
+                             uint16_t *v_out) {
+    if (!c || row < 0 || row >= c->rows) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    const mlxcat_model_config &cf = ctx->cfg;
+    if (cf.kind != MLXCAT_MODEL_TRANSFORMER || layer < 0 || layer >= cf.n_layers)
+        return set_err(ctx, MLXCAT_E_INVALID, "no such layer");
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    int32_t L = 0;
+    CK(ctx, cudaMemcpy(&L, c->kv_len + row, 4, cudaMemcpyDeviceToHost));
+    const KVLayer kv = c->layer(layer);
+    const size_t D = cf.head_dim;
+    for (int h = 0; h < cf.n_kv_heads; ++h) {
+        const size_t src = (((size_t)row * cf.n_kv_heads + h) * c->max_len) * D;
+        if (k_out) CK(ctx, cudaMemcpy(k_out + (size_t)h * L * D, kv.k + src, 2 * L * D, cudaMemcpyDeviceToHost));
+        if (v_out) CK(ctx, cudaMemcpy(v_out + (size_t)h * L * D, kv.v + src, 2 * L * D, cudaMemcpyDeviceToHost));
+    }
+    return MLXCAT_OK;
+}
+
+int mlxcat_draft(mlxcat_cache *c, const mlxcat_spec_config *spec, int32_t *drafts, int32_t *counts) {
+    if (!c) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    int rc = validate_spec(ctx, spec);
+    if (rc) return rc;
+    CK(ctx, cudaSetDevice(ctx->device));
+    const SpecParams sp = params_of(spec);
+    const int K1 = sp.k + 1;
+    cudaStream_t st = ctx->stream;
+    LK(ctx, draft(c->rs(), sp, c->vtok, c->count, c->trow, c->tpos, st));
+    c->last_k = sp.k;
+    std::vector<int32_t> vt((size_t)c->rows * K1);
+    CK(ctx, cudaMemcpyAsync(vt.data(), c->vtok, 4 * vt.size(), cudaMemcpyDeviceToHost, st));
+    if (counts) CK(ctx, cudaMemcpyAsync(counts, c->count, 4 * c->rows, cudaMemcpyDeviceToHost, st));
+    CK(ctx, cudaStreamSynchronize(st));
+    if (drafts)
+        for (int r = 0; r < c->rows; ++r)
+            for (int i = 0; i < sp.k; ++i) drafts[r * sp.k + i] = vt[(size_t)r * K1 + 1 + i];
+    return MLXCAT_OK;
+}
+
+int mlxcat_verify_forward(mlxcat_cache *c, const mlxcat_spec_config *spec, float *logits) {
+    if (!c) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    int rc = validate_spec(ctx, spec);
+    if (rc) return rc;
+    if ((rc = check_weights(ctx))) return rc;
+    const SpecParams sp = params_of(spec);
+    if (c->last_k != sp.k) return set_err(ctx, MLXCAT_E_STATE, "mlxcat_draft with the same config must come first");
+    CK(ctx, cudaSetDevice(ctx->device));
+    const int K1 = sp.k + 1, M = c->rows * K1;
+    rc = forward(c, M, K1, c->vtok, c->trow, c->tpos, 0);
+    if (rc) return rc;
+    if (logits)
+        CK(ctx, cudaMemcpyAsync(logits, c->logits, sizeof(float) * (size_t)M * ctx->cfg.vocab,
+                                cudaMemcpyDeviceToHost, ctx->stream));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    return MLXCAT_OK;
+}
+
+int mlxcat_accept(mlxcat_cache *c, const mlxcat_spec_config *spec, int32_t *out_tokens,
+                  int32_t *out_counts, int32_t *out_fin, mlxcat_stats *stats) {
+    if (!c) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    int rc = validate_spec(ctx, spec);
+    if (rc) return rc;
+    const SpecParams sp = params_of(spec);
+    if (c->last_k != sp.k) return set_err(ctx, MLXCAT_E_STATE, "mlxcat_verify_forward with the same config must come first");
+    CK(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    const int K1 = sp.k + 1, M = c->rows * K1;
+    LK(ctx, argmax_rows(c->logits, M, ctx->cfg.vocab, c->amax, st));
+    LK(ctx, accept_greedy(c->rs(), sp, c->vtok, c->count, c->amax, step_out(c), st));
+    if (any_sampled(c)) {
+        ctx->launches++;
+        LK(ctx, accept_sampled(c->rs(), sp, c->vtok, c->count, c->logits, ctx->cfg.vocab, c->samp, step_out(c), st));
+    }
+    CK(ctx, cudaMemcpyAsync(c->h_tok, c->out_tok, sizeof(int32_t) * M, cudaMemcpyDeviceToHost, st));
+    CK(ctx, cudaMemcpyAsync(c->h_n, c->out_n, sizeof(int32_t) * c->rows, cudaMemcpyDeviceToHost, st));
+    CK(ctx, cudaMemcpyAsync(c->h_fin, c->out_fin, sizeof(int32_t) * c->rows, cudaMemcpyDeviceToHost, st));
+    CK(ctx, cudaMemcpyAsync(c->h_stats, c->stats, 32, cudaMemcpyDeviceToHost, st));
+    CK(ctx, cudaStreamSynchronize(st));
+    copy_out(c, K1, out_tokens, out_counts, out_fin, stats);
+    c->last_k = -1;
+    return MLXCAT_OK;
+}
+
+int mlxcat_spec_step(mlxcat_cache *c, const mlxcat_spec_config *spec, int32_t *out_tokens,
+                     int32_t *out_counts, int32_t *out_fin, mlxcat_stats *stats) {
+    if (!c) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    int rc = validate_spec(ctx, spec);
+    if (rc) return rc;
+    if ((rc = check_weights(ctx))) return rc;
+    CK(ctx, cudaSetDevice(ctx->device));
+    const SpecParams sp = params_of(spec);
+    const bool sampled = any_sampled(c);
+    const bool same = c->graph && memcmp(&c->gkey, spec, sizeof *spec) == 0 && c->gsampled == sampled;
+    cudaStream_t st = ctx->stream;
+    if (!same) {
+        drop_graph(c);
+        CK(ctx, cudaStreamSynchronize(st));
+        const int64_t before = ctx->launches;
+        cudaGraph_t g = nullptr;
+        CK(ctx, cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        rc = enqueue_step(c, sp, sampled, true);
+        cudaError_t ec = cudaStreamEndCapture(st, &g);
+        if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+        CK(ctx, ec);
+        cudaError_t ei = cudaGraphInstantiate(&c->graph, g, 0);
+        cudaGraphDestroy(g);
+        CK(ctx, ei);
+        c->graph_launches = ctx->launches - before;
+        ctx->launches = before;
+        c->gkey = *spec;
+        c->gsampled = sampled;
+    }
+    CK(ctx, cudaGraphLaunch(c->graph, st));
+    ctx->launches += c->graph_launches;
+    CK(ctx, cudaStreamSynchronize(st));
+    copy_out(c, sp.k + 1, out_tokens, out_counts, out_fin, stats);
+    c->last_k = -1;
+    return MLXCAT_OK;
+}
+
+int mlxcat_last_verify_ms(mlxcat_cache *c, float *ms) {
+    if (!c || !ms) return MLXCAT_E_INVALID;
+    CK(c->ctx, cudaEventElapsedTime(ms, c->ev0, c->ev1));
+    return MLXCAT_OK;
+}
+
+// ---------------------------------------------------------------------------
+// device-pointer operators
+// ---------------------------------------------------------------------------
+static int op_sm_count() {
+    int dev = 0, sm = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev);
+    return sm;
+}
+
+size_t mlxcat_op_q4_linear_workspace(int32_t N, int32_t K, int32_t M) {
+    if (N <= 0 || K <= 0 || M <= 0) return 0;
+    const int sp = q4_linear_real_splits(K, q4_linear_splits(N, K, M, op_sm_count()));
+    return (size_t)M * K * 2 + 256 + (size_t)sp * M * N * 4;
+}
+
+int mlxcat_op_q4_linear(const uint32_t *wq, const uint16_t *scales, const uint16_t *biases, int32_t N,
+                        int32_t K, const uint16_t *x, int32_t M, float *y, void *ws, size_t ws_bytes,
+                        void *stream) {
+    if (!wq || !scales || !biases || !x || !y || N <= 0 || K <= 0 || M <= 0)
+        return op_err(MLXCAT_E_INVALID, "bad q4_linear arguments");
+    if (N % 128 || K % 128) return op_err(MLXCAT_E_INVALID, "N and K must be multiples of 128");
+    const size_t need = mlxcat_op_q4_linear_workspace(N, K, M);
+    if (!ws || ws_bytes < need) return op_err(MLXCAT_E_INVALID, "workspace of %zu bytes required", need);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int plan = q4_linear_splits(N, K, M, op_sm_count());
+    const int sp = q4_linear_real_splits(K, plan);
+    __half *xp = static_cast<__half *>(ws);
+    float *part = reinterpret_cast<float *>(static_cast<char *>(ws) + (((size_t)M * K * 2 + 255) & ~(size_t)255));
+    Q4Weight w;
+    w.wq = wq; w.scales = reinterpret_cast<const __half *>(scales);
+    w.biases = reinterpret_cast<const __half *>(biases); w.N = N; w.K = K;
+    cudaError_t e = permute_activations(reinterpret_cast<const __half *>(x), xp, M, K, st);
+    if (e == cudaSuccess) e = q4_linear(w, xp, M, K, plan, sp == 1 ? y : part, st);
+    if (e == cudaSuccess && sp > 1) e = reduce_splits(part, sp, (size_t)M * N, y, st);
+    if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "q4_linear: %s", cudaGetErrorString(e));
+    return MLXCAT_OK;
+}
+
+size_t mlxcat_op_attention_workspace(int32_t M, int32_t qg, int32_t n_heads, int32_t n_kv, int32_t D,
+                                     int32_t max_len) {
+    if (M <= 0 || qg <= 0 || n_kv <= 0) return 0;
+    const int groups = (M + qg - 1) / qg;
+    const int splits = attention_max_splits(max_len, KEY_CHUNK);
+    const size_t items = attention_scratch_items(groups, n_kv, splits);
+    const int qrows = attention_qrows(qg, n_heads, n_kv);
+    return items * qrows * (size_t)D * 4 + 256 + items * qrows * 2 * 4;
+}
+
+int mlxcat_op_attention(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                        int32_t max_len, const int32_t *trow, const int32_t *tpos, int32_t M, int32_t qg,
+                        int32_t n_heads, int32_t n_kv, int32_t D, uint16_t *out, void *ws,
+                        size_t ws_bytes, void *stream) {
+    if (!q || !k_cache || !v_cache || !trow || !tpos || !out || M <= 0 || qg <= 0 || n_kv <= 0 ||
+        n_heads % n_kv || (D != 64 && D != 128) || qg * (n_heads / n_kv) > 64)
+        return op_err(MLXCAT_E_INVALID, "bad attention arguments");
+    const size_t need = mlxcat_op_attention_workspace(M, qg, n_heads, n_kv, D, max_len);
+    if (!ws || ws_bytes < need) return op_err(MLXCAT_E_INVALID, "workspace of %zu bytes required", need);
+    const int groups = (M + qg - 1) / qg;
+    const int splits = attention_max_splits(max_len, KEY_CHUNK);
+    const size_t items = attention_scratch_items(groups, n_kv, splits);
+    const int qrows = attention_qrows(qg, n_heads, n_kv);
+    AttnScratch sc;
+    sc.o = static_cast<float *>(ws);
+    sc.ml = reinterpret_cast<float *>(static_cast<char *>(ws) + ((items * qrows * (size_t)D * 4 + 255) & ~(size_t)255));
+    sc.items = items;
+    KVLayer kv;
+    kv.k = const_cast<__half *>(reinterpret_cast<const __half *>(k_cache));
+    kv.v = const_cast<__half *>(reinterpret_cast<const __half *>(v_cache));
+    kv.max_len = max_len;
+    cudaError_t e = attention(reinterpret_cast<const __half *>(q), kv, trow, tpos, M, qg, n_heads, n_kv, D,
+                              KEY_CHUNK, splits, sc, reinterpret_cast<__half *>(out), false,
+                              (cudaStream_t)stream);
+    if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "attention: %s", cudaGetErrorString(e));
+    return MLXCAT_OK;
+}
+
+int mlxcat_op_synth_q4(uint64_t seed, uint32_t tensor_id, float stddev, int32_t N, int32_t K, uint32_t *wq,
+                       uint16_t *scales, uint16_t *biases, void *stream) {
+    if (!wq || !scales || !biases || N <= 0 || K <= 0 || K % 64)
+        return op_err(MLXCAT_E_INVALID, "bad synth arguments");
+    cudaError_t e = synth_q4(seed, tensor_id, stddev, N, K, wq, reinterpret_cast<__half *>(scales),
+                             reinterpret_cast<__half *>(biases), 0, (cudaStream_t)stream);
+    if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "synth: %s", cudaGetErrorString(e));
+    return MLXCAT_OK;
+}
+
+static RowState rows_of(const mlxcat_rows *r) {
+    RowState s;
+    s.hist = r->hist; s.hist_cap = r->hist_cap; s.rows = r->rows; s.hist_len = r->hist_len;
+    s.kv_len = r->kv_len; s.n_gen = r->n_gen; s.max_new = r->max_new; s.active = r->active;
+    s.temperature = r->temperature; s.top_p = r->top_p; s.seed = r->seed; s.has_seed = r->has_seed;
+    s.eos = r->eos; s.n_eos = r->n_eos; s.trigger = r->trigger;
+    return s;
+}
+
+int mlxcat_op_draft(const mlxcat_rows *rows, const mlxcat_spec_config *spec, int32_t *vtok, int32_t *count,
+                    int32_t *trow, int32_t *tpos, void *stream) {
+    if (!rows || !spec || !vtok || !count || !trow || !tpos || rows->rows <= 0)
+        return op_err(MLXCAT_E_INVALID, "bad draft arguments");
+    if (spec->max_proposal < 0 || spec->max_proposal > 16 || spec->max_suffix < 1)
+        return op_err(MLXCAT_E_INVALID, "bad spec config");
+    cudaError_t e = draft(rows_of(rows), params_of(spec), vtok, count, trow, tpos, (cudaStream_t)stream);
+    if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "draft: %s", cudaGetErrorString(e));
+    return MLXCAT_OK;
+}
+
+size_t mlxcat_op_accept_workspace(int32_t rows, int32_t k) {
+    const size_t n = (size_t)rows * (k + 1);
+    return n * 4 + n * 4 + n * 8 + n * 8 + n * 4 + 2048;
+}
+
+int mlxcat_op_accept(const mlxcat_rows *rows, const mlxcat_spec_config *spec, const int32_t *vtok,
+                     const int32_t *count, const float *logits, int32_t vocab, int32_t *tokens, int32_t *n,
+                     int32_t *finished, uint64_t *stats, void *ws, size_t ws_bytes, void *stream) {
+    if (!rows || !spec || !vtok || !count || !logits || !tokens || !n || !finished || !stats || vocab <= 0)
+        return op_err(MLXCAT_E_INVALID, "bad accept arguments");
+    if (spec->max_proposal < 0 || spec->max_proposal > 16) return op_err(MLXCAT_E_INVALID, "bad k");
+    const SpecParams sp = params_of(spec);
+    const size_t need = mlxcat_op_accept_workspace(rows->rows, sp.k);
+    if (!ws || ws_bytes < need) return op_err(MLXCAT_E_INVALID, "workspace of %zu bytes required", need);
+    const size_t cnt = (size_t)rows->rows * (sp.k + 1);
+    char *p = static_cast<char *>(ws);
+    auto take = [&](size_t bytes) { void *q = p; p += (bytes + 255) & ~(size_t)255; return q; };
+    SampleScratch sc;
+    sc.S = static_cast<unsigned long long *>(take(cnt * 8));
+    sc.Pd = static_cast<unsigned long long *>(take(cnt * 8));
+    sc.m = static_cast<float *>(take(cnt * 4));
+    sc.thr = static_cast<uint32_t *>(take(cnt * 4));
+    int32_t *amax = static_cast<int32_t *>(take(cnt * 4));
+    (void)p;
+    cudaStream_t st = (cudaStream_t)stream;
+    StepOut out;
+    out.tokens = tokens; out.n = n; out.finished = finished;
+    out.stats = reinterpret_cast<unsigned long long *>(stats);
+    cudaError_t e = argmax_rows(logits, (int)cnt, vocab, amax, st);
+    if (e == cudaSuccess) e = accept_greedy(rows_of(rows), sp, vtok, count, amax, out, st);
+    if (e == cudaSuccess) e = accept_sampled(rows_of(rows), sp, vtok, count, logits, vocab, sc, out, st);
+    if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "accept: %s", cudaGetErrorString(e));
+    return MLXCAT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,847 @@
+/*
+ * oracle.c -- CPU restatement of mlxcat's n-gram speculative-decode path.
+ *
+ * TEST INFRASTRUCTURE ONLY: the checker for mlxcat_b200's CUDA kernels, never
+ * part of the product.  Compile with -ffp-contract=off: the deterministic
+ * arithmetic below (Philox streams, exp/log, fixed-point distributions, weight
+ * synthesis) must round exactly like the device code, which uses the explicit
+ * __f*_rn intrinsics.
+ *
+ * Reference citations are paths inside the mlxcat project.
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ========================================================================== */
+/* Philox4x32-10 (Salmon, Moraes, Dror, Shaw: "Parallel random numbers: as     */
+/* easy as 1, 2, 3", SC'11).                                                  */
+/* ========================================================================== */
+void orc_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]) {
+    uint32_t c0 = ctr[0], c1 = ctr[1], c2 = ctr[2], c3 = ctr[3];
+    uint32_t k0 = key[0], k1 = key[1];
+    for (int r = 0; r < 10; ++r) {
+        uint64_t p0 = (uint64_t)0xD2511F53u * c0;
+        uint64_t p1 = (uint64_t)0xCD9E8D57u * c2;
+        uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0;
+        uint32_t hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+        c0 = hi1 ^ c1 ^ k0;
+        c1 = lo1;
+        c2 = hi0 ^ c3 ^ k1;
+        c3 = lo0;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+/* ========================================================================== */
+/* exp / log from first principles: Cody-Waite reduction by ln2 (the fdlibm   */
+/* hi/lo split of ln2), Taylor polynomial for e^r on |r| <= ln2/2, and the     */
+/* atanh series log(m) = 2 atanh((m-1)/(m+1)) on m in [sqrt(1/2), sqrt(2)).   */
+/* ========================================================================== */
+static const float LN2_HI = 6.9314575195e-01f;
+static const float LN2_LO = 1.4286067653e-06f;
+
+static inline float bits_to_f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline uint32_t f_to_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+
+float orc_exp_neg(float x) {
+    if (!(x > -87.0f)) return 0.0f;
+    if (x > 0.0f) x = 0.0f;
+    float n = rintf(x * 1.44269504f);
+    float r = fmaf(-n, LN2_HI, x);
+    r = fmaf(-n, LN2_LO, r);
+    float p = 1.0f / 5040.0f;
+    p = fmaf(p, r, 1.0f / 720.0f);
+    p = fmaf(p, r, 1.0f / 120.0f);
+    p = fmaf(p, r, 1.0f / 24.0f);
+    p = fmaf(p, r, 1.0f / 6.0f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    int e = (int)n;
+    float scale = bits_to_f((uint32_t)(e + 127) << 23);
+    return p * scale;
+}
+
+float orc_log(float x) {
+    uint32_t b = f_to_bits(x);
+    int e = (int)((b >> 23) & 0xffu) - 127;
+    float m = bits_to_f((b & 0x7fffffu) | 0x3f800000u);
+    if (m > 1.41421356f) { m = m * 0.5f; e += 1; }
+    float f = (m - 1.0f) / (m + 1.0f);
+    float f2 = f * f;
+    float p = 2.0f / 9.0f;
+    p = fmaf(p, f2, 2.0f / 7.0f);
+    p = fmaf(p, f2, 2.0f / 5.0f);
+    p = fmaf(p, f2, 2.0f / 3.0f);
+    p = fmaf(p, f2, 2.0f);
+    float lm = p * f;
+    float fe = (float)e;
+    return fmaf(fe, LN2_HI, fmaf(fe, LN2_LO, lm));
+}
+
+uint16_t orc_f32_to_f16(float x) {
+    _Float16 h = (_Float16)x;
+    uint16_t u; memcpy(&u, &h, 2); return u;
+}
+float orc_f16_to_f32(uint16_t u) {
+    _Float16 h; memcpy(&h, &u, 2); return (float)h;
+}
+
+/* Marsaglia polar method over the Philox stream keyed by the weight seed. */
+float orc_normal(uint64_t seed, uint32_t tensor_id, uint64_t index) {
+    const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+    for (uint32_t a = 0; a < 8; ++a) {
+        const uint32_t ctr[4] = {(uint32_t)index, (uint32_t)(index >> 32), tensor_id, a};
+        uint32_t r[4];
+        orc_philox4x32_10(ctr, key, r);
+        for (int p = 0; p < 2; ++p) {
+            float u1 = (float)(r[2 * p] >> 8) * 1.1920928955078125e-07f - 1.0f;
+            float u2 = (float)(r[2 * p + 1] >> 8) * 1.1920928955078125e-07f - 1.0f;
+            float s = u1 * u1 + u2 * u2;
+            if (s < 1.0f && s > 0.0f) {
+                float t = (-2.0f * orc_log(s)) / s;
+                return u1 * sqrtf(t);
+            }
+        }
+    }
+    return 0.0f;
+}
+
+uint32_t orc_uniform_u32(uint64_t seed, uint64_t gen_index, uint32_t purpose) {
+    const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+    const uint32_t ctr[4] = {(uint32_t)gen_index, (uint32_t)(gen_index >> 32), purpose, 0u};
+    uint32_t r[4];
+    orc_philox4x32_10(ctr, key, r);
+    return r[0];
+}
+
+/* ========================================================================== */
+/* MLX affine 4-bit, group 64: w = scale * q + bias, q in [0,15], packed 8     */
+/* per uint32 with the lowest nibble first; fp16 scales/biases [N, K/64].      */
+/* The quantizer (min/max affine) is this build's own.                        */
+/* ========================================================================== */
+#define GS 64
+
+static void quantize_group(const float *w, uint32_t *wq, uint16_t *s_out, uint16_t *b_out) {
+    float mn = w[0], mx = w[0];
+    for (int i = 1; i < GS; ++i) {
+        if (w[i] < mn) mn = w[i];
+        if (w[i] > mx) mx = w[i];
+    }
+    float sc = (mx - mn) / 15.0f;
+    uint16_t sh = orc_f32_to_f16(sc);
+    float sf = orc_f16_to_f32(sh);
+    uint16_t bh = orc_f32_to_f16(mn);
+    float bf = orc_f16_to_f32(bh);
+    for (int j = 0; j < GS / 8; ++j) wq[j] = 0;
+    for (int i = 0; i < GS; ++i) {
+        int q = 0;
+        if (sf > 0.0f) {
+            float t = (w[i] - bf) / sf;
+            q = (int)rintf(t);
+            if (q < 0) q = 0;
+            if (q > 15) q = 15;
+        }
+        wq[i / 8] |= (uint32_t)q << (4 * (i % 8));
+    }
+    *s_out = sh;
+    *b_out = bh;
+}
+
+void orc_q4_quantize_row(const float *w, int K, uint32_t *wq, uint16_t *scales,
+                         uint16_t *biases) {
+    for (int g = 0; g < K / GS; ++g)
+        quantize_group(w + g * GS, wq + g * (GS / 8), scales + g, biases + g);
+}
+
+void orc_q4_synth(uint64_t seed, uint32_t tensor_id, float stddev, int N, int K,
+                  uint32_t *wq, uint16_t *scales, uint16_t *biases) {
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) {
+        float buf[GS];
+        for (int g = 0; g < K / GS; ++g) {
+            for (int i = 0; i < GS; ++i) {
+                uint64_t idx = (uint64_t)n * (uint64_t)K + (uint64_t)(g * GS + i);
+                buf[i] = orc_normal(seed, tensor_id, idx) * stddev;
+            }
+            size_t go = (size_t)n * (K / GS) + g;
+            quantize_group(buf, wq + (size_t)n * (K / 8) + g * (GS / 8), scales + go,
+                           biases + go);
+        }
+    }
+}
+
+static inline void dequant_row(const uint32_t *wq, const uint16_t *s, const uint16_t *b,
+                               int K, float *out) {
+    for (int g = 0; g < K / GS; ++g) {
+        float sf = orc_f16_to_f32(s[g]), bf = orc_f16_to_f32(b[g]);
+        for (int i = 0; i < GS; ++i) {
+            int k = g * GS + i;
+            uint32_t q = (wq[k / 8] >> (4 * (k % 8))) & 0xfu;
+            out[k] = sf * (float)q + bf;
+        }
+    }
+}
+
+void orc_q4_dequant(const uint32_t *wq, const uint16_t *scales, const uint16_t *biases,
+                    int N, int K, float *w) {
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n)
+        dequant_row(wq + (size_t)n * (K / 8), scales + (size_t)n * (K / GS),
+                    biases + (size_t)n * (K / GS), K, w + (size_t)n * K);
+}
+
+void orc_q4_linear(const uint32_t *wq, const uint16_t *scales, const uint16_t *biases,
+                   int N, int K, const float *x, int M, float *y) {
+    /* x transposed to [K][M] so the inner loop runs over tokens: each token's
+     * dot product is still accumulated in k order, and the loop vectorises
+     * without reassociating any sum. */
+    float *xt = (float *)malloc(sizeof(float) * (size_t)K * M);
+    for (int m = 0; m < M; ++m)
+        for (int k = 0; k < K; ++k) xt[(size_t)k * M + m] = x[(size_t)m * K + k];
+#pragma omp parallel
+    {
+        float *row = (float *)malloc(sizeof(float) * (size_t)K);
+        float *acc = (float *)malloc(sizeof(float) * (size_t)M);
+#pragma omp for schedule(static)
+        for (int n = 0; n < N; ++n) {
+            dequant_row(wq + (size_t)n * (K / 8), scales + (size_t)n * (K / GS),
+                        biases + (size_t)n * (K / GS), K, row);
+            for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+            for (int k = 0; k < K; ++k) {
+                const float w = row[k];
+                const float *xk = xt + (size_t)k * M;
+                for (int m = 0; m < M; ++m) acc[m] += xk[m] * w;
+            }
+            for (int m = 0; m < M; ++m) y[(size_t)m * N + n] = acc[m];
+        }
+        free(row);
+        free(acc);
+    }
+    free(xt);
+}
+
+/* ========================================================================== */
+/* Drafter: proposeSuffixTokens, BatchGenerator.swift:982-1010, restated loop  */
+/* for loop.  Longest suffix first (maxSuffix..1); for each, the most recent   */
+/* earlier occurrence that ends at or before the suffix start; the proposal is */
+/* the tokens after it, clipped at the context end and at `limit`.            */
+/* ========================================================================== */
+int orc_propose_suffix(const int32_t *ctx, int n_ctx, int max_suffix, int min_ctx,
+                       int limit, int32_t *out) {
+    if (n_ctx < min_ctx || limit <= 0) return 0;
+    int max_len = max_suffix < n_ctx - 1 ? max_suffix : n_ctx - 1;
+    if (max_len <= 0) return 0;
+    for (int L = max_len; L >= 1; --L) {
+        int suffix_start = n_ctx - L;
+        if (suffix_start <= 0) continue;
+        for (int c = suffix_start - 1; c >= 0; --c) {
+            int cend = c + L;
+            if (cend > suffix_start) continue;
+            if (memcmp(ctx + c, ctx + suffix_start, sizeof(int32_t) * (size_t)L) == 0) {
+                int ps = cend;
+                int pe = n_ctx < ps + limit ? n_ctx : ps + limit;
+                if (ps >= pe) continue;
+                for (int i = ps; i < pe; ++i) out[i - ps] = ctx[i];
+                return pe - ps;
+            }
+        }
+    }
+    return 0;
+}
+
+/* ========================================================================== */
+/* Sampling                                                                   */
+/* ========================================================================== */
+int orc_argmax(const float *logits, int V) {
+    int best = 0;
+    float bv = logits[0];
+    for (int i = 1; i < V; ++i)
+        if (logits[i] > bv) { bv = logits[i]; best = i; }
+    return best;
+}
+
+static inline uint32_t fix24(float e) { return (uint32_t)(e * 16777216.0f); }
+
+static float row_max(const float *l, int V) {
+    float m = l[0];
+    for (int i = 1; i < V; ++i) if (l[i] > m) m = l[i];
+    return m;
+}
+
+typedef struct { float v; int i; } vi_t;
+static int cmp_desc(const void *a, const void *b) {
+    float x = ((const vi_t *)a)->v, y = ((const vi_t *)b)->v;
+    return (x < y) - (x > y);
+}
+
+/* Sampling.swift:847-858 keeps the smallest set of most likely tokens whose
+ * mass reaches topP: token i survives iff the probability mass strictly above
+ * it is below topP * total.  Here the mass is the fixed-point e^(l-max) at
+ * temperature 1 (the reference applies top-p before dividing by the
+ * temperature, :504-506, :523), summed exactly in integers so the device
+ * result is bit-identical; topP is taken to 20 fractional bits with a floor of
+ * one unit so the most likely token always survives (TopPSamplingTests:10-23). */
+void orc_top_p_keep(const float *logits, int V, float top_p, uint8_t *keep) {
+    float m = row_max(logits, V);
+    vi_t *s = (vi_t *)malloc(sizeof(vi_t) * (size_t)V);
+    uint32_t *P = (uint32_t *)malloc(sizeof(uint32_t) * (size_t)V);
+    uint64_t S = 0;
+    for (int i = 0; i < V; ++i) {
+        P[i] = fix24(orc_exp_neg(logits[i] - m));
+        S += P[i];
+        s[i].v = logits[i];
+        s[i].i = i;
+    }
+    int64_t tp = (int64_t)rintf(top_p * 1048576.0f);
+    if (tp < 1) tp = 1;
+    if (tp > 1048576) tp = 1048576;
+    qsort(s, (size_t)V, sizeof(vi_t), cmp_desc);
+    uint64_t above = 0;
+    int i = 0;
+    while (i < V) {
+        int j = i;
+        uint64_t group = 0;
+        while (j < V && s[j].v == s[i].v) { group += P[s[j].i]; ++j; }
+        uint8_t k = (above << 20) < S * (uint64_t)tp;
+        for (int t = i; t < j; ++t) keep[s[t].i] = k;
+        above += group;
+        i = j;
+    }
+    free(s);
+    free(P);
+}
+
+uint64_t orc_fixed_dist(const float *logits, int V, float temperature, float top_p,
+                        uint32_t *P) {
+    float m = row_max(logits, V);
+    uint8_t *keep = NULL;
+    if (top_p > 0.0f && top_p < 1.0f) {
+        keep = (uint8_t *)malloc((size_t)V);
+        orc_top_p_keep(logits, V, top_p, keep);
+    }
+    uint64_t S = 0;
+    for (int i = 0; i < V; ++i) {
+        uint32_t p = 0;
+        if (!keep || keep[i]) p = fix24(orc_exp_neg((logits[i] - m) / temperature));
+        P[i] = p;
+        S += p;
+    }
+    free(keep);
+    return S;
+}
+
+static inline uint64_t scale_u32(uint32_t u, uint64_t S) {
+    return (uint64_t)u * (S >> 32) + (((uint64_t)u * (S & 0xffffffffu)) >> 32);
+}
+
+int orc_pick(const uint32_t *P, int V, uint64_t S, uint32_t u, int skip) {
+    if (skip >= 0) S -= P[skip];
+    uint64_t t = scale_u32(u, S);
+    uint64_t c = 0;
+    int last = -1;
+    for (int i = 0; i < V; ++i) {
+        if (i == skip) continue;
+        c += P[i];
+        if (P[i]) last = i;
+        if (c > t) return i;
+    }
+    return last;
+}
+
+static int is_eos(const orc_sampling *sp, int tok) {
+    for (int i = 0; i < sp->n_eos; ++i) if (sp->eos[i] == tok) return 1;
+    return 0;
+}
+
+/* One row's acceptance.  Greedy COMPAT restates BatchGenerator.swift:906-940:
+ * all-or-nothing, trigger aborts, EOS stops, a rejected batch falls back to an
+ * ordinary one-token decode whose token is position 0's sample (the verify
+ * forward computes position 0 exactly as a one-token decode would).  PREFIX
+ * keeps the matching prefix plus the correcting/bonus token.  Temperature rows
+ * run single-draft rejection sampling: draft d at position p survives iff
+ * floor(u*S/2^32) < P[d]; otherwise the residual (P without d) is sampled. */
+int orc_accept_row(int mode, const float *logits, int V, const int32_t *drafts, int count,
+                   const orc_sampling *sp, uint64_t gen_index, int32_t *out, int *rejected) {
+    *rejected = 0;
+    int n = 0;
+    if (sp->temperature == 0.0f) {
+        if (mode == ORC_MODE_COMPAT) {
+            int ok = 1;
+            for (int p = 0; p <= count; ++p) {
+                int s = orc_argmax(logits + (size_t)p * V, V);
+                if (s == sp->trigger) { ok = 0; break; }
+                if (p < count && s != drafts[p]) { ok = 0; break; }
+                out[n++] = s;
+                if (is_eos(sp, s)) break;
+            }
+            if (!ok) {
+                *rejected = count > 0;
+                out[0] = orc_argmax(logits, V);
+                return 1;
+            }
+            return n;
+        }
+        for (int p = 0; p <= count; ++p) {
+            int s = orc_argmax(logits + (size_t)p * V, V);
+            out[n++] = s;
+            if (s == sp->trigger) { *rejected = p < count; break; }
+            if (p < count && s != drafts[p]) { *rejected = 1; break; }
+            if (is_eos(sp, s)) break;
+        }
+        return n;
+    }
+    uint32_t *P = (uint32_t *)malloc(sizeof(uint32_t) * (size_t)V);
+    for (int p = 0; p <= count; ++p) {
+        const float *l = logits + (size_t)p * V;
+        uint64_t S = orc_fixed_dist(l, V, sp->temperature, sp->top_p, P);
+        int s;
+        if (p < count) {
+            uint32_t ua = orc_uniform_u32(sp->seed, gen_index + (uint64_t)p, 0);
+            int d = drafts[p];
+            if (scale_u32(ua, S) < (uint64_t)P[d]) {
+                s = d;
+            } else {
+                uint32_t us = orc_uniform_u32(sp->seed, gen_index + (uint64_t)p, 1);
+                out[n++] = orc_pick(P, V, S, us, d);
+                *rejected = 1;
+                break;
+            }
+        } else {
+            uint32_t us = orc_uniform_u32(sp->seed, gen_index + (uint64_t)p, 1);
+            s = orc_pick(P, V, S, us, -1);
+        }
+        out[n++] = s;
+        if (s == sp->trigger) { *rejected = p < count; break; }
+        if (is_eos(sp, s)) break;
+    }
+    free(P);
+    return n;
+}
+
+/* ========================================================================== */
+/* Model                                                                       */
+/* ========================================================================== */
+typedef struct {
+    uint32_t *wq;
+    uint16_t *s, *b;
+    int N, K;
+} q4_t;
+
+struct orc_model {
+    orc_config cfg;
+    int is_table;
+    int32_t *table_next;
+    q4_t embed, lm_head;
+    q4_t *lin;                   /* n_layers * 7 */
+    float *ones;                 /* norm weights (all ones) */
+    float *inv_freq;
+};
+
+struct orc_kv {
+    int max_rows, max_len, n_layers, n_kv, head_dim;
+    int *len;
+    float *k, *v;                /* [row][layer][kvh][max_len][D] */
+};
+
+uint32_t orc_tensor_id(int layer, int kind) { return (uint32_t)layer * 16u + (uint32_t)kind; }
+
+static void q4_alloc(q4_t *t, int N, int K) {
+    t->N = N;
+    t->K = K;
+    t->wq = (uint32_t *)calloc((size_t)N * (K / 8), 4);
+    t->s = (uint16_t *)calloc((size_t)N * (K / GS), 2);
+    t->b = (uint16_t *)calloc((size_t)N * (K / GS), 2);
+}
+static void q4_free(q4_t *t) { free(t->wq); free(t->s); free(t->b); }
+
+static void tensor_shape(const orc_config *c, int kind, int *N, int *K) {
+    int qd = c->n_heads * c->head_dim, kvd = c->n_kv_heads * c->head_dim;
+    switch (kind) {
+    case ORC_T_Q: *N = qd; *K = c->hidden; break;
+    case ORC_T_K: *N = kvd; *K = c->hidden; break;
+    case ORC_T_V: *N = kvd; *K = c->hidden; break;
+    case ORC_T_O: *N = c->hidden; *K = qd; break;
+    case ORC_T_GATE: *N = c->intermediate; *K = c->hidden; break;
+    case ORC_T_UP: *N = c->intermediate; *K = c->hidden; break;
+    default: *N = c->hidden; *K = c->intermediate; break;
+    }
+}
+
+static q4_t *find_tensor(orc_model *m, uint32_t id) {
+    if (id == ORC_TENSOR_EMBED) return &m->embed;
+    if (id == ORC_TENSOR_LM_HEAD) return m->cfg.tie_embeddings ? NULL : &m->lm_head;
+    int layer = (int)(id / 16u), kind = (int)(id % 16u);
+    if (layer >= m->cfg.n_layers || kind > ORC_T_DOWN) return NULL;
+    return &m->lin[layer * 7 + kind];
+}
+
+orc_model *orc_model_empty(const orc_config *cfg) {
+    orc_model *m = (orc_model *)calloc(1, sizeof(orc_model));
+    m->cfg = *cfg;
+    q4_alloc(&m->embed, cfg->vocab, cfg->hidden);
+    if (!cfg->tie_embeddings) q4_alloc(&m->lm_head, cfg->vocab, cfg->hidden);
+    m->lin = (q4_t *)calloc((size_t)cfg->n_layers * 7, sizeof(q4_t));
+    for (int l = 0; l < cfg->n_layers; ++l)
+        for (int k = 0; k < 7; ++k) {
+            int N, K;
+            tensor_shape(cfg, k, &N, &K);
+            q4_alloc(&m->lin[l * 7 + k], N, K);
+        }
+    int big = cfg->hidden > cfg->head_dim ? cfg->hidden : cfg->head_dim;
+    m->ones = (float *)malloc(sizeof(float) * (size_t)big);
+    for (int i = 0; i < big; ++i) m->ones[i] = 1.0f;
+    m->inv_freq = (float *)malloc(sizeof(float) * (size_t)(cfg->head_dim / 2));
+    for (int i = 0; i < cfg->head_dim / 2; ++i)
+        m->inv_freq[i] =
+            (float)(1.0 / pow((double)cfg->rope_theta, (2.0 * i) / (double)cfg->head_dim));
+    return m;
+}
+
+orc_model *orc_model_synth(const orc_config *cfg, uint64_t seed, float stddev) {
+    orc_model *m = orc_model_empty(cfg);
+    q4_t *e = &m->embed;
+    orc_q4_synth(seed, ORC_TENSOR_EMBED, stddev, e->N, e->K, e->wq, e->s, e->b);
+    if (!cfg->tie_embeddings) {
+        q4_t *h = &m->lm_head;
+        orc_q4_synth(seed, ORC_TENSOR_LM_HEAD, stddev, h->N, h->K, h->wq, h->s, h->b);
+    }
+    for (int l = 0; l < cfg->n_layers; ++l)
+        for (int k = 0; k < 7; ++k) {
+            q4_t *t = &m->lin[l * 7 + k];
+            orc_q4_synth(seed, orc_tensor_id(l, k), stddev, t->N, t->K, t->wq, t->s, t->b);
+        }
+    return m;
+}
+
+orc_model *orc_model_table(const int32_t *next, int vocab) {
+    orc_model *m = (orc_model *)calloc(1, sizeof(orc_model));
+    m->is_table = 1;
+    m->cfg.vocab = vocab;
+    m->table_next = (int32_t *)malloc(sizeof(int32_t) * (size_t)vocab);
+    memcpy(m->table_next, next, sizeof(int32_t) * (size_t)vocab);
+    return m;
+}
+
+int orc_model_set_q4(orc_model *m, uint32_t tensor_id, const uint32_t *wq,
+                     const uint16_t *scales, const uint16_t *biases) {
+    q4_t *t = find_tensor(m, tensor_id);
+    if (!t) return -1;
+    memcpy(t->wq, wq, (size_t)t->N * (t->K / 8) * 4);
+    memcpy(t->s, scales, (size_t)t->N * (t->K / GS) * 2);
+    memcpy(t->b, biases, (size_t)t->N * (t->K / GS) * 2);
+    return 0;
+}
+
+void orc_model_get_q4(const orc_model *m, uint32_t tensor_id, const uint32_t **wq,
+                      const uint16_t **scales, const uint16_t **biases, int *N, int *K) {
+    q4_t *t = find_tensor((orc_model *)m, tensor_id);
+    if (!t) { *wq = NULL; *scales = NULL; *biases = NULL; *N = *K = 0; return; }
+    *wq = t->wq; *scales = t->s; *biases = t->b; *N = t->N; *K = t->K;
+}
+
+void orc_model_free(orc_model *m) {
+    if (!m) return;
+    if (!m->is_table) {
+        q4_free(&m->embed);
+        if (!m->cfg.tie_embeddings) q4_free(&m->lm_head);
+        for (int i = 0; i < m->cfg.n_layers * 7; ++i) q4_free(&m->lin[i]);
+        free(m->lin);
+        free(m->ones);
+        free(m->inv_freq);
+    }
+    free(m->table_next);
+    free(m);
+}
+
+const orc_config *orc_model_config(const orc_model *m) { return &m->cfg; }
+
+orc_kv *orc_kv_create(const orc_model *m, int max_rows, int max_len) {
+    orc_kv *kv = (orc_kv *)calloc(1, sizeof(orc_kv));
+    kv->max_rows = max_rows;
+    kv->max_len = max_len;
+    kv->n_layers = m->is_table ? 0 : m->cfg.n_layers;
+    kv->n_kv = m->cfg.n_kv_heads;
+    kv->head_dim = m->cfg.head_dim;
+    kv->len = (int *)calloc((size_t)max_rows, sizeof(int));
+    size_t per = (size_t)kv->n_layers * kv->n_kv * (size_t)max_len * kv->head_dim;
+    if (per) {
+        kv->k = (float *)calloc(per * (size_t)max_rows, sizeof(float));
+        kv->v = (float *)calloc(per * (size_t)max_rows, sizeof(float));
+    }
+    return kv;
+}
+
+void orc_kv_free(orc_kv *kv) {
+    if (!kv) return;
+    free(kv->len); free(kv->k); free(kv->v); free(kv);
+}
+int orc_kv_len(const orc_kv *kv, int row) { return kv->len[row]; }
+void orc_kv_set_len(orc_kv *kv, int row, int len) { kv->len[row] = len; }
+
+/* BatchCache.swift:403-424: trimmed = min(idx, n); each row loses
+ * min(trimmed, its own length).  On a right-ragged cache `idx` is the longest
+ * row, and the per-row RoPE offset equals the row length. */
+int orc_kv_trim(orc_kv *kv, int n) {
+    int idx = 0;
+    for (int r = 0; r < kv->max_rows; ++r) if (kv->len[r] > idx) idx = kv->len[r];
+    int trimmed = n < idx ? n : idx;
+    if (trimmed <= 0) return 0;
+    for (int r = 0; r < kv->max_rows; ++r) {
+        int t = trimmed < kv->len[r] ? trimmed : kv->len[r];
+        kv->len[r] -= t;
+    }
+    return trimmed;
+}
+
+static inline size_t kv_off(const orc_kv *kv, int row, int layer, int h, int pos) {
+    return ((((size_t)row * kv->n_layers + layer) * kv->n_kv + h) * kv->max_len + pos) *
+           kv->head_dim;
+}
+float *orc_kv_k(orc_kv *kv, int row, int layer) { return kv->k + kv_off(kv, row, layer, 0, 0); }
+float *orc_kv_v(orc_kv *kv, int row, int layer) { return kv->v + kv_off(kv, row, layer, 0, 0); }
+
+static void rmsnorm(const float *x, const float *w, int n, float eps, float *out) {
+    double ss = 0.0;
+    for (int i = 0; i < n; ++i) ss += (double)x[i] * x[i];
+    float r = (float)(1.0 / sqrt(ss / n + (double)eps));
+    for (int i = 0; i < n; ++i) out[i] = x[i] * r * w[i];
+}
+
+static void rope(float *x, int D, int pos, const float *inv_freq) {
+    int h = D / 2;
+    for (int i = 0; i < h; ++i) {
+        float ang = (float)pos * inv_freq[i];
+        float c = cosf(ang), s = sinf(ang);
+        float a = x[i], b = x[i + h];
+        x[i] = a * c - b * s;
+        x[i + h] = a * s + b * c;
+    }
+}
+
+static void lin(const q4_t *t, const float *x, int M, float *y) {
+    orc_q4_linear(t->wq, t->s, t->b, t->N, t->K, x, M, y);
+}
+
+void orc_forward(const orc_model *m, orc_kv *kv, int M, const int32_t *tokens,
+                 const int32_t *rows, const int32_t *pos, float *logits) {
+    const orc_config *c = &m->cfg;
+    if (m->is_table) {
+        if (!logits) return;
+        for (int i = 0; i < M; ++i) {
+            float *l = logits + (size_t)i * c->vocab;
+            for (int v = 0; v < c->vocab; ++v) l[v] = -20.0f;
+            l[m->table_next[tokens[i]]] = 20.0f;
+        }
+        return;
+    }
+    const int H = c->hidden, D = c->head_dim, Hq = c->n_heads, Hkv = c->n_kv_heads;
+    const int I = c->intermediate, G = Hq / Hkv;
+    float *h = (float *)malloc(sizeof(float) * (size_t)M * H);
+    float *x = (float *)malloc(sizeof(float) * (size_t)M * (H > I ? H : I));
+    float *q = (float *)malloc(sizeof(float) * (size_t)M * Hq * D);
+    float *k = (float *)malloc(sizeof(float) * (size_t)M * Hkv * D);
+    float *v = (float *)malloc(sizeof(float) * (size_t)M * Hkv * D);
+    float *att = (float *)malloc(sizeof(float) * (size_t)M * Hq * D);
+    float *g = (float *)malloc(sizeof(float) * (size_t)M * I);
+    float *u = (float *)malloc(sizeof(float) * (size_t)M * I);
+    float *o = (float *)malloc(sizeof(float) * (size_t)M * H);
+
+    for (int i = 0; i < M; ++i)
+        dequant_row(m->embed.wq + (size_t)tokens[i] * (H / 8),
+                    m->embed.s + (size_t)tokens[i] * (H / GS),
+                    m->embed.b + (size_t)tokens[i] * (H / GS), H, h + (size_t)i * H);
+
+    const float scale = 1.0f / sqrtf((float)D);
+    for (int l = 0; l < c->n_layers; ++l) {
+        const q4_t *W = m->lin + l * 7;
+        for (int i = 0; i < M; ++i) rmsnorm(h + (size_t)i * H, m->ones, H, c->rms_eps, x + (size_t)i * H);
+        lin(&W[ORC_T_Q], x, M, q);
+        lin(&W[ORC_T_K], x, M, k);
+        lin(&W[ORC_T_V], x, M, v);
+        for (int i = 0; i < M; ++i) {
+            for (int hh = 0; hh < Hq; ++hh) {
+                float *qh = q + ((size_t)i * Hq + hh) * D;
+                if (c->qk_norm) rmsnorm(qh, m->ones, D, c->rms_eps, qh);
+                rope(qh, D, pos[i], m->inv_freq);
+            }
+            for (int hh = 0; hh < Hkv; ++hh) {
+                float *kh = k + ((size_t)i * Hkv + hh) * D;
+                if (c->qk_norm) rmsnorm(kh, m->ones, D, c->rms_eps, kh);
+                rope(kh, D, pos[i], m->inv_freq);
+                memcpy(kv->k + kv_off(kv, rows[i], l, hh, pos[i]), kh, sizeof(float) * D);
+                memcpy(kv->v + kv_off(kv, rows[i], l, hh, pos[i]),
+                       v + ((size_t)i * Hkv + hh) * D, sizeof(float) * D);
+            }
+        }
+#pragma omp parallel for collapse(2) schedule(dynamic)
+        for (int i = 0; i < M; ++i) {
+            for (int hh = 0; hh < Hq; ++hh) {
+                const float *qh = q + ((size_t)i * Hq + hh) * D;
+                const int kvh = hh / G, T = pos[i] + 1;
+                const float *K = kv->k + kv_off(kv, rows[i], l, kvh, 0);
+                const float *Vv = kv->v + kv_off(kv, rows[i], l, kvh, 0);
+                float *sc = (float *)malloc(sizeof(float) * (size_t)T);
+                float mx = -INFINITY;
+                for (int t = 0; t < T; ++t) {
+                    float d = 0.0f;
+                    for (int e = 0; e < D; ++e) d += qh[e] * K[(size_t)t * D + e];
+                    sc[t] = d * scale;
+                    if (sc[t] > mx) mx = sc[t];
+                }
+                float den = 0.0f;
+                for (int t = 0; t < T; ++t) { sc[t] = expf(sc[t] - mx); den += sc[t]; }
+                float *out = att + ((size_t)i * Hq + hh) * D;
+                for (int e = 0; e < D; ++e) out[e] = 0.0f;
+                for (int t = 0; t < T; ++t) {
+                    float p = sc[t] / den;
+                    for (int e = 0; e < D; ++e) out[e] += p * Vv[(size_t)t * D + e];
+                }
+                free(sc);
+            }
+        }
+        lin(&W[ORC_T_O], att, M, o);
+        for (size_t i = 0; i < (size_t)M * H; ++i) h[i] += o[i];
+        for (int i = 0; i < M; ++i) rmsnorm(h + (size_t)i * H, m->ones, H, c->rms_eps, x + (size_t)i * H);
+        lin(&W[ORC_T_GATE], x, M, g);
+        lin(&W[ORC_T_UP], x, M, u);
+        for (size_t i = 0; i < (size_t)M * I; ++i) {
+            float gg = g[i];
+            x[i] = gg / (1.0f + expf(-gg)) * u[i];
+        }
+        lin(&W[ORC_T_DOWN], x, M, o);
+        for (size_t i = 0; i < (size_t)M * H; ++i) h[i] += o[i];
+    }
+    if (logits) {
+        for (int i = 0; i < M; ++i) rmsnorm(h + (size_t)i * H, m->ones, H, c->rms_eps, x + (size_t)i * H);
+        lin(c->tie_embeddings ? &m->embed : &m->lm_head, x, M, logits);
+    }
+    free(h); free(x); free(q); free(k); free(v); free(att); free(g); free(u); free(o);
+}
+
+/* ========================================================================== */
+/* Batched speculative step and admission                                      */
+/* ========================================================================== */
+static void hist_push(orc_row *r, int32_t tok) {
+    if (r->hist_len == r->hist_cap) {
+        r->hist_cap = r->hist_cap ? r->hist_cap * 2 : 64;
+        r->hist = (int32_t *)realloc(r->hist, sizeof(int32_t) * (size_t)r->hist_cap);
+    }
+    r->hist[r->hist_len++] = tok;
+}
+
+static int sample_one(const float *l, int V, const orc_sampling *sp, uint64_t gen_index) {
+    if (sp->temperature == 0.0f) return orc_argmax(l, V);
+    uint32_t *P = (uint32_t *)malloc(sizeof(uint32_t) * (size_t)V);
+    uint64_t S = orc_fixed_dist(l, V, sp->temperature, sp->top_p, P);
+    int s = orc_pick(P, V, S, orc_uniform_u32(sp->seed, gen_index, 1), -1);
+    free(P);
+    return s;
+}
+
+int orc_admit(const orc_model *m, orc_kv *kv, orc_row *r, int row, const int32_t *prompt,
+              int len, int chunk) {
+    const int V = m->cfg.vocab;
+    if (chunk <= 0) chunk = len;
+    float *logits = (float *)malloc(sizeof(float) * (size_t)V);
+    int32_t *rows = (int32_t *)malloc(sizeof(int32_t) * (size_t)chunk);
+    int32_t *pos = (int32_t *)malloc(sizeof(int32_t) * (size_t)chunk);
+    for (int s = 0; s < len; s += chunk) {
+        int n = len - s < chunk ? len - s : chunk;
+        for (int i = 0; i < n; ++i) { rows[i] = row; pos[i] = s + i; }
+        int last = s + n == len;
+        if (last) {
+            /* only the final token's logits are needed */
+            if (n > 1) orc_forward(m, kv, n - 1, prompt + s, rows, pos, NULL);
+            orc_forward(m, kv, 1, prompt + s + n - 1, rows + n - 1, pos + n - 1, logits);
+        } else {
+            orc_forward(m, kv, n, prompt + s, rows, pos, NULL);
+        }
+    }
+    r->hist_len = 0;
+    for (int i = 0; i < len; ++i) hist_push(r, prompt[i]);
+    int t0 = sample_one(logits, V, &r->sp, 0);
+    hist_push(r, t0);
+    r->n_gen = 1;
+    r->active = 1;
+    kv->len[row] = len;
+    free(logits); free(rows); free(pos);
+    return t0;
+}
+
+void orc_spec_step(const orc_model *m, orc_kv *kv, orc_row *rows, int n_rows,
+                   const orc_spec_config *cfg, int32_t *out, int32_t *n_out,
+                   orc_stats *stats) {
+    const int V = m->cfg.vocab, K1 = cfg->max_proposal + 1;
+    int n_active = 0;
+    for (int r = 0; r < n_rows; ++r) n_active += rows[r].active;
+    int32_t *drafts = (int32_t *)calloc((size_t)n_rows * K1, sizeof(int32_t));
+    int *count = (int *)calloc((size_t)n_rows, sizeof(int));
+    int *base = (int *)calloc((size_t)n_rows, sizeof(int));
+    int M = 0;
+    for (int r = 0; r < n_rows; ++r) {
+        orc_row *R = &rows[r];
+        n_out[r] = 0;
+        if (!R->active) continue;
+        int remaining = R->max_new - R->n_gen;
+        int gate = cfg->enabled && cfg->max_proposal > 0 &&
+                   R->hist_len >= cfg->min_context && remaining > 1;
+        if (cfg->mode == ORC_MODE_COMPAT)
+            gate = gate && n_active == 1 && R->sp.temperature == 0.0f && !R->sp.has_seed;
+        if (gate) {
+            int limit = cfg->max_proposal < remaining - 1 ? cfg->max_proposal : remaining - 1;
+            count[r] = orc_propose_suffix(R->hist, R->hist_len, cfg->max_suffix,
+                                          cfg->min_context, limit, drafts + (size_t)r * K1);
+        }
+        base[r] = M;
+        M += count[r] + 1;
+    }
+    int32_t *tok = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M ? M : 1));
+    int32_t *rid = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M ? M : 1));
+    int32_t *ps = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M ? M : 1));
+    for (int r = 0; r < n_rows; ++r) {
+        orc_row *R = &rows[r];
+        if (!R->active) continue;
+        int kl = kv->len[r];
+        for (int j = 0; j <= count[r]; ++j) {
+            tok[base[r] + j] = j == 0 ? R->hist[R->hist_len - 1] : drafts[(size_t)r * K1 + j - 1];
+            rid[base[r] + j] = r;
+            ps[base[r] + j] = kl + j;
+        }
+    }
+    float *logits = (float *)malloc(sizeof(float) * (size_t)(M ? M : 1) * V);
+    if (M) orc_forward(m, kv, M, tok, rid, ps, logits);
+    for (int r = 0; r < n_rows; ++r) {
+        orc_row *R = &rows[r];
+        if (!R->active) continue;
+        int rej = 0;
+        int n = orc_accept_row(cfg->mode, logits + (size_t)base[r] * V, V,
+                               drafts + (size_t)r * K1, count[r], &R->sp, (uint64_t)R->n_gen,
+                               out + (size_t)r * K1, &rej);
+        n_out[r] = n;
+        if (count[r] > 0) {
+            stats->proposal_batches += 1;
+            stats->proposed += count[r];
+            if (rej) stats->rejected_batches += 1;
+            stats->accepted += n - 1;
+        }
+        kv->len[r] += n;
+        for (int i = 0; i < n; ++i) {
+            int t = out[(size_t)r * K1 + i];
+            hist_push(R, t);
+            R->n_gen += 1;
+        }
+        int last = out[(size_t)r * K1 + n - 1];
+        if (is_eos(&R->sp, last) || R->n_gen >= R->max_new) R->active = 0;
+    }
+    free(drafts); free(count); free(base); free(tok); free(rid); free(ps); free(logits);
+}

@@ -1,0 +1,85 @@
+"""C-ABI checks that need no GPU: the library loads, exports every entry point
+include/mlxcat_cuda.h declares, validates arguments before touching a device,
+and the host mirror keeps the reference's configuration semantics."""
+import ctypes as C
+import os
+import subprocess
+
+import pytest
+
+import mlxcat_b200 as M
+from mlxcat_b200 import _abi as A
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def have_gpu():
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except Exception:
+        return False
+
+
+def test_library_exports_every_header_function():
+    declared = A.header_functions()
+    assert len(declared) >= 30
+    L = A.lib()
+    for name in declared:
+        assert hasattr(L, name), name
+    assert sorted(A.PROTOTYPES) == declared
+    out = subprocess.run(["nm", "-D", "--defined-only", A.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    assert set(declared) <= exported
+
+
+def test_library_links_no_torch():
+    out = subprocess.run(["ldd", A.LIB_PATH], capture_output=True, text=True).stdout
+    assert "torch" not in out and "python" not in out
+
+
+def test_invalid_config_rejected_before_device():
+    cfg = M.ModelConfig(2, 500, 8, 2, 64, 1408, 32000)   # hidden not a multiple of 128
+    h = C.c_void_p()
+    c = cfg.to_c()
+    rc = A.lib().mlxcat_ctx_create(C.byref(c), 0, C.byref(h))
+    assert rc == A.E_INVALID
+    assert b"multiple" in A.lib().mlxcat_op_last_error()
+    c2 = M.TINY.to_c()
+    c2.group_size = 32
+    assert A.lib().mlxcat_ctx_create(C.byref(c2), 0, C.byref(h)) == A.E_INVALID
+
+
+@pytest.mark.skipif(have_gpu(), reason="checks the no-device error path")
+def test_no_device_fails_loudly():
+    with pytest.raises(A.MlxcatError) as ei:
+        M.Context(M.TINY, 0)
+    assert ei.value.code == A.E_CUDA
+
+
+def test_operator_argument_validation():
+    L = A.lib()
+    assert L.mlxcat_op_q4_linear(None, None, None, 128, 128, None, 1, None, None, 0, None) == A.E_INVALID
+    assert L.mlxcat_op_q4_linear_workspace(128, 256, 4) >= 4 * 256 * 2
+    assert L.mlxcat_op_attention_workspace(5, 5, 8, 2, 64, 600) > 0
+    assert L.mlxcat_op_accept_workspace(8, 5) > 0
+
+
+def test_spec_config_clamps_like_reference():
+    # BatchGenerator.swift:16-27: maxProposal >= 0, maxSuffix >= 1, minContext >= 2
+    s = M.SpeculativeDecodingConfiguration(True, -3, 0, 0)
+    assert (s.max_proposal_tokens, s.max_suffix_tokens, s.min_context_tokens) == (0, 1, 2)
+    d = M.SpeculativeDecodingConfiguration()
+    assert (d.enabled, d.max_proposal_tokens, d.max_suffix_tokens, d.min_context_tokens) == (
+        False, 4, 16, 8)
+    with pytest.raises(ValueError):
+        M.SpeculativeDecodingConfiguration(True, 99)
+
+
+def test_baseline_configs_are_valid_shapes():
+    for cfg in M.CONFIGS.values():
+        c = cfg.to_c()
+        for d in (c.hidden, c.intermediate, c.n_heads * c.head_dim, c.vocab):
+            assert d % 128 == 0
+        assert c.n_heads % c.n_kv_heads == 0
