@@ -159,6 +159,16 @@ MLXCAT_API int mlxcat_spec_step(mlxcat_cache *cache, const mlxcat_spec_config *s
                      int32_t *out_counts, int32_t *out_finished, mlxcat_stats *stats);
 /* device time (ms) of the verify forward inside the last mlxcat_spec_step */
 MLXCAT_API int mlxcat_last_verify_ms(mlxcat_cache *cache, float *ms);
+/* device time (ms) of the whole last mlxcat_spec_step (draft through the
+ * device-to-host copy of its outputs) */
+MLXCAT_API int mlxcat_last_step_ms(mlxcat_cache *cache, float *ms);
+/* Per-kernel CUDA-event timing inside the captured step (off by default):
+ * when enabled, every q4 linear and attention launch of the verify forward is
+ * bracketed by events; mlxcat_cache_profile returns the summed device time of
+ * each class in the last step and the number of launches timed. */
+MLXCAT_API int mlxcat_cache_set_profiling(mlxcat_cache *cache, int32_t enabled);
+MLXCAT_API int mlxcat_cache_profile(mlxcat_cache *cache, float *q4_linear_ms, float *attention_ms,
+                                    int32_t *q4_linear_launches, int32_t *attention_launches);
 
 /* ---- device-pointer operators ------------------------------------------------
  * Stream-ordered kernels on caller-owned device memory (fp16 passed as
@@ -168,7 +178,9 @@ MLXCAT_API int mlxcat_last_verify_ms(mlxcat_cache *cache, float *ms);
 MLXCAT_API const char *mlxcat_op_last_error(void);
 
 /* quantizedMatmul (mlx-swift, called by QuantizedLinear): y[M][N] fp32 =
- * x[M][K] fp16 . dequant(W)^T, W MLX affine q4 g64. */
+ * x[M][K] fp16 . dequant(W)^T, W MLX affine q4 g64 (tcgen05 tensor cores).
+ * The workspace holds the re-ordered activations, split-K partials and
+ * tickets, and a device error flag (non-zero after a pipeline wait timed out). */
 MLXCAT_API size_t mlxcat_op_q4_linear_workspace(int32_t N, int32_t K, int32_t M);
 MLXCAT_API int mlxcat_op_q4_linear(const uint32_t *wq, const uint16_t *scales, const uint16_t *biases,
                         int32_t N, int32_t K, const uint16_t *x, int32_t M, float *y,

@@ -99,6 +99,10 @@ PROTOTYPES = {
     "mlxcat_accept": (C.c_int, [_vp, C.POINTER(SpecConfigC), _vp, _vp, _vp, C.POINTER(StatsC)]),
     "mlxcat_spec_step": (C.c_int, [_vp, C.POINTER(SpecConfigC), _vp, _vp, _vp, C.POINTER(StatsC)]),
     "mlxcat_last_verify_ms": (C.c_int, [_vp, C.POINTER(_f32)]),
+    "mlxcat_last_step_ms": (C.c_int, [_vp, C.POINTER(_f32)]),
+    "mlxcat_cache_set_profiling": (C.c_int, [_vp, _i32]),
+    "mlxcat_cache_profile": (C.c_int, [_vp, C.POINTER(_f32), C.POINTER(_f32), C.POINTER(_i32),
+                                       C.POINTER(_i32)]),
     "mlxcat_op_last_error": (C.c_char_p, []),
     "mlxcat_op_q4_linear_workspace": (_sz, [_i32, _i32, _i32]),
     "mlxcat_op_q4_linear": (C.c_int, [_vp, _vp, _vp, _i32, _i32, _vp, _i32, _vp, _vp, _sz, _vp]),

@@ -75,16 +75,12 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
     const int mt = warp >> 1, kh = warp & 1;
     const int g = lane >> 2, t = lane & 3;
 
-    const size_t item = (((size_t)grp * Hkv + h) * splits + s) * 2 + kh;
+    const size_t item = ((size_t)grp * Hkv + h) * splits + s;
     float *op = o_part + item * QROWS * D;
     float *mlp = ml_part + item * QROWS * 2;
 
     if (kb >= ke) {
-        for (int i = threadIdx.x; i < QROWS * 2; i += NTHREADS) {
-            const size_t it0 = (((size_t)grp * Hkv + h) * splits + s) * 2;
-            ml_part[it0 * QROWS * 2 + i] = (i & 1) ? 0.f : -INFINITY;
-            ml_part[(it0 + 1) * QROWS * 2 + i] = (i & 1) ? 0.f : -INFINITY;
-        }
+        for (int i = threadIdx.x; i < QROWS * 2; i += NTHREADS) mlp[i] = (i & 1) ? 0.f : -INFINITY;
         return;
     }
 
@@ -217,40 +213,72 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
         __syncthreads();
     }
     cp_wait<0>();
+    __syncthreads();   // K/V tiles no longer read: reuse shared memory for the merge
 
 #pragma unroll
     for (int rI = 0; rI < 2; ++rI) {
         l_r[rI] += __shfl_xor_sync(0xffffffffu, l_r[rI], 1);
         l_r[rI] += __shfl_xor_sync(0xffffffffu, l_r[rI], 2);
     }
+    // merge the two key halves of this split inside the CTA
+    float *o_s = reinterpret_cast<float *>(smem);          // [QROWS][D]
+    float *ml_s = o_s + QROWS * D;                          // [QROWS][2]
+    if (kh == 1) {
 #pragma unroll
-    for (int i = 0; i < D / 8; ++i) {
-        const int d = i * 8 + 2 * t;
-        *reinterpret_cast<float2 *>(op + (size_t)qrow0 * D + d) = make_float2(o[i][0], o[i][1]);
-        *reinterpret_cast<float2 *>(op + (size_t)qrow1 * D + d) = make_float2(o[i][2], o[i][3]);
+        for (int i = 0; i < D / 8; ++i) {
+            const int d = i * 8 + 2 * t;
+            *reinterpret_cast<float2 *>(o_s + qrow0 * D + d) = make_float2(o[i][0], o[i][1]);
+            *reinterpret_cast<float2 *>(o_s + qrow1 * D + d) = make_float2(o[i][2], o[i][3]);
+        }
+        if (t == 0) {
+            ml_s[qrow0 * 2] = m_r[0]; ml_s[qrow0 * 2 + 1] = l_r[0];
+            ml_s[qrow1 * 2] = m_r[1]; ml_s[qrow1 * 2 + 1] = l_r[1];
+        }
     }
-    if (t == 0) {
-        mlp[qrow0 * 2] = m_r[0]; mlp[qrow0 * 2 + 1] = l_r[0];
-        mlp[qrow1 * 2] = m_r[1]; mlp[qrow1 * 2 + 1] = l_r[1];
+    __syncthreads();
+    if (kh == 0) {
+        float a0[2], a1[2];
+        const int rws[2] = {qrow0, qrow1};
+#pragma unroll
+        for (int rI = 0; rI < 2; ++rI) {
+            const float m1 = ml_s[rws[rI] * 2], l1 = ml_s[rws[rI] * 2 + 1];
+            const float mm = fmaxf(m_r[rI], m1);
+            a0[rI] = m_r[rI] == -INFINITY ? 0.f : exp2f(m_r[rI] - mm);
+            a1[rI] = m1 == -INFINITY ? 0.f : exp2f(m1 - mm);
+            if (t == 0) {
+                mlp[rws[rI] * 2] = mm;
+                mlp[rws[rI] * 2 + 1] = a0[rI] * l_r[rI] + a1[rI] * l1;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) {
+            const int d = i * 8 + 2 * t;
+            const float2 x0 = *reinterpret_cast<const float2 *>(o_s + qrow0 * D + d);
+            const float2 x1 = *reinterpret_cast<const float2 *>(o_s + qrow1 * D + d);
+            *reinterpret_cast<float2 *>(op + (size_t)qrow0 * D + d) =
+                make_float2(a0[0] * o[i][0] + a1[0] * x0.x, a0[0] * o[i][1] + a1[0] * x0.y);
+            *reinterpret_cast<float2 *>(op + (size_t)qrow1 * D + d) =
+                make_float2(a0[1] * o[i][2] + a1[1] * x1.x, a0[1] * o[i][3] + a1[1] * x1.y);
+        }
     }
 }
 
-// merge 2*splits partials per (group, kv head); one thread per (query, d)
+// merge the split partials of one (group, kv head, query row); thread = d
 template <int QT>
 __global__ void attn_combine_kernel(const float *__restrict__ o_part, const float *__restrict__ ml_part,
                                     int M, int qg, int Hq, int Hkv, int D, int splits,
                                     __half *__restrict__ out, int permuted) {
     constexpr int QROWS = QT * 16;
-    const int grp = blockIdx.x, h = blockIdx.y;
+    const int grp = blockIdx.x, h = blockIdx.y, qi = blockIdx.z;
     const int G = Hq / Hkv;
     const int t0 = grp * qg;
     const int ntok = min(qg, M - t0);
     const int NQ = ntok * G;
-    const int P = splits * 2;
+    if (qi >= NQ) return;
+    const int P = splits;
     const size_t it0 = ((size_t)grp * Hkv + h) * P;
     const int KO = Hq * D;
-    for (int v = threadIdx.x; v < NQ * D; v += blockDim.x) {
-        const int qi = v / D, d = v - qi * D;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float mmax = -INFINITY;
         for (int p = 0; p < P; ++p) mmax = fmaxf(mmax, ml_part[((it0 + p) * QROWS + qi) * 2]);
         float num = 0.f, den = 0.f;
@@ -266,7 +294,7 @@ __global__ void attn_combine_kernel(const float *__restrict__ o_part, const floa
         const float r = den > 0.f ? num / den : 0.f;
         const int j = qi / G, gh = qi - j * G;
         const int k = (h * G + gh) * D + d;
-        out[(size_t)(t0 + j) * KO + (permuted ? xperm(k) : k)] = __float2half_rn(r);
+        out[(size_t)(t0 + j) * KO + (permuted ? perm8(k) : k)] = __float2half_rn(r);
     }
 }
 
@@ -292,8 +320,8 @@ cudaError_t launch_attn(const __half *qbuf, KVLayer kv, const int32_t *trow, con
                                                     Hq, Hkv, key_chunk, splits, scale_log2, sc.o, sc.ml);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    dim3 g2(groups, Hkv);
-    attn_combine_kernel<QT><<<g2, 256, 0, st>>>(sc.o, sc.ml, M, qg, Hq, Hkv, D, splits, out, permuted ? 1 : 0);
+    dim3 g2(groups, Hkv, QT * 16);
+    attn_combine_kernel<QT><<<g2, D, 0, st>>>(sc.o, sc.ml, M, qg, Hq, Hkv, D, splits, out, permuted ? 1 : 0);
     return cudaGetLastError();
 }
 
@@ -307,7 +335,7 @@ int attention_qrows(int qg, int n_heads, int n_kv) {
 int attention_max_splits(int max_len, int key_chunk) { return (max_len + key_chunk - 1) / key_chunk; }
 
 size_t attention_scratch_items(int groups, int n_kv, int splits) {
-    return (size_t)groups * n_kv * splits * 2;
+    return (size_t)groups * n_kv * splits;
 }
 
 cudaError_t attention(const __half *qbuf, KVLayer kv, const int32_t *trow, const int32_t *tpos,

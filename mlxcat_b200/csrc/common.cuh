@@ -144,4 +144,11 @@ __host__ __device__ __forceinline__ int xperm(int k) {
     return blk + (((2 * i + e) * 2 + h) * 8 + 2 * t + j);
 }
 
+// Token-operand layout of the tensor-core q4 linear: inside every block of 8
+// features the fp16 values are stored in the order (0,4,1,5,2,6,3,7) -- the
+// order in which the kernel unpacks the nibbles of one packed weight word.
+__host__ __device__ __forceinline__ int perm8(int k) {
+    return (k & ~7) | (((k & 3) << 1) | ((k >> 2) & 1));
+}
+
 }  // namespace mlxcat

@@ -53,8 +53,22 @@ __global__ void embed_norm_kernel(const uint32_t *__restrict__ wq, const __half 
     for (int w = threadIdx.x; w < H / 8; w += blockDim.x)
         for (int i = 0; i < 8; ++i) {
             const int k = w * 8 + i;
-            xn[(size_t)m * H + xperm(k)] = __float2half_rn(hm[k] * r * nw[k]);
+            xn[(size_t)m * H + perm8(k)] = __float2half_rn(hm[k] * r * nw[k]);
         }
+}
+
+// xn = rmsnorm(h) * w for one token per CTA (perm8 layout for the q4 linear)
+__global__ void rmsnorm_kernel(const float *__restrict__ h, int H, const float *__restrict__ nw,
+                               float eps, __half *__restrict__ xn) {
+    __shared__ float sh[32];
+    const int m = blockIdx.x;
+    const float *hm = h + (size_t)m * H;
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < H; k += blockDim.x) ss += hm[k] * hm[k];
+    ss = block_sum(ss, sh);
+    const float r = 1.0f / sqrtf(ss / (float)H + eps);
+    for (int k = threadIdx.x; k < H; k += blockDim.x)
+        xn[(size_t)m * H + perm8(k)] = __float2half_rn(hm[k] * r * nw[k]);
 }
 
 __global__ void residual_norm_kernel(const float *__restrict__ part, int splits, int M, int H,
@@ -76,7 +90,7 @@ __global__ void residual_norm_kernel(const float *__restrict__ part, int splits,
     ss = block_sum(ss, sh);
     const float r = 1.0f / sqrtf(ss / (float)H + eps);
     for (int k = threadIdx.x; k < H; k += blockDim.x)
-        xn[(size_t)m * H + xperm(k)] = __float2half_rn(hm[k] * r * nw[k]);
+        xn[(size_t)m * H + perm8(k)] = __float2half_rn(hm[k] * r * nw[k]);
 }
 
 // one warp per head; lanes own rotate-half pairs (i, i + D/2)
@@ -180,7 +194,7 @@ __global__ void permute_kernel(const __half *__restrict__ x, __half *__restrict_
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x) {
         const int m = (int)(i / K), k = (int)(i - (size_t)m * K);
-        y[(size_t)m * K + xperm(k)] = x[i];
+        y[(size_t)m * K + perm8(k)] = x[i];
     }
 }
 
@@ -226,6 +240,12 @@ cudaError_t embed_norm(const Q4Weight &embed, const int32_t *tok, int M, const f
     return cudaGetLastError();
 }
 
+cudaError_t rmsnorm(const float *h, int M, int H, const float *norm_w, float eps, __half *xn,
+                    cudaStream_t st) {
+    rmsnorm_kernel<<<M, TPB, 0, st>>>(h, H, norm_w, eps, xn);
+    return cudaGetLastError();
+}
+
 cudaError_t residual_norm(const float *part, int splits, int M, int H, const float *norm_w,
                           float eps, float *h, __half *xn, cudaStream_t st) {
     residual_norm_kernel<<<M, TPB, 0, st>>>(part, splits, M, H, norm_w, eps, h, xn);
@@ -249,7 +269,7 @@ cudaError_t swiglu(const float *part, int splits, int M, int I, __half *xn, cuda
 }
 
 cudaError_t permute_activations(const __half *x, __half *x_perm, int M, int K, cudaStream_t st) {
-    if (K % 128) return cudaErrorInvalidValue;
+    if (K % 8) return cudaErrorInvalidValue;
     const size_t n = (size_t)M * K;
     const int blocks = (int)((n + TPB - 1) / TPB < 4096 ? (n + TPB - 1) / TPB : 4096);
     permute_kernel<<<blocks > 0 ? blocks : 1, TPB, 0, st>>>(x, x_perm, M, K);

@@ -21,13 +21,50 @@ struct Q4Weight {
 //      CPU restatement) ------------------------------------------------------
 cudaError_t synth_q4(uint64_t seed, uint32_t tensor_id, float stddev, int N, int K,
                      uint32_t *wq, __half *scales, __half *biases, int row_offset,
-                     cudaStream_t st);
+                     cudaStream_t st, int rgroup = 0, int rstride = 0);
 
 // ---- q4 linear (small-M path): out[s][M][N] fp32 partials over split s ----
 int q4_linear_splits(int N, int K, int M, int sm_count);
 int q4_linear_real_splits(int K, int splits);
 cudaError_t q4_linear(const Q4Weight &w, const __half *x_perm, int M, int ldx, int splits,
                       float *out, cudaStream_t st);
+
+// ---- q4 linear on tcgen05 (TMA + TMEM) with fused split-K and epilogue ------
+}  // namespace mlxcat
+#include <cuda.h>
+namespace mlxcat {
+struct Q4WeightTC {
+    const uint32_t *wq = nullptr;
+    const __half *scales = nullptr;
+    const __half *biases = nullptr;
+    int N = 0, K = 0;
+    CUtensorMap map;          // 2-D TMA map over the packed words (bytes x rows)
+};
+struct Q4Epilogue {
+    enum Op { STORE = 0, RESID = 1, SWIGLU = 2, QKV = 3 };
+    int op = STORE;
+    float *out = nullptr;     // STORE: [M][ldo] fp32; RESID: residual stream [M][ldo]
+    int ldo = 0;
+    __half *xout = nullptr;   // SWIGLU: next activations [M][ldx] (perm8 order)
+    int ldx = 0;
+    // QKV
+    __half *qbuf = nullptr, *kc = nullptr, *vc = nullptr;
+    int max_len = 0, n_heads = 0, n_kv = 0, head_dim = 0;
+    const float *q_norm = nullptr, *k_norm = nullptr, *inv_freq = nullptr;
+    float eps = 0.f;
+    const int32_t *trow = nullptr, *tpos = nullptr;
+    // split-K
+    float *part = nullptr;
+    unsigned *counters = nullptr;
+    int *err = nullptr;
+};
+bool make_weight_map(Q4WeightTC &w);
+int q4_tc_tile(int M);
+int q4_tc_splits(int N, int K, int M, int sm_count);
+size_t q4_tc_partial_floats(int N, int K, int M, int sm_count);
+size_t q4_tc_counters(int N, int M);
+cudaError_t q4_tc(const Q4WeightTC &w, const __half *x_perm8, int M, int sm_count,
+                  const Q4Epilogue &ep, cudaStream_t st);
 
 // ---- activation layout helpers --------------------------------------------
 cudaError_t permute_activations(const __half *x, __half *x_perm, int M, int K, cudaStream_t st);
@@ -38,6 +75,9 @@ cudaError_t reduce_splits(const float *part, int splits, size_t n, float *y, cud
 // h = dequant(embed[tok]);  xn = rmsnorm(h) * w   (xn permuted fp16)
 cudaError_t embed_norm(const Q4Weight &embed, const int32_t *tok, int M, const float *norm_w,
                        float eps, float *h, __half *xn, cudaStream_t st);
+// xn = rmsnorm(h) * w  (perm8 layout)
+cudaError_t rmsnorm(const float *h, int M, int H, const float *norm_w, float eps, __half *xn,
+                    cudaStream_t st);
 // h += sum_s part[s];  xn = rmsnorm(h) * w
 cudaError_t residual_norm(const float *part, int splits, int M, int H, const float *norm_w,
                           float eps, float *h, __half *xn, cudaStream_t st);

@@ -35,12 +35,27 @@ struct DevLin {
     uint32_t *wq = nullptr;
     __half *s = nullptr, *b = nullptr;
     int N = 0, K = 0;
+    Q4WeightTC tcw;       // TMA map over the packed words (built once the buffer exists)
+    const Q4WeightTC &tc() const { return tcw; }
     Q4Weight view() const {
         Q4Weight w;
         w.wq = wq; w.scales = s; w.biases = b; w.N = N; w.K = K;
         return w;
     }
+    bool build_map() {
+        tcw.wq = wq; tcw.scales = s; tcw.biases = b; tcw.N = N; tcw.K = K;
+        return make_weight_map(tcw);
+    }
     size_t bytes() const { return (size_t)N * K / 2 + (size_t)N * (K / 64) * 4; }
+};
+
+// Row placement of a logical tensor inside a fused matrix: logical row n goes
+// to (n / group) * stride + n % group + offset.  q|k|v are stacked; gate and up
+// are interleaved in blocks of 64 rows so one 128-row tile of the fused
+// gate/up linear holds 64 gate rows and the 64 matching up rows.
+struct RowMap {
+    int offset = 0, group = 0, stride = 0, rows = 0;
+    int row(int n) const { return group ? (n / group) * stride + n % group + offset : n + offset; }
 };
 
 }  // namespace
@@ -92,8 +107,11 @@ struct mlxcat_cache {
             *ptok = nullptr;
     unsigned long long *stats = nullptr;
     float *h = nullptr, *part = nullptr, *logits = nullptr;
-    __half *xn = nullptr, *qbuf = nullptr;
+    __half *xn = nullptr, *xa = nullptr, *qbuf = nullptr;
     size_t part_floats = 0;
+    unsigned *counters = nullptr;     // split-K tickets of the q4 linear (self-resetting)
+    int *err = nullptr;               // device-side wait timeouts
+    int32_t *h_err = nullptr;
     AttnScratch attn;
     int attn_splits = 1;
     SampleScratch samp{};
@@ -105,8 +123,15 @@ struct mlxcat_cache {
     mlxcat_spec_config gkey{};
     bool gsampled = false;
     int64_t graph_launches = 0;
-    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;     // verify forward
+    cudaEvent_t es0 = nullptr, es1 = nullptr;     // whole step
     int last_k = -1;
+    // per-kernel profiling: event pairs around q4 linears / attention
+    bool profiling = false;
+    std::vector<cudaEvent_t> prof_ev;
+    std::vector<int> prof_class;       // 0 = q4 linear, 1 = attention (per pair)
+    size_t prof_used = 0;
+    bool prof_recording = false;
 
     RowState rs() const {
         RowState r;
@@ -198,6 +223,30 @@ int splits_for(const mlxcat_ctx *ctx, int N, int K, int M) {
     return q4_linear_real_splits(K, q4_linear_splits(N, K, M, ctx->sm_count));
 }
 
+// bracket one launch with a pair of events when the step is being profiled
+struct ProfScope {
+    mlxcat_cache *c;
+    cudaEvent_t e1 = nullptr;
+    ProfScope(mlxcat_cache *cc, int cls) : c(cc) {
+        if (!c->prof_recording) return;
+        if (c->prof_used + 2 > c->prof_ev.size()) {
+            for (int i = 0; i < 64; ++i) {
+                cudaEvent_t e;
+                if (cudaEventCreate(&e) != cudaSuccess) return;
+                c->prof_ev.push_back(e);
+            }
+        }
+        cudaEvent_t e0 = c->prof_ev[c->prof_used];
+        e1 = c->prof_ev[c->prof_used + 1];
+        c->prof_used += 2;
+        c->prof_class.push_back(cls);
+        cudaEventRecordWithFlags(e0, c->ctx->stream, cudaEventRecordExternal);
+    }
+    ~ProfScope() {
+        if (e1) cudaEventRecordWithFlags(e1, c->ctx->stream, cudaEventRecordExternal);
+    }
+};
+
 // ---------------------------------------------------------------------------
 // forward over M tokens (tok/trow/tpos on device); logits for tokens
 // [lg_from, M) into c->logits (rows in that order); lg_from = M: no logits
@@ -215,29 +264,53 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
               I = cf.intermediate, L = cf.n_layers;
     const float eps = cf.rms_eps;
     LK(ctx, embed_norm(ctx->embed.view(), tok, M, ctx->attn_norm(0), eps, c->h, c->xn, st));
+    Q4Epilogue ep;
+    ep.part = c->part;
+    ep.counters = c->counters;
+    ep.err = c->err;
     for (int l = 0; l < L; ++l) {
         const KVLayer kv = c->layer(l);
-        int sp = splits_for(ctx, ctx->qkv[l].N, H, M);
-        LK(ctx, q4_linear(ctx->qkv[l].view(), c->xn, M, H, q4_linear_splits(ctx->qkv[l].N, H, M, ctx->sm_count), c->part, st));
-        LK(ctx, qkv_epilogue(c->part, sp, M, Hq, Hkv, D, ctx->q_norm(l), ctx->k_norm(l), eps,
-                             ctx->inv_freq, trow, tpos, c->qbuf, kv, st));
+        {   // q|k|v projection + q/k norm + RoPE + KV append
+            Q4Epilogue e = ep;
+            e.op = Q4Epilogue::QKV;
+            e.qbuf = c->qbuf; e.kc = kv.k; e.vc = kv.v; e.max_len = kv.max_len;
+            e.n_heads = Hq; e.n_kv = Hkv; e.head_dim = D;
+            e.q_norm = ctx->q_norm(l); e.k_norm = ctx->k_norm(l); e.eps = eps;
+            e.inv_freq = ctx->inv_freq; e.trow = trow; e.tpos = tpos;
+            ProfScope ps(c, 0);
+            LK(ctx, q4_tc(ctx->qkv[l].tc(), c->xn, M, ctx->sm_count, e, st));
+        }
         ctx->launches++;  // attention is two kernels
-        LK(ctx, attention(c->qbuf, kv, trow, tpos, M, qg, Hq, Hkv, D, KEY_CHUNK, c->attn_splits,
-                          c->attn, c->xn, true, st));
-        sp = splits_for(ctx, H, Hq * D, M);
-        LK(ctx, q4_linear(ctx->o[l].view(), c->xn, M, Hq * D, q4_linear_splits(H, Hq * D, M, ctx->sm_count), c->part, st));
-        LK(ctx, residual_norm(c->part, sp, M, H, ctx->mlp_norm(l), eps, c->h, c->xn, st));
-        sp = splits_for(ctx, 2 * I, H, M);
-        LK(ctx, q4_linear(ctx->gu[l].view(), c->xn, M, H, q4_linear_splits(2 * I, H, M, ctx->sm_count), c->part, st));
-        LK(ctx, swiglu(c->part, sp, M, I, c->xn, st));
-        sp = splits_for(ctx, H, I, M);
-        LK(ctx, q4_linear(ctx->down[l].view(), c->xn, M, I, q4_linear_splits(H, I, M, ctx->sm_count), c->part, st));
-        LK(ctx, residual_norm(c->part, sp, M, H, l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(),
-                              eps, c->h, c->xn, st));
+        { ProfScope ps(c, 1);
+          LK(ctx, attention(c->qbuf, kv, trow, tpos, M, qg, Hq, Hkv, D, KEY_CHUNK, c->attn_splits,
+                            c->attn, c->xn, true, st)); }
+        {   // output projection into the residual stream
+            Q4Epilogue e = ep;
+            e.op = Q4Epilogue::RESID; e.out = c->h; e.ldo = H;
+            ProfScope ps(c, 0);
+            LK(ctx, q4_tc(ctx->o[l].tc(), c->xn, M, ctx->sm_count, e, st));
+        }
+        LK(ctx, rmsnorm(c->h, M, H, ctx->mlp_norm(l), eps, c->xn, st));
+        {   // gate/up + SwiGLU
+            Q4Epilogue e = ep;
+            e.op = Q4Epilogue::SWIGLU; e.xout = c->xa; e.ldx = I;
+            ProfScope ps(c, 0);
+            LK(ctx, q4_tc(ctx->gu[l].tc(), c->xn, M, ctx->sm_count, e, st));
+        }
+        {   // down projection into the residual stream
+            Q4Epilogue e = ep;
+            e.op = Q4Epilogue::RESID; e.out = c->h; e.ldo = H;
+            ProfScope ps(c, 0);
+            LK(ctx, q4_tc(ctx->down[l].tc(), c->xa, M, ctx->sm_count, e, st));
+        }
+        LK(ctx, rmsnorm(c->h, M, H, l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(), eps, c->xn, st));
     }
     if (lg_from < M) {
         const DevLin &head = cf.tie_embeddings ? ctx->embed : ctx->lm_head;
-        LK(ctx, q4_linear(head.view(), c->xn + (size_t)lg_from * H, M - lg_from, H, 1, c->logits, st));
+        Q4Epilogue e = ep;
+        e.op = Q4Epilogue::STORE; e.out = c->logits; e.ldo = cf.vocab;
+        ProfScope ps(c, 0);
+        LK(ctx, q4_tc(head.tc(), c->xn + (size_t)lg_from * H, M - lg_from, ctx->sm_count, e, st));
     }
     return MLXCAT_OK;
 }
@@ -283,11 +356,16 @@ int enqueue_step(mlxcat_cache *c, const SpecParams &sp, bool sampled, bool timed
     mlxcat_ctx *ctx = c->ctx;
     cudaStream_t st = ctx->stream;
     const int K1 = sp.k + 1, M = c->rows * K1;
+    if (timed) CK(ctx, cudaEventRecordWithFlags(c->es0, st, cudaEventRecordExternal));
     LK(ctx, draft(c->rs(), sp, c->vtok, c->count, c->trow, c->tpos, st));
-    if (timed) CK(ctx, cudaEventRecord(c->ev0, st));
+    if (timed) CK(ctx, cudaEventRecordWithFlags(c->ev0, st, cudaEventRecordExternal));
+    c->prof_used = 0;
+    c->prof_class.clear();
+    c->prof_recording = timed && c->profiling;
     int rc = forward(c, M, K1, c->vtok, c->trow, c->tpos, 0);
+    c->prof_recording = false;
     if (rc) return rc;
-    if (timed) CK(ctx, cudaEventRecord(c->ev1, st));
+    if (timed) CK(ctx, cudaEventRecordWithFlags(c->ev1, st, cudaEventRecordExternal));
     LK(ctx, argmax_rows(c->logits, M, ctx->cfg.vocab, c->amax, st));
     LK(ctx, accept_greedy(c->rs(), sp, c->vtok, c->count, c->amax, step_out(c), st));
     if (sampled) {
@@ -299,6 +377,8 @@ int enqueue_step(mlxcat_cache *c, const SpecParams &sp, bool sampled, bool timed
     CK(ctx, cudaMemcpyAsync(c->h_n, c->out_n, sizeof(int32_t) * c->rows, cudaMemcpyDeviceToHost, st));
     CK(ctx, cudaMemcpyAsync(c->h_fin, c->out_fin, sizeof(int32_t) * c->rows, cudaMemcpyDeviceToHost, st));
     CK(ctx, cudaMemcpyAsync(c->h_stats, c->stats, sizeof(unsigned long long) * 4, cudaMemcpyDeviceToHost, st));
+    if (c->err) CK(ctx, cudaMemcpyAsync(c->h_err, c->err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    if (timed) CK(ctx, cudaEventRecordWithFlags(c->es1, st, cudaEventRecordExternal));
     return MLXCAT_OK;
 }
 
@@ -315,6 +395,22 @@ void copy_out(mlxcat_cache *c, int K1, int32_t *out_tokens, int32_t *out_counts,
     }
     for (int r = 0; r < c->rows; ++r)
         if (c->h_fin[r]) c->host_temp[r] = 0.0f;
+}
+
+// a device wait that timed out (bounded mbarrier polls) poisons the cache's
+// results: report it and clear the flag
+int device_err(mlxcat_cache *c, bool from_pinned) {
+    int e = 0;
+    if (!c->err) return MLXCAT_OK;
+    if (from_pinned) {
+        e = *c->h_err;
+    } else if (cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        return set_err(c->ctx, MLXCAT_E_CUDA, "reading the device error flag failed");
+    }
+    if (e == 0) return MLXCAT_OK;
+    cudaMemset(c->err, 0, sizeof(int));
+    *c->h_err = 0;
+    return set_err(c->ctx, MLXCAT_E_CUDA, "a device pipeline wait timed out (code %d)", e);
 }
 
 void drop_graph(mlxcat_cache *c) {
@@ -364,6 +460,8 @@ int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx
             dalloc(ctx->allocs, &w.s, (size_t)N * K / 64) != cudaSuccess ||
             dalloc(ctx->allocs, &w.b, (size_t)N * K / 64) != cudaSuccess)
             rc = set_err(ctx, MLXCAT_E_OOM, "weight allocation failed (%d x %d)", N, K);
+        else if (!w.build_map())
+            rc = set_err(ctx, MLXCAT_E_CUDA, "TMA descriptor for a %d x %d weight failed", N, K);
     };
     if (c.kind == MLXCAT_MODEL_TABLE) {
         if (dalloc(ctx->allocs, &ctx->table, (size_t)c.vocab) != cudaSuccess)
@@ -424,27 +522,53 @@ int mlxcat_ctx_synchronize(mlxcat_ctx *ctx) {
 
 int64_t mlxcat_ctx_launch_count(const mlxcat_ctx *ctx) { return ctx ? ctx->launches : -1; }
 
-static DevLin *lin_for(mlxcat_ctx *ctx, uint32_t id, int *row_off, int *rows) {
+static DevLin *lin_for(mlxcat_ctx *ctx, uint32_t id, RowMap *rm) {
     const mlxcat_model_config &c = ctx->cfg;
     if (c.kind != MLXCAT_MODEL_TRANSFORMER) return nullptr;
-    if (id == 0xFFFF0000u) { *row_off = 0; *rows = c.vocab; return &ctx->embed; }
+    *rm = RowMap();
+    if (id == 0xFFFF0000u) { rm->rows = c.vocab; return &ctx->embed; }
     if (id == 0xFFFF0001u) {
         if (c.tie_embeddings) return nullptr;
-        *row_off = 0; *rows = c.vocab; return &ctx->lm_head;
+        rm->rows = c.vocab; return &ctx->lm_head;
     }
     const int l = (int)(id / 16u), kind = (int)(id % 16u);
     if (l >= c.n_layers) return nullptr;
     const int D = c.head_dim, qd = c.n_heads * D, kvd = c.n_kv_heads * D;
     switch (kind) {
-    case 0: *row_off = 0; *rows = qd; return &ctx->qkv[l];
-    case 1: *row_off = qd; *rows = kvd; return &ctx->qkv[l];
-    case 2: *row_off = qd + kvd; *rows = kvd; return &ctx->qkv[l];
-    case 3: *row_off = 0; *rows = c.hidden; return &ctx->o[l];
-    case 4: *row_off = 0; *rows = c.intermediate; return &ctx->gu[l];
-    case 5: *row_off = c.intermediate; *rows = c.intermediate; return &ctx->gu[l];
-    case 6: *row_off = 0; *rows = c.hidden; return &ctx->down[l];
+    case 0: rm->rows = qd; return &ctx->qkv[l];
+    case 1: rm->offset = qd; rm->rows = kvd; return &ctx->qkv[l];
+    case 2: rm->offset = qd + kvd; rm->rows = kvd; return &ctx->qkv[l];
+    case 3: rm->rows = c.hidden; return &ctx->o[l];
+    case 4: rm->group = 64; rm->stride = 128; rm->rows = c.intermediate; return &ctx->gu[l];
+    case 5: rm->group = 64; rm->stride = 128; rm->offset = 64; rm->rows = c.intermediate; return &ctx->gu[l];
+    case 6: rm->rows = c.hidden; return &ctx->down[l];
     default: return nullptr;
     }
+}
+
+// copy `rows` logical rows between a host tensor and their placement in a fused matrix
+static cudaError_t copy_rows(const DevLin *w, const RowMap &rm, void *host_wq, void *host_s, void *host_b,
+                             bool to_device) {
+    const size_t wb = (size_t)w->K / 2, sb = (size_t)w->K / 64 * 2;
+    const int run = rm.group ? rm.group : rm.rows;
+    for (int n0 = 0; n0 < rm.rows; n0 += run) {
+        const int cnt = std::min(run, rm.rows - n0);
+        const size_t dr = (size_t)rm.row(n0);
+        char *dw = reinterpret_cast<char *>(w->wq) + dr * wb, *hw = static_cast<char *>(host_wq) + n0 * wb;
+        char *ds = reinterpret_cast<char *>(w->s) + dr * sb, *hs = static_cast<char *>(host_s) + n0 * sb;
+        char *db = reinterpret_cast<char *>(w->b) + dr * sb, *hb = static_cast<char *>(host_b) + n0 * sb;
+        cudaError_t e;
+        if (to_device) {
+            if ((e = cudaMemcpy(dw, hw, cnt * wb, cudaMemcpyHostToDevice)) != cudaSuccess) return e;
+            if ((e = cudaMemcpy(ds, hs, cnt * sb, cudaMemcpyHostToDevice)) != cudaSuccess) return e;
+            if ((e = cudaMemcpy(db, hb, cnt * sb, cudaMemcpyHostToDevice)) != cudaSuccess) return e;
+        } else {
+            if (host_wq && (e = cudaMemcpy(hw, dw, cnt * wb, cudaMemcpyDeviceToHost)) != cudaSuccess) return e;
+            if (host_s && (e = cudaMemcpy(hs, ds, cnt * sb, cudaMemcpyDeviceToHost)) != cudaSuccess) return e;
+            if (host_b && (e = cudaMemcpy(hb, db, cnt * sb, cudaMemcpyDeviceToHost)) != cudaSuccess) return e;
+        }
+    }
+    return cudaSuccess;
 }
 
 int mlxcat_weights_synth(mlxcat_ctx *ctx, uint64_t seed, float stddev) {
@@ -457,9 +581,10 @@ int mlxcat_weights_synth(mlxcat_ctx *ctx, uint64_t seed, float stddev) {
     for (int l = 0; l < c.n_layers; ++l)
         for (int k = 0; k < 7; ++k) ids.push_back((uint32_t)l * 16u + (uint32_t)k);
     for (uint32_t id : ids) {
-        int off = 0, rows = 0;
-        DevLin *w = lin_for(ctx, id, &off, &rows);
-        LK(ctx, synth_q4(seed, id, stddev, rows, w->K, w->wq, w->s, w->b, off, ctx->stream));
+        RowMap rm;
+        DevLin *w = lin_for(ctx, id, &rm);
+        LK(ctx, synth_q4(seed, id, stddev, rm.rows, w->K, w->wq, w->s, w->b, rm.offset, ctx->stream,
+                         rm.group, rm.stride));
     }
     CK(ctx, cudaStreamSynchronize(ctx->stream));
     ctx->have_weights = true;
@@ -469,29 +594,24 @@ int mlxcat_weights_synth(mlxcat_ctx *ctx, uint64_t seed, float stddev) {
 int mlxcat_weights_set_q4(mlxcat_ctx *ctx, uint32_t id, const uint32_t *wq, const uint16_t *scales,
                           const uint16_t *biases) {
     if (!ctx || !wq || !scales || !biases) return MLXCAT_E_INVALID;
-    int off = 0, rows = 0;
-    DevLin *w = lin_for(ctx, id, &off, &rows);
+    RowMap rm;
+    DevLin *w = lin_for(ctx, id, &rm);
     if (!w) return set_err(ctx, MLXCAT_E_INVALID, "unknown tensor id 0x%x", id);
     CK(ctx, cudaSetDevice(ctx->device));
-    const int K = w->K;
-    CK(ctx, cudaMemcpy(w->wq + (size_t)off * (K / 8), wq, (size_t)rows * (K / 8) * 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(w->s + (size_t)off * (K / 64), scales, (size_t)rows * (K / 64) * 2, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(w->b + (size_t)off * (K / 64), biases, (size_t)rows * (K / 64) * 2, cudaMemcpyHostToDevice));
+    CK(ctx, copy_rows(w, rm, const_cast<uint32_t *>(wq), const_cast<uint16_t *>(scales),
+                      const_cast<uint16_t *>(biases), true));
     ctx->have_weights = true;
     return MLXCAT_OK;
 }
 
 int mlxcat_weights_get_q4(mlxcat_ctx *ctx, uint32_t id, uint32_t *wq, uint16_t *scales, uint16_t *biases) {
     if (!ctx) return MLXCAT_E_INVALID;
-    int off = 0, rows = 0;
-    DevLin *w = lin_for(ctx, id, &off, &rows);
+    RowMap rm;
+    DevLin *w = lin_for(ctx, id, &rm);
     if (!w) return set_err(ctx, MLXCAT_E_INVALID, "unknown tensor id 0x%x", id);
     CK(ctx, cudaSetDevice(ctx->device));
     CK(ctx, cudaStreamSynchronize(ctx->stream));
-    const int K = w->K;
-    if (wq) CK(ctx, cudaMemcpy(wq, w->wq + (size_t)off * (K / 8), (size_t)rows * (K / 8) * 4, cudaMemcpyDeviceToHost));
-    if (scales) CK(ctx, cudaMemcpy(scales, w->s + (size_t)off * (K / 64), (size_t)rows * (K / 64) * 2, cudaMemcpyDeviceToHost));
-    if (biases) CK(ctx, cudaMemcpy(biases, w->b + (size_t)off * (K / 64), (size_t)rows * (K / 64) * 2, cudaMemcpyDeviceToHost));
+    CK(ctx, copy_rows(w, rm, wq, scales, biases, false));
     return MLXCAT_OK;
 }
 
@@ -563,14 +683,20 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
         const int xw = std::max(std::max(H, I), Hq * D);
         chk(dalloc(A, &c->h, (size_t)Mc * H));
         chk(dalloc(A, &c->xn, (size_t)Mc * xw));
+        chk(dalloc(A, &c->xa, (size_t)Mc * I));
         chk(dalloc(A, &c->qbuf, (size_t)Mc * Hq * D));
-        // split-K partials: max over the linears and every token count
-        size_t pf = 0;
-        const int NK[4][2] = {{(Hq + 2 * Hkv) * D, H}, {H, Hq * D}, {2 * I, H}, {H, I}};
+        // split-K partials and tickets: max over the linears and every token count
+        size_t pf = 0, nc = 0;
+        const int NK[5][2] = {{(Hq + 2 * Hkv) * D, H}, {H, Hq * D}, {2 * I, H}, {H, I}, {cf.vocab, H}};
         for (int m = 1; m <= Mc; ++m)
-            for (auto &nk : NK) pf = std::max(pf, (size_t)splits_for(ctx, nk[0], nk[1], m) * m * nk[0]);
+            for (auto &nk : NK) {
+                pf = std::max(pf, q4_tc_partial_floats(nk[0], nk[1], m, ctx->sm_count));
+                nc = std::max(nc, q4_tc_counters(nk[0], m));
+            }
         c->part_floats = pf;
         chk(dalloc(A, &c->part, pf));
+        chk(dalloc(A, &c->counters, nc));
+        if (rc == MLXCAT_OK) chk(cudaMemset(c->counters, 0, nc * sizeof(unsigned)));
         // attention scratch
         c->attn_splits = attention_max_splits(max_len, KEY_CHUNK);
         int groups = std::max(R, (PREFILL_CHUNK + PREFILL_QG - 1) / PREFILL_QG);
@@ -587,8 +713,13 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
     chk(cudaMallocHost((void **)&c->h_n, sizeof(int32_t) * R));
     chk(cudaMallocHost((void **)&c->h_fin, sizeof(int32_t) * R));
     chk(cudaMallocHost((void **)&c->h_stats, sizeof(unsigned long long) * 4));
+    chk(cudaMallocHost((void **)&c->h_err, sizeof(int32_t)));
+    chk(dalloc(A, &c->err, 1));
+    if (rc == MLXCAT_OK) chk(cudaMemset(c->err, 0, sizeof(int)));
     chk(cudaEventCreate(&c->ev0));
     chk(cudaEventCreate(&c->ev1));
+    chk(cudaEventCreate(&c->es0));
+    chk(cudaEventCreate(&c->es1));
     if (rc == MLXCAT_OK) {
         chk(cudaMemset(c->active, 0, sizeof(int32_t) * R));
         chk(cudaMemset(c->hist_len, 0, sizeof(int32_t) * R));
@@ -622,8 +753,12 @@ int mlxcat_cache_destroy(mlxcat_cache *c) {
     if (c->h_n) cudaFreeHost(c->h_n);
     if (c->h_fin) cudaFreeHost(c->h_fin);
     if (c->h_stats) cudaFreeHost(c->h_stats);
+    if (c->h_err) cudaFreeHost(c->h_err);
     if (c->ev0) cudaEventDestroy(c->ev0);
     if (c->ev1) cudaEventDestroy(c->ev1);
+    if (c->es0) cudaEventDestroy(c->es0);
+    if (c->es1) cudaEventDestroy(c->es1);
+    for (cudaEvent_t e : c->prof_ev) cudaEventDestroy(e);
     delete c;
     return MLXCAT_OK;
 }
@@ -682,6 +817,7 @@ int mlxcat_cache_insert_row(mlxcat_cache *c, int32_t row, const int32_t *prompt,
     int32_t t0 = 0;
     CK(ctx, cudaMemcpyAsync(&t0, c->first_tok, 4, cudaMemcpyDeviceToHost, st));
     CK(ctx, cudaStreamSynchronize(st));
+    if ((rc = device_err(c, false))) return rc;
     if (first_token) *first_token = t0;
     return MLXCAT_OK;
 }
@@ -805,6 +941,7 @@ int mlxcat_verify_forward(mlxcat_cache *c, const mlxcat_spec_config *spec, float
         CK(ctx, cudaMemcpyAsync(logits, c->logits, sizeof(float) * (size_t)M * ctx->cfg.vocab,
                                 cudaMemcpyDeviceToHost, ctx->stream));
     CK(ctx, cudaStreamSynchronize(ctx->stream));
+    if ((rc = device_err(c, false))) return rc;
     return MLXCAT_OK;
 }
 
@@ -868,6 +1005,7 @@ int mlxcat_spec_step(mlxcat_cache *c, const mlxcat_spec_config *spec, int32_t *o
     CK(ctx, cudaGraphLaunch(c->graph, st));
     ctx->launches += c->graph_launches;
     CK(ctx, cudaStreamSynchronize(st));
+    if ((rc = device_err(c, true))) return rc;
     copy_out(c, sp.k + 1, out_tokens, out_counts, out_fin, stats);
     c->last_k = -1;
     return MLXCAT_OK;
@@ -876,6 +1014,36 @@ int mlxcat_spec_step(mlxcat_cache *c, const mlxcat_spec_config *spec, int32_t *o
 int mlxcat_last_verify_ms(mlxcat_cache *c, float *ms) {
     if (!c || !ms) return MLXCAT_E_INVALID;
     CK(c->ctx, cudaEventElapsedTime(ms, c->ev0, c->ev1));
+    return MLXCAT_OK;
+}
+
+int mlxcat_last_step_ms(mlxcat_cache *c, float *ms) {
+    if (!c || !ms) return MLXCAT_E_INVALID;
+    CK(c->ctx, cudaEventElapsedTime(ms, c->es0, c->es1));
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_set_profiling(mlxcat_cache *c, int32_t enabled) {
+    if (!c) return MLXCAT_E_INVALID;
+    if (c->profiling != (enabled != 0)) drop_graph(c);
+    c->profiling = enabled != 0;
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_profile(mlxcat_cache *c, float *q4_ms, float *attn_ms, int32_t *q4_n, int32_t *attn_n) {
+    if (!c) return MLXCAT_E_INVALID;
+    float sum[2] = {0.f, 0.f};
+    int cnt[2] = {0, 0};
+    for (size_t i = 0; i < c->prof_class.size(); ++i) {
+        float ms = 0.f;
+        CK(c->ctx, cudaEventElapsedTime(&ms, c->prof_ev[2 * i], c->prof_ev[2 * i + 1]));
+        sum[c->prof_class[i]] += ms;
+        cnt[c->prof_class[i]] += 1;
+    }
+    if (q4_ms) *q4_ms = sum[0];
+    if (attn_ms) *attn_ms = sum[1];
+    if (q4_n) *q4_n = cnt[0];
+    if (attn_n) *attn_n = cnt[1];
     return MLXCAT_OK;
 }
 
@@ -888,10 +1056,22 @@ static int op_sm_count() {
     return sm;
 }
 
+// workspace: [x in perm8 order | split-K partials | split-K tickets | error flag]
+static void q4_ws_layout(int32_t N, int32_t K, int32_t M, size_t *off_part, size_t *off_ctr, size_t *off_err,
+                         size_t *total) {
+    const int sm = op_sm_count();
+    auto up = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    *off_part = up((size_t)M * K * 2);
+    *off_ctr = *off_part + up(q4_tc_partial_floats(N, K, M, sm) * 4);
+    *off_err = *off_ctr + up(q4_tc_counters(N, M) * 4);
+    *total = *off_err + 256;
+}
+
 size_t mlxcat_op_q4_linear_workspace(int32_t N, int32_t K, int32_t M) {
     if (N <= 0 || K <= 0 || M <= 0) return 0;
-    const int sp = q4_linear_real_splits(K, q4_linear_splits(N, K, M, op_sm_count()));
-    return (size_t)M * K * 2 + 256 + (size_t)sp * M * N * 4;
+    size_t a, b, c, t;
+    q4_ws_layout(N, K, M, &a, &b, &c, &t);
+    return t;
 }
 
 int mlxcat_op_q4_linear(const uint32_t *wq, const uint16_t *scales, const uint16_t *biases, int32_t N,
@@ -900,19 +1080,24 @@ int mlxcat_op_q4_linear(const uint32_t *wq, const uint16_t *scales, const uint16
     if (!wq || !scales || !biases || !x || !y || N <= 0 || K <= 0 || M <= 0)
         return op_err(MLXCAT_E_INVALID, "bad q4_linear arguments");
     if (N % 128 || K % 128) return op_err(MLXCAT_E_INVALID, "N and K must be multiples of 128");
-    const size_t need = mlxcat_op_q4_linear_workspace(N, K, M);
+    size_t off_part, off_ctr, off_err, need;
+    q4_ws_layout(N, K, M, &off_part, &off_ctr, &off_err, &need);
     if (!ws || ws_bytes < need) return op_err(MLXCAT_E_INVALID, "workspace of %zu bytes required", need);
     cudaStream_t st = (cudaStream_t)stream;
-    const int plan = q4_linear_splits(N, K, M, op_sm_count());
-    const int sp = q4_linear_real_splits(K, plan);
-    __half *xp = static_cast<__half *>(ws);
-    float *part = reinterpret_cast<float *>(static_cast<char *>(ws) + (((size_t)M * K * 2 + 255) & ~(size_t)255));
-    Q4Weight w;
+    char *w8 = static_cast<char *>(ws);
+    Q4WeightTC w;
     w.wq = wq; w.scales = reinterpret_cast<const __half *>(scales);
     w.biases = reinterpret_cast<const __half *>(biases); w.N = N; w.K = K;
-    cudaError_t e = permute_activations(reinterpret_cast<const __half *>(x), xp, M, K, st);
-    if (e == cudaSuccess) e = q4_linear(w, xp, M, K, plan, sp == 1 ? y : part, st);
-    if (e == cudaSuccess && sp > 1) e = reduce_splits(part, sp, (size_t)M * N, y, st);
+    if (!make_weight_map(w)) return op_err(MLXCAT_E_CUDA, "TMA descriptor for the weights failed");
+    Q4Epilogue ep;
+    ep.op = Q4Epilogue::STORE; ep.out = y; ep.ldo = N;
+    ep.part = reinterpret_cast<float *>(w8 + off_part);
+    ep.counters = reinterpret_cast<unsigned *>(w8 + off_ctr);
+    ep.err = reinterpret_cast<int *>(w8 + off_err);
+    __half *xp = reinterpret_cast<__half *>(w8);
+    cudaError_t e = cudaMemsetAsync(w8 + off_ctr, 0, need - off_ctr, st);
+    if (e == cudaSuccess) e = permute_activations(reinterpret_cast<const __half *>(x), xp, M, K, st);
+    if (e == cudaSuccess) e = q4_tc(w, xp, M, op_sm_count(), ep, st);
     if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "q4_linear: %s", cudaGetErrorString(e));
     return MLXCAT_OK;
 }

@@ -4,7 +4,9 @@
 // stream (element index n*K + k, tensor id), then the min/max affine
 // quantizer: scale = fp16((max-min)/15), bias = fp16(min),
 // q = clamp(rint((w - bias)/scale), 0, 15), nibbles packed lowest first.
-// Bit-identical with the CPU restatement (orc_q4_synth).
+// Bit-identical with the CPU restatement (orc_q4_synth).  Logical row n is
+// written to row (n / rgroup) * rstride + n % rgroup + row_offset of the
+// destination (fused matrices: contiguous q|k|v, gate/up interleaved per 64).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -12,7 +14,8 @@ namespace mlxcat {
 
 __global__ void synth_q4_kernel(uint64_t seed, uint32_t tensor_id, float stddev, int N, int K,
                                 uint32_t *__restrict__ wq, __half *__restrict__ scales,
-                                __half *__restrict__ biases, int row_offset) {
+                                __half *__restrict__ biases, int row_offset, int rgroup,
+                                int rstride) {
     const int G = K / MLXCAT_GS;
     const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (long long)N * G) return;
@@ -30,7 +33,7 @@ __global__ void synth_q4_kernel(uint64_t seed, uint32_t tensor_id, float stddev,
     const float sf = __half2float(sh);
     const __half bh = __float2half_rn(mn);
     const float bf = __half2float(bh);
-    const int orow = n + row_offset;
+    const int orow = (n / rgroup) * rstride + (n % rgroup) + row_offset;
     uint32_t *dst = wq + (size_t)orow * (K / 8) + grp * (MLXCAT_GS / 8);
     for (int j = 0; j < MLXCAT_GS / 8; ++j) {
         uint32_t word = 0;
@@ -50,12 +53,13 @@ __global__ void synth_q4_kernel(uint64_t seed, uint32_t tensor_id, float stddev,
 
 cudaError_t synth_q4(uint64_t seed, uint32_t tensor_id, float stddev, int N, int K,
                      uint32_t *wq, __half *scales, __half *biases, int row_offset,
-                     cudaStream_t st) {
+                     cudaStream_t st, int rgroup, int rstride) {
+    if (rgroup <= 0) { rgroup = N; rstride = 0; }
     const long long groups = (long long)N * (K / MLXCAT_GS);
     const int threads = 128;
     const long long blocks = (groups + threads - 1) / threads;
     synth_q4_kernel<<<(unsigned)blocks, threads, 0, st>>>(seed, tensor_id, stddev, N, K, wq,
-                                                          scales, biases, row_offset);
+                                                          scales, biases, row_offset, rgroup, rstride);
     return cudaGetLastError();
 }
 

@@ -300,9 +300,25 @@ class BatchKVCache:
                                          st.rejected_batches)
         return tok, n, fin, stats
 
+    def set_profiling(self, enabled: bool):
+        self.ctx.check(self.L.mlxcat_cache_set_profiling(self.h, int(enabled)))
+
+    def profile(self):
+        """(q4 linear ms, attention ms, q4 launches, attention launches) of the last step."""
+        a, b = C.c_float(), C.c_float()
+        na, nb = C.c_int32(), C.c_int32()
+        self.ctx.check(self.L.mlxcat_cache_profile(self.h, C.byref(a), C.byref(b), C.byref(na),
+                                                   C.byref(nb)))
+        return a.value, b.value, na.value, nb.value
+
     def last_verify_ms(self) -> float:
         ms = C.c_float()
         self.ctx.check(self.L.mlxcat_last_verify_ms(self.h, C.byref(ms)))
+        return ms.value
+
+    def last_step_ms(self) -> float:
+        ms = C.c_float()
+        self.ctx.check(self.L.mlxcat_last_step_ms(self.h, C.byref(ms)))
         return ms.value
 
     def close(self):

@@ -383,6 +383,23 @@ class Generator:
         return lib().orc_admit(self.model.h, self.kv.h, C.byref(R), row, _ptr(p, C.c_int32),
                                len(p), chunk)
 
+    def set_row(self, row: int, history, n_gen: int, max_new: int, kv_len: int, sp: Sampling,
+                active: bool = True):
+        """Install a row's state without prefill (used to continue from a state
+        produced elsewhere, e.g. copied from the device)."""
+        cap = len(history) + max_new + 16
+        buf = (C.c_int32 * cap)(*history)
+        self._hist_bufs[row] = buf
+        R = self.rows[row]
+        R.hist = C.cast(buf, C.POINTER(C.c_int32))
+        R.hist_len = len(history)
+        R.hist_cap = cap
+        R.n_gen = n_gen
+        R.max_new = max_new
+        R.active = int(active)
+        R.sp = sp
+        self.kv.set_len(row, kv_len)
+
     def step(self):
         K1 = self.spec.max_proposal + 1
         out = np.zeros((self.n_rows, K1), np.int32)

@@ -40,8 +40,8 @@ def test_synth_q4_bit_exact(N, K, tid):
 # --------------------------------------------------------------------------- #
 # q4 linear
 # --------------------------------------------------------------------------- #
-@pytest.mark.parametrize("M", [1, 5, 16, 17, 48, 64, 100])
-@pytest.mark.parametrize("N,K", [(256, 512), (384, 1408), (1024, 2560), (128, 9728)])
+@pytest.mark.parametrize("M", [1, 5, 16, 17, 48, 64, 100, 200])
+@pytest.mark.parametrize("N,K", [(256, 512), (384, 1408), (1024, 2560), (128, 9728), (128, 128)])
 def test_q4_linear_matches_oracle(M, N, K):
     rng = np.random.default_rng(M * 7 + N)
     wq, s, b = O.q4_synth(5, N, 0.02, N, K)
