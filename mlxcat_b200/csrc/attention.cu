@@ -267,7 +267,7 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
 template <int QT>
 __global__ void attn_combine_kernel(const float *__restrict__ o_part, const float *__restrict__ ml_part,
                                     int M, int qg, int Hq, int Hkv, int D, int splits,
-                                    __half *__restrict__ out, int permuted) {
+                                    __half *__restrict__ out, int permuted, int out_rows) {
     constexpr int QROWS = QT * 16;
     const int grp = blockIdx.x, h = blockIdx.y, qi = blockIdx.z;
     const int G = Hq / Hkv;
@@ -294,14 +294,14 @@ __global__ void attn_combine_kernel(const float *__restrict__ o_part, const floa
         const float r = den > 0.f ? num / den : 0.f;
         const int j = qi / G, gh = qi - j * G;
         const int k = (h * G + gh) * D + d;
-        out[(size_t)(t0 + j) * KO + (permuted ? perm8(k) : k)] = __float2half_rn(r);
+        out[permuted ? xblk(t0 + j, k, out_rows) : (size_t)(t0 + j) * KO + k] = __float2half_rn(r);
     }
 }
 
 template <int QT, int D>
 cudaError_t launch_attn(const __half *qbuf, KVLayer kv, const int32_t *trow, const int32_t *tpos,
                         int M, int qg, int Hq, int Hkv, int key_chunk, int splits,
-                        AttnScratch sc, __half *out, bool permuted, cudaStream_t st) {
+                        AttnScratch sc, __half *out, bool permuted, int out_rows, cudaStream_t st) {
     constexpr int PITCH = D + 8;
     const size_t smem = (size_t)(QT * 16 + 4 * KB) * PITCH * 2;
     static bool attr[64] = {};
@@ -321,7 +321,8 @@ cudaError_t launch_attn(const __half *qbuf, KVLayer kv, const int32_t *trow, con
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     dim3 g2(groups, Hkv, QT * 16);
-    attn_combine_kernel<QT><<<g2, D, 0, st>>>(sc.o, sc.ml, M, qg, Hq, Hkv, D, splits, out, permuted ? 1 : 0);
+    attn_combine_kernel<QT><<<g2, D, 0, st>>>(sc.o, sc.ml, M, qg, Hq, Hkv, D, splits, out, permuted ? 1 : 0,
+                                              out_rows);
     return cudaGetLastError();
 }
 
@@ -340,19 +341,20 @@ size_t attention_scratch_items(int groups, int n_kv, int splits) {
 
 cudaError_t attention(const __half *qbuf, KVLayer kv, const int32_t *trow, const int32_t *tpos,
                       int M, int qg, int n_heads, int n_kv, int D, int key_chunk, int splits,
-                      AttnScratch scratch, __half *out, bool permuted_out, cudaStream_t st) {
+                      AttnScratch scratch, __half *out, bool permuted_out, int out_rows,
+                      cudaStream_t st) {
     if (key_chunk % KB || n_heads % n_kv) return cudaErrorInvalidValue;
     const int nq = qg * (n_heads / n_kv);
     const int groups = (M + qg - 1) / qg;
     if (attention_scratch_items(groups, n_kv, splits) > scratch.items) return cudaErrorInvalidValue;
     if (D == 128) {
-        if (nq <= 16) return launch_attn<1, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, st);
-        if (nq <= 32) return launch_attn<2, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, st);
-        if (nq <= 64) return launch_attn<4, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, st);
+        if (nq <= 16) return launch_attn<1, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, st);
+        if (nq <= 32) return launch_attn<2, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, st);
+        if (nq <= 64) return launch_attn<4, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, st);
     } else if (D == 64) {
-        if (nq <= 16) return launch_attn<1, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, st);
-        if (nq <= 32) return launch_attn<2, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, st);
-        if (nq <= 64) return launch_attn<4, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, st);
+        if (nq <= 16) return launch_attn<1, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, st);
+        if (nq <= 32) return launch_attn<2, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, st);
+        if (nq <= 64) return launch_attn<4, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, st);
     }
     return cudaErrorInvalidValue;
 }

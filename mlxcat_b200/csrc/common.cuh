@@ -151,4 +151,12 @@ __host__ __device__ __forceinline__ int perm8(int k) {
     return (k & ~7) | (((k & 3) << 1) | ((k >> 2) & 1));
 }
 
+// Token operand of the tensor-core q4 linear in memory: blocked by 64
+// features, [K/64][rows][64] fp16, perm8 order inside each 8-block, so one
+// 3-D TMA box fetches a [256 k x tokens] tile.  Element (m, k) of a buffer
+// with `rows` token rows:
+__host__ __device__ __forceinline__ size_t xblk(int m, int k, int rows) {
+    return ((size_t)(k >> 6) * rows + m) * 64 + perm8(k & 63);
+}
+
 }  // namespace mlxcat

@@ -30,7 +30,7 @@ __device__ __forceinline__ float block_sum(float v, float *sh) {
 __global__ void embed_norm_kernel(const uint32_t *__restrict__ wq, const __half *__restrict__ sc,
                                   const __half *__restrict__ bi, int H, const int32_t *tok,
                                   const float *__restrict__ nw, float eps, float *__restrict__ h,
-                                  __half *__restrict__ xn) {
+                                  __half *__restrict__ xn, int ldx_rows) {
     __shared__ float sh[32];
     const int m = blockIdx.x;
     const int t = tok[m];
@@ -53,13 +53,13 @@ __global__ void embed_norm_kernel(const uint32_t *__restrict__ wq, const __half 
     for (int w = threadIdx.x; w < H / 8; w += blockDim.x)
         for (int i = 0; i < 8; ++i) {
             const int k = w * 8 + i;
-            xn[(size_t)m * H + perm8(k)] = __float2half_rn(hm[k] * r * nw[k]);
+            xn[xblk(m, k, ldx_rows)] = __float2half_rn(hm[k] * r * nw[k]);
         }
 }
 
 // xn = rmsnorm(h) * w for one token per CTA (perm8 layout for the q4 linear)
 __global__ void rmsnorm_kernel(const float *__restrict__ h, int H, const float *__restrict__ nw,
-                               float eps, __half *__restrict__ xn) {
+                               float eps, __half *__restrict__ xn, int ldx_rows) {
     __shared__ float sh[32];
     const int m = blockIdx.x;
     const float *hm = h + (size_t)m * H;
@@ -68,7 +68,7 @@ __global__ void rmsnorm_kernel(const float *__restrict__ h, int H, const float *
     ss = block_sum(ss, sh);
     const float r = 1.0f / sqrtf(ss / (float)H + eps);
     for (int k = threadIdx.x; k < H; k += blockDim.x)
-        xn[(size_t)m * H + perm8(k)] = __float2half_rn(hm[k] * r * nw[k]);
+        xn[xblk(m, k, ldx_rows)] = __float2half_rn(hm[k] * r * nw[k]);
 }
 
 __global__ void residual_norm_kernel(const float *__restrict__ part, int splits, int M, int H,
@@ -194,7 +194,7 @@ __global__ void permute_kernel(const __half *__restrict__ x, __half *__restrict_
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x) {
         const int m = (int)(i / K), k = (int)(i - (size_t)m * K);
-        y[(size_t)m * K + perm8(k)] = x[i];
+        y[xblk(m, k, M)] = x[i];
     }
 }
 
@@ -234,15 +234,15 @@ __global__ void table_logits_kernel(const int32_t *next, const int32_t *tok, int
 }  // namespace
 
 cudaError_t embed_norm(const Q4Weight &embed, const int32_t *tok, int M, const float *norm_w,
-                       float eps, float *h, __half *xn, cudaStream_t st) {
+                       float eps, float *h, __half *xn, int ldx_rows, cudaStream_t st) {
     embed_norm_kernel<<<M, TPB, 0, st>>>(embed.wq, embed.scales, embed.biases, embed.K, tok,
-                                         norm_w, eps, h, xn);
+                                         norm_w, eps, h, xn, ldx_rows);
     return cudaGetLastError();
 }
 
 cudaError_t rmsnorm(const float *h, int M, int H, const float *norm_w, float eps, __half *xn,
-                    cudaStream_t st) {
-    rmsnorm_kernel<<<M, TPB, 0, st>>>(h, H, norm_w, eps, xn);
+                    int ldx_rows, cudaStream_t st) {
+    rmsnorm_kernel<<<M, TPB, 0, st>>>(h, H, norm_w, eps, xn, ldx_rows);
     return cudaGetLastError();
 }
 
@@ -269,7 +269,7 @@ cudaError_t swiglu(const float *part, int splits, int M, int I, __half *xn, cuda
 }
 
 cudaError_t permute_activations(const __half *x, __half *x_perm, int M, int K, cudaStream_t st) {
-    if (K % 8) return cudaErrorInvalidValue;
+    if (K % 64) return cudaErrorInvalidValue;
     const size_t n = (size_t)M * K;
     const int blocks = (int)((n + TPB - 1) / TPB < 4096 ? (n + TPB - 1) / TPB : 4096);
     permute_kernel<<<blocks > 0 ? blocks : 1, TPB, 0, st>>>(x, x_perm, M, K);

@@ -45,8 +45,8 @@ struct Q4Epilogue {
     int op = STORE;
     float *out = nullptr;     // STORE: [M][ldo] fp32; RESID: residual stream [M][ldo]
     int ldo = 0;
-    __half *xout = nullptr;   // SWIGLU: next activations [M][ldx] (perm8 order)
-    int ldx = 0;
+    __half *xout = nullptr;   // SWIGLU: next activations, blocked token layout (xblk)
+    int ldx_rows = 0;         // token rows of xout
     // QKV
     __half *qbuf = nullptr, *kc = nullptr, *vc = nullptr;
     int max_len = 0, n_heads = 0, n_kv = 0, head_dim = 0;
@@ -60,24 +60,26 @@ struct Q4Epilogue {
 };
 bool make_weight_map(Q4WeightTC &w);
 int q4_tc_tile(int M);
-int q4_tc_splits(int N, int K, int M, int sm_count);
 size_t q4_tc_partial_floats(int N, int K, int M, int sm_count);
 size_t q4_tc_counters(int N, int M);
-cudaError_t q4_tc(const Q4WeightTC &w, const __half *x_perm8, int M, int sm_count,
-                  const Q4Epilogue &ep, cudaStream_t st);
+// tokens [tok_base, tok_base + M) of the blocked operand x_blk ([K/64][ldx_rows][64]);
+// output rows are 0..M-1
+cudaError_t q4_tc(const Q4WeightTC &w, const __half *x_blk, int ldx_rows, int tok_base, int M,
+                  int sm_count, const Q4Epilogue &ep, cudaStream_t st);
 
 // ---- activation layout helpers --------------------------------------------
-cudaError_t permute_activations(const __half *x, __half *x_perm, int M, int K, cudaStream_t st);
+// natural [M][K] fp16 -> blocked token layout with M rows
+cudaError_t permute_activations(const __half *x, __half *x_blk, int M, int K, cudaStream_t st);
 // y[i] = sum_s part[s][i] for i < n (fixed split order)
 cudaError_t reduce_splits(const float *part, int splits, size_t n, float *y, cudaStream_t st);
 
 // ---- per-token fused kernels ------------------------------------------------
 // h = dequant(embed[tok]);  xn = rmsnorm(h) * w   (xn permuted fp16)
 cudaError_t embed_norm(const Q4Weight &embed, const int32_t *tok, int M, const float *norm_w,
-                       float eps, float *h, __half *xn, cudaStream_t st);
+                       float eps, float *h, __half *xn, int ldx_rows, cudaStream_t st);
 // xn = rmsnorm(h) * w  (perm8 layout)
 cudaError_t rmsnorm(const float *h, int M, int H, const float *norm_w, float eps, __half *xn,
-                    cudaStream_t st);
+                    int ldx_rows, cudaStream_t st);
 // h += sum_s part[s];  xn = rmsnorm(h) * w
 cudaError_t residual_norm(const float *part, int splits, int M, int H, const float *norm_w,
                           float eps, float *h, __half *xn, cudaStream_t st);
@@ -107,7 +109,8 @@ size_t attention_scratch_items(int groups, int n_kv, int splits);
 int attention_qrows(int qg, int n_heads, int n_kv);
 cudaError_t attention(const __half *qbuf, KVLayer kv, const int32_t *trow, const int32_t *tpos,
                       int M, int qg, int n_heads, int n_kv, int D, int key_chunk, int splits,
-                      AttnScratch scratch, __half *out, bool permuted_out, cudaStream_t st);
+                      AttnScratch scratch, __half *out, bool permuted_out, int out_rows,
+                      cudaStream_t st);
 
 // ---- lm head / sampling ----------------------------------------------------
 cudaError_t argmax_rows(const float *logits, int M, int V, int32_t *out, cudaStream_t st);

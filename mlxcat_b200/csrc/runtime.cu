@@ -263,7 +263,8 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
     const int H = cf.hidden, D = cf.head_dim, Hq = cf.n_heads, Hkv = cf.n_kv_heads,
               I = cf.intermediate, L = cf.n_layers;
     const float eps = cf.rms_eps;
-    LK(ctx, embed_norm(ctx->embed.view(), tok, M, ctx->attn_norm(0), eps, c->h, c->xn, st));
+    const int R = c->m_cap;   // token rows of the blocked activation buffers
+    LK(ctx, embed_norm(ctx->embed.view(), tok, M, ctx->attn_norm(0), eps, c->h, c->xn, R, st));
     Q4Epilogue ep;
     ep.part = c->part;
     ep.counters = c->counters;
@@ -278,39 +279,39 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
             e.q_norm = ctx->q_norm(l); e.k_norm = ctx->k_norm(l); e.eps = eps;
             e.inv_freq = ctx->inv_freq; e.trow = trow; e.tpos = tpos;
             ProfScope ps(c, 0);
-            LK(ctx, q4_tc(ctx->qkv[l].tc(), c->xn, M, ctx->sm_count, e, st));
+            LK(ctx, q4_tc(ctx->qkv[l].tc(), c->xn, R, 0, M, ctx->sm_count, e, st));
         }
         ctx->launches++;  // attention is two kernels
         { ProfScope ps(c, 1);
           LK(ctx, attention(c->qbuf, kv, trow, tpos, M, qg, Hq, Hkv, D, KEY_CHUNK, c->attn_splits,
-                            c->attn, c->xn, true, st)); }
+                            c->attn, c->xn, true, R, st)); }
         {   // output projection into the residual stream
             Q4Epilogue e = ep;
             e.op = Q4Epilogue::RESID; e.out = c->h; e.ldo = H;
             ProfScope ps(c, 0);
-            LK(ctx, q4_tc(ctx->o[l].tc(), c->xn, M, ctx->sm_count, e, st));
+            LK(ctx, q4_tc(ctx->o[l].tc(), c->xn, R, 0, M, ctx->sm_count, e, st));
         }
-        LK(ctx, rmsnorm(c->h, M, H, ctx->mlp_norm(l), eps, c->xn, st));
+        LK(ctx, rmsnorm(c->h, M, H, ctx->mlp_norm(l), eps, c->xn, R, st));
         {   // gate/up + SwiGLU
             Q4Epilogue e = ep;
-            e.op = Q4Epilogue::SWIGLU; e.xout = c->xa; e.ldx = I;
+            e.op = Q4Epilogue::SWIGLU; e.xout = c->xa; e.ldx_rows = R;
             ProfScope ps(c, 0);
-            LK(ctx, q4_tc(ctx->gu[l].tc(), c->xn, M, ctx->sm_count, e, st));
+            LK(ctx, q4_tc(ctx->gu[l].tc(), c->xn, R, 0, M, ctx->sm_count, e, st));
         }
         {   // down projection into the residual stream
             Q4Epilogue e = ep;
             e.op = Q4Epilogue::RESID; e.out = c->h; e.ldo = H;
             ProfScope ps(c, 0);
-            LK(ctx, q4_tc(ctx->down[l].tc(), c->xa, M, ctx->sm_count, e, st));
+            LK(ctx, q4_tc(ctx->down[l].tc(), c->xa, R, 0, M, ctx->sm_count, e, st));
         }
-        LK(ctx, rmsnorm(c->h, M, H, l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(), eps, c->xn, st));
+        LK(ctx, rmsnorm(c->h, M, H, l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(), eps, c->xn, R, st));
     }
     if (lg_from < M) {
         const DevLin &head = cf.tie_embeddings ? ctx->embed : ctx->lm_head;
         Q4Epilogue e = ep;
         e.op = Q4Epilogue::STORE; e.out = c->logits; e.ldo = cf.vocab;
         ProfScope ps(c, 0);
-        LK(ctx, q4_tc(head.tc(), c->xn + (size_t)lg_from * H, M - lg_from, ctx->sm_count, e, st));
+        LK(ctx, q4_tc(head.tc(), c->xn, R, lg_from, M - lg_from, ctx->sm_count, e, st));
     }
     return MLXCAT_OK;
 }
@@ -1097,7 +1098,7 @@ int mlxcat_op_q4_linear(const uint32_t *wq, const uint16_t *scales, const uint16
     __half *xp = reinterpret_cast<__half *>(w8);
     cudaError_t e = cudaMemsetAsync(w8 + off_ctr, 0, need - off_ctr, st);
     if (e == cudaSuccess) e = permute_activations(reinterpret_cast<const __half *>(x), xp, M, K, st);
-    if (e == cudaSuccess) e = q4_tc(w, xp, M, op_sm_count(), ep, st);
+    if (e == cudaSuccess) e = q4_tc(w, xp, M, 0, M, op_sm_count(), ep, st);
     if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "q4_linear: %s", cudaGetErrorString(e));
     return MLXCAT_OK;
 }
@@ -1134,7 +1135,7 @@ int mlxcat_op_attention(const uint16_t *q, const uint16_t *k_cache, const uint16
     kv.v = const_cast<__half *>(reinterpret_cast<const __half *>(v_cache));
     kv.max_len = max_len;
     cudaError_t e = attention(reinterpret_cast<const __half *>(q), kv, trow, tpos, M, qg, n_heads, n_kv, D,
-                              KEY_CHUNK, splits, sc, reinterpret_cast<__half *>(out), false,
+                              KEY_CHUNK, splits, sc, reinterpret_cast<__half *>(out), false, M,
                               (cudaStream_t)stream);
     if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "attention: %s", cudaGetErrorString(e));
     return MLXCAT_OK;
