@@ -197,6 +197,23 @@ MLXCAT_API int mlxcat_op_attention(const uint16_t *q, const uint16_t *k_cache, c
                         int32_t qg, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                         uint16_t *out, void *workspace, size_t workspace_bytes, void *stream);
 
+/* No counterpart in the reference: the attention operator above for callers
+ * that cannot allocate device memory.  Same arguments and result as
+ * mlxcat_op_attention, but its scratch lives in a fixed device array of
+ * MLXCAT_NOALLOC_ATTN_SCRATCH_BYTES inside the library (held on every GPU that
+ * loads it until exit); a shape whose mlxcat_op_attention_workspace exceeds
+ * that size is rejected with MLXCAT_E_INVALID.  It allocates nothing.  The
+ * first call on a device resolves the array's address with
+ * cudaGetSymbolAddress (this can load the library's device code on that
+ * device): make that first call before any stream capture.  All calls share
+ * the one array, so calls whose kernels overlap on the GPU (different streams
+ * without ordering) race on it. */
+#define MLXCAT_NOALLOC_ATTN_SCRATCH_BYTES (16u << 20)
+MLXCAT_API int mlxcat_op_attention_noalloc(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                        int32_t max_len, const int32_t *trow, const int32_t *tpos, int32_t M,
+                        int32_t qg, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                        uint16_t *out, void *stream);
+
 /* Seeded N(0, stddev) weights quantised to MLX affine q4 g64 (bit-identical
  * with the CPU restatement). */
 MLXCAT_API int mlxcat_op_synth_q4(uint64_t seed, uint32_t tensor_id, float stddev, int32_t N, int32_t K,

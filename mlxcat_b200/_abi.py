@@ -109,6 +109,8 @@ PROTOTYPES = {
     "mlxcat_op_attention_workspace": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "mlxcat_op_attention": (C.c_int, [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
                                       _vp, _vp, _sz, _vp]),
+    "mlxcat_op_attention_noalloc": (C.c_int, [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32,
+                                              _i32, _vp, _vp]),
     "mlxcat_op_synth_q4": (C.c_int, [_u64, _u32, _f32, _i32, _i32, _vp, _vp, _vp, _vp]),
     "mlxcat_op_draft": (C.c_int, [C.POINTER(RowsC), C.POINTER(SpecConfigC), _vp, _vp, _vp, _vp, _vp]),
     "mlxcat_op_accept_workspace": (_sz, [_i32, _i32]),

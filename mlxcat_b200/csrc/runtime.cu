@@ -14,6 +14,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1138,6 +1139,78 @@ int mlxcat_op_attention(const uint16_t *q, const uint16_t *k_cache, const uint16
                               KEY_CHUNK, splits, sc, reinterpret_cast<__half *>(out), false, M,
                               (cudaStream_t)stream);
     if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "attention: %s", cudaGetErrorString(e));
+    return MLXCAT_OK;
+}
+
+// ---------------------------------------------------------------------------
+// attention for callers that cannot allocate device memory
+// ---------------------------------------------------------------------------
+// Some callers of the attention operator have no way to allocate device
+// memory where they call it: a host runtime whose device buffers all come
+// from a foreign arena it does not own (a Swift / MLX-style buffer pool, a
+// ctypes or JNI binding without a CUDA allocator), or an inference loop that
+// must not allocate between steps.  For them the split-K scratch (partial
+// outputs and running max / sum per key split) lives in one fixed device array
+// of MLXCAT_NOALLOC_ATTN_SCRATCH_BYTES, declared below at file scope.  Every
+// GPU that loads this library holds that array until the process exits.
+//
+// In host code `g_attn_noalloc_scratch` is only a stand-in for the device
+// symbol; its device address is fetched once per device with
+// cudaGetSymbolAddress and cached.
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[MLXCAT_NOALLOC_ATTN_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void *g_noalloc_base[64] = {};   // device address of the array, per device ordinal
+}  // namespace
+
+int mlxcat_op_attention_noalloc(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                                int32_t max_len, const int32_t *trow, const int32_t *tpos, int32_t M,
+                                int32_t qg, int32_t n_heads, int32_t n_kv, int32_t D, uint16_t *out,
+                                void *stream) {
+    if (!q || !k_cache || !v_cache || !trow || !tpos || !out || M <= 0 || qg <= 0 || n_kv <= 0 ||
+        n_heads % n_kv || (D != 64 && D != 128) || qg * (n_heads / n_kv) > 64)
+        return op_err(MLXCAT_E_INVALID, "bad attention arguments");
+    const size_t need = mlxcat_op_attention_workspace(M, qg, n_heads, n_kv, D, max_len);
+    if (need > (size_t)MLXCAT_NOALLOC_ATTN_SCRATCH_BYTES)
+        return op_err(MLXCAT_E_INVALID,
+                      "attention_noalloc: this shape needs %zu bytes of scratch but the fixed array holds %zu; "
+                      "use mlxcat_op_attention with a workspace",
+                      need, (size_t)MLXCAT_NOALLOC_ATTN_SCRATCH_BYTES);
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "attention_noalloc: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return op_err(MLXCAT_E_INVALID, "attention_noalloc: device ordinal %d >= 64", dev);
+    char *base = nullptr;
+    {
+        // first call on this device (the current one): resolve the array's address
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_base[dev]) {
+            void *p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+            if (e != cudaSuccess)
+                return op_err(MLXCAT_E_CUDA, "attention_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+            g_noalloc_base[dev] = p;
+        }
+        base = static_cast<char *>(g_noalloc_base[dev]);
+    }
+    // Nothing in the array needs clearing: every partial and every (max, sum)
+    // pair the combine pass reads is written by the split pass of the same call.
+    const int groups = (M + qg - 1) / qg;
+    const int splits = attention_max_splits(max_len, KEY_CHUNK);
+    const size_t items = attention_scratch_items(groups, n_kv, splits);
+    const int qrows = attention_qrows(qg, n_heads, n_kv);
+    AttnScratch sc;
+    sc.o = reinterpret_cast<float *>(base);
+    sc.ml = reinterpret_cast<float *>(base + ((items * qrows * (size_t)D * 4 + 255) & ~(size_t)255));
+    sc.items = items;
+    KVLayer kv;
+    kv.k = const_cast<__half *>(reinterpret_cast<const __half *>(k_cache));
+    kv.v = const_cast<__half *>(reinterpret_cast<const __half *>(v_cache));
+    kv.max_len = max_len;
+    e = attention(reinterpret_cast<const __half *>(q), kv, trow, tpos, M, qg, n_heads, n_kv, D, KEY_CHUNK,
+                  splits, sc, reinterpret_cast<__half *>(out), false, M, (cudaStream_t)stream);
+    if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "attention_noalloc: %s", cudaGetErrorString(e));
     return MLXCAT_OK;
 }
 
