@@ -179,8 +179,9 @@ MLXCAT_API const char *mlxcat_op_last_error(void);
 
 /* quantizedMatmul (mlx-swift, called by QuantizedLinear): y[M][N] fp32 =
  * x[M][K] fp16 . dequant(W)^T, W MLX affine q4 g64 (tcgen05 tensor cores).
- * The workspace holds the re-ordered activations, split-K partials and
- * tickets, and a device error flag (non-zero after a pipeline wait timed out). */
+ * The workspace holds the re-ordered activations, the scales and biases
+ * re-packed per 512-wide k unit, split-K partials and tickets, and a device
+ * error flag (non-zero after a pipeline wait timed out). */
 MLXCAT_API size_t mlxcat_op_q4_linear_workspace(int32_t N, int32_t K, int32_t M);
 MLXCAT_API int mlxcat_op_q4_linear(const uint32_t *wq, const uint16_t *scales, const uint16_t *biases,
                         int32_t N, int32_t K, const uint16_t *x, int32_t M, float *y,

@@ -269,6 +269,7 @@ __global__ void attn_combine_kernel(const float *__restrict__ o_part, const floa
                                     int M, int qg, int Hq, int Hkv, int D, int splits,
                                     __half *__restrict__ out, int permuted, int out_rows) {
     constexpr int QROWS = QT * 16;
+    griddep_launch_dependents();   // the output projection may start prefetching its weights
     const int grp = blockIdx.x, h = blockIdx.y, qi = blockIdx.z;
     const int G = Hq / Hkv;
     const int t0 = grp * qg;

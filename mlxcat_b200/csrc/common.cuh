@@ -119,6 +119,13 @@ __device__ __forceinline__ uint32_t float_key(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start while its predecessor still runs; it must call
+// griddep_wait() before touching anything the predecessor writes.  A
+// predecessor calls griddep_launch_dependents() to let that happen early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

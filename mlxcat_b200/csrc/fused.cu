@@ -60,6 +60,7 @@ __global__ void embed_norm_kernel(const uint32_t *__restrict__ wq, const __half 
 // xn = rmsnorm(h) * w for one token per CTA (perm8 layout for the q4 linear)
 __global__ void rmsnorm_kernel(const float *__restrict__ h, int H, const float *__restrict__ nw,
                                float eps, __half *__restrict__ xn, int ldx_rows) {
+    griddep_launch_dependents();   // the next linear may start prefetching its weights
     __shared__ float sh[32];
     const int m = blockIdx.x;
     const float *hm = h + (size_t)m * H;

@@ -37,12 +37,14 @@ struct Q4WeightTC {
     const uint32_t *wq = nullptr;
     const __half *scales = nullptr;
     const __half *biases = nullptr;
+    const uint32_t *sbp = nullptr;   // (scale, bias) pairs re-packed by pack_q4_sb
     int N = 0, K = 0;
     CUtensorMap map;          // 2-D TMA map over the packed words (bytes x rows)
 };
 struct Q4Epilogue {
     enum Op { STORE = 0, RESID = 1, SWIGLU = 2, QKV = 3 };
     int op = STORE;
+    int pdl = 0;              // launch with programmatic stream serialisation
     float *out = nullptr;     // STORE: [M][ldo] fp32; RESID: residual stream [M][ldo]
     int ldo = 0;
     __half *xout = nullptr;   // SWIGLU: next activations, blocked token layout (xblk)
@@ -59,6 +61,9 @@ struct Q4Epilogue {
     int *err = nullptr;
 };
 bool make_weight_map(Q4WeightTC &w);
+// words of the re-packed (scale, bias) pairs of an N x K weight, and the packer
+size_t q4_sbp_words(int N, int K);
+cudaError_t pack_q4_sb(const __half *scales, const __half *biases, int N, int K, uint32_t *sbp, cudaStream_t st);
 int q4_tc_tile(int M);
 size_t q4_tc_partial_floats(int N, int K, int M, int sm_count);
 size_t q4_tc_counters(int N, int M);

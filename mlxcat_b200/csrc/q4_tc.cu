@@ -4,45 +4,60 @@
 //   y[m][n] = sum_k x[m][k] * (scale[n][k/64] * q[n][k] + bias[n][k/64])
 //
 // Replaces mlx-swift's quantizedMatmul (QuantizedLinear in mlx-swift-lm) on
-// the verify forward (BatchGenerator.swift:900-904).  Weights stay in the MLX
-// layout: packed uint32 [N][K/8] with the lowest nibble first, fp16 scales and
-// biases [N][K/64].
+// the verify forward (BatchGenerator.swift:900-904).  The packed weights stay
+// in the MLX layout (uint32 [N][K/8], lowest nibble first); scales and biases
+// are re-packed once per weight into (scale, bias) fp16 pairs ordered
+// [N/128][K/512][8 groups][128 rows] so that one bulk copy brings a unit's
+// 4 KB of them next to its weight tile (pack_q4_sb below).
 //
-// Swap-AB: the 128 weight rows of a CTA are the MMA's M dimension, the tokens
-// of the verify batch (16..128) its N dimension.  One 256-wide k chunk per
-// pipeline stage:
+// Swap-AB: the 128 weight rows of a block are the MMA's M dimension, the
+// tokens of the verify batch (16..128) its N dimension.
 //
-//   warp 16 (one lane)  TMA producer: weight tile [128 rows x 128 B] (128B
-//                       swizzle) and the token tile [4 x NT x 64] (one 3-D box,
-//                       128B swizzle) into a ring of shared-memory stages.
-//   warps 0-15          dequantisers: warp w owns rows 32*(w%4).. and the
-//                       64-wide quantisation group w/4 of the chunk; 32 bytes
-//                       per thread from the staged tile, nibbles unpacked with
-//                       the 0x6400 fp16 magic and dequantised in registers
-//                       (hfma2 / hadd2), stored to tensor memory (tcgen05.st)
-//                       as the MMA's A operand.
-//   (persistent, one CTA per SM, stream-K: see unit_begin below)
-//   warps 17-18 (lane0) MMA issuers: each issues half of the chunk's sixteen
-//                       tcgen05.mma (M=128, N=NT, K=16, A from TMEM, B from
-//                       shared memory) into its own fp32 accumulator in TMEM;
-//                       one thread issues at most one MMA per ~65 cycles, two
-//                       keep the tensor pipe fed at small N.
+// Schedule: persistent, one CTA per SM, stream-K over units of (128-row block
+// x 512-wide k chunk); a block whose chunks span several CTAs is finished by
+// the last of them (deterministic slot-ordered sum).  Within a unit the k
+// range is processed as two 256-wide sub-chunks.
+//
+// Warp roles (20 warps):
+//   warp 18 (one lane)  W producer: per unit one W stage = two TMA boxes of
+//                       [128 rows x 128 B] (128B swizzle) + the unit's packed
+//                       scale/bias (bulk copy).  A W stage is released as soon
+//                       as the dequant warps have read it.
+//   warp 19 (one lane)  x producer: per sub-chunk one x stage = the token tile
+//                       [4 x NT x 64] fp16 (3-D box, 128B swizzle), released
+//                       when the MMAs reading it have completed.  x stages and
+//                       TMEM A buffers form one ring: sub-chunk j uses slot
+//                       j % R of both, and one MMA-completion barrier per slot
+//                       (one commit per issuer per sub-chunk) frees both.
+//   warps 0-15          dequantisers: warp w owns rows 32*(w%4).. (its TMEM
+//                       lane quarter) and 64-wide group g = w/4 of each
+//                       sub-chunk: nibbles -> fp16 in registers (0x6400 magic,
+//                       hfma2 / hadd2), tcgen05.st into TMEM (the MMA's A
+//                       operand, a ring of three sub-chunk buffers for
+//                       NT <= 64, two above), then a named-barrier arrive for
+//                       the issuer of group g.
+//   warps 16-17         MMA issuers (lane 0): issuer i waits on its named
+//                       barrier, then issues tcgen05.mma (M=128, N=NT, K=16,
+//                       A from TMEM, B from shared memory) for groups 2i, 2i+1
+//                       into its own fp32 accumulator in TMEM (one issuing
+//                       thread sustains about one MMA per 50 cycles; two keep
+//                       up with the dequantisers).
 //
 // Inside each 8-wide k block the unpack order is (0,4,1,5,2,6,3,7); the token
 // operand is stored in that order and blocked by 64 features ([K/64][rows][64],
 // see common.cuh: xblk) by its producers.
 //
-// A row block whose k range is shared by several CTAs: each writes its fp32
-// partial to its slot; the last to finish (atomic ticket) sums the slots in
-// slot order -- deterministic -- and runs the epilogue:
+// Epilogue (dequant warps, after the last sub-chunk of a block segment):
 //   STORE   logits  out[m][n] = y
 //   RESID   residual stream h[m][n] += y
 //   SWIGLU  gate/up rows interleaved per 64 -> x_next[m][i] = silu(g) * u
 //   QKV     per-head q/k RMSNorm (Qwen3), rotate-half RoPE, q to the query
 //           buffer, k/v appended to the KV cache at each token's position
 //
-// Every mbarrier wait is bounded (tc.cuh); a timeout sets *err and the CTA
-// drains its in-flight copies and MMAs (bounded) before freeing TMEM.
+// Every mbarrier wait is bounded (tc.cuh).  A timeout sets *err and an abort
+// flag; from then on every role skips its waits and work but still walks the
+// same sequence of named barriers, so no thread is left waiting on one, and
+// the CTA drains its in-flight copies and MMAs (bounded) before freeing TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -56,33 +71,41 @@ int q4_tc_pmax(int U, int G, int nc);
 
 namespace {
 
-constexpr int ROWS = 128;              // weight rows per CTA (MMA M)
-constexpr int CHUNK = 256;             // k per pipeline stage
+constexpr int ROWS = 128;              // weight rows per block (MMA M)
+constexpr int KU = 512;                // k per stream-K unit (one W stage)
+constexpr int KS = 256;                // k per sub-chunk (one x stage, one A buffer)
 constexpr int DQ_WARPS = 16;           // dequant / epilogue warps
 constexpr int DQ_THREADS = DQ_WARPS * 32;
-constexpr int TMA_WARP = DQ_WARPS;
-constexpr int MMA_WARP0 = DQ_WARPS + 1;
-constexpr int ISSUERS = 2;
-constexpr int THREADS = (DQ_WARPS + 1 + ISSUERS) * 32;
-constexpr int A_COLS = CHUNK / 2;      // TMEM columns of one A stage (fp16 pairs)
-constexpr int PF = 4;                  // chunks of scale/bias prefetch
-constexpr int MAX_STAGES = 8;
+constexpr int ISS_WARP0 = DQ_WARPS;    // issuer warps 16..17
+constexpr int NI = 2;                  // MMA issuers
+constexpr int GPI = 4 / NI;            // 64-k groups per issuer
+constexpr int WP_WARP = DQ_WARPS + NI; // W producer
+constexpr int XP_WARP = WP_WARP + 1;   // x producer
+constexpr int THREADS = (XP_WARP + 1) * 32;
+constexpr int BAR_COUNT = 32 + 128 * GPI;   // issuer warp + its dequant warps
+constexpr int A_COLS = KS / 2;         // TMEM columns of one A buffer (fp16 pairs)
+constexpr int WBOX = ROWS * 128;       // one [128 rows x 128 B] weight box
+constexpr int SB_BYTES = 8 * ROWS * 4; // packed (scale, bias) of one unit
+constexpr int WSTAGE = 2 * WBOX + SB_BYTES;
+constexpr int MAX_SW = 4, MAX_AST = 3;
+constexpr int EPI_BAR = 9;             // named barrier of the epilogue (1..6: issuers)
 
-enum ErrCode { ERR_FULL = 1, ERR_AFULL = 2, ERR_MMA = 3, ERR_DONE = 4 };
+enum ErrCode { ERR_WFULL = 1, ERR_XFULL = 2, ERR_MDONE = 3, ERR_XFREE = 4, ERR_WFREE = 5, ERR_DFREE = 6 };
 
 template <int NT>
 struct Cfg {
-    static constexpr int A_STAGES = NT <= 64 ? 3 : 2;
-    static constexpr int DCOLS = NT <= 64 ? 64 : 128;        // columns per accumulator
-    static constexpr int D_COL = A_STAGES * A_COLS;
-    static constexpr int XBYTES = 4 * NT * 128;              // four 64-k boxes
-    static constexpr int WBYTES = ROWS * 128;
-    static constexpr int STAGE = XBYTES + WBYTES;
-    static_assert(D_COL + ISSUERS * DCOLS <= 512, "TMEM budget");
+    static constexpr int AST = NT <= 64 ? 3 : 2;             // ring slots: A buffers in TMEM = x stages
+    static constexpr int DCOLS = NT <= 64 ? 64 : 128;        // TMEM columns per accumulator
+    static constexpr int D_COL = AST * A_COLS;
+    static constexpr int XSTAGE = 4 * NT * 128;              // 256 k of NT tokens
+    static_assert(D_COL + NI * DCOLS <= 512, "TMEM budget");
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int n) {
+    asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(n) : "memory");
 }
 
 // named barrier over the dequant warps that also ORs a predicate across them
@@ -97,6 +120,12 @@ __device__ __forceinline__ bool named_bar_or(int id, int n, bool pred) {
         : "r"(id), "r"(n), "r"((uint32_t)pred)
         : "memory");
     return r != 0;
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
 }
 
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
@@ -125,50 +154,83 @@ __device__ __forceinline__ void dequant_word(uint32_t w, __half2 s1, __half2 m1,
     }
 }
 
+// 16 bytes (32 nibbles) of one row -> 16 fp16 pairs, with the group's
+// (scale, bias) pair sb
+__device__ __forceinline__ void dequant16(const uint4 &w, uint32_t sb, uint32_t *a) {
+    const __half2 sbh = *reinterpret_cast<const __half2 *>(&sb);
+    const __half2 s1 = __low2half2(sbh), b2 = __high2half2(sbh);
+    const __half2 m1 = __hmul2(s1, __float2half2_rn(-1024.0f));
+    const __half2 s16 = __hmul2(s1, __float2half2_rn(0.0625f));
+    const __half2 m64 = __hmul2(s1, __float2half2_rn(-64.0f));
+    dequant_word(w.x, s1, m1, s16, m64, b2, &a[0]);
+    dequant_word(w.y, s1, m1, s16, m64, b2, &a[4]);
+    dequant_word(w.z, s1, m1, s16, m64, b2, &a[8]);
+    dequant_word(w.w, s1, m1, s16, m64, b2, &a[12]);
+}
+
 struct Smem {
-    uint64_t full[MAX_STAGES], mma_done[MAX_STAGES], a_full[3], d_free;
+    uint64_t full_w[MAX_SW], w_free[MAX_SW], full_x[MAX_AST], mma_done[MAX_AST], d_free;
     uint32_t tmem_base;
     int abort_flag;
     int last_flag;
-    float wsum[4][4][16];   // [token group][row quarter][token]
-    float xch[4][ROWS * 16];   // epilogue exchange: [token group][row][token]
+    float wsum[4][4][16];       // [token group][row quarter][token]
+    float xch[2][ROWS * 16];    // epilogue exchange: [token group pair][row][token]
 };
 
-// Stream-K schedule: the flattened (row block, k chunk) units are split into
-// gridDim.x contiguous, equal ranges, one per CTA (one CTA per SM).  A row
-// block whose chunks span several CTAs is finished by the last of them.
-__device__ __forceinline__ int unit_begin(int c, int U, int G) { return (int)(((long long)c * U) / G); }
+// Stream-K schedule: the flattened (row block, k unit) space is split into
+// gridDim.x contiguous, equal ranges, one per CTA.
+// (U * G < 2^32 for every launch: checked on the host)
+__device__ __forceinline__ int unit_begin(int c, int U, int G) { return (int)(((uint32_t)c * (uint32_t)U) / (uint32_t)G); }
 __device__ __forceinline__ int unit_owner(int u, int U, int G) {
-    int c = (int)(((long long)u * G) / U);
+    int c = (int)(((uint32_t)u * (uint32_t)G) / (uint32_t)U);
     while (c + 1 < G && unit_begin(c + 1, U, G) <= u) ++c;
     while (c > 0 && unit_begin(c, U, G) > u) --c;
     return c;
 }
 
+// bounded wait that gives up at once after an abort
+__device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int *abort_flag, int *err,
+                                              int code) {
+    if (*abort_flag) return false;
+    if (tc::mbar_wait(bar, parity, err, code)) return true;
+    *abort_flag = 1;
+    return false;
+}
+
 template <int NT>
 __global__ void __launch_bounds__(THREADS, 1)
 q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-             const __half *__restrict__ scales, const __half *__restrict__ biases, int N, int K,
-             int M, int tok_base, int nblk, int nc, int U, int pmax, int stages, Q4Epilogue ep) {
+             const uint32_t *__restrict__ sbp, int N, int K, int M, int tok_base, int nblk, int nc, int U,
+             int pmax, int sw, Q4Epilogue ep) {
     using C = Cfg<NT>;
     constexpr int PIECES = NT <= 64 ? 1 : 2;      // 16-token pieces per token group
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char *ring = reinterpret_cast<unsigned char *>(
+    unsigned char *wring = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    Smem &cs = *reinterpret_cast<Smem *>(ring + (size_t)stages * C::STAGE);
+    unsigned char *xring = wring + (size_t)sw * WSTAGE;
+    constexpr int R = C::AST;
+    Smem &cs = *reinterpret_cast<Smem *>(xring + (size_t)R * C::XSTAGE);
 
+    // The weights do not depend on the previous kernel: let the next launch be
+    // scheduled early, and (launched with programmatic serialisation) start
+    // streaming and dequantising weights before the previous kernel finishes;
+    // only the token operand waits for it (griddep_wait in the x producer).
+    griddep_launch_dependents();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     const int u0 = unit_begin(cta, U, G), u1 = unit_begin(cta + 1, U, G);
-    const int n = u1 - u0;                        // chunks of this CTA
-    const uint32_t ring_a = tc::smem_u32(ring);
+    const int n = u1 - u0;                        // units of this CTA
+    const int nsub = 2 * n;                       // sub-chunks of this CTA
 
-    if (warp == TMA_WARP && lane == 0) {
-        for (int s = 0; s < stages; ++s) {
-            tc::mbar_init(tc::smem_u32(&cs.full[s]), 1);
-            tc::mbar_init(tc::smem_u32(&cs.mma_done[s]), ISSUERS);
+    if (warp == WP_WARP && lane == 0) {
+        for (int s = 0; s < sw; ++s) {
+            tc::mbar_init(tc::smem_u32(&cs.full_w[s]), 1);
+            tc::mbar_init(tc::smem_u32(&cs.w_free[s]), DQ_WARPS);
         }
-        for (int a = 0; a < C::A_STAGES; ++a) tc::mbar_init(tc::smem_u32(&cs.a_full[a]), DQ_WARPS);
+        for (int r = 0; r < R; ++r) {
+            tc::mbar_init(tc::smem_u32(&cs.full_x[r]), 1);
+            tc::mbar_init(tc::smem_u32(&cs.mma_done[r]), NI);
+        }
         tc::mbar_init(tc::smem_u32(&cs.d_free), DQ_WARPS);
         cs.abort_flag = 0;
         tc::fence_barrier_init();
@@ -182,219 +244,243 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
     const uint32_t tmem = cs.tmem_base;
     volatile int *abort_flag = &cs.abort_flag;
 
-    if (warp == TMA_WARP) {
+    if (warp == WP_WARP) {
         if (lane == 0) {
-            // ---------------- TMA producer ----------------
+            // ---------------- W producer: one stage per unit ----------------
             int issued = 0;
+            int b = u0 / nc, c = u0 - b * nc;
             for (int i = 0; i < n && !*abort_flag; ++i) {
-                const int s = i % stages;
-                if (i >= stages) {
-                    const int pc = i - stages;   // previous user of this stage
-                    if (!tc::mbar_wait(tc::smem_u32(&cs.mma_done[s]), (pc / stages) & 1, ep.err, ERR_MMA)) {
-                        *abort_flag = 1;
-                        break;
-                    }
-                }
-                const int u = u0 + i, b = u / nc, c = u - b * nc;
-                const int tile = b / nblk, blk = b - tile * nblk;
-                const uint32_t st = ring_a + (uint32_t)(s * C::STAGE);
-                const uint32_t bar = tc::smem_u32(&cs.full[s]);
-                tc::mbar_arrive_expect_tx(bar, C::STAGE);
-                tc::tma_load_3d(st, &xmap, 0, tok_base + tile * NT, c * (CHUNK / 64), bar);
-                tc::tma_load_2d(st + C::XBYTES, &wmap, c * (CHUNK / 2), blk * ROWS, bar);
-                issued = i + 1;
-            }
-            if (*abort_flag) {
-                // let every issued copy land before the CTA can exit
-                for (int i = max(0, issued - stages); i < issued; ++i)
-                    tc::mbar_wait(tc::smem_u32(&cs.full[i % stages]), (i / stages) & 1, nullptr, 0);
-            }
-        }
-    } else if (warp >= MMA_WARP0) {
-        if (lane == 0) {
-            // ---------------- MMA issuer j: k steps [8j, 8j+8) of every chunk ----------------
-            const int j = warp - MMA_WARP0;
-            const uint32_t idesc = tc::idesc_f16_f32(ROWS, NT);
-            const uint32_t dcol = tmem + C::D_COL + j * C::DCOLS;
-            int done = 0, seg = 0;
-            for (int i = 0; i < n && !*abort_flag; ++i) {
-                const int u = u0 + i, c = u % nc;
-                const bool first = i == 0 || c == 0;             // first chunk of a segment
-                if (first && seg > 0) {
-                    // the epilogue of the previous segment has read the accumulator
-                    if (!tc::mbar_wait(tc::smem_u32(&cs.d_free), (seg - 1) & 1, ep.err, ERR_DONE)) {
-                        *abort_flag = 1;
-                        break;
-                    }
-                }
-                const int s = i % stages, as = i % C::A_STAGES;
-                if (!tc::mbar_wait(tc::smem_u32(&cs.full[s]), (i / stages) & 1, ep.err, ERR_FULL) ||
-                    !tc::mbar_wait(tc::smem_u32(&cs.a_full[as]), (i / C::A_STAGES) & 1, ep.err, ERR_AFULL)) {
-                    *abort_flag = 1;
+                const int blk = b % nblk;
+                const int s = i % sw;
+                if (i >= sw && !wait_or_abort(tc::smem_u32(&cs.w_free[s]), ((i - sw) / sw) & 1, abort_flag, ep.err,
+                                              ERR_WFREE))
                     break;
-                }
-                tc::fence_after_sync();
-                const uint32_t xs = ring_a + (uint32_t)(s * C::STAGE);
+                const uint32_t st = tc::smem_u32(wring + (size_t)s * WSTAGE);
+                const uint32_t bar = tc::smem_u32(&cs.full_w[s]);
+                tc::mbar_arrive_expect_tx(bar, WSTAGE);
+                tc::tma_load_2d(st, &wmap, c * (KU / 2), blk * ROWS, bar);
+                tc::tma_load_2d(st + WBOX, &wmap, c * (KU / 2) + KS / 2, blk * ROWS, bar);
+                bulk_load(st + 2 * WBOX, sbp + (size_t)(blk * nc + c) * (8 * ROWS), SB_BYTES, bar);
+                issued = i + 1;
+                if (++c == nc) { c = 0; ++b; }
+            }
+            if (*abort_flag)   // let every issued copy land before the CTA can exit
+                for (int i = max(0, issued - sw); i < issued; ++i)
+                    tc::mbar_wait(tc::smem_u32(&cs.full_w[i % sw]), (i / sw) & 1, nullptr, 0);
+        }
+    } else if (warp == XP_WARP) {
+        if (lane == 0) {
+            // ---------------- x producer: one stage per sub-chunk ----------------
+            griddep_wait();   // the token operand is the previous kernel's output
+            int issued = 0;
+            int b = u0 / nc, c = u0 - b * nc;
+            for (int j = 0; j < nsub && !*abort_flag; ++j) {
+                const int h = j & 1, tile = b / nblk;
+                const int xs = j % R;
+                if (j >= R && !wait_or_abort(tc::smem_u32(&cs.mma_done[xs]), ((j - R) / R) & 1, abort_flag,
+                                             ep.err, ERR_XFREE))
+                    break;
+                const uint32_t bar = tc::smem_u32(&cs.full_x[xs]);
+                tc::mbar_arrive_expect_tx(bar, C::XSTAGE);
+                tc::tma_load_3d(tc::smem_u32(xring + (size_t)xs * C::XSTAGE), &xmap, 0, tok_base + tile * NT,
+                                c * (KU / 64) + h * (KS / 64), bar);
+                issued = j + 1;
+                if (h == 1 && ++c == nc) { c = 0; ++b; }
+            }
+            if (*abort_flag)
+                for (int j = max(0, issued - R); j < issued; ++j)
+                    tc::mbar_wait(tc::smem_u32(&cs.full_x[j % R]), (j / R) & 1, nullptr, 0);
+        }
+    } else if (warp >= ISS_WARP0) {
+        const int is = warp - ISS_WARP0;
+        {
+            // ---------------- MMA issuer `is`: groups [is*GPI, (is+1)*GPI) ----------------
+            constexpr uint32_t idesc = tc::idesc_f16_f32(ROWS, NT);
+            const uint32_t dcol = tmem + C::D_COL + is * C::DCOLS;
+            const uint64_t bdesc0 = tc::sdesc_k_sw128(tc::smem_u32(xring));   // slot r: + r * XSTAGE
+            int c = u0 % nc, seg = 0, last = -1;
+            for (int j = 0; j < nsub; ++j) {
+                const int h = j & 1, as = j % R;
+                const bool first = h == 0 && (j == 0 || c == 0);   // first sub-chunk of a block segment
+                const bool seg_end = h == 1 && (c == nc - 1 || j == nsub - 1);
+                if (first && seg > 0 && lane == 0)
+                    wait_or_abort(tc::smem_u32(&cs.d_free), (seg - 1) & 1, abort_flag, ep.err, ERR_DFREE);
+                __syncwarp();
+                named_bar_sync(1 + is * MAX_AST + as, BAR_COUNT);
+                if (lane == 0) {
+                    if (wait_or_abort(tc::smem_u32(&cs.full_x[as]), (j / R) & 1, abort_flag, ep.err, ERR_XFULL)) {
+                        tc::fence_after_sync();
+                        const uint64_t bdesc = bdesc0 + (uint64_t)(as * (C::XSTAGE >> 4));
 #pragma unroll
-                for (int kk = 8 * j; kk < 8 * j + 8; ++kk) {
-                    const uint32_t baddr = xs + (uint32_t)((kk >> 2) * NT * 128 + (kk & 3) * 32);
-                    tc::mma_ts_f16(dcol, tmem + as * A_COLS + kk * 8, tc::sdesc_k_sw128(baddr), idesc,
-                                   (!first || kk > 8 * j) ? 1u : 0u);
+                        for (int gg = 0; gg < GPI; ++gg) {
+                            const int grp = is * GPI + gg;
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const int kk = grp * 4 + q;             // k step of 16 inside the sub-chunk
+                                const uint32_t boff = (uint32_t)(grp * NT * 128 + q * 32);
+                                tc::mma_ts_f16(dcol, tmem + as * A_COLS + kk * 8, bdesc + (boff >> 4), idesc,
+                                               (first && gg == 0 && q == 0) ? 0u : 1u);
+                            }
+                        }
+                        tc::mma_commit(tc::smem_u32(&cs.mma_done[as]));   // frees A buffer and x stage
+                        last = j;
+                    }
                 }
-                tc::mma_commit(tc::smem_u32(&cs.mma_done[s]));
-                done = i + 1;
-                if (c == nc - 1 || i == n - 1) ++seg;
+                __syncwarp();
+                if (seg_end) ++seg;
+                if (h == 1 && ++c == nc) c = 0;
             }
-            if (*abort_flag && done > 0) {
-                const int pc = done - 1;   // committed MMAs must finish before TMEM is freed
-                tc::mbar_wait(tc::smem_u32(&cs.mma_done[pc % stages]), (pc / stages) & 1, nullptr, 0);
-            }
+            if (lane == 0 && last >= 0)   // committed MMAs must finish before TMEM is freed
+                tc::mbar_wait(tc::smem_u32(&cs.mma_done[last % R]), (last / R) & 1, nullptr, 0);
         }
     } else {
-        // ------- dequant warps: rows 32*quarter.., quantisation group g of each chunk -------
+        // ------- dequant warps: rows 32*quarter.., group g of each sub-chunk -------
         const int quarter = warp & 3, g = warp >> 2;
         const int r = quarter * 32 + lane;       // row within the block, 0..127
+        const int is = g / GPI;                  // issuer of this group
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        const int KG = K / MLXCAT_GS;
-        constexpr int GPC = CHUNK / MLXCAT_GS;   // groups per chunk
-        // scale / bias of unit u for this thread's row and group; groups past K
-        // (a half last chunk) read zero weights from TMA and use s = b = 0
-        auto sb_of = [&](int u, __half &sv, __half &bv) {
-            const int b = u / nc, c = u - b * nc, blk = b % nblk;
-            const int grp = GPC * c + g;
-            if (grp < KG) {
-                const size_t o = (size_t)(blk * ROWS + r) * KG + grp;
-                sv = scales[o];
-                bv = biases[o];
-            } else {
-                sv = bv = __float2half(0.f);
-            }
-        };
-        __half sc_pf[PF], bi_pf[PF];
-#pragma unroll
-        for (int p = 0; p < PF; ++p)
-            if (p < n) sb_of(u0 + p, sc_pf[p], bi_pf[p]);
-        const int sw = r & 7;                    // 128B swizzle of this row
+        const int sw8 = r & 7;                   // 128B swizzle of this row
         const int tg = g;                        // token group of this warp in the epilogue
-        for (int i = 0; i < n; ++i) {
-            const int u = u0 + i, b = u / nc, c = u - b * nc;
-            const int s = i % stages, as = i % C::A_STAGES;
-            const __half2 s1 = __half2half2(sc_pf[0]);
-            const __half2 b2 = __half2half2(bi_pf[0]);
-#pragma unroll
-            for (int p = 0; p + 1 < PF; ++p) { sc_pf[p] = sc_pf[p + 1]; bi_pf[p] = bi_pf[p + 1]; }
-            if (i + PF < n) sb_of(u + PF, sc_pf[PF - 1], bi_pf[PF - 1]);
-            // after an abort every wait is skipped, but the warp still walks the
-            // chunk sequence so that all dequant warps meet the same named barriers
-            bool ok = !*abort_flag && tc::mbar_wait(tc::smem_u32(&cs.full[s]), (i / stages) & 1, ep.err, ERR_FULL);
-            if (!ok) *abort_flag = 1;
-            const unsigned char *wt = ring + (size_t)s * C::STAGE + C::XBYTES + r * 128;
-            const uint4 w0 = *reinterpret_cast<const uint4 *>(wt + (((2 * g) ^ sw) << 4));
-            const uint4 w1 = *reinterpret_cast<const uint4 *>(wt + (((2 * g + 1) ^ sw) << 4));
-            const __half2 m1 = __hmul2(s1, __float2half2_rn(-1024.0f));
-            const __half2 s16 = __hmul2(s1, __float2half2_rn(0.0625f));
-            const __half2 m64 = __hmul2(s1, __float2half2_rn(-64.0f));
-            uint32_t a[32];
-            dequant_word(w0.x, s1, m1, s16, m64, b2, &a[0]);
-            dequant_word(w0.y, s1, m1, s16, m64, b2, &a[4]);
-            dequant_word(w0.z, s1, m1, s16, m64, b2, &a[8]);
-            dequant_word(w0.w, s1, m1, s16, m64, b2, &a[12]);
-            dequant_word(w1.x, s1, m1, s16, m64, b2, &a[16]);
-            dequant_word(w1.y, s1, m1, s16, m64, b2, &a[20]);
-            dequant_word(w1.z, s1, m1, s16, m64, b2, &a[24]);
-            dequant_word(w1.w, s1, m1, s16, m64, b2, &a[28]);
-            if (ok && i >= C::A_STAGES) {
-                const int pc = i - C::A_STAGES;   // last chunk that used this A stage
-                ok = tc::mbar_wait(tc::smem_u32(&cs.mma_done[pc % stages]), (pc / stages) & 1, ep.err, ERR_MMA);
-                if (!ok) *abort_flag = 1;
+        int b = u0 / nc, c = u0 - b * nc;
+        for (int j = 0; j < nsub; ++j) {
+            const int i = j >> 1, h = j & 1, as = j % R;
+            const int s = i % sw;
+            bool ok = true;
+            if (h == 0) {
+                if (lane == 0)
+                    ok = wait_or_abort(tc::smem_u32(&cs.full_w[s]), (i / sw) & 1, abort_flag, ep.err, ERR_WFULL);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
             }
-            if (!__any_sync(0xffffffffu, !ok || *abort_flag)) {
-                const uint32_t ta = tmem + lane_base + (uint32_t)(as * A_COLS + g * 32);
-                tc::tmem_st16(ta + 0, &a[0]);
-                tc::tmem_st16(ta + 16, &a[16]);
-                tc::tmem_wait_st();
-                tc::fence_before_sync();
+            uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
+            uint32_t sbv = 0;
+            if (!*abort_flag) {
+                const unsigned char *wt = wring + (size_t)s * WSTAGE + h * WBOX + r * 128;
+                w0 = *reinterpret_cast<const uint4 *>(wt + (((2 * g) ^ sw8) << 4));
+                w1 = *reinterpret_cast<const uint4 *>(wt + (((2 * g + 1) ^ sw8) << 4));
+                sbv = reinterpret_cast<const uint32_t *>(wring + (size_t)s * WSTAGE + 2 * WBOX)[(h * 4 + g) * ROWS + r];
+            }
+            if (h == 1) {
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.a_full[as]));
-            } else {
-                *abort_flag = 1;
+                if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.w_free[s]));   // both boxes of the stage read
             }
+            if (j >= R) {
+                const int pj = j - R;   // last sub-chunk that used this A buffer
+                if (lane == 0)
+                    ok = ok && wait_or_abort(tc::smem_u32(&cs.mma_done[as]), (pj / R) & 1, abort_flag, ep.err,
+                                             ERR_MDONE);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                tc::fence_after_sync();
+            }
+            if (ok && !*abort_flag) {
+                const uint32_t ta = tmem + lane_base + (uint32_t)(as * A_COLS + g * 32);
+                uint32_t a[16];
+                dequant16(w0, sbv, a);
+                tc::tmem_st16(ta + 0, a);
+                dequant16(w1, sbv, a);
+                tc::tmem_st16(ta + 16, a);
+                tc::tmem_wait_st();
+            }
+            tc::fence_before_sync();
+            named_bar_arrive(1 + is * MAX_AST + as, BAR_COUNT);
 
-            if (c != nc - 1 && i != n - 1) continue;
-            // ---------------- epilogue of the segment ending with this chunk ----------------
-            const int seg_first_unit = max(u0, b * nc);
-            const bool full = seg_first_unit == b * nc && c == nc - 1;
-            const int tile = b / nblk, blk = b - tile * nblk;
+            const int ub = b, uc = c;            // block / unit of this sub-chunk
+            if (h == 1 && ++c == nc) { c = 0; ++b; }
+            if (h != 1 || (uc != nc - 1 && j != nsub - 1)) continue;
+
+            // ---------------- epilogue of the block segment ending here ----------------
+            const int seg_first_unit = max(u0, ub * nc);
+            const bool full = seg_first_unit == ub * nc && uc == nc - 1;
+            const int tile = ub / nblk, blk = ub - tile * nblk;
             const int f = blk * ROWS + r;
             bool bad = *abort_flag != 0;
-            if (!bad) bad = !tc::mbar_wait(tc::smem_u32(&cs.mma_done[s]), (i / stages) & 1, ep.err, ERR_DONE);
-            if (named_bar_or(1, DQ_THREADS, bad)) { *abort_flag = 1; break; }
+            if (lane == 0 && !bad)
+                bad = !wait_or_abort(tc::smem_u32(&cs.mma_done[j % R]), (j / R) & 1, abort_flag, ep.err, ERR_XFREE);
+            bad = __shfl_sync(0xffffffffu, bad, 0);
+            if (named_bar_or(EPI_BAR, DQ_THREADS, bad)) { *abort_flag = 1; continue; }
             tc::fence_after_sync();
             float acc[PIECES][16];
 #pragma unroll
             for (int p = 0; p < PIECES; ++p) {
                 const int cc = p * 64 + tg * 16;
+#pragma unroll
+                for (int q = 0; q < 16; ++q) acc[p][q] = 0.f;
                 if (cc < NT) {   // warp-uniform
-                    uint32_t v0[16], v1[16];
-                    tc::tmem_ld16(tmem + lane_base + C::D_COL + cc, v0);
-                    tc::tmem_ld16(tmem + lane_base + C::D_COL + C::DCOLS + cc, v1);
-                    tc::tmem_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) acc[p][q] = __uint_as_float(v0[q]) + __uint_as_float(v1[q]);
-                } else {
+                    for (int d = 0; d < NI; ++d) {
+                        uint32_t v[16];
+                        tc::tmem_ld16(tmem + lane_base + C::D_COL + d * C::DCOLS + cc, v);
+                        tc::tmem_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) acc[p][q] = 0.f;
+                        for (int q = 0; q < 16; ++q) acc[p][q] += __uint_as_float(v[q]);
+                    }
                 }
             }
             tc::fence_before_sync();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.d_free));   // accumulator may be reused
+            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.d_free));   // accumulators may be reused
 
             if (!full) {
-                // partial block: slot of this CTA among the block's contributors
-                const int first_owner = unit_owner(b * nc, U, G);
-                const int ncontrib = unit_owner(b * nc + nc - 1, U, G) - first_owner + 1;
-                float *pblk = ep.part + ((size_t)b * pmax) * ROWS * NT;
-                float *mine = pblk + ((size_t)(cta - first_owner) * ROWS + r) * NT;
+                // partial block: slot of this CTA among the block's contributors.
+                // Partials are stored [slot][token][row] so that a warp (32
+                // consecutive rows) reads and writes 128 contiguous bytes.
+                const int first_owner = unit_owner(ub * nc, U, G);
+                const int ncontrib = unit_owner(ub * nc + nc - 1, U, G) - first_owner + 1;
+                float *pblk = ep.part + (size_t)ub * pmax * NT * ROWS;
+                float *mine = pblk + (size_t)(cta - first_owner) * NT * ROWS + r;
 #pragma unroll
                 for (int p = 0; p < PIECES; ++p) {
                     const int cc = p * 64 + tg * 16;
                     if (cc < NT) {
 #pragma unroll
-                        for (int q = 0; q < 16; q += 4)
-                            *reinterpret_cast<float4 *>(mine + cc + q) =
-                                make_float4(acc[p][q], acc[p][q + 1], acc[p][q + 2], acc[p][q + 3]);
+                        for (int q = 0; q < 16; ++q) mine[(size_t)(cc + q) * ROWS] = acc[p][q];
                     }
                 }
-                __threadfence();
-                named_bar_sync(1, DQ_THREADS);
+                // the CTA barrier orders every thread's partial stores before thread
+                // 0's gpu-scope fence (fences are cumulative), which orders them
+                // before the ticket; the last contributor fences again before the
+                // barrier that releases its readers
+                named_bar_sync(EPI_BAR, DQ_THREADS);
                 if (tid == 0) {
-                    unsigned *ctr = ep.counters + b;
+                    unsigned *ctr = ep.counters + ub;
+                    __threadfence();
                     const unsigned prev = atomicAdd(ctr, 1u);
-                    cs.last_flag = prev == (unsigned)(ncontrib - 1);
-                    if (cs.last_flag) *ctr = 0u;   // ready for the next launch
+                    const int last = prev == (unsigned)(ncontrib - 1);
+                    if (last) {
+                        *ctr = 0u;   // ready for the next launch
+                        __threadfence();
+                    }
+                    cs.last_flag = last;
                 }
-                named_bar_sync(1, DQ_THREADS);
+                named_bar_sync(EPI_BAR, DQ_THREADS);
                 if (!cs.last_flag) continue;
-                __threadfence();
 #pragma unroll
                 for (int p = 0; p < PIECES; ++p) {
                     const int cc = p * 64 + tg * 16;
 #pragma unroll
                     for (int q = 0; q < 16; ++q) acc[p][q] = 0.f;
                     if (cc < NT) {
-                        for (int sl = 0; sl < ncontrib; ++sl) {
-                            const float *pp = pblk + ((size_t)sl * ROWS + r) * NT + cc;
+                        // slots are summed in slot order; the loads of a batch of slots
+                        // are issued together so their L2 latencies overlap
+                        const float *pp = pblk + (size_t)cc * ROWS + r;
+                        const size_t slot_stride = (size_t)NT * ROWS;
+                        constexpr int BATCH = PIECES == 1 ? 2 : 1;
+                        for (int sl = 0; sl < ncontrib; sl += BATCH) {
+                            float t[BATCH][16];
 #pragma unroll
-                            for (int q = 0; q < 16; q += 4) {
-                                const float4 t4 = __ldcg(reinterpret_cast<const float4 *>(pp + q));
-                                acc[p][q] += t4.x; acc[p][q + 1] += t4.y; acc[p][q + 2] += t4.z; acc[p][q + 3] += t4.w;
+                            for (int k = 0; k < BATCH; ++k)
+#pragma unroll
+                                for (int q = 0; q < 16; ++q)
+                                    t[k][q] = sl + k < ncontrib ? __ldcg(pp + (sl + k) * slot_stride + (size_t)q * ROWS) : 0.f;
+#pragma unroll
+                            for (int k = 0; k < BATCH; ++k) {
+                                if (sl + k >= ncontrib) break;
+#pragma unroll
+                                for (int q = 0; q < 16; ++q) acc[p][q] += t[k][q];
                             }
                         }
                     }
                 }
             }
-            float *xch = cs.xch[tg];
 #pragma unroll
             for (int p = 0; p < PIECES; ++p) {
                 const int cc = p * 64 + tg * 16;
@@ -410,23 +496,29 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                     for (int q = 0; q < 16; ++q)
                         if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] += y[q];
                 } else if (ep.op == Q4Epilogue::SWIGLU) {
-                    // rows [0,64) gate, [64,128) up of the same 64 outputs
-                    if (r >= 64) {
+                    // rows [0,64) gate, [64,128) up of the same 64 outputs; token
+                    // groups exchange through the buffer in two rounds of two
 #pragma unroll
-                        for (int q = 0; q < 16; ++q) xch[(r - 64) * 16 + q] = y[q];
-                    }
-                    named_bar_sync(1, DQ_THREADS);
-                    if (r < 64) {
-                        const int oi = blk * 64 + r;
+                    for (int ph = 0; ph < 2; ++ph) {
+                        float *xch = cs.xch[tg & 1];
+                        const bool mine = (tg >> 1) == ph;
+                        if (mine && r >= 64) {
 #pragma unroll
-                        for (int q = 0; q < 16; ++q) {
-                            if (q >= mlim) break;
-                            const float gv = y[q], uv = xch[r * 16 + q];
-                            const float av = gv / (1.0f + expf(-gv)) * uv;
-                            ep.xout[xblk(m0 + q, oi, ep.ldx_rows)] = __float2half_rn(av);
+                            for (int q = 0; q < 16; ++q) xch[(r - 64) * 16 + q] = y[q];
                         }
+                        named_bar_sync(EPI_BAR, DQ_THREADS);
+                        if (mine && r < 64) {
+                            const int oi = blk * 64 + r;
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) {
+                                if (q >= mlim) break;
+                                const float gv = y[q], uv = xch[r * 16 + q];
+                                const float av = gv / (1.0f + expf(-gv)) * uv;
+                                ep.xout[xblk(m0 + q, oi, ep.ldx_rows)] = __float2half_rn(av);
+                            }
+                        }
+                        named_bar_sync(EPI_BAR, DQ_THREADS);
                     }
-                    named_bar_sync(1, DQ_THREADS);
                 } else {   // QKV
                     const int D = ep.head_dim;
                     const int hh = f / D;      // head index in q|k|v order
@@ -441,7 +533,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                             if (lane == q) cs.wsum[tg][quarter][q] = t2;
                         }
                     }
-                    named_bar_sync(1, DQ_THREADS);
+                    named_bar_sync(EPI_BAR, DQ_THREADS);
                     if (nw) {
                         const int wpk = D / 32, w0 = (quarter / wpk) * wpk;
 #pragma unroll
@@ -451,23 +543,32 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                             y[q] = y[q] * (1.0f / sqrtf(ss / (float)D + ep.eps)) * nw[d];
                         }
                     }
-                    // rotate-half RoPE on q and k: partner row r +- D/2
+                    // rotate-half RoPE on q and k: partner row r +- D/2, exchanged
+                    // through the buffer in two rounds of two token groups
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) xch[r * 16 + q] = y[q];
-                    named_bar_sync(1, DQ_THREADS);
-                    if (is_q || is_k) {
-                        const int half = D / 2;
-                        const int pr = d < half ? r + half : r - half;
-                        const float fr = ep.inv_freq[d % half];
+                    for (int ph = 0; ph < 2; ++ph) {
+                        float *xch = cs.xch[tg & 1];
+                        const bool mine = (tg >> 1) == ph;
+                        if (mine) {
 #pragma unroll
-                        for (int q = 0; q < 16; ++q) {
-                            if (q >= mlim) break;
-                            const float ang = __fmul_rn((float)ep.tpos[m0 + q], fr);
-                            float sn, cn;
-                            sincosf(ang, &sn, &cn);
-                            const float pv = xch[pr * 16 + q];
-                            y[q] = d < half ? y[q] * cn - pv * sn : pv * sn + y[q] * cn;
+                            for (int q = 0; q < 16; ++q) xch[r * 16 + q] = y[q];
                         }
+                        named_bar_sync(EPI_BAR, DQ_THREADS);
+                        if (mine && (is_q || is_k)) {
+                            const int half = D / 2;
+                            const int pr = d < half ? r + half : r - half;
+                            const float fr = ep.inv_freq[d % half];
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) {
+                                if (q >= mlim) break;
+                                const float ang = __fmul_rn((float)ep.tpos[m0 + q], fr);
+                                float sn, cn;
+                                sincosf(ang, &sn, &cn);
+                                const float pv = xch[pr * 16 + q];
+                                y[q] = d < half ? y[q] * cn - pv * sn : pv * sn + y[q] * cn;
+                            }
+                        }
+                        named_bar_sync(EPI_BAR, DQ_THREADS);
                     }
 #pragma unroll
                     for (int q = 0; q < 16; ++q) {
@@ -483,7 +584,6 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                         }
                         dst[d] = __float2half_rn(y[q]);
                     }
-                    named_bar_sync(1, DQ_THREADS);
                 }
             }
         }
@@ -493,6 +593,26 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
     if (warp == 0) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, 512);
+    }
+}
+
+// (scale, bias) fp16 pairs of rows blk*128.. and groups 8c.. of unit (blk, c):
+// sbp[((blk * nc + c) * 8 + gi) * 128 + r]; groups past K are zero
+__global__ void pack_sb_kernel(const __half *__restrict__ scales, const __half *__restrict__ biases, int N, int K,
+                               uint32_t *__restrict__ sbp) {
+    const int KG = K / MLXCAT_GS, nc = (K + KU - 1) / KU;
+    const long long total = (long long)N * nc * 8;
+    for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(t % ROWS);
+        const long long rest = t / ROWS;
+        const int gi = (int)(rest % 8);
+        const long long bc = rest / 8;
+        const int c = (int)(bc % nc), blk = (int)(bc / nc);
+        const int row = blk * ROWS + r, grp = c * 8 + gi;
+        __half2 v = __halves2half2(__float2half(0.f), __float2half(0.f));
+        if (grp < KG) v = __halves2half2(scales[(size_t)row * KG + grp], biases[(size_t)row * KG + grp]);
+        sbp[t] = *reinterpret_cast<uint32_t *>(&v);
     }
 }
 
@@ -511,15 +631,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-template <int NT>
-int stages_for() {
-    int s = (int)((227 * 1024 - 1024 - sizeof(Smem)) / Cfg<NT>::STAGE);
-    return s < 2 ? 2 : (s > MAX_STAGES ? MAX_STAGES : s);
-}
+constexpr size_t SMEM_LIMIT = 227 * 1024;
 
 template <int NT>
-size_t smem_for(int stages) {
-    return 1024 + (size_t)stages * Cfg<NT>::STAGE + sizeof(Smem);
+size_t smem_for(int sw) {
+    return 1024 + (size_t)sw * WSTAGE + (size_t)Cfg<NT>::AST * Cfg<NT>::XSTAGE + sizeof(Smem);
+}
+
+// deepest W ring that fits the shared memory of one CTA
+template <int NT>
+int stages_for() {
+    for (int sw = MAX_SW; sw > 2; --sw)
+        if (smem_for<NT>(sw) <= SMEM_LIMIT) return sw;
+    return 2;
 }
 
 template <int NT>
@@ -528,21 +652,32 @@ cudaError_t launch_nt(const Q4WeightTC &w, const CUtensorMap &xmap, int M, int t
     static bool attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    const int stages = stages_for<NT>();
-    const size_t sm = smem_for<NT>(stages);
+    const int sw = stages_for<NT>();
+    const size_t sm = smem_for<NT>(sw);
+    if (sm > SMEM_LIMIT) return cudaErrorInvalidConfiguration;
     if (!attr[dev & 63]) {
         cudaError_t e = cudaFuncSetAttribute(q4_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
         if (e != cudaSuccess) return e;
         attr[dev & 63] = true;
     }
-    const int nblk = w.N / ROWS, nc = (w.K + CHUNK - 1) / CHUNK;
+    const int nblk = w.N / ROWS, nc = (w.K + KU - 1) / KU;
     const int U = tiles * nblk * nc;
     const int G = U < sm_count ? U : sm_count;
     const int pmax = q4_tc_pmax(U, G, nc);
     if (pmax > 1 && (!ep.part || !ep.counters)) return cudaErrorInvalidValue;
-    q4_tc_kernel<NT><<<G, THREADS, sm, st>>>(w.map, xmap, w.scales, w.biases, w.N, w.K, M, tok_base, nblk, nc,
-                                             U, pmax, stages, ep);
-    return cudaGetLastError();
+    if ((unsigned long long)U * (unsigned long long)(G + 1) >= (1ull << 32)) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = sm;
+    cfg.stream = st;
+    cudaLaunchAttribute attr1[1];
+    attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr1[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr1;
+    cfg.numAttrs = ep.pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, q4_tc_kernel<NT>, w.map, xmap, w.sbp, w.N, w.K, M, tok_base, nblk, nc, U, pmax,
+                              sw, ep);
 }
 
 }  // namespace
@@ -550,13 +685,25 @@ cudaError_t launch_nt(const Q4WeightTC &w, const CUtensorMap &xmap, int M, int t
 bool make_weight_map(Q4WeightTC &w) {
     auto fn = encode_fn();
     if (!fn) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)(w.K / 2), (cuuint64_t)w.N};
+    const cuuint64_t dims[2] = {(cuuint64_t)(w.K / 2), (cuuint64_t)w.N};   // boxes past K read 0
     const cuuint64_t strides[1] = {(cuuint64_t)(w.K / 2)};
     const cuuint32_t box[2] = {128, ROWS};
     const cuuint32_t es[2] = {1, 1};
     return fn(&w.map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint32_t *>(w.wq), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t q4_sbp_words(int N, int K) { return (size_t)N * ((K + KU - 1) / KU) * 8; }
+
+cudaError_t pack_q4_sb(const __half *scales, const __half *biases, int N, int K, uint32_t *sbp, cudaStream_t st) {
+    if (N % ROWS || K % MLXCAT_GS || !scales || !biases || !sbp) return cudaErrorInvalidValue;
+    const long long total = (long long)q4_sbp_words(N, K);
+    const int threads = 256;
+    const long long want = (total + threads - 1) / threads;
+    const unsigned blocks = (unsigned)(want < 4096 ? want : 4096);
+    pack_sb_kernel<<<blocks, threads, 0, st>>>(scales, biases, N, K, sbp);
+    return cudaGetLastError();
 }
 
 int q4_tc_tile(int M) {
@@ -575,7 +722,7 @@ int q4_tc_pmax(int U, int G, int nc) {
 size_t q4_tc_partial_floats(int N, int K, int M, int sm_count) {
     const int nt = q4_tc_tile(M);
     const int tiles = (M + nt - 1) / nt;
-    const int nblk = N / ROWS, nc = (K + CHUNK - 1) / CHUNK;
+    const int nblk = N / ROWS, nc = (K + KU - 1) / KU;
     const int U = tiles * nblk * nc, G = U < sm_count ? U : sm_count;
     return (size_t)tiles * nblk * q4_tc_pmax(U, G, nc) * ROWS * nt;
 }
@@ -587,7 +734,7 @@ size_t q4_tc_counters(int N, int M) {
 
 cudaError_t q4_tc(const Q4WeightTC &w, const __half *x_blk, int ldx_rows, int tok_base, int M,
                   int sm_count, const Q4Epilogue &ep, cudaStream_t st) {
-    if (w.N % ROWS || w.K % 128 || M <= 0 || tok_base + M > ldx_rows) return cudaErrorInvalidValue;
+    if (w.N % ROWS || w.K % 128 || M <= 0 || tok_base + M > ldx_rows || !w.sbp) return cudaErrorInvalidValue;
     auto fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
     const int nt = q4_tc_tile(M);
@@ -596,7 +743,7 @@ cudaError_t q4_tc(const Q4WeightTC &w, const __half *x_blk, int ldx_rows, int to
     CUtensorMap xmap;
     const cuuint64_t dims[3] = {64, (cuuint64_t)ldx_rows, (cuuint64_t)(w.K / 64)};   // boxes past K read 0
     const cuuint64_t strides[2] = {128, (cuuint64_t)ldx_rows * 128};
-    const cuuint32_t box[3] = {64, (cuuint32_t)nt, CHUNK / 64};
+    const cuuint32_t box[3] = {64, (cuuint32_t)nt, KS / 64};
     const cuuint32_t es[3] = {1, 1, 1};
     if (fn(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half *>(x_blk), dims, strides, box, es,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -35,6 +35,7 @@ thread_local std::string g_op_err;
 struct DevLin {
     uint32_t *wq = nullptr;
     __half *s = nullptr, *b = nullptr;
+    uint32_t *sbp = nullptr;   // (scale, bias) pairs in the tensor-core kernel's order
     int N = 0, K = 0;
     Q4WeightTC tcw;       // TMA map over the packed words (built once the buffer exists)
     const Q4WeightTC &tc() const { return tcw; }
@@ -44,7 +45,7 @@ struct DevLin {
         return w;
     }
     bool build_map() {
-        tcw.wq = wq; tcw.scales = s; tcw.biases = b; tcw.N = N; tcw.K = K;
+        tcw.wq = wq; tcw.scales = s; tcw.biases = b; tcw.sbp = sbp; tcw.N = N; tcw.K = K;
         return make_weight_map(tcw);
     }
     size_t bytes() const { return (size_t)N * K / 2 + (size_t)N * (K / 64) * 4; }
@@ -270,6 +271,7 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
     ep.part = c->part;
     ep.counters = c->counters;
     ep.err = c->err;
+    ep.pdl = 1;   // each linear streams its weights while its predecessor finishes
     for (int l = 0; l < L; ++l) {
         const KVLayer kv = c->layer(l);
         {   // q|k|v projection + q/k norm + RoPE + KV append
@@ -460,7 +462,8 @@ int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx
         w.N = N; w.K = K;
         if (dalloc(ctx->allocs, &w.wq, (size_t)N * K / 8) != cudaSuccess ||
             dalloc(ctx->allocs, &w.s, (size_t)N * K / 64) != cudaSuccess ||
-            dalloc(ctx->allocs, &w.b, (size_t)N * K / 64) != cudaSuccess)
+            dalloc(ctx->allocs, &w.b, (size_t)N * K / 64) != cudaSuccess ||
+            dalloc(ctx->allocs, &w.sbp, q4_sbp_words(N, K)) != cudaSuccess)
             rc = set_err(ctx, MLXCAT_E_OOM, "weight allocation failed (%d x %d)", N, K);
         else if (!w.build_map())
             rc = set_err(ctx, MLXCAT_E_CUDA, "TMA descriptor for a %d x %d weight failed", N, K);
@@ -588,6 +591,11 @@ int mlxcat_weights_synth(mlxcat_ctx *ctx, uint64_t seed, float stddev) {
         LK(ctx, synth_q4(seed, id, stddev, rm.rows, w->K, w->wq, w->s, w->b, rm.offset, ctx->stream,
                          rm.group, rm.stride));
     }
+    for (uint32_t id : ids) {   // fused matrices are packed once per distinct buffer (repeats are harmless)
+        RowMap rm;
+        DevLin *w = lin_for(ctx, id, &rm);
+        LK(ctx, pack_q4_sb(w->s, w->b, w->N, w->K, w->sbp, ctx->stream));
+    }
     CK(ctx, cudaStreamSynchronize(ctx->stream));
     ctx->have_weights = true;
     return MLXCAT_OK;
@@ -602,6 +610,8 @@ int mlxcat_weights_set_q4(mlxcat_ctx *ctx, uint32_t id, const uint32_t *wq, cons
     CK(ctx, cudaSetDevice(ctx->device));
     CK(ctx, copy_rows(w, rm, const_cast<uint32_t *>(wq), const_cast<uint16_t *>(scales),
                       const_cast<uint16_t *>(biases), true));
+    CK(ctx, pack_q4_sb(w->s, w->b, w->N, w->K, w->sbp, ctx->stream));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
     ctx->have_weights = true;
     return MLXCAT_OK;
 }
@@ -1058,12 +1068,14 @@ static int op_sm_count() {
     return sm;
 }
 
-// workspace: [x in perm8 order | split-K partials | split-K tickets | error flag]
-static void q4_ws_layout(int32_t N, int32_t K, int32_t M, size_t *off_part, size_t *off_ctr, size_t *off_err,
-                         size_t *total) {
+// workspace: [x in perm8 order | packed (scale, bias) | split-K partials |
+//             split-K tickets | error flag]
+static void q4_ws_layout(int32_t N, int32_t K, int32_t M, size_t *off_sbp, size_t *off_part, size_t *off_ctr,
+                         size_t *off_err, size_t *total) {
     const int sm = op_sm_count();
     auto up = [](size_t v) { return (v + 255) & ~(size_t)255; };
-    *off_part = up((size_t)M * K * 2);
+    *off_sbp = up((size_t)M * K * 2);
+    *off_part = *off_sbp + up(q4_sbp_words(N, K) * 4);
     *off_ctr = *off_part + up(q4_tc_partial_floats(N, K, M, sm) * 4);
     *off_err = *off_ctr + up(q4_tc_counters(N, M) * 4);
     *total = *off_err + 256;
@@ -1071,8 +1083,8 @@ static void q4_ws_layout(int32_t N, int32_t K, int32_t M, size_t *off_part, size
 
 size_t mlxcat_op_q4_linear_workspace(int32_t N, int32_t K, int32_t M) {
     if (N <= 0 || K <= 0 || M <= 0) return 0;
-    size_t a, b, c, t;
-    q4_ws_layout(N, K, M, &a, &b, &c, &t);
+    size_t a, b, c, d, t;
+    q4_ws_layout(N, K, M, &a, &b, &c, &d, &t);
     return t;
 }
 
@@ -1082,14 +1094,15 @@ int mlxcat_op_q4_linear(const uint32_t *wq, const uint16_t *scales, const uint16
     if (!wq || !scales || !biases || !x || !y || N <= 0 || K <= 0 || M <= 0)
         return op_err(MLXCAT_E_INVALID, "bad q4_linear arguments");
     if (N % 128 || K % 128) return op_err(MLXCAT_E_INVALID, "N and K must be multiples of 128");
-    size_t off_part, off_ctr, off_err, need;
-    q4_ws_layout(N, K, M, &off_part, &off_ctr, &off_err, &need);
+    size_t off_sbp, off_part, off_ctr, off_err, need;
+    q4_ws_layout(N, K, M, &off_sbp, &off_part, &off_ctr, &off_err, &need);
     if (!ws || ws_bytes < need) return op_err(MLXCAT_E_INVALID, "workspace of %zu bytes required", need);
     cudaStream_t st = (cudaStream_t)stream;
     char *w8 = static_cast<char *>(ws);
     Q4WeightTC w;
     w.wq = wq; w.scales = reinterpret_cast<const __half *>(scales);
     w.biases = reinterpret_cast<const __half *>(biases); w.N = N; w.K = K;
+    w.sbp = reinterpret_cast<const uint32_t *>(w8 + off_sbp);
     if (!make_weight_map(w)) return op_err(MLXCAT_E_CUDA, "TMA descriptor for the weights failed");
     Q4Epilogue ep;
     ep.op = Q4Epilogue::STORE; ep.out = y; ep.ldo = N;
@@ -1099,6 +1112,8 @@ int mlxcat_op_q4_linear(const uint32_t *wq, const uint16_t *scales, const uint16
     __half *xp = reinterpret_cast<__half *>(w8);
     cudaError_t e = cudaMemsetAsync(w8 + off_ctr, 0, need - off_ctr, st);
     if (e == cudaSuccess) e = permute_activations(reinterpret_cast<const __half *>(x), xp, M, K, st);
+    if (e == cudaSuccess)
+        e = pack_q4_sb(w.scales, w.biases, N, K, reinterpret_cast<uint32_t *>(w8 + off_sbp), st);
     if (e == cudaSuccess) e = q4_tc(w, xp, M, 0, M, op_sm_count(), ep, st);
     if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "q4_linear: %s", cudaGetErrorString(e));
     return MLXCAT_OK;
