@@ -200,28 +200,99 @@ __global__ void permute_kernel(const __half *__restrict__ x, __half *__restrict_
 }
 
 // max value, lowest index on ties (MLX argMax returns the first maximum)
+// Row argmax as a 64-bit key: (order-preserving float bits, ~index), so the
+// largest key is the largest logit and, among equal logits, the lowest index.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+    return ((unsigned long long)float_key(v) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
+}
+
+__device__ __forceinline__ unsigned long long block_max_u64(unsigned long long v, unsigned long long *sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xffffffffu, v, o);
+        v = t > v ? t : v;
+    }
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        v = lane < (int)(blockDim.x >> 5) ? sh[lane] : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long t = __shfl_xor_sync(0xffffffffu, v, o);
+            v = t > v ? t : v;
+        }
+    }
+    return v;   // valid in thread 0
+}
+
+// best key of logits[lo, hi) of one row (float4 loads when the row is 16-byte aligned)
+__device__ __forceinline__ unsigned long long range_best(const float *l, int lo, int hi, bool vec) {
+    unsigned long long best = 0;
+    if (vec) {
+        const int lo4 = (lo + 3) & ~3, hi4 = hi & ~3;
+        for (int i = lo + threadIdx.x; i < min(lo4, hi); i += blockDim.x) {
+            const unsigned long long k = argmax_key(l[i], i);
+            best = k > best ? k : best;
+        }
+        for (int i = lo4 + 4 * threadIdx.x; i < hi4; i += 4 * blockDim.x) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(l + i));
+            unsigned long long k = argmax_key(v.x, i);     best = k > best ? k : best;
+            k = argmax_key(v.y, i + 1); best = k > best ? k : best;
+            k = argmax_key(v.z, i + 2); best = k > best ? k : best;
+            k = argmax_key(v.w, i + 3); best = k > best ? k : best;
+        }
+        for (int i = max(hi4, lo4) + threadIdx.x; i < hi; i += blockDim.x) {
+            const unsigned long long k = argmax_key(l[i], i);
+            best = k > best ? k : best;
+        }
+    } else {
+        for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+            const unsigned long long k = argmax_key(l[i], i);
+            best = k > best ? k : best;
+        }
+    }
+    return best;
+}
+
+// one CTA per row
 __global__ void argmax_kernel(const float *__restrict__ logits, int V, int32_t *out) {
     __shared__ unsigned long long sh[32];
     const int m = blockIdx.x;
     const float *l = logits + (size_t)m * V;
-    unsigned long long best = 0;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const unsigned long long key =
-            ((unsigned long long)float_key(l[i]) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
-        best = key > best ? key : best;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
-        best = v > best ? v : best;
-    }
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    if (lane == 0) sh[w] = best;
-    __syncthreads();
+    const bool vec = (V & 3) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
+    const unsigned long long b = block_max_u64(range_best(l, 0, V, vec), sh);
+    if (threadIdx.x == 0) out[m] = (int32_t)(0xffffffffu - (uint32_t)(b & 0xffffffffull));
+}
+
+// S CTAs per row; the last CTA of a row (ticket) reduces the S partial keys
+// (max is order-independent, so the result does not depend on timing)
+__global__ void argmax_split_kernel(const float *__restrict__ logits, int V, int S,
+                                    unsigned long long *__restrict__ part, unsigned *__restrict__ ctr,
+                                    int32_t *out) {
+    __shared__ unsigned long long sh[32];
+    __shared__ int last;
+    const int s = blockIdx.x, m = blockIdx.y;
+    const float *l = logits + (size_t)m * V;
+    const bool vec = (V & 3) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
+    const int chunk = ((V + S - 1) / S + 3) & ~3;
+    const int lo = min(V, s * chunk), hi = min(V, lo + chunk);
+    const unsigned long long b = block_max_u64(range_best(l, lo, hi, vec), sh);
     if (threadIdx.x == 0) {
-        unsigned long long b = 0;
-        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) b = sh[i] > b ? sh[i] : b;
-        out[m] = (int32_t)(0xffffffffu - (uint32_t)(b & 0xffffffffull));
+        part[(size_t)m * S + s] = b;
+        __threadfence();
+        const unsigned prev = atomicAdd(ctr + m, 1u);
+        last = prev == (unsigned)(S - 1);
+        if (last) {
+            ctr[m] = 0u;   // ready for the next launch
+            __threadfence();
+            unsigned long long best = 0;
+            for (int i = 0; i < S; ++i) {
+                const unsigned long long k = __ldcg(part + (size_t)m * S + i);
+                best = k > best ? k : best;
+            }
+            out[m] = (int32_t)(0xffffffffu - (uint32_t)(best & 0xffffffffull));
+        }
     }
 }
 
@@ -283,8 +354,15 @@ cudaError_t reduce_splits(const float *part, int splits, size_t n, float *y, cud
     return cudaGetLastError();
 }
 
-cudaError_t argmax_rows(const float *logits, int M, int V, int32_t *out, cudaStream_t st) {
-    argmax_kernel<<<M, 1024, 0, st>>>(logits, V, out);
+size_t argmax_scratch_words(int M) { return (size_t)M * ARGMAX_SPLITS; }
+
+cudaError_t argmax_rows(const float *logits, int M, int V, int32_t *out, cudaStream_t st,
+                        unsigned long long *part, unsigned *ctr) {
+    if (part && ctr && V >= 4096 * ARGMAX_SPLITS / 8) {
+        argmax_split_kernel<<<dim3(ARGMAX_SPLITS, M), 256, 0, st>>>(logits, V, ARGMAX_SPLITS, part, ctr, out);
+    } else {
+        argmax_kernel<<<M, 1024, 0, st>>>(logits, V, out);
+    }
     return cudaGetLastError();
 }
 

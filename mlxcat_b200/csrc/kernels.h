@@ -118,7 +118,13 @@ cudaError_t attention(const __half *qbuf, KVLayer kv, const int32_t *trow, const
                       cudaStream_t st);
 
 // ---- lm head / sampling ----------------------------------------------------
-cudaError_t argmax_rows(const float *logits, int M, int V, int32_t *out, cudaStream_t st);
+// argmax of each row of logits [M][V]; with scratch (part: argmax_scratch_words(M)
+// u64, ctr: M u32 that start at zero and are left at zero) the rows are split
+// over ARGMAX_SPLITS CTAs each
+constexpr int ARGMAX_SPLITS = 16;
+size_t argmax_scratch_words(int M);
+cudaError_t argmax_rows(const float *logits, int M, int V, int32_t *out, cudaStream_t st,
+                        unsigned long long *part = nullptr, unsigned *ctr = nullptr);
 
 // ---- drafter ----------------------------------------------------------------
 struct RowState {

@@ -77,12 +77,10 @@ constexpr int KS = 256;                // k per sub-chunk (one x stage, one A bu
 constexpr int DQ_WARPS = 16;           // dequant / epilogue warps
 constexpr int DQ_THREADS = DQ_WARPS * 32;
 constexpr int ISS_WARP0 = DQ_WARPS;    // issuer warps 16..17
-constexpr int NI = 2;                  // MMA issuers
-constexpr int GPI = 4 / NI;            // 64-k groups per issuer
-constexpr int WP_WARP = DQ_WARPS + NI; // W producer
+constexpr int MAX_NI = 2;              // MMA issuer warps
+constexpr int WP_WARP = DQ_WARPS + MAX_NI; // W producer
 constexpr int XP_WARP = WP_WARP + 1;   // x producer
 constexpr int THREADS = (XP_WARP + 1) * 32;
-constexpr int BAR_COUNT = 32 + 128 * GPI;   // issuer warp + its dequant warps
 constexpr int A_COLS = KS / 2;         // TMEM columns of one A buffer (fp16 pairs)
 constexpr int WBOX = ROWS * 128;       // one [128 rows x 128 B] weight box
 constexpr int SB_BYTES = 8 * ROWS * 4; // packed (scale, bias) of one unit
@@ -94,6 +92,9 @@ enum ErrCode { ERR_WFULL = 1, ERR_XFULL = 2, ERR_MDONE = 3, ERR_XFREE = 4, ERR_W
 
 template <int NT>
 struct Cfg {
+    static constexpr int NI = 2;                             // MMA issuers
+    static constexpr int GPI = 4 / NI;                       // 64-k groups per issuer
+    static constexpr int BAR_COUNT = 32 + 128 * GPI;         // issuer warp + its dequant warps
     static constexpr int AST = NT <= 64 ? 3 : 2;             // ring slots: A buffers in TMEM = x stages
     static constexpr int DCOLS = NT <= 64 ? 64 : 128;        // TMEM columns per accumulator
     static constexpr int D_COL = AST * A_COLS;
@@ -154,18 +155,25 @@ __device__ __forceinline__ void dequant_word(uint32_t w, __half2 s1, __half2 m1,
     }
 }
 
-// 16 bytes (32 nibbles) of one row -> 16 fp16 pairs, with the group's
-// (scale, bias) pair sb
-__device__ __forceinline__ void dequant16(const uint4 &w, uint32_t sb, uint32_t *a) {
-    const __half2 sbh = *reinterpret_cast<const __half2 *>(&sb);
-    const __half2 s1 = __low2half2(sbh), b2 = __high2half2(sbh);
-    const __half2 m1 = __hmul2(s1, __float2half2_rn(-1024.0f));
-    const __half2 s16 = __hmul2(s1, __float2half2_rn(0.0625f));
-    const __half2 m64 = __hmul2(s1, __float2half2_rn(-64.0f));
-    dequant_word(w.x, s1, m1, s16, m64, b2, &a[0]);
-    dequant_word(w.y, s1, m1, s16, m64, b2, &a[4]);
-    dequant_word(w.z, s1, m1, s16, m64, b2, &a[8]);
-    dequant_word(w.w, s1, m1, s16, m64, b2, &a[12]);
+// the constants of one quantisation group, from its (scale, bias) pair
+struct GroupConst {
+    __half2 s1, m1, s16, m64, b2;
+    __device__ __forceinline__ explicit GroupConst(uint32_t sb) {
+        const __half2 sbh = *reinterpret_cast<const __half2 *>(&sb);
+        s1 = __low2half2(sbh);
+        b2 = __high2half2(sbh);
+        m1 = __hmul2(s1, __float2half2_rn(-1024.0f));
+        s16 = __hmul2(s1, __float2half2_rn(0.0625f));
+        m64 = __hmul2(s1, __float2half2_rn(-64.0f));
+    }
+};
+
+// 16 bytes (32 nibbles) of one row -> 16 fp16 pairs
+__device__ __forceinline__ void dequant16(const uint4 &w, const GroupConst &k, uint32_t *a) {
+    dequant_word(w.x, k.s1, k.m1, k.s16, k.m64, k.b2, &a[0]);
+    dequant_word(w.y, k.s1, k.m1, k.s16, k.m64, k.b2, &a[4]);
+    dequant_word(w.z, k.s1, k.m1, k.s16, k.m64, k.b2, &a[8]);
+    dequant_word(w.w, k.s1, k.m1, k.s16, k.m64, k.b2, &a[12]);
 }
 
 struct Smem {
@@ -229,7 +237,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
         }
         for (int r = 0; r < R; ++r) {
             tc::mbar_init(tc::smem_u32(&cs.full_x[r]), 1);
-            tc::mbar_init(tc::smem_u32(&cs.mma_done[r]), NI);
+            tc::mbar_init(tc::smem_u32(&cs.mma_done[r]), C::NI);
         }
         tc::mbar_init(tc::smem_u32(&cs.d_free), DQ_WARPS);
         cs.abort_flag = 0;
@@ -293,7 +301,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
         }
     } else if (warp >= ISS_WARP0) {
         const int is = warp - ISS_WARP0;
-        {
+        if (is < C::NI) {
             // ---------------- MMA issuer `is`: groups [is*GPI, (is+1)*GPI) ----------------
             constexpr uint32_t idesc = tc::idesc_f16_f32(ROWS, NT);
             const uint32_t dcol = tmem + C::D_COL + is * C::DCOLS;
@@ -306,14 +314,14 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                 if (first && seg > 0 && lane == 0)
                     wait_or_abort(tc::smem_u32(&cs.d_free), (seg - 1) & 1, abort_flag, ep.err, ERR_DFREE);
                 __syncwarp();
-                named_bar_sync(1 + is * MAX_AST + as, BAR_COUNT);
+                named_bar_sync(1 + is * MAX_AST + as, C::BAR_COUNT);
                 if (lane == 0) {
                     if (wait_or_abort(tc::smem_u32(&cs.full_x[as]), (j / R) & 1, abort_flag, ep.err, ERR_XFULL)) {
                         tc::fence_after_sync();
                         const uint64_t bdesc = bdesc0 + (uint64_t)(as * (C::XSTAGE >> 4));
 #pragma unroll
-                        for (int gg = 0; gg < GPI; ++gg) {
-                            const int grp = is * GPI + gg;
+                        for (int gg = 0; gg < C::GPI; ++gg) {
+                            const int grp = is * C::GPI + gg;
 #pragma unroll
                             for (int q = 0; q < 4; ++q) {
                                 const int kk = grp * 4 + q;             // k step of 16 inside the sub-chunk
@@ -337,51 +345,54 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
         // ------- dequant warps: rows 32*quarter.., group g of each sub-chunk -------
         const int quarter = warp & 3, g = warp >> 2;
         const int r = quarter * 32 + lane;       // row within the block, 0..127
-        const int is = g / GPI;                  // issuer of this group
+        const int is = g / C::GPI;               // issuer of this group
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         const int sw8 = r & 7;                   // 128B swizzle of this row
         const int tg = g;                        // token group of this warp in the epilogue
         int b = u0 / nc, c = u0 - b * nc;
+        int s = 0, wpar = 0;            // W stage of the current unit and its phase parity
+        int as = 0;                     // ring slot (A buffer, x stage) of the current sub-chunk
+        uint32_t mpar = 0;              // per slot: parity of its next MMA-completion wait
+        const uint32_t lane_col = lane_base + (uint32_t)(g * 32);
+        const int sw_off = (((2 * g) ^ sw8) << 4), sw_off1 = (((2 * g + 1) ^ sw8) << 4);
         for (int j = 0; j < nsub; ++j) {
-            const int i = j >> 1, h = j & 1, as = j % R;
-            const int s = i % sw;
+            const int h = j & 1;
+            const unsigned char *wst = wring + (size_t)s * WSTAGE;
             bool ok = true;
             if (h == 0) {
-                if (lane == 0)
-                    ok = wait_or_abort(tc::smem_u32(&cs.full_w[s]), (i / sw) & 1, abort_flag, ep.err, ERR_WFULL);
+                if (lane == 0) ok = wait_or_abort(tc::smem_u32(&cs.full_w[s]), wpar, abort_flag, ep.err, ERR_WFULL);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
             }
-            uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
-            uint32_t sbv = 0;
-            if (!*abort_flag) {
-                const unsigned char *wt = wring + (size_t)s * WSTAGE + h * WBOX + r * 128;
-                w0 = *reinterpret_cast<const uint4 *>(wt + (((2 * g) ^ sw8) << 4));
-                w1 = *reinterpret_cast<const uint4 *>(wt + (((2 * g + 1) ^ sw8) << 4));
-                sbv = reinterpret_cast<const uint32_t *>(wring + (size_t)s * WSTAGE + 2 * WBOX)[(h * 4 + g) * ROWS + r];
-            }
+            const unsigned char *wt = wst + h * WBOX + r * 128;
+            const uint4 w0 = *reinterpret_cast<const uint4 *>(wt + sw_off);
+            const uint4 w1 = *reinterpret_cast<const uint4 *>(wt + sw_off1);
+            const uint32_t sbv = reinterpret_cast<const uint32_t *>(wst + 2 * WBOX)[(h * 4 + g) * ROWS + r];
             if (h == 1) {
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.w_free[s]));   // both boxes of the stage read
+                if (++s == sw) { s = 0; wpar ^= 1; }
             }
-            if (j >= R) {
-                const int pj = j - R;   // last sub-chunk that used this A buffer
+            if (j >= R) {   // the MMAs that last read this A buffer have completed
                 if (lane == 0)
-                    ok = ok && wait_or_abort(tc::smem_u32(&cs.mma_done[as]), (pj / R) & 1, abort_flag, ep.err,
+                    ok = ok && wait_or_abort(tc::smem_u32(&cs.mma_done[as]), (mpar >> as) & 1, abort_flag, ep.err,
                                              ERR_MDONE);
+                mpar ^= 1u << as;
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 tc::fence_after_sync();
             }
-            if (ok && !*abort_flag) {
-                const uint32_t ta = tmem + lane_base + (uint32_t)(as * A_COLS + g * 32);
+            if (ok) {
+                const GroupConst kc(sbv);
+                const uint32_t ta = tmem + lane_col + (uint32_t)(as * A_COLS);
                 uint32_t a[16];
-                dequant16(w0, sbv, a);
+                dequant16(w0, kc, a);
                 tc::tmem_st16(ta + 0, a);
-                dequant16(w1, sbv, a);
+                dequant16(w1, kc, a);
                 tc::tmem_st16(ta + 16, a);
                 tc::tmem_wait_st();
             }
             tc::fence_before_sync();
-            named_bar_arrive(1 + is * MAX_AST + as, BAR_COUNT);
+            named_bar_arrive(1 + is * MAX_AST + as, C::BAR_COUNT);
+            if (++as == R) as = 0;
 
             const int ub = b, uc = c;            // block / unit of this sub-chunk
             if (h == 1 && ++c == nc) { c = 0; ++b; }
@@ -406,7 +417,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                 for (int q = 0; q < 16; ++q) acc[p][q] = 0.f;
                 if (cc < NT) {   // warp-uniform
 #pragma unroll
-                    for (int d = 0; d < NI; ++d) {
+                    for (int d = 0; d < C::NI; ++d) {
                         uint32_t v[16];
                         tc::tmem_ld16(tmem + lane_base + C::D_COL + d * C::DCOLS + cc, v);
                         tc::tmem_wait_ld();

@@ -112,6 +112,8 @@ struct mlxcat_cache {
     __half *xn = nullptr, *xa = nullptr, *qbuf = nullptr;
     size_t part_floats = 0;
     unsigned *counters = nullptr;     // split-K tickets of the q4 linear (self-resetting)
+    unsigned long long *amax_part = nullptr;   // split argmax partial keys
+    unsigned *amax_ctr = nullptr;              // split argmax tickets (self-resetting)
     int *err = nullptr;               // device-side wait timeouts
     int32_t *h_err = nullptr;
     AttnScratch attn;
@@ -370,7 +372,7 @@ int enqueue_step(mlxcat_cache *c, const SpecParams &sp, bool sampled, bool timed
     c->prof_recording = false;
     if (rc) return rc;
     if (timed) CK(ctx, cudaEventRecordWithFlags(c->ev1, st, cudaEventRecordExternal));
-    LK(ctx, argmax_rows(c->logits, M, ctx->cfg.vocab, c->amax, st));
+    LK(ctx, argmax_rows(c->logits, M, ctx->cfg.vocab, c->amax, st, c->amax_part, c->amax_ctr));
     LK(ctx, accept_greedy(c->rs(), sp, c->vtok, c->count, c->amax, step_out(c), st));
     if (sampled) {
         ctx->launches++;
@@ -685,6 +687,8 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
     chk(dalloc(A, &c->tpos, Mc)); chk(dalloc(A, &c->amax, Mc)); chk(dalloc(A, &c->out_tok, Mc));
     chk(dalloc(A, &c->out_n, R)); chk(dalloc(A, &c->out_fin, R)); chk(dalloc(A, &c->first_tok, 1));
     chk(dalloc(A, &c->ptok, Mc)); chk(dalloc(A, &c->stats, 4));
+    chk(dalloc(A, &c->amax_part, argmax_scratch_words(Mc))); chk(dalloc(A, &c->amax_ctr, Mc));
+    if (rc == MLXCAT_OK) chk(cudaMemset(c->amax_ctr, 0, sizeof(unsigned) * Mc));
     chk(dalloc(A, &c->logits, (size_t)Mc * cf.vocab));
     const int KS = Mc;   // sampling scratch slots (rows*(k+1))
     chk(dalloc(A, &c->samp.m, KS)); chk(dalloc(A, &c->samp.thr, KS));
@@ -824,7 +828,7 @@ int mlxcat_cache_insert_row(mlxcat_cache *c, int32_t row, const int32_t *prompt,
         if (rc) return rc;
         CK(ctx, cudaStreamSynchronize(st));   // host staging vectors are reused
     }
-    LK(ctx, argmax_rows(c->logits, 1, ctx->cfg.vocab, c->amax, st));
+    LK(ctx, argmax_rows(c->logits, 1, ctx->cfg.vocab, c->amax, st, c->amax_part, c->amax_ctr));
     LK(ctx, sample_first(c->rs(), row, c->logits, ctx->cfg.vocab, c->amax, c->samp, c->first_tok, st));
     int32_t t0 = 0;
     CK(ctx, cudaMemcpyAsync(&t0, c->first_tok, 4, cudaMemcpyDeviceToHost, st));
@@ -968,7 +972,7 @@ int mlxcat_accept(mlxcat_cache *c, const mlxcat_spec_config *spec, int32_t *out_
     CK(ctx, cudaSetDevice(ctx->device));
     cudaStream_t st = ctx->stream;
     const int K1 = sp.k + 1, M = c->rows * K1;
-    LK(ctx, argmax_rows(c->logits, M, ctx->cfg.vocab, c->amax, st));
+    LK(ctx, argmax_rows(c->logits, M, ctx->cfg.vocab, c->amax, st, c->amax_part, c->amax_ctr));
     LK(ctx, accept_greedy(c->rs(), sp, c->vtok, c->count, c->amax, step_out(c), st));
     if (any_sampled(c)) {
         ctx->launches++;
@@ -1261,7 +1265,7 @@ int mlxcat_op_draft(const mlxcat_rows *rows, const mlxcat_spec_config *spec, int
 
 size_t mlxcat_op_accept_workspace(int32_t rows, int32_t k) {
     const size_t n = (size_t)rows * (k + 1);
-    return n * 4 + n * 4 + n * 8 + n * 8 + n * 4 + 2048;
+    return n * 4 + n * 4 + n * 8 + n * 8 + n * 4 + argmax_scratch_words((int)n) * 8 + n * 4 + 2560;
 }
 
 int mlxcat_op_accept(const mlxcat_rows *rows, const mlxcat_spec_config *spec, const int32_t *vtok,
@@ -1282,12 +1286,15 @@ int mlxcat_op_accept(const mlxcat_rows *rows, const mlxcat_spec_config *spec, co
     sc.m = static_cast<float *>(take(cnt * 4));
     sc.thr = static_cast<uint32_t *>(take(cnt * 4));
     int32_t *amax = static_cast<int32_t *>(take(cnt * 4));
+    unsigned long long *amax_part = static_cast<unsigned long long *>(take(argmax_scratch_words((int)cnt) * 8));
+    unsigned *amax_ctr = static_cast<unsigned *>(take(cnt * 4));
     (void)p;
     cudaStream_t st = (cudaStream_t)stream;
     StepOut out;
     out.tokens = tokens; out.n = n; out.finished = finished;
     out.stats = reinterpret_cast<unsigned long long *>(stats);
-    cudaError_t e = argmax_rows(logits, (int)cnt, vocab, amax, st);
+    cudaError_t e = cudaMemsetAsync(amax_ctr, 0, cnt * 4, st);
+    if (e == cudaSuccess) e = argmax_rows(logits, (int)cnt, vocab, amax, st, amax_part, amax_ctr);
     if (e == cudaSuccess) e = accept_greedy(rows_of(rows), sp, vtok, count, amax, out, st);
     if (e == cudaSuccess) e = accept_sampled(rows_of(rows), sp, vtok, count, logits, vocab, sc, out, st);
     if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "accept: %s", cudaGetErrorString(e));
