@@ -241,15 +241,17 @@ def run_ours(args, wl, rank, world, local_rank):
                                    "frac": at_gbs / hbm}}
             dom = "q4_linear" if q4_ms >= at_ms else "attention"
             d = extra[dom]
+            # DRAM traffic per step: the algorithmic bytes scaled by the DRAM/algorithmic
+            # ratio that one ncu capture of this kernel measured (profiles/traffic.json)
             traffic = None
             tp = os.path.join(ROOT, "profiles", "traffic.json")
             if os.path.exists(tp):
                 tj = json.load(open(tp)).get(args.config, {})
                 if dom in tj:
-                    traffic = tj[dom] * d["launches_per_step"]
+                    traffic = tj[dom]["ratio"] * d["algorithmic_bytes_per_step"]
             roof = {"kernel": dom, "bound": "hbm", "achieved": d["achieved_gbs"], "peak": hbm,
                     "unit": "GB/s", "frac": d["frac"], "traffic": traffic,
-                    "traffic_scope": "bytes per step (all launches of the class)",
+                    "traffic_scope": "DRAM bytes per step (all launches of the class; algorithmic x the ncu-measured ratio)",
                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
         result = {
             "metric": "accepted tok/s", "value": value, "unit": "tok/s", "n_gpus": world,
