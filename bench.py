@@ -125,6 +125,19 @@ class ClockSampler:
 # --------------------------------------------------------------------------- #
 # our arm
 # --------------------------------------------------------------------------- #
+def reduce_over_ranks(dev_ms, wall, tokens, world, device):
+    """Whole-job figures of the timed region: the slowest rank's device and wall
+    time (max over ranks) and the tokens of all ranks (sum)."""
+    import torch
+    if world <= 1:
+        return dev_ms, wall, float(tokens)
+    t = torch.tensor([dev_ms, wall], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    n = torch.tensor([float(tokens)], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(n, op=torch.distributed.ReduceOp.SUM)
+    return float(t[0]), float(t[1]), float(n[0])
+
+
 def run_ours(args, wl, rank, world, local_rank):
     import torch
     import mlxcat_b200 as M
@@ -204,15 +217,7 @@ def run_ours(args, wl, rank, world, local_rank):
     cache.set_profiling(False)
 
     # ---- aggregate over ranks ----
-    t = torch.tensor([dev_ms, wall, float(tokens)], dtype=torch.float64, device="cuda")
-    if world > 1:
-        tmax = t.clone()
-        torch.distributed.all_reduce(tmax[:2], op=torch.distributed.ReduceOp.MAX)
-        tsum = t.clone()
-        torch.distributed.all_reduce(tsum[2:], op=torch.distributed.ReduceOp.SUM)
-        dev_ms_max, wall_max, tokens_all = float(tmax[0]), float(tmax[1]), float(tsum[2])
-    else:
-        dev_ms_max, wall_max, tokens_all = dev_ms, wall, float(tokens)
+    dev_ms_max, wall_max, tokens_all = reduce_over_ranks(dev_ms, wall, tokens, world, "cuda")
 
     result = None
     if rank == 0:
@@ -483,7 +488,7 @@ def main():
         import datetime
         import torch
         torch.cuda.set_device(local_rank)
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     res = run_ours(args, wl, rank, world, local_rank)
     if rank == 0:
