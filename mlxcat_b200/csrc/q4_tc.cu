@@ -205,7 +205,7 @@ __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, vol
     return false;
 }
 
-template <int NT>
+template <int NT, int OP>
 __global__ void __launch_bounds__(THREADS, 1)
 q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
              const uint32_t *__restrict__ sbp, int N, int K, int M, int tok_base, int nblk, int nc, int U,
@@ -498,15 +498,15 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                 const int m0 = tile * NT + cc;
                 const int mlim = cc < NT ? max(0, min(16, M - m0)) : 0;   // valid tokens in this piece
                 float *y = acc[p];
-                if (ep.op == Q4Epilogue::STORE) {
+                if constexpr (OP == Q4Epilogue::STORE) {
 #pragma unroll
                     for (int q = 0; q < 16; ++q)
                         if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] = y[q];
-                } else if (ep.op == Q4Epilogue::RESID) {
+                } else if constexpr (OP == Q4Epilogue::RESID) {
 #pragma unroll
                     for (int q = 0; q < 16; ++q)
                         if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] += y[q];
-                } else if (ep.op == Q4Epilogue::SWIGLU) {
+                } else if constexpr (OP == Q4Epilogue::SWIGLU) {
                     // rows [0,64) gate, [64,128) up of the same 64 outputs; token
                     // groups exchange through the buffer in two rounds of two
 #pragma unroll
@@ -657,17 +657,17 @@ int stages_for() {
     return 2;
 }
 
-template <int NT>
-cudaError_t launch_nt(const Q4WeightTC &w, const CUtensorMap &xmap, int M, int tok_base, int tiles,
+template <int NT, int OP>
+cudaError_t launch_op(const Q4WeightTC &w, const CUtensorMap &xmap, int M, int tok_base, int tiles,
                       int sm_count, const Q4Epilogue &ep, cudaStream_t st) {
-    static bool attr[64] = {};
+    static bool attr[64] = {};   // per instantiation
     int dev = 0;
     cudaGetDevice(&dev);
     const int sw = stages_for<NT>();
     const size_t sm = smem_for<NT>(sw);
     if (sm > SMEM_LIMIT) return cudaErrorInvalidConfiguration;
     if (!attr[dev & 63]) {
-        cudaError_t e = cudaFuncSetAttribute(q4_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        cudaError_t e = cudaFuncSetAttribute(q4_tc_kernel<NT, OP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
         if (e != cudaSuccess) return e;
         attr[dev & 63] = true;
     }
@@ -687,8 +687,20 @@ cudaError_t launch_nt(const Q4WeightTC &w, const CUtensorMap &xmap, int M, int t
     attr1[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr1;
     cfg.numAttrs = ep.pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, q4_tc_kernel<NT>, w.map, xmap, w.sbp, w.N, w.K, M, tok_base, nblk, nc, U, pmax,
+    return cudaLaunchKernelEx(&cfg, q4_tc_kernel<NT, OP>, w.map, xmap, w.sbp, w.N, w.K, M, tok_base, nblk, nc, U, pmax,
                               sw, ep);
+}
+
+template <int NT>
+cudaError_t launch_nt(const Q4WeightTC &w, const CUtensorMap &xmap, int M, int tok_base, int tiles,
+                      int sm_count, const Q4Epilogue &ep, cudaStream_t st) {
+    switch (ep.op) {
+    case Q4Epilogue::STORE: return launch_op<NT, Q4Epilogue::STORE>(w, xmap, M, tok_base, tiles, sm_count, ep, st);
+    case Q4Epilogue::RESID: return launch_op<NT, Q4Epilogue::RESID>(w, xmap, M, tok_base, tiles, sm_count, ep, st);
+    case Q4Epilogue::SWIGLU: return launch_op<NT, Q4Epilogue::SWIGLU>(w, xmap, M, tok_base, tiles, sm_count, ep, st);
+    case Q4Epilogue::QKV: return launch_op<NT, Q4Epilogue::QKV>(w, xmap, M, tok_base, tiles, sm_count, ep, st);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 }  // namespace
