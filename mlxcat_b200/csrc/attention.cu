@@ -10,9 +10,12 @@
 // the qg consecutive verify tokens of one row; all G = Hq/Hkv query heads of
 // the kv head and all qg tokens form the MMA M dimension (qg*G <= 16*QT), so
 // every K/V tile fetched from HBM is used by every query of the group.
-// K/V tiles of 64 keys are double-buffered in shared memory with cp.async;
-// each of the two warps per query tile takes 32 keys of a tile (its own online
+// K/V tiles of 32 keys go through a 3-deep cp.async ring in shared memory
+// (small tiles keep several CTAs per SM, so enough loads are in flight); each
+// of the two warps per query tile takes 16 keys of a tile (its own online
 // softmax).  Partials (m, l, O) go to scratch; attention_combine merges them.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -20,7 +23,8 @@ namespace mlxcat {
 
 namespace {
 
-constexpr int KB = 64;   // keys per staged block
+constexpr int KB = 32;       // keys per staged block
+constexpr int KSTAGES = 2;   // cp.async ring depth (blocks in flight)
 
 __device__ __forceinline__ void mma16816(float *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -60,9 +64,13 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
     constexpr int NTHREADS = QT * 64;
     extern __shared__ __align__(16) unsigned char smem[];
     __half *qs = reinterpret_cast<__half *>(smem);                 // [QROWS][PITCH]
-    __half *ks = qs + QROWS * PITCH;                                // [2][KB][PITCH]
-    __half *vs = ks + 2 * KB * PITCH;                               // [2][KB][PITCH]
+    __half *ks = qs + QROWS * PITCH;                                // [KSTAGES][KB][PITCH]
+    __half *vs = ks + KSTAGES * KB * PITCH;                         // [KSTAGES][KB][PITCH]
+    constexpr int KPW = KB / 2;                                     // keys per warp per block
+    constexpr int NU = KPW / 16, NN = KPW / 8;
 
+    griddep_launch_dependents();   // the combine pass may be scheduled
+    griddep_wait();                // queries and the new K/V come from the previous kernel
     const int grp = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
     const int G = Hq / Hkv;
     const int t0 = grp * qg;
@@ -111,8 +119,11 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
         }
     };
     const int nblk = (ke - kb + KB - 1) / KB;
-    stage_kv(0, 0);
-    cp_commit();
+#pragma unroll
+    for (int p = 0; p < KSTAGES - 1; ++p) {   // prologue: the first blocks (Q rides with block 0)
+        if (p < nblk) stage_kv(p, p);
+        cp_commit();
+    }
 
     uint32_t qf[D / 16][4];
     float o[D / 8][4];
@@ -125,9 +136,9 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
     const int lim1 = qrow1 < NQ ? pos0 + qrow1 / G : -1;
 
     for (int b = 0; b < nblk; ++b) {
-        if (b + 1 < nblk) stage_kv(b + 1, (b + 1) & 1);
+        if (b + KSTAGES - 1 < nblk) stage_kv(b + KSTAGES - 1, (b + KSTAGES - 1) % KSTAGES);
         cp_commit();
-        cp_wait<1>();
+        cp_wait<KSTAGES - 1>();
         __syncthreads();
         if (b == 0) {
 #pragma unroll
@@ -137,18 +148,18 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
                 ldsm_x4(qf[ks16], qs_a + (uint32_t)(qr * PITCH + ks16 * 16 + (mi >> 1) * 8) * 2);
             }
         }
-        const int buf = b & 1;
-        const int key_base = kb + b * KB + kh * 32;
-        // S = Q K^T over 32 keys (4 n8 tiles)
-        float sc[4][4];
+        const int buf = b % KSTAGES;
+        const int key_base = kb + b * KB + kh * KPW;
+        // S = Q K^T over this warp's KPW keys (NN n8 tiles)
+        float sc[NN][4];
 #pragma unroll
-        for (int n = 0; n < 4; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+        for (int n = 0; n < NN; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
 #pragma unroll
         for (int ks16 = 0; ks16 < D / 16; ++ks16) {
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
+            for (int u = 0; u < NU; ++u) {
                 const int mi = lane >> 3, rr = lane & 7;
-                const int kr = kh * 32 + u * 16 + (mi >> 1) * 8 + rr;
+                const int kr = kh * KPW + u * 16 + (mi >> 1) * 8 + rr;
                 uint32_t bb[4];
                 ldsm_x4(bb, ks_a + (uint32_t)((buf * KB + kr) * PITCH + ks16 * 16 + (mi & 1) * 8) * 2);
                 mma16816(sc[2 * u], qf[ks16], bb[0], bb[1]);
@@ -158,7 +169,7 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
         // mask + online softmax (scores in log2 units)
         float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
+        for (int n = 0; n < NN; ++n) {
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 const int key = key_base + n * 8 + 2 * t + (c & 1);
@@ -178,9 +189,9 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
             m_r[rI] = mn;
             l_r[rI] *= alpha[rI];
         }
-        uint32_t pa[2][4];
+        uint32_t pa[NU][4];
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
+        for (int n = 0; n < NN; ++n) {
             float p[4];
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -199,11 +210,11 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
         }
         // O += P V
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
+        for (int u = 0; u < NU; ++u) {
 #pragma unroll
             for (int dv = 0; dv < D / 16; ++dv) {
                 const int mi = lane >> 3, rr = lane & 7;
-                const int kr = kh * 32 + u * 16 + (mi & 1) * 8 + rr;
+                const int kr = kh * KPW + u * 16 + (mi & 1) * 8 + rr;
                 uint32_t bb[4];
                 ldsm_x4_t(bb, vs_a + (uint32_t)((buf * KB + kr) * PITCH + dv * 16 + (mi >> 1) * 8) * 2);
                 mma16816(o[2 * dv], pa[u], bb[0], bb[1]);
@@ -270,6 +281,7 @@ __global__ void attn_combine_kernel(const float *__restrict__ o_part, const floa
                                     __half *__restrict__ out, int permuted, int out_rows) {
     constexpr int QROWS = QT * 16;
     griddep_launch_dependents();   // the output projection may start prefetching its weights
+    griddep_wait();                // the split partials come from the split pass
     const int grp = blockIdx.x, h = blockIdx.y, qi = blockIdx.z;
     const int G = Hq / Hkv;
     const int t0 = grp * qg;
@@ -304,7 +316,8 @@ cudaError_t launch_attn(const __half *qbuf, KVLayer kv, const int32_t *trow, con
                         int M, int qg, int Hq, int Hkv, int key_chunk, int splits,
                         AttnScratch sc, __half *out, bool permuted, int out_rows, cudaStream_t st) {
     constexpr int PITCH = D + 8;
-    const size_t smem = (size_t)(QT * 16 + 4 * KB) * PITCH * 2;
+    const size_t smem = std::max((size_t)(QT * 16 + 2 * KSTAGES * KB) * PITCH * 2,
+                                 (size_t)QT * 16 * (D + 2) * 4);   // K/V ring, then the split merge
     static bool attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -317,14 +330,12 @@ cudaError_t launch_attn(const __half *qbuf, KVLayer kv, const int32_t *trow, con
     const int groups = (M + qg - 1) / qg;
     dim3 grid(groups, Hkv, splits);
     const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
-    attn_kernel<QT, D><<<grid, QT * 64, smem, st>>>(qbuf, kv.k, kv.v, kv.max_len, trow, tpos, M, qg,
-                                                    Hq, Hkv, key_chunk, splits, scale_log2, sc.o, sc.ml);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(attn_kernel<QT, D>, grid, dim3(QT * 64), smem, st, qbuf, kv.k, kv.v, kv.max_len,
+                               trow, tpos, M, qg, Hq, Hkv, key_chunk, splits, scale_log2, sc.o, sc.ml);
     if (e != cudaSuccess) return e;
     dim3 g2(groups, Hkv, QT * 16);
-    attn_combine_kernel<QT><<<g2, D, 0, st>>>(sc.o, sc.ml, M, qg, Hq, Hkv, D, splits, out, permuted ? 1 : 0,
-                                              out_rows);
-    return cudaGetLastError();
+    return launch_pdl(attn_combine_kernel<QT>, g2, dim3(D), 0, st, (const float *)sc.o, (const float *)sc.ml, M, qg,
+                      Hq, Hkv, D, splits, out, permuted ? 1 : 0, out_rows);
 }
 
 }  // namespace

@@ -61,6 +61,7 @@ __global__ void embed_norm_kernel(const uint32_t *__restrict__ wq, const __half 
 __global__ void rmsnorm_kernel(const float *__restrict__ h, int H, const float *__restrict__ nw,
                                float eps, __half *__restrict__ xn, int ldx_rows) {
     griddep_launch_dependents();   // the next linear may start prefetching its weights
+    griddep_wait();                // h is the previous kernel's output
     __shared__ float sh[32];
     const int m = blockIdx.x;
     const float *hm = h + (size_t)m * H;
@@ -314,8 +315,7 @@ cudaError_t embed_norm(const Q4Weight &embed, const int32_t *tok, int M, const f
 
 cudaError_t rmsnorm(const float *h, int M, int H, const float *norm_w, float eps, __half *xn,
                     int ldx_rows, cudaStream_t st) {
-    rmsnorm_kernel<<<M, TPB, 0, st>>>(h, H, norm_w, eps, xn, ldx_rows);
-    return cudaGetLastError();
+    return launch_pdl(rmsnorm_kernel, dim3(M), dim3(TPB), 0, st, h, H, norm_w, eps, xn, ldx_rows);
 }
 
 cudaError_t residual_norm(const float *part, int splits, int M, int H, const float *norm_w,

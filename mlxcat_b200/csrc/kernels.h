@@ -3,11 +3,33 @@
 // include/mlxcat_cuda.h sits on top.
 #pragma once
 
+#include <utility>
+
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace mlxcat {
+
+// Launch with programmatic stream serialisation: the kernel may start while
+// its predecessor on the stream is still running; it must call griddep_wait()
+// (common.cuh) before reading anything the predecessor writes.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 
 // One MLX affine-q4 matrix [N][K]: packed words, fp16 scales and biases.
 struct Q4Weight {

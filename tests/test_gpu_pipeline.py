@@ -327,3 +327,40 @@ def test_sampled_step_matches_oracle_given_device_logits():
             n_gen = len(hist[r]) - len(prompts[r])
             out, _ = O.accept_row(A.ACCEPT_PREFIX, logits[r, :len(drafts[r]) + 1], drafts[r], osp, n_gen)
             assert tok[r, :n[r]].tolist() == out
+
+
+# Llama-3-8B layer shape (hidden 4096, 32/8 heads of 128, SwiGLU 14336, untied
+# head, no q/k norm, theta 5e5) at one layer and a reduced vocabulary: the q4
+# linears at K = 4096 and 14336 and the sampled acceptance of that config
+LLAMA8B_LAYER = M.ModelConfig(1, 4096, 32, 8, 128, 14336, 8192, False, False, 1e-5, 500000.0,
+                              name="llama8b-layer")
+
+
+def test_llama8b_layer_verify_and_sampled_acceptance_match_oracle():
+    cfg = LLAMA8B_LAYER
+    seed, k = 11, 4
+    ctx = M.Context(cfg)
+    ctx.synth_weights(seed)
+    om = oracle_model(cfg, seed)
+    rows = 2
+    prompts = [segment_prompt(cfg.vocab, 4, 12, L, 700 + r) for r, L in enumerate([48, 30])]
+    sps = [M.SamplingParameters(temperature=0.7, top_p=0.9, seed=9000 + r) for r in range(rows)]
+    spec = M.SpeculativeDecodingConfiguration(True, k, 4, 8, A.ACCEPT_PREFIX)
+    cache = M.BatchKVCache(ctx, rows, 128)
+    gen = O.Generator(om, rows, 128, O.SpecConfig(A.ACCEPT_PREFIX, 1, k, 4, 8))
+    for r, p in enumerate(prompts):
+        cache.insert_row(r, p, 32, sps[r])
+        gen.admit(r, p, 32, O.sampling(temperature=0.7, top_p=0.9, seed=9000 + r))
+    hist = [cache.history(r) for r in range(rows)]
+    drafts = cache.draft(spec)
+    logits = cache.verify_forward(spec)
+    tok, n, fin, _ = cache.accept(spec)
+    for r in range(rows):
+        assert drafts[r] == (O.propose_suffix(hist[r], 4, 8, k) or [])
+        toks = [hist[r][-1]] + drafts[r]
+        kvlen = len(prompts[r])
+        ol = O.forward(om, gen.kv, toks, [r] * len(toks), list(range(kvlen, kvlen + len(toks))))
+        np.testing.assert_allclose(logits[r, :len(toks)], ol, rtol=TOL, atol=TOL)
+        osp = O.sampling(temperature=0.7, top_p=0.9, seed=9000 + r)
+        out, _ = O.accept_row(A.ACCEPT_PREFIX, logits[r, :len(toks)], drafts[r], osp, len(hist[r]) - kvlen)
+        assert tok[r, :n[r]].tolist() == out
