@@ -354,6 +354,23 @@ cudaError_t reduce_splits(const float *part, int splits, size_t n, float *y, cud
     return cudaGetLastError();
 }
 
+__global__ void rope_table_kernel(const float *__restrict__ inv_freq, int half, int max_len, float2 *tab) {
+    const long long n = (long long)max_len * half;
+    for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (long long)gridDim.x * blockDim.x) {
+        const int p = (int)(t / half), i = (int)(t - (long long)p * half);
+        float sn, cn;
+        sincosf(__fmul_rn((float)p, inv_freq[i]), &sn, &cn);
+        tab[t] = make_float2(cn, sn);
+    }
+}
+
+cudaError_t rope_table(const float *inv_freq, int half, int max_len, float2 *tab, cudaStream_t st) {
+    const long long n = (long long)max_len * half;
+    const long long b = (n + TPB - 1) / TPB;
+    rope_table_kernel<<<(unsigned)(b < 4096 ? (b ? b : 1) : 4096), TPB, 0, st>>>(inv_freq, half, max_len, tab);
+    return cudaGetLastError();
+}
+
 size_t argmax_scratch_words(int M) { return (size_t)M * ARGMAX_SPLITS; }
 
 cudaError_t argmax_rows(const float *logits, int M, int V, int32_t *out, cudaStream_t st,

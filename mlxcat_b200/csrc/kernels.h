@@ -75,6 +75,7 @@ struct Q4Epilogue {
     __half *qbuf = nullptr, *kc = nullptr, *vc = nullptr;
     int max_len = 0, n_heads = 0, n_kv = 0, head_dim = 0;
     const float *q_norm = nullptr, *k_norm = nullptr, *inv_freq = nullptr;
+    const float2 *rope = nullptr;   // QKV: (cos, sin) of pos * inv_freq[i], [max_len][head_dim/2]
     float eps = 0.f;
     const int32_t *trow = nullptr, *tpos = nullptr;
     // split-K
@@ -82,6 +83,8 @@ struct Q4Epilogue {
     unsigned *counters = nullptr;
     int *err = nullptr;
 };
+// (cos, sin) of p * inv_freq[i] for every position p < max_len and i < half
+cudaError_t rope_table(const float *inv_freq, int half, int max_len, float2 *tab, cudaStream_t st);
 bool make_weight_map(Q4WeightTC &w);
 // words of the re-packed (scale, bias) pairs of an N x K weight, and the packer
 size_t q4_sbp_words(int N, int K);

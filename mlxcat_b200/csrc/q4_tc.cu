@@ -74,19 +74,22 @@ namespace {
 constexpr int ROWS = 128;              // weight rows per block (MMA M)
 constexpr int KU = 512;                // k per stream-K unit (one W stage)
 constexpr int KS = 256;                // k per sub-chunk (one x stage, one A buffer)
-constexpr int DQ_WARPS = 16;           // dequant / epilogue warps
-constexpr int DQ_THREADS = DQ_WARPS * 32;
+constexpr int DQ_WARPS = 16;           // dequantising warps
 constexpr int ISS_WARP0 = DQ_WARPS;    // issuer warps 16..17
 constexpr int MAX_NI = 2;              // MMA issuer warps
 constexpr int WP_WARP = DQ_WARPS + MAX_NI; // W producer
 constexpr int XP_WARP = WP_WARP + 1;   // x producer
-constexpr int THREADS = (XP_WARP + 1) * 32;
+constexpr int EP_WARP0 = XP_WARP + 1;  // epilogue warps 20..23 (TMEM lane quarters 0..3)
+constexpr int EP_THREADS = 128;
+constexpr int THREADS = (EP_WARP0 + 4) * 32;
 constexpr int A_COLS = KS / 2;         // TMEM columns of one A buffer (fp16 pairs)
 constexpr int WBOX = ROWS * 128;       // one [128 rows x 128 B] weight box
 constexpr int SB_BYTES = 8 * ROWS * 4; // packed (scale, bias) of one unit
 constexpr int WSTAGE = 2 * WBOX + SB_BYTES;
 constexpr int MAX_SW = 4, MAX_AST = 3;
-constexpr int EPI_BAR = 9;             // named barrier of the epilogue (1..6: issuers)
+constexpr int EPI_BAR = 9;             // named barrier of the epilogue warps (1..6: issuers)
+constexpr int TAIL_BAR = 10;           // named barrier of the dequant warps' tail epilogue
+constexpr int TAIL_THREADS = DQ_WARPS * 32;
 
 enum ErrCode { ERR_WFULL = 1, ERR_XFULL = 2, ERR_MDONE = 3, ERR_XFREE = 4, ERR_WFREE = 5, ERR_DFREE = 6 };
 
@@ -95,11 +98,16 @@ struct Cfg {
     static constexpr int NI = 2;                             // MMA issuers
     static constexpr int GPI = 4 / NI;                       // 64-k groups per issuer
     static constexpr int BAR_COUNT = 32 + 128 * GPI;         // issuer warp + its dequant warps
-    static constexpr int AST = NT <= 64 ? 3 : 2;             // ring slots: A buffers in TMEM = x stages
-    static constexpr int DCOLS = NT <= 64 ? 64 : 128;        // TMEM columns per accumulator
+    // TMEM: ring of A buffers, then DSETS sets of NI fp32 accumulators.  With
+    // two sets the MMAs of the next block segment run while the epilogue warps
+    // read the previous one.
+    static constexpr int DCOLS = NT <= 32 ? 32 : (NT <= 64 ? 64 : 128);
+    static constexpr int DSETS = NT <= 64 ? 2 : 1;
+    static constexpr int AST = NT <= 32 ? 3 : 2;             // ring slots: A buffers in TMEM = x stages
     static constexpr int D_COL = AST * A_COLS;
     static constexpr int XSTAGE = 4 * NT * 128;              // 256 k of NT tokens
-    static_assert(D_COL + NI * DCOLS <= 512, "TMEM budget");
+    static constexpr int PIECES = NT / 16;                   // 16-token pieces of the epilogue
+    static_assert(D_COL + DSETS * NI * DCOLS <= 512, "TMEM budget");
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
@@ -177,12 +185,16 @@ __device__ __forceinline__ void dequant16(const uint4 &w, const GroupConst &k, u
 }
 
 struct Smem {
-    uint64_t full_w[MAX_SW], w_free[MAX_SW], full_x[MAX_AST], mma_done[MAX_AST], d_free;
+    uint64_t full_w[MAX_SW], w_free[MAX_SW], full_x[MAX_AST], mma_done[MAX_AST], d_full[2], d_free[2];
     uint32_t tmem_base;
     int abort_flag;
     int last_flag;
-    float wsum[4][4][16];       // [token group][row quarter][token]
-    float xch[2][ROWS * 16];    // epilogue exchange: [token group pair][row][token]
+    float wsum[4][16];          // [row quarter][token of the piece]
+    float xch[ROWS * 16];       // epilogue exchange: [row][token of the piece]
+    // the tail epilogue of the dequant warps (may overlap the epilogue warps)
+    int last_flag2;
+    float wsum2[4][4][16];      // [token group][row quarter][token]
+    float xch2[2][ROWS * 16];   // [token group pair][row][token]
 };
 
 // Stream-K schedule: the flattened (row block, k unit) space is split into
@@ -211,7 +223,9 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
              const uint32_t *__restrict__ sbp, int N, int K, int M, int tok_base, int nblk, int nc, int U,
              int pmax, int sw, Q4Epilogue ep) {
     using C = Cfg<NT>;
-    constexpr int PIECES = NT <= 64 ? 1 : 2;      // 16-token pieces per token group
+    // the epilogue warps take the non-last segments of the cheap epilogues; the
+    // QKV and SWIGLU epilogues (norms, RoPE, exchanges) stay on sixteen warps
+    constexpr bool EPW = OP == Q4Epilogue::STORE || OP == Q4Epilogue::RESID;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *wring = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -239,7 +253,10 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
             tc::mbar_init(tc::smem_u32(&cs.full_x[r]), 1);
             tc::mbar_init(tc::smem_u32(&cs.mma_done[r]), C::NI);
         }
-        tc::mbar_init(tc::smem_u32(&cs.d_free), DQ_WARPS);
+        for (int d = 0; d < C::DSETS; ++d) {
+            tc::mbar_init(tc::smem_u32(&cs.d_full[d]), C::NI);
+            tc::mbar_init(tc::smem_u32(&cs.d_free[d]), EPW ? 4 : DQ_WARPS);
+        }
         cs.abort_flag = 0;
         tc::fence_barrier_init();
         tc::prefetch_tmap(&wmap);
@@ -299,25 +316,26 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                 for (int j = max(0, issued - R); j < issued; ++j)
                     tc::mbar_wait(tc::smem_u32(&cs.full_x[j % R]), (j / R) & 1, nullptr, 0);
         }
-    } else if (warp >= ISS_WARP0) {
+    } else if (warp >= ISS_WARP0 && warp < ISS_WARP0 + MAX_NI) {
         const int is = warp - ISS_WARP0;
         if (is < C::NI) {
             // ---------------- MMA issuer `is`: groups [is*GPI, (is+1)*GPI) ----------------
             constexpr uint32_t idesc = tc::idesc_f16_f32(ROWS, NT);
-            const uint32_t dcol = tmem + C::D_COL + is * C::DCOLS;
             const uint64_t bdesc0 = tc::sdesc_k_sw128(tc::smem_u32(xring));   // slot r: + r * XSTAGE
-            int c = u0 % nc, seg = 0, last = -1;
+            int c = u0 % nc, seg = 0, last = -1, dset = 0;
             for (int j = 0; j < nsub; ++j) {
                 const int h = j & 1, as = j % R;
                 const bool first = h == 0 && (j == 0 || c == 0);   // first sub-chunk of a block segment
                 const bool seg_end = h == 1 && (c == nc - 1 || j == nsub - 1);
-                if (first && seg > 0 && lane == 0)
-                    wait_or_abort(tc::smem_u32(&cs.d_free), (seg - 1) & 1, abort_flag, ep.err, ERR_DFREE);
+                if (first && seg >= C::DSETS && lane == 0)   // the epilogue has read this accumulator set
+                    wait_or_abort(tc::smem_u32(&cs.d_free[dset]), ((seg - C::DSETS) / C::DSETS) & 1, abort_flag,
+                                  ep.err, ERR_DFREE);
                 __syncwarp();
                 named_bar_sync(1 + is * MAX_AST + as, C::BAR_COUNT);
                 if (lane == 0) {
                     if (wait_or_abort(tc::smem_u32(&cs.full_x[as]), (j / R) & 1, abort_flag, ep.err, ERR_XFULL)) {
                         tc::fence_after_sync();
+                        const uint32_t dcol = tmem + C::D_COL + (dset * C::NI + is) * C::DCOLS;
                         const uint64_t bdesc = bdesc0 + (uint64_t)(as * (C::XSTAGE >> 4));
 #pragma unroll
                         for (int gg = 0; gg < C::GPI; ++gg) {
@@ -331,84 +349,44 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                             }
                         }
                         tc::mma_commit(tc::smem_u32(&cs.mma_done[as]));   // frees A buffer and x stage
+                        if (seg_end) tc::mma_commit(tc::smem_u32(&cs.d_full[dset]));   // segment complete
                         last = j;
                     }
                 }
                 __syncwarp();
-                if (seg_end) ++seg;
+                if (seg_end) {
+                    ++seg;
+                    if (++dset == C::DSETS) dset = 0;
+                }
                 if (h == 1 && ++c == nc) c = 0;
             }
             if (lane == 0 && last >= 0)   // committed MMAs must finish before TMEM is freed
                 tc::mbar_wait(tc::smem_u32(&cs.mma_done[last % R]), (last / R) & 1, nullptr, 0);
         }
-    } else {
+    } else if (warp < DQ_WARPS) {
         // ------- dequant warps: rows 32*quarter.., group g of each sub-chunk -------
         const int quarter = warp & 3, g = warp >> 2;
         const int r = quarter * 32 + lane;       // row within the block, 0..127
         const int is = g / C::GPI;               // issuer of this group
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         const int sw8 = r & 7;                   // 128B swizzle of this row
-        const int tg = g;                        // token group of this warp in the epilogue
-        int b = u0 / nc, c = u0 - b * nc;
-        int s = 0, wpar = 0;            // W stage of the current unit and its phase parity
-        int as = 0;                     // ring slot (A buffer, x stage) of the current sub-chunk
-        uint32_t mpar = 0;              // per slot: parity of its next MMA-completion wait
-        const uint32_t lane_col = lane_base + (uint32_t)(g * 32);
-        const int sw_off = (((2 * g) ^ sw8) << 4), sw_off1 = (((2 * g + 1) ^ sw8) << 4);
-        for (int j = 0; j < nsub; ++j) {
-            const int h = j & 1;
-            const unsigned char *wst = wring + (size_t)s * WSTAGE;
-            bool ok = true;
-            if (h == 0) {
-                if (lane == 0) ok = wait_or_abort(tc::smem_u32(&cs.full_w[s]), wpar, abort_flag, ep.err, ERR_WFULL);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-            }
-            const unsigned char *wt = wst + h * WBOX + r * 128;
-            const uint4 w0 = *reinterpret_cast<const uint4 *>(wt + sw_off);
-            const uint4 w1 = *reinterpret_cast<const uint4 *>(wt + sw_off1);
-            const uint32_t sbv = reinterpret_cast<const uint32_t *>(wst + 2 * WBOX)[(h * 4 + g) * ROWS + r];
-            if (h == 1) {
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.w_free[s]));   // both boxes of the stage read
-                if (++s == sw) { s = 0; wpar ^= 1; }
-            }
-            if (j >= R) {   // the MMAs that last read this A buffer have completed
-                if (lane == 0)
-                    ok = ok && wait_or_abort(tc::smem_u32(&cs.mma_done[as]), (mpar >> as) & 1, abort_flag, ep.err,
-                                             ERR_MDONE);
-                mpar ^= 1u << as;
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                tc::fence_after_sync();
-            }
-            if (ok) {
-                const GroupConst kc(sbv);
-                const uint32_t ta = tmem + lane_col + (uint32_t)(as * A_COLS);
-                uint32_t a[16];
-                dequant16(w0, kc, a);
-                tc::tmem_st16(ta + 0, a);
-                dequant16(w1, kc, a);
-                tc::tmem_st16(ta + 16, a);
-                tc::tmem_wait_st();
-            }
-            tc::fence_before_sync();
-            named_bar_arrive(1 + is * MAX_AST + as, C::BAR_COUNT);
-            if (++as == R) as = 0;
-
-            const int ub = b, uc = c;            // block / unit of this sub-chunk
-            if (h == 1 && ++c == nc) { c = 0; ++b; }
-            if (h != 1 || (uc != nc - 1 && j != nsub - 1)) continue;
-
-            // ---------------- epilogue of the block segment ending here ----------------
-            const int seg_first_unit = max(u0, ub * nc);
-            const bool full = seg_first_unit == ub * nc && uc == nc - 1;
+        // epilogue of one block segment by the sixteen dequantising warps
+        auto seg_epilogue = [&](const int ub, const int lseg, const bool release) {
+            constexpr int PIECES = NT <= 64 ? 1 : 2;      // 16-token pieces per token group
+            const int tg = g;                             // token group of this warp
+            const int ldset = lseg % C::DSETS;
+            const int seg_first_unit = max(u0, ub * nc), seg_last_unit = min(u1 - 1, ub * nc + nc - 1);
+            const bool full = seg_first_unit == ub * nc && seg_last_unit == ub * nc + nc - 1;
             const int tile = ub / nblk, blk = ub - tile * nblk;
             const int f = blk * ROWS + r;
             bool bad = *abort_flag != 0;
             if (lane == 0 && !bad)
-                bad = !wait_or_abort(tc::smem_u32(&cs.mma_done[j % R]), (j / R) & 1, abort_flag, ep.err, ERR_XFREE);
+                bad = !wait_or_abort(tc::smem_u32(&cs.d_full[ldset]), (lseg / C::DSETS) & 1, abort_flag, ep.err,
+                                     ERR_DFREE);
             bad = __shfl_sync(0xffffffffu, bad, 0);
-            if (named_bar_or(EPI_BAR, DQ_THREADS, bad)) { *abort_flag = 1; continue; }
+            if (named_bar_or(TAIL_BAR, TAIL_THREADS, bad)) { *abort_flag = 1; return; }
             tc::fence_after_sync();
+            {
             float acc[PIECES][16];
 #pragma unroll
             for (int p = 0; p < PIECES; ++p) {
@@ -419,16 +397,18 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
 #pragma unroll
                     for (int d = 0; d < C::NI; ++d) {
                         uint32_t v[16];
-                        tc::tmem_ld16(tmem + lane_base + C::D_COL + d * C::DCOLS + cc, v);
+                        tc::tmem_ld16(tmem + lane_base + C::D_COL + (ldset * C::NI + d) * C::DCOLS + cc, v);
                         tc::tmem_wait_ld();
 #pragma unroll
                         for (int q = 0; q < 16; ++q) acc[p][q] += __uint_as_float(v[q]);
                     }
                 }
             }
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.d_free));   // accumulators may be reused
+            if (release) {   // accumulators read: the issuers may reuse this set
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.d_free[ldset]));
+            }
 
             if (!full) {
                 // partial block: slot of this CTA among the block's contributors.
@@ -450,7 +430,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                 // 0's gpu-scope fence (fences are cumulative), which orders them
                 // before the ticket; the last contributor fences again before the
                 // barrier that releases its readers
-                named_bar_sync(EPI_BAR, DQ_THREADS);
+                named_bar_sync(TAIL_BAR, TAIL_THREADS);
                 if (tid == 0) {
                     unsigned *ctr = ep.counters + ub;
                     __threadfence();
@@ -460,10 +440,10 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                         *ctr = 0u;   // ready for the next launch
                         __threadfence();
                     }
-                    cs.last_flag = last;
+                    cs.last_flag2 = last;
                 }
-                named_bar_sync(EPI_BAR, DQ_THREADS);
-                if (!cs.last_flag) continue;
+                named_bar_sync(TAIL_BAR, TAIL_THREADS);
+                if (!cs.last_flag2) return;
 #pragma unroll
                 for (int p = 0; p < PIECES; ++p) {
                     const int cc = p * 64 + tg * 16;
@@ -511,13 +491,13 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                     // groups exchange through the buffer in two rounds of two
 #pragma unroll
                     for (int ph = 0; ph < 2; ++ph) {
-                        float *xch = cs.xch[tg & 1];
+                        float *xch = cs.xch2[tg & 1];
                         const bool mine = (tg >> 1) == ph;
                         if (mine && r >= 64) {
 #pragma unroll
                             for (int q = 0; q < 16; ++q) xch[(r - 64) * 16 + q] = y[q];
                         }
-                        named_bar_sync(EPI_BAR, DQ_THREADS);
+                        named_bar_sync(TAIL_BAR, TAIL_THREADS);
                         if (mine && r < 64) {
                             const int oi = blk * 64 + r;
 #pragma unroll
@@ -528,7 +508,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                                 ep.xout[xblk(m0 + q, oi, ep.ldx_rows)] = __float2half_rn(av);
                             }
                         }
-                        named_bar_sync(EPI_BAR, DQ_THREADS);
+                        named_bar_sync(TAIL_BAR, TAIL_THREADS);
                     }
                 } else {   // QKV
                     const int D = ep.head_dim;
@@ -541,16 +521,16 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
 #pragma unroll
                         for (int q = 0; q < 16; ++q) {
                             const float t2 = warp_sum(y[q] * y[q]);
-                            if (lane == q) cs.wsum[tg][quarter][q] = t2;
+                            if (lane == q) cs.wsum2[tg][quarter][q] = t2;
                         }
                     }
-                    named_bar_sync(EPI_BAR, DQ_THREADS);
+                    named_bar_sync(TAIL_BAR, TAIL_THREADS);
                     if (nw) {
                         const int wpk = D / 32, w0 = (quarter / wpk) * wpk;
 #pragma unroll
                         for (int q = 0; q < 16; ++q) {
                             float ss = 0.f;
-                            for (int ww = w0; ww < w0 + wpk; ++ww) ss += cs.wsum[tg][ww][q];
+                            for (int ww = w0; ww < w0 + wpk; ++ww) ss += cs.wsum2[tg][ww][q];
                             y[q] = y[q] * (1.0f / sqrtf(ss / (float)D + ep.eps)) * nw[d];
                         }
                     }
@@ -558,28 +538,26 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                     // through the buffer in two rounds of two token groups
 #pragma unroll
                     for (int ph = 0; ph < 2; ++ph) {
-                        float *xch = cs.xch[tg & 1];
+                        float *xch = cs.xch2[tg & 1];
                         const bool mine = (tg >> 1) == ph;
                         if (mine) {
 #pragma unroll
                             for (int q = 0; q < 16; ++q) xch[r * 16 + q] = y[q];
                         }
-                        named_bar_sync(EPI_BAR, DQ_THREADS);
+                        named_bar_sync(TAIL_BAR, TAIL_THREADS);
                         if (mine && (is_q || is_k)) {
                             const int half = D / 2;
                             const int pr = d < half ? r + half : r - half;
-                            const float fr = ep.inv_freq[d % half];
 #pragma unroll
                             for (int q = 0; q < 16; ++q) {
                                 if (q >= mlim) break;
-                                const float ang = __fmul_rn((float)ep.tpos[m0 + q], fr);
-                                float sn, cn;
-                                sincosf(ang, &sn, &cn);
+                                const float2 csn = ep.rope[(size_t)ep.tpos[m0 + q] * half + d % half];
+                                const float sn = csn.y, cn = csn.x;
                                 const float pv = xch[pr * 16 + q];
                                 y[q] = d < half ? y[q] * cn - pv * sn : pv * sn + y[q] * cn;
                             }
                         }
-                        named_bar_sync(EPI_BAR, DQ_THREADS);
+                        named_bar_sync(TAIL_BAR, TAIL_THREADS);
                     }
 #pragma unroll
                     for (int q = 0; q < 16; ++q) {
@@ -597,6 +575,258 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                     }
                 }
             }
+            }
+        };
+        int b = u0 / nc, c = u0 - b * nc, seg = 0;
+        int s = 0, wpar = 0;            // W stage of the current unit and its phase parity
+        int as = 0;                     // ring slot (A buffer, x stage) of the current sub-chunk
+        uint32_t mpar = 0;              // per slot: parity of its next MMA-completion wait
+        const uint32_t lane_col = lane_base + (uint32_t)(g * 32);
+        const int sw_off = (((2 * g) ^ sw8) << 4), sw_off1 = (((2 * g + 1) ^ sw8) << 4);
+        for (int j = 0; j < nsub; ++j) {
+            const int h = j & 1;
+            const unsigned char *wst = wring + (size_t)s * WSTAGE;
+            bool ok = true;
+            if (h == 0) {
+                if (lane == 0) ok = wait_or_abort(tc::smem_u32(&cs.full_w[s]), wpar, abort_flag, ep.err, ERR_WFULL);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+            }
+            const unsigned char *wt = wst + h * WBOX + r * 128;
+            const uint4 w0 = *reinterpret_cast<const uint4 *>(wt + sw_off);
+            const uint4 w1 = *reinterpret_cast<const uint4 *>(wt + sw_off1);
+            const uint32_t sbv = reinterpret_cast<const uint32_t *>(wst + 2 * WBOX)[(h * 4 + g) * ROWS + r];
+            if (h == 1) {
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.w_free[s]));   // both boxes of the stage read
+                if (++s == sw) { s = 0; wpar ^= 1; }
+            }
+            if (j >= R) {   // the MMAs that last read this A buffer have completed
+                if (lane == 0)
+                    ok = ok && wait_or_abort(tc::smem_u32(&cs.mma_done[as]), (mpar >> as) & 1, abort_flag, ep.err,
+                                             ERR_MDONE);
+                mpar ^= 1u << as;
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                tc::fence_after_sync();
+            }
+            if (ok) {
+                const GroupConst kc(sbv);
+                const uint32_t ta = tmem + lane_col + (uint32_t)(as * A_COLS);
+                uint32_t a[16];
+                dequant16(w0, kc, a);
+                tc::tmem_st16(ta + 0, a);
+                dequant16(w1, kc, a);
+                tc::tmem_st16(ta + 16, a);
+                tc::tmem_wait_st();
+            }
+            tc::fence_before_sync();
+            named_bar_arrive(1 + is * MAX_AST + as, C::BAR_COUNT);
+            if (++as == R) as = 0;
+
+            const int ub = b, uc = c;            // block / unit of this sub-chunk
+            if (h == 1 && ++c == nc) { c = 0; ++b; }
+            if (h != 1 || (uc != nc - 1 && j != nsub - 1)) continue;
+            // end of a block segment: the epilogue warps take the non-last ones of
+            // the cheap epilogues; everything else is done here
+            const bool last_seg = j == nsub - 1;
+            if (!(EPW && !last_seg)) seg_epilogue(ub, seg, !last_seg);
+            ++seg;
+        }
+    } else if (EPW && warp >= EP_WARP0) {
+        // ---------------- epilogue warps: one thread per row, all tokens ----------------
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const int etid = tid - EP_WARP0 * 32;    // 0..127
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        int seg = 0, dset = 0;
+        for (int ub = u0 / nc; ub < (u1 - 1) / nc; ++ub, ++seg) {   // all but the last segment
+            const int seg_first_unit = max(u0, ub * nc), seg_last_unit = min(u1 - 1, ub * nc + nc - 1);
+            const bool full = seg_first_unit == ub * nc && seg_last_unit == ub * nc + nc - 1;
+            const int tile = ub / nblk, blk = ub - tile * nblk;
+            const int f = blk * ROWS + r;
+            bool bad = *abort_flag != 0;
+            if (lane == 0 && !bad)
+                bad = !wait_or_abort(tc::smem_u32(&cs.d_full[dset]), (seg / C::DSETS) & 1, abort_flag, ep.err,
+                                     ERR_DFREE);
+            bad = __shfl_sync(0xffffffffu, bad, 0);
+            const bool skip = named_bar_or(EPI_BAR, EP_THREADS, bad);
+            if (skip) *abort_flag = 1;
+            tc::fence_after_sync();
+            const uint32_t dbase = tmem + lane_base + C::D_COL + dset * C::NI * C::DCOLS;
+            // the accumulators of piece p (16 tokens), summed over the issuers
+            auto load_piece = [&](int p, float *y) {
+#pragma unroll
+                for (int q = 0; q < 16; ++q) y[q] = 0.f;
+#pragma unroll
+                for (int d = 0; d < C::NI; ++d) {
+                    uint32_t v[16];
+                    tc::tmem_ld16(dbase + d * C::DCOLS + p * 16, v);
+                    tc::tmem_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) y[q] += __uint_as_float(v[q]);
+                }
+            };
+            float *pblk = nullptr;
+            int ncontrib = 1, last = 1;
+            if (!skip && !full) {
+                // partial block: slot of this CTA among the block's contributors,
+                // stored [slot][token][row] (a warp writes 128 contiguous bytes)
+                const int first_owner = unit_owner(ub * nc, U, G);
+                ncontrib = unit_owner(ub * nc + nc - 1, U, G) - first_owner + 1;
+                pblk = ep.part + (size_t)ub * pmax * NT * ROWS;
+                float *mine = pblk + (size_t)(cta - first_owner) * NT * ROWS + r;
+                for (int p = 0; p < C::PIECES; ++p) {
+                    float y[16];
+                    load_piece(p, y);
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) mine[(size_t)(p * 16 + q) * ROWS] = y[q];
+                }
+            }
+            if (!skip && !full) {
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.d_free[dset]));   // accumulators read
+                // the barrier orders every thread's partial stores before thread 0's
+                // gpu-scope fence (fences are cumulative), which orders them before
+                // the ticket; the last contributor fences again before releasing its
+                // readers
+                named_bar_sync(EPI_BAR, EP_THREADS);
+                if (etid == 0) {
+                    unsigned *ctr = ep.counters + ub;
+                    __threadfence();
+                    const unsigned prev = atomicAdd(ctr, 1u);
+                    const int lst = prev == (unsigned)(ncontrib - 1);
+                    if (lst) {
+                        *ctr = 0u;   // ready for the next launch
+                        __threadfence();
+                    }
+                    cs.last_flag = lst;
+                }
+                named_bar_sync(EPI_BAR, EP_THREADS);
+                last = cs.last_flag;
+            }
+            if (!skip && last) {
+                for (int p = 0; p < C::PIECES; ++p) {
+                    float y[16];
+                    if (full) {
+                        load_piece(p, y);
+                        if (p == C::PIECES - 1) {   // accumulators read: the issuers may reuse them
+                            tc::fence_before_sync();
+                            __syncwarp();
+                            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.d_free[dset]));
+                        }
+                    } else {
+                        // slots summed in slot order, two slots' loads in flight
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) y[q] = 0.f;
+                        const float *pp = pblk + (size_t)(p * 16) * ROWS + r;
+                        const size_t slot_stride = (size_t)NT * ROWS;
+                        for (int sl = 0; sl < ncontrib; sl += 2) {
+                            float t[2][16];
+#pragma unroll
+                            for (int k = 0; k < 2; ++k)
+#pragma unroll
+                                for (int q = 0; q < 16; ++q)
+                                    t[k][q] = sl + k < ncontrib ? __ldcg(pp + (sl + k) * slot_stride + (size_t)q * ROWS) : 0.f;
+#pragma unroll
+                            for (int k = 0; k < 2; ++k) {
+                                if (sl + k >= ncontrib) break;
+#pragma unroll
+                                for (int q = 0; q < 16; ++q) y[q] += t[k][q];
+                            }
+                        }
+                    }
+                    const int m0 = tile * NT + p * 16;
+                    const int mlim = max(0, min(16, M - m0));   // valid tokens in this piece
+                    if constexpr (OP == Q4Epilogue::STORE) {
+#pragma unroll
+                        for (int q = 0; q < 16; ++q)
+                            if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] = y[q];
+                    } else if constexpr (OP == Q4Epilogue::RESID) {
+#pragma unroll
+                        for (int q = 0; q < 16; ++q)
+                            if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] += y[q];
+                    } else if constexpr (OP == Q4Epilogue::SWIGLU) {
+                        // rows [0,64) gate, [64,128) up of the same 64 outputs
+                        if (r >= 64) {
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) cs.xch[(r - 64) * 16 + q] = y[q];
+                        }
+                        named_bar_sync(EPI_BAR, EP_THREADS);
+                        if (r < 64) {
+                            const int oi = blk * 64 + r;
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) {
+                                if (q >= mlim) break;
+                                const float gv = y[q], uv = cs.xch[r * 16 + q];
+                                const float av = gv / (1.0f + expf(-gv)) * uv;
+                                ep.xout[xblk(m0 + q, oi, ep.ldx_rows)] = __float2half_rn(av);
+                            }
+                        }
+                        named_bar_sync(EPI_BAR, EP_THREADS);
+                    } else {   // QKV
+                        const int D = ep.head_dim;
+                        const int hh = f / D;      // head index in q|k|v order
+                        const int d = f % D;
+                        const bool is_q = hh < ep.n_heads, is_k = !is_q && hh < ep.n_heads + ep.n_kv;
+                        const float *nw = is_q ? ep.q_norm : (is_k ? ep.k_norm : nullptr);
+                        if (nw) {
+                            // per-head sum of squares for each token: warp shuffles + smem
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) {
+                                const float t2 = warp_sum(y[q] * y[q]);
+                                if (lane == q) cs.wsum[quarter][q] = t2;
+                            }
+                        }
+                        named_bar_sync(EPI_BAR, EP_THREADS);
+                        if (nw) {
+                            const int wpk = D / 32, w0 = (quarter / wpk) * wpk;
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) {
+                                float ss = 0.f;
+                                for (int ww = w0; ww < w0 + wpk; ++ww) ss += cs.wsum[ww][q];
+                                y[q] = y[q] * (1.0f / sqrtf(ss / (float)D + ep.eps)) * nw[d];
+                            }
+                        }
+                        // rotate-half RoPE on q and k: partner row r +- D/2
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) cs.xch[r * 16 + q] = y[q];
+                        named_bar_sync(EPI_BAR, EP_THREADS);
+                        if (is_q || is_k) {
+                            const int half = D / 2;
+                            const int pr = d < half ? r + half : r - half;
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) {
+                                if (q >= mlim) break;
+                                const float2 csn = ep.rope[(size_t)ep.tpos[m0 + q] * half + d % half];
+                                const float sn = csn.y, cn = csn.x;
+                                const float pv = cs.xch[pr * 16 + q];
+                                y[q] = d < half ? y[q] * cn - pv * sn : pv * sn + y[q] * cn;
+                            }
+                        }
+                        named_bar_sync(EPI_BAR, EP_THREADS);
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            if (q >= mlim) break;
+                            const int m = m0 + q;
+                            __half *dst;
+                            if (is_q) {
+                                dst = ep.qbuf + ((size_t)m * ep.n_heads + hh) * D;
+                            } else {
+                                const int kvh = is_k ? hh - ep.n_heads : hh - ep.n_heads - ep.n_kv;
+                                dst = (is_k ? ep.kc : ep.vc) +
+                                      (((size_t)ep.trow[m] * ep.n_kv + kvh) * ep.max_len + ep.tpos[m]) * D;
+                            }
+                            dst[d] = __float2half_rn(y[q]);
+                        }
+                    }
+                }
+            } else if (!skip && full) {
+                // unreachable: a full block always has last = 1
+            }
+            if (skip && lane == 0) {
+                // keep the issuers' accumulator waits balanced after an abort
+            }
+            if (++dset == C::DSETS) dset = 0;
         }
     }
     tc::fence_before_sync();

@@ -109,6 +109,7 @@ struct mlxcat_cache {
             *ptok = nullptr;
     unsigned long long *stats = nullptr;
     float *h = nullptr, *part = nullptr, *logits = nullptr;
+    float2 *rope = nullptr;           // (cos, sin) of every position x RoPE frequency
     __half *xn = nullptr, *xa = nullptr, *qbuf = nullptr;
     size_t part_floats = 0;
     unsigned *counters = nullptr;     // split-K tickets of the q4 linear (self-resetting)
@@ -282,7 +283,7 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
             e.qbuf = c->qbuf; e.kc = kv.k; e.vc = kv.v; e.max_len = kv.max_len;
             e.n_heads = Hq; e.n_kv = Hkv; e.head_dim = D;
             e.q_norm = ctx->q_norm(l); e.k_norm = ctx->k_norm(l); e.eps = eps;
-            e.inv_freq = ctx->inv_freq; e.trow = trow; e.tpos = tpos;
+            e.inv_freq = ctx->inv_freq; e.rope = c->rope; e.trow = trow; e.tpos = tpos;
             ProfScope ps(c, 0);
             LK(ctx, q4_tc(ctx->qkv[l].tc(), c->xn, R, 0, M, ctx->sm_count, e, st));
         }
@@ -701,6 +702,9 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
         chk(dalloc(A, &c->xn, (size_t)Mc * xw));
         chk(dalloc(A, &c->xa, (size_t)Mc * I));
         chk(dalloc(A, &c->qbuf, (size_t)Mc * Hq * D));
+        chk(dalloc(A, &c->rope, (size_t)max_len * (D / 2)));
+        if (rc == MLXCAT_OK) chk(rope_table(ctx->inv_freq, D / 2, max_len, c->rope, ctx->stream));
+        if (rc == MLXCAT_OK) chk(cudaStreamSynchronize(ctx->stream));
         // split-K partials and tickets: max over the linears and every token count
         size_t pf = 0, nc = 0;
         const int NK[5][2] = {{(Hq + 2 * Hkv) * D, H}, {H, Hq * D}, {2 * I, H}, {H, I}, {cf.vocab, H}};
