@@ -54,7 +54,7 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 }
 
 template <int QT, int D>
-__global__ void __launch_bounds__(QT * 64)
+__global__ void __launch_bounds__(QT * 64, 8 / QT)
 attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
             const __half *__restrict__ vc, int max_len, const int32_t *__restrict__ trow,
             const int32_t *__restrict__ tpos, int M, int qg, int Hq, int Hkv, int key_chunk,
@@ -166,47 +166,61 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
                 mma16816(sc[2 * u + 1], qf[ks16], bb[2], bb[3]);
             }
         }
-        // mask + online softmax (scores in log2 units)
+        // Mask only where a key can lie past a query's position: the causal
+        // corner and the zero-filled keys past kend (both beyond pos0).  Rows
+        // past NQ (zero queries) are never written.
+        if (key_base + KPW - 1 > pos0) {
+#pragma unroll
+            for (int n = 0; n < NN; ++n)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const int key = key_base + n * 8 + 2 * t + (c & 1);
+                    const int lim = c < 2 ? lim0 : lim1;
+                    if (!(key <= lim && key < ke)) sc[n][c] = -INFINITY;
+                }
+        }
         float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-        for (int n = 0; n < NN; ++n) {
+        for (int n = 0; n < NN; ++n)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int key = key_base + n * 8 + 2 * t + (c & 1);
-                const int lim = c < 2 ? lim0 : lim1;
-                const float v = (key <= lim && key < ke) ? sc[n][c] * scale_log2 : -INFINITY;
-                sc[n][c] = v;
-                mx[c >> 1] = fmaxf(mx[c >> 1], v);
-            }
-        }
-        float alpha[2];
+            for (int c = 0; c < 4; ++c) mx[c >> 1] = fmaxf(mx[c >> 1], sc[n][c]);
+        // Online softmax in log2 units, z = s * scale_log2.  The running
+        // reference m_r is raised only when a row's block max exceeds it by more
+        // than 8 (then every row of the warp is rescaled), so exp2(z - m_r) <= 256
+        // fits the fp16 P operand and most blocks skip the O rescale.
+        bool raise = false;
 #pragma unroll
         for (int rI = 0; rI < 2; ++rI) {
             mx[rI] = fmaxf(mx[rI], __shfl_xor_sync(0xffffffffu, mx[rI], 1));
             mx[rI] = fmaxf(mx[rI], __shfl_xor_sync(0xffffffffu, mx[rI], 2));
-            const float mn = fmaxf(m_r[rI], mx[rI]);
-            alpha[rI] = (mn == -INFINITY) ? 0.f : exp2f(m_r[rI] - mn);
-            m_r[rI] = mn;
-            l_r[rI] *= alpha[rI];
+            mx[rI] *= scale_log2;
+            raise |= mx[rI] > m_r[rI] + 8.f;
         }
+        if (__any_sync(0xffffffffu, raise)) {
+#pragma unroll
+            for (int rI = 0; rI < 2; ++rI) {
+                const float mn = fmaxf(m_r[rI], mx[rI]);
+                const float alpha = (mn == -INFINITY || m_r[rI] == -INFINITY) ? 0.f : exp2f(m_r[rI] - mn);
+                m_r[rI] = mn;
+                l_r[rI] *= alpha;
+#pragma unroll
+                for (int i = 0; i < D / 8; ++i) { o[i][2 * rI] *= alpha; o[i][2 * rI + 1] *= alpha; }
+            }
+        }
+        const float nm0 = m_r[0] == -INFINITY ? 0.f : -m_r[0];
+        const float nm1 = m_r[1] == -INFINITY ? 0.f : -m_r[1];
         uint32_t pa[NU][4];
 #pragma unroll
         for (int n = 0; n < NN; ++n) {
             float p[4];
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-                const float mref = m_r[c >> 1];
-                p[c] = (mref == -INFINITY) ? 0.f : exp2f(sc[n][c] - mref);
+                p[c] = exp2f(fmaf(sc[n][c], scale_log2, c < 2 ? nm0 : nm1));
                 l_r[c >> 1] += p[c];
             }
             const int u = n >> 1;
             if ((n & 1) == 0) { pa[u][0] = pack_h2(p[0], p[1]); pa[u][1] = pack_h2(p[2], p[3]); }
             else { pa[u][2] = pack_h2(p[0], p[1]); pa[u][3] = pack_h2(p[2], p[3]); }
-        }
-#pragma unroll
-        for (int i = 0; i < D / 8; ++i) {
-            o[i][0] *= alpha[0]; o[i][1] *= alpha[0];
-            o[i][2] *= alpha[1]; o[i][3] *= alpha[1];
         }
         // O += P V
 #pragma unroll
