@@ -30,7 +30,7 @@ __device__ __forceinline__ float block_sum(float v, float *sh) {
 __global__ void embed_norm_kernel(const uint32_t *__restrict__ wq, const __half *__restrict__ sc,
                                   const __half *__restrict__ bi, int H, const int32_t *tok,
                                   const float *__restrict__ nw, float eps, float *__restrict__ h,
-                                  __half *__restrict__ xn, int ldx_rows) {
+                                  __half *__restrict__ xn, int ldx_rows, float *__restrict__ rstd_out) {
     __shared__ float sh[32];
     const int m = blockIdx.x;
     const int t = tok[m];
@@ -50,6 +50,7 @@ __global__ void embed_norm_kernel(const uint32_t *__restrict__ wq, const __half 
     }
     ss = block_sum(ss, sh);
     const float r = 1.0f / sqrtf(ss / (float)H + eps);
+    if (rstd_out && threadIdx.x == 0) rstd_out[m] = r;
     for (int w = threadIdx.x; w < H / 8; w += blockDim.x)
         for (int i = 0; i < 8; ++i) {
             const int k = w * 8 + i;
@@ -307,9 +308,9 @@ __global__ void table_logits_kernel(const int32_t *next, const int32_t *tok, int
 }  // namespace
 
 cudaError_t embed_norm(const Q4Weight &embed, const int32_t *tok, int M, const float *norm_w,
-                       float eps, float *h, __half *xn, int ldx_rows, cudaStream_t st) {
+                       float eps, float *h, __half *xn, int ldx_rows, cudaStream_t st, float *rstd_out) {
     embed_norm_kernel<<<M, TPB, 0, st>>>(embed.wq, embed.scales, embed.biases, embed.K, tok,
-                                         norm_w, eps, h, xn, ldx_rows);
+                                         norm_w, eps, h, xn, ldx_rows, rstd_out);
     return cudaGetLastError();
 }
 

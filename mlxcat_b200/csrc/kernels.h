@@ -82,6 +82,21 @@ struct Q4Epilogue {
     float *part = nullptr;
     unsigned *counters = nullptr;
     int *err = nullptr;
+    // Folded RMSNorm.  Producer (RESID with norm_w): besides h += y it writes the
+    // next linear's operand xout = fp16(h * norm_w * norm_scale[m]) (blocked,
+    // ldx_rows rows) and the per-block sums of squares of h.  The pre-scale is an
+    // earlier rstd of the same row, which keeps the operand in fp16 range.
+    const float *norm_w = nullptr;
+    const float *norm_scale = nullptr;   // [rows]
+    float *norm_part = nullptr;          // [N/128][norm_rows]
+    int norm_rows = 0;                   // token rows of the sums-of-squares scratch
+    // Consumer (any op): accumulators of operand row m are multiplied by
+    // rstd(m) / col_prev[m], rstd = 1/sqrt(sum_b col_part[b][m] / K + col_eps);
+    // rstd is also written to col_rstd when set.
+    const float *col_part = nullptr;     // [K/128][norm_rows]
+    const float *col_prev = nullptr;     // [rows] the producer's pre-scale
+    float *col_rstd = nullptr;
+    float col_eps = 0.f;
 };
 // (cos, sin) of p * inv_freq[i] for every position p < max_len and i < half
 cudaError_t rope_table(const float *inv_freq, int half, int max_len, float2 *tab, cudaStream_t st);
@@ -105,8 +120,10 @@ cudaError_t reduce_splits(const float *part, int splits, size_t n, float *y, cud
 
 // ---- per-token fused kernels ------------------------------------------------
 // h = dequant(embed[tok]);  xn = rmsnorm(h) * w   (xn permuted fp16)
+// rstd_out (optional): the per-token 1/sqrt(mean(h^2) + eps) of the normalisation
 cudaError_t embed_norm(const Q4Weight &embed, const int32_t *tok, int M, const float *norm_w,
-                       float eps, float *h, __half *xn, int ldx_rows, cudaStream_t st);
+                       float eps, float *h, __half *xn, int ldx_rows, cudaStream_t st,
+                       float *rstd_out = nullptr);
 // xn = rmsnorm(h) * w  (perm8 layout)
 cudaError_t rmsnorm(const float *h, int M, int H, const float *norm_w, float eps, __half *xn,
                     int ldx_rows, cudaStream_t st);

@@ -195,6 +195,7 @@ struct Smem {
     int last_flag2;
     float wsum2[4][4][16];      // [token group][row quarter][token]
     float xch2[2][ROWS * 16];   // [token group pair][row][token]
+    float cscale[128];          // folded RMSNorm: per-token column scale of the tail epilogue
 };
 
 // Stream-K schedule: the flattened (row block, k unit) space is split into
@@ -206,6 +207,36 @@ __device__ __forceinline__ int unit_owner(int u, int U, int G) {
     while (c + 1 < G && unit_begin(c + 1, U, G) <= u) ++c;
     while (c > 0 && unit_begin(c, U, G) > u) --c;
     return c;
+}
+
+// Folded RMSNorm, consumer side: the token operand rows are fp16(h * w * s[m])
+// with a pre-scale s (an earlier rstd of the same row); the accumulators of row m
+// are multiplied by rstd(m) / s[m], rstd from the producer's per-block sums of
+// squares (summed in block order).  Threads 0..NT-1 fill dst[] for x rows
+// xrow0..xrow0+NT-1 (rows past the operand give 0).
+__device__ __forceinline__ void fold_scale(const Q4Epilogue &ep, int K, int xrow0, int nrows, int t, float *dst,
+                                           int NT) {
+    if (t >= NT) return;
+    const int m = xrow0 + t;
+    float c = 0.f;
+    if (t < nrows) {
+        // 16 loads in flight per batch; summed in block order
+        const float prev = __ldcg(ep.col_prev + m);
+        const int nb = K / 128;
+        float ss = 0.f;
+        for (int b0 = 0; b0 < nb; b0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+                v[k] = b0 + k < nb ? __ldcg(ep.col_part + (size_t)(b0 + k) * ep.norm_rows + m) : 0.f;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) ss += v[k];
+        }
+        const float r = 1.0f / sqrtf(ss / (float)K + ep.col_eps);
+        if (ep.col_rstd) ep.col_rstd[m] = r;
+        c = r / prev;
+    }
+    dst[t] = c;
 }
 
 // bounded wait that gives up at once after an abort
@@ -370,6 +401,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
         const int is = g / C::GPI;               // issuer of this group
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         const int sw8 = r & 7;                   // 128B swizzle of this row
+        int ctile = -1;                          // token tile whose folded-norm scales are in cs.cscale
         // epilogue of one block segment by the sixteen dequantising warps
         auto seg_epilogue = [&](const int ub, const int lseg, const bool release) {
             constexpr int PIECES = NT <= 64 ? 1 : 2;      // 16-token pieces per token group
@@ -472,20 +504,63 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                     }
                 }
             }
+            if (ep.col_part && ctile != tile) {   // folded RMSNorm of the token operand
+                griddep_wait();
+                fold_scale(ep, K, tok_base + tile * NT, max(0, min(NT, M - tile * NT)), tid, cs.cscale, NT);
+                named_bar_sync(TAIL_BAR, TAIL_THREADS);
+                ctile = tile;
+            }
 #pragma unroll
             for (int p = 0; p < PIECES; ++p) {
                 const int cc = p * 64 + tg * 16;
                 const int m0 = tile * NT + cc;
                 const int mlim = cc < NT ? max(0, min(16, M - m0)) : 0;   // valid tokens in this piece
                 float *y = acc[p];
+                if (ep.col_part) {
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) y[q] *= cs.cscale[cc + q];
+                }
                 if constexpr (OP == Q4Epilogue::STORE) {
 #pragma unroll
                     for (int q = 0; q < 16; ++q)
                         if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] = y[q];
                 } else if constexpr (OP == Q4Epilogue::RESID) {
+                    // every load of the piece is issued before its first store (the
+                    // compiler cannot tell the pointers apart, so interleaving would
+                    // serialise one L2 round trip per token)
 #pragma unroll
-                    for (int q = 0; q < 16; ++q)
-                        if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] += y[q];
+                    for (int q = 0; q < 16; ++q) y[q] = q < mlim ? y[q] + ep.out[(size_t)(m0 + q) * ep.ldo + f] : 0.f;
+                    if (!ep.norm_w) {
+#pragma unroll
+                        for (int q = 0; q < 16; ++q)
+                            if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] = y[q];
+                    } else {
+                        // updated residual, the next linear's operand fp16(h * w * s), and
+                        // this block's sum of squares per token
+                        const float nw = ep.norm_w[f];
+                        float sv[16];
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) sv[q] = q < mlim ? __ldcg(ep.norm_scale + m0 + q) : 0.f;
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            const float v = y[q];
+                            if (q < mlim) {
+                                ep.out[(size_t)(m0 + q) * ep.ldo + f] = v;
+                                ep.xout[xblk(m0 + q, f, ep.ldx_rows)] = __float2half_rn(v * nw * sv[q]);
+                            }
+                            const float t2 = warp_sum(v * v);
+                            if (lane == q) cs.wsum2[tg][quarter][q] = t2;
+                        }
+                        named_bar_sync(TAIL_BAR, TAIL_THREADS);
+                        if (tid < 64) {
+                            const int tg2 = tid >> 4, q = tid & 15, cc2 = p * 64 + tg2 * 16;
+                            const int m = tile * NT + cc2 + q;
+                            if (cc2 < NT && m < M)
+                                ep.norm_part[(size_t)blk * ep.norm_rows + m] =
+                                    cs.wsum2[tg2][0][q] + cs.wsum2[tg2][1][q] + cs.wsum2[tg2][2][q] + cs.wsum2[tg2][3][q];
+                        }
+                        named_bar_sync(TAIL_BAR, TAIL_THREADS);
+                    }
                 } else if constexpr (OP == Q4Epilogue::SWIGLU) {
                     // rows [0,64) gate, [64,128) up of the same 64 outputs; token
                     // groups exchange through the buffer in two rounds of two
@@ -516,6 +591,17 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                     const int d = f % D;
                     const bool is_q = hh < ep.n_heads, is_k = !is_q && hh < ep.n_heads + ep.n_kv;
                     const float *nw = is_q ? ep.q_norm : (is_k ? ep.k_norm : nullptr);
+                    // cache row and position of the piece's tokens, staged once in shared
+                    // memory (the epilogue-warp buffer cs.xch is idle for QKV): the
+                    // stores below then wait on no global loads
+                    int *tok_pos = reinterpret_cast<int *>(cs.xch), *tok_row = tok_pos + 64;
+                    if (tid < 64) {
+                        const int tg2 = tid >> 4, q = tid & 15, cc2 = p * 64 + tg2 * 16;
+                        const int m = tile * NT + cc2 + q;
+                        const bool ok = cc2 < NT && m < M;
+                        tok_pos[tid] = ok ? ep.tpos[m] : 0;
+                        tok_row[tid] = ok ? ep.trow[m] : 0;
+                    }
                     if (nw) {
                         // per-head sum of squares for each token: warp shuffles + smem
 #pragma unroll
@@ -551,7 +637,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
 #pragma unroll
                             for (int q = 0; q < 16; ++q) {
                                 if (q >= mlim) break;
-                                const float2 csn = ep.rope[(size_t)ep.tpos[m0 + q] * half + d % half];
+                                const float2 csn = ep.rope[(size_t)tok_pos[tg * 16 + q] * half + d % half];
                                 const float sn = csn.y, cn = csn.x;
                                 const float pv = xch[pr * 16 + q];
                                 y[q] = d < half ? y[q] * cn - pv * sn : pv * sn + y[q] * cn;
@@ -569,7 +655,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                         } else {
                             const int kvh = is_k ? hh - ep.n_heads : hh - ep.n_heads - ep.n_kv;
                             dst = (is_k ? ep.kc : ep.vc) +
-                                  (((size_t)ep.trow[m] * ep.n_kv + kvh) * ep.max_len + ep.tpos[m]) * D;
+                                  (((size_t)tok_row[tg * 16 + q] * ep.n_kv + kvh) * ep.max_len + tok_pos[tg * 16 + q]) * D;
                         }
                         dst[d] = __float2half_rn(y[q]);
                     }
@@ -638,6 +724,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
         const int etid = tid - EP_WARP0 * 32;    // 0..127
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         int seg = 0, dset = 0;
+        int ctile = -1;                          // token tile whose folded-norm scales are in cs.xch
         for (int ub = u0 / nc; ub < (u1 - 1) / nc; ++ub, ++seg) {   // all but the last segment
             const int seg_first_unit = max(u0, ub * nc), seg_last_unit = min(u1 - 1, ub * nc + nc - 1);
             const bool full = seg_first_unit == ub * nc && seg_last_unit == ub * nc + nc - 1;
@@ -705,6 +792,12 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                 last = cs.last_flag;
             }
             if (!skip && last) {
+                if (ep.col_part && ctile != tile) {   // folded RMSNorm of the token operand (STORE only)
+                    griddep_wait();
+                    fold_scale(ep, K, tok_base + tile * NT, max(0, min(NT, M - tile * NT)), etid, cs.xch, NT);
+                    named_bar_sync(EPI_BAR, EP_THREADS);
+                    ctile = tile;
+                }
                 for (int p = 0; p < C::PIECES; ++p) {
                     float y[16];
                     if (full) {
@@ -737,14 +830,45 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                     }
                     const int m0 = tile * NT + p * 16;
                     const int mlim = max(0, min(16, M - m0));   // valid tokens in this piece
+                    if (ep.col_part) {
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) y[q] *= cs.xch[p * 16 + q];
+                    }
                     if constexpr (OP == Q4Epilogue::STORE) {
 #pragma unroll
                         for (int q = 0; q < 16; ++q)
                             if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] = y[q];
                     } else if constexpr (OP == Q4Epilogue::RESID) {
+                        // loads of the piece before its stores (see the tail epilogue)
 #pragma unroll
-                        for (int q = 0; q < 16; ++q)
-                            if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] += y[q];
+                        for (int q = 0; q < 16; ++q) y[q] = q < mlim ? y[q] + ep.out[(size_t)(m0 + q) * ep.ldo + f] : 0.f;
+                        if (!ep.norm_w) {
+#pragma unroll
+                            for (int q = 0; q < 16; ++q)
+                                if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] = y[q];
+                        } else {
+                            // updated residual, the next linear's operand fp16(h * w * s), and
+                            // this block's sum of squares per token
+                            const float nw = ep.norm_w[f];
+                            float sv[16];
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) sv[q] = q < mlim ? __ldcg(ep.norm_scale + m0 + q) : 0.f;
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) {
+                                const float v = y[q];
+                                if (q < mlim) {
+                                    ep.out[(size_t)(m0 + q) * ep.ldo + f] = v;
+                                    ep.xout[xblk(m0 + q, f, ep.ldx_rows)] = __float2half_rn(v * nw * sv[q]);
+                                }
+                                const float t2 = warp_sum(v * v);
+                                if (lane == q) cs.wsum[quarter][q] = t2;
+                            }
+                            named_bar_sync(EPI_BAR, EP_THREADS);
+                            if (etid < mlim)
+                                ep.norm_part[(size_t)blk * ep.norm_rows + m0 + etid] =
+                                    cs.wsum[0][etid] + cs.wsum[1][etid] + cs.wsum[2][etid] + cs.wsum[3][etid];
+                            named_bar_sync(EPI_BAR, EP_THREADS);
+                        }
                     } else if constexpr (OP == Q4Epilogue::SWIGLU) {
                         // rows [0,64) gate, [64,128) up of the same 64 outputs
                         if (r >= 64) {
@@ -907,6 +1031,10 @@ cudaError_t launch_op(const Q4WeightTC &w, const CUtensorMap &xmap, int M, int t
     const int pmax = q4_tc_pmax(U, G, nc);
     if (pmax > 1 && (!ep.part || !ep.counters)) return cudaErrorInvalidValue;
     if ((unsigned long long)U * (unsigned long long)(G + 1) >= (1ull << 32)) return cudaErrorInvalidValue;
+    if (OP == Q4Epilogue::RESID && ep.norm_w &&
+        (!ep.xout || !ep.norm_scale || !ep.norm_part || tok_base != 0 || M > ep.ldx_rows || M > ep.norm_rows))
+        return cudaErrorInvalidValue;
+    if (ep.col_part && (!ep.col_prev || w.K % 128 || tok_base + M > ep.norm_rows)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(G);
     cfg.blockDim = dim3(THREADS);

@@ -111,6 +111,10 @@ struct mlxcat_cache {
     float *h = nullptr, *part = nullptr, *logits = nullptr;
     float2 *rope = nullptr;           // (cos, sin) of every position x RoPE frequency
     __half *xn = nullptr, *xa = nullptr, *qbuf = nullptr;
+    __half *xg = nullptr;             // MLP input operand (blocked), written by the O projection
+    // folded RMSNorm: per-block sums of squares of h [H/128][rows], and the rstd of
+    // the attention-norm and MLP-norm inputs of each token row (pre-scales)
+    float *norm_part = nullptr, *r_attn = nullptr, *r_mlp = nullptr;
     size_t part_floats = 0;
     unsigned *counters = nullptr;     // split-K tickets of the q4 linear (self-resetting)
     unsigned long long *amax_part = nullptr;   // split argmax partial keys
@@ -269,7 +273,11 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
               I = cf.intermediate, L = cf.n_layers;
     const float eps = cf.rms_eps;
     const int R = c->m_cap;   // token rows of the blocked activation buffers
-    LK(ctx, embed_norm(ctx->embed.view(), tok, M, ctx->attn_norm(0), eps, c->h, c->xn, R, st));
+    // The RMSNorms between the linears are folded into them: a residual linear
+    // writes fp16(h * w * s) with s an earlier rstd of the row and the per-block
+    // sums of squares of h; the next linear scales its accumulators by rstd / s.
+    // Layer 0's input is normalised exactly here.
+    LK(ctx, embed_norm(ctx->embed.view(), tok, M, ctx->attn_norm(0), eps, c->h, c->xn, R, st, c->r_attn));
     Q4Epilogue ep;
     ep.part = c->part;
     ep.counters = c->counters;
@@ -284,6 +292,10 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
             e.n_heads = Hq; e.n_kv = Hkv; e.head_dim = D;
             e.q_norm = ctx->q_norm(l); e.k_norm = ctx->k_norm(l); e.eps = eps;
             e.inv_freq = ctx->inv_freq; e.rope = c->rope; e.trow = trow; e.tpos = tpos;
+            if (l > 0) {   // operand = down projection's fp16(h * attn_norm * r_mlp)
+                e.col_part = c->norm_part; e.col_prev = c->r_mlp; e.col_rstd = c->r_attn;
+                e.col_eps = eps; e.norm_rows = R;
+            }
             ProfScope ps(c, 0);
             LK(ctx, q4_tc(ctx->qkv[l].tc(), c->xn, R, 0, M, ctx->sm_count, e, st));
         }
@@ -294,28 +306,37 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
         {   // output projection into the residual stream
             Q4Epilogue e = ep;
             e.op = Q4Epilogue::RESID; e.out = c->h; e.ldo = H;
+            // + the MLP input fp16(h * mlp_norm * r_attn) (not into xn: other CTAs
+            // may still be reading this projection's own operand there)
+            e.norm_w = ctx->mlp_norm(l); e.norm_scale = c->r_attn; e.xout = c->xg; e.ldx_rows = R;
+            e.norm_part = c->norm_part; e.norm_rows = R;
             ProfScope ps(c, 0);
             LK(ctx, q4_tc(ctx->o[l].tc(), c->xn, R, 0, M, ctx->sm_count, e, st));
         }
-        LK(ctx, rmsnorm(c->h, M, H, ctx->mlp_norm(l), eps, c->xn, R, st));
         {   // gate/up + SwiGLU
             Q4Epilogue e = ep;
             e.op = Q4Epilogue::SWIGLU; e.xout = c->xa; e.ldx_rows = R;
+            e.col_part = c->norm_part; e.col_prev = c->r_attn; e.col_rstd = c->r_mlp;
+            e.col_eps = eps; e.norm_rows = R;
             ProfScope ps(c, 0);
-            LK(ctx, q4_tc(ctx->gu[l].tc(), c->xn, R, 0, M, ctx->sm_count, e, st));
+            LK(ctx, q4_tc(ctx->gu[l].tc(), c->xg, R, 0, M, ctx->sm_count, e, st));
         }
         {   // down projection into the residual stream
             Q4Epilogue e = ep;
             e.op = Q4Epilogue::RESID; e.out = c->h; e.ldo = H;
+            // + the next layer's (or the head's) input fp16(h * norm * r_mlp)
+            e.norm_w = l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(); e.norm_scale = c->r_mlp;
+            e.xout = c->xn; e.ldx_rows = R;
+            e.norm_part = c->norm_part; e.norm_rows = R;
             ProfScope ps(c, 0);
             LK(ctx, q4_tc(ctx->down[l].tc(), c->xa, R, 0, M, ctx->sm_count, e, st));
         }
-        LK(ctx, rmsnorm(c->h, M, H, l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(), eps, c->xn, R, st));
     }
     if (lg_from < M) {
         const DevLin &head = cf.tie_embeddings ? ctx->embed : ctx->lm_head;
         Q4Epilogue e = ep;
         e.op = Q4Epilogue::STORE; e.out = c->logits; e.ldo = cf.vocab;
+        e.col_part = c->norm_part; e.col_prev = c->r_mlp; e.col_eps = eps; e.norm_rows = R;
         ProfScope ps(c, 0);
         LK(ctx, q4_tc(head.tc(), c->xn, R, lg_from, M - lg_from, ctx->sm_count, e, st));
     }
@@ -701,6 +722,10 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
         chk(dalloc(A, &c->h, (size_t)Mc * H));
         chk(dalloc(A, &c->xn, (size_t)Mc * xw));
         chk(dalloc(A, &c->xa, (size_t)Mc * I));
+        chk(dalloc(A, &c->xg, (size_t)Mc * H));
+        chk(dalloc(A, &c->norm_part, (size_t)Mc * ((H + 127) / 128)));
+        chk(dalloc(A, &c->r_attn, (size_t)Mc));
+        chk(dalloc(A, &c->r_mlp, (size_t)Mc));
         chk(dalloc(A, &c->qbuf, (size_t)Mc * Hq * D));
         chk(dalloc(A, &c->rope, (size_t)max_len * (D / 2)));
         if (rc == MLXCAT_OK) chk(rope_table(ctx->inv_freq, D / 2, max_len, c->rope, ctx->stream));
