@@ -196,6 +196,7 @@ struct Smem {
     float wsum2[4][4][16];      // [token group][row quarter][token]
     float xch2[2][ROWS * 16];   // [token group pair][row][token]
     float cscale[128];          // folded RMSNorm: per-token column scale of the tail epilogue
+    int cscale_tile;            // token tile whose scales the idle epilogue warps put in cscale
 };
 
 // Stream-K schedule: the flattened (row block, k unit) space is split into
@@ -289,6 +290,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
             tc::mbar_init(tc::smem_u32(&cs.d_free[d]), EPW ? 4 : DQ_WARPS);
         }
         cs.abort_flag = 0;
+        cs.cscale_tile = -1;
         tc::fence_barrier_init();
         tc::prefetch_tmap(&wmap);
         tc::prefetch_tmap(&xmap);
@@ -505,9 +507,26 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                 }
             }
             if (ep.col_part && ctile != tile) {   // folded RMSNorm of the token operand
-                griddep_wait();
-                fold_scale(ep, K, tok_base + tile * NT, max(0, min(NT, M - tile * NT)), tid, cs.cscale, NT);
-                named_bar_sync(TAIL_BAR, TAIL_THREADS);
+                bool have = false;
+                if constexpr (!EPW) {
+                    // the idle epilogue warps computed the first tile's scales during
+                    // the main loop (bounded wait for their flag)
+                    if (tid == 0) {
+                        const uint64_t t0 = tc::global_ns();
+                        while (*reinterpret_cast<volatile int *>(&cs.cscale_tile) < 0)
+                            if (tc::global_ns() - t0 > tc::WAIT_LIMIT_NS) {
+                                if (ep.err) atomicExch(ep.err, ERR_DFREE);
+                                break;
+                            }
+                    }
+                    named_bar_sync(TAIL_BAR, TAIL_THREADS);
+                    have = *reinterpret_cast<volatile int *>(&cs.cscale_tile) == tile;
+                }
+                if (!have) {
+                    griddep_wait();
+                    fold_scale(ep, K, tok_base + tile * NT, max(0, min(NT, M - tile * NT)), tid, cs.cscale, NT);
+                    named_bar_sync(TAIL_BAR, TAIL_THREADS);
+                }
                 ctile = tile;
             }
 #pragma unroll
@@ -591,6 +610,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                     const int d = f % D;
                     const bool is_q = hh < ep.n_heads, is_k = !is_q && hh < ep.n_heads + ep.n_kv;
                     const float *nw = is_q ? ep.q_norm : (is_k ? ep.k_norm : nullptr);
+                    const float nwd = nw ? nw[d] : 1.f;   // issued early: its latency overlaps the sums
                     // cache row and position of the piece's tokens, staged once in shared
                     // memory (the epilogue-warp buffer cs.xch is idle for QKV): the
                     // stores below then wait on no global loads
@@ -611,14 +631,23 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                         }
                     }
                     named_bar_sync(TAIL_BAR, TAIL_THREADS);
-                    if (nw) {
-                        const int wpk = D / 32, w0 = (quarter / wpk) * wpk;
-#pragma unroll
-                        for (int q = 0; q < 16; ++q) {
+                    if (ep.q_norm || ep.k_norm) {
+                        // one thread per (token group, head of the block, token) turns the
+                        // head's sum of squares into its rstd, kept in the head's first
+                        // quarter slot; the head's rows then only multiply
+                        const int wpk = D / 32, hpb = 4 / wpk;   // quarters per head, heads per block
+                        if (tid < 4 * hpb * 16) {
+                            const int tg2 = tid / (hpb * 16), hq = (tid / 16) % hpb, q = tid & 15;
                             float ss = 0.f;
-                            for (int ww = w0; ww < w0 + wpk; ++ww) ss += cs.wsum2[tg][ww][q];
-                            y[q] = y[q] * (1.0f / sqrtf(ss / (float)D + ep.eps)) * nw[d];
+                            for (int ww = hq * wpk; ww < hq * wpk + wpk; ++ww) ss += cs.wsum2[tg2][ww][q];
+                            cs.wsum2[tg2][hq * wpk][q] = 1.0f / sqrtf(ss / (float)D + ep.eps);
                         }
+                        named_bar_sync(TAIL_BAR, TAIL_THREADS);
+                    }
+                    if (nw) {
+                        const int w0 = (quarter / (D / 32)) * (D / 32);
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) y[q] = y[q] * cs.wsum2[tg][w0][q] * nwd;
                     }
                     // rotate-half RoPE on q and k: partner row r +- D/2, exchanged
                     // through the buffer in two rounds of two token groups
@@ -716,6 +745,20 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
             const bool last_seg = j == nsub - 1;
             if (!(EPW && !last_seg)) seg_epilogue(ub, seg, !last_seg);
             ++seg;
+        }
+    } else if (!EPW && warp >= EP_WARP0) {
+        // idle in QKV and SWIGLU: the folded-norm scales of the first token tile,
+        // computed while the main loop runs (the tail epilogue picks them up)
+        if (ep.col_part) {
+            const int et = tid - EP_WARP0 * 32;
+            const int tile0 = u0 / (nblk * nc);
+            griddep_wait();   // the sums of squares come from the previous kernel
+            fold_scale(ep, K, tok_base + tile0 * NT, max(0, min(NT, M - tile0 * NT)), et, cs.cscale, NT);
+            named_bar_sync(EPI_BAR, EP_THREADS);
+            if (et == 0) {
+                __threadfence_block();
+                *reinterpret_cast<volatile int *>(&cs.cscale_tile) = tile0;
+            }
         }
     } else if (EPW && warp >= EP_WARP0) {
         // ---------------- epilogue warps: one thread per row, all tokens ----------------
@@ -1035,6 +1078,8 @@ cudaError_t launch_op(const Q4WeightTC &w, const CUtensorMap &xmap, int M, int t
         (!ep.xout || !ep.norm_scale || !ep.norm_part || tok_base != 0 || M > ep.ldx_rows || M > ep.norm_rows))
         return cudaErrorInvalidValue;
     if (ep.col_part && (!ep.col_prev || w.K % 128 || tok_base + M > ep.norm_rows)) return cudaErrorInvalidValue;
+    // the QKV epilogue keeps every head inside one 128-row block
+    if (OP == Q4Epilogue::QKV && (ep.head_dim < 32 || ROWS % ep.head_dim)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(G);
     cfg.blockDim = dim3(THREADS);
