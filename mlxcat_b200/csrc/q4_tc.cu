@@ -240,6 +240,27 @@ __device__ __forceinline__ void fold_scale(const Q4Epilogue &ep, int K, int xrow
     dst[t] = c;
 }
 
+// Sums over the warp of sixteen per-lane values (one per token of a piece) in
+// 16 shuffles instead of 16 x 5: at each of five butterfly steps a lane keeps
+// the half of its tokens picked by one lane bit and adds the partner's copy of
+// that half.  Returns the total of token (lane >> 1) & 15 (held by both lanes of
+// a pair); the summation order is fixed.
+__device__ __forceinline__ float warp_sum16(const float *v, int lane) {
+    float a[8], b[4], c[2];
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        a[i] = (b4 ? v[i + 8] : v[i]) + __shfl_xor_sync(0xffffffffu, b4 ? v[i] : v[i + 8], 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        b[i] = (b3 ? a[i + 4] : a[i]) + __shfl_xor_sync(0xffffffffu, b3 ? a[i] : a[i + 4], 8);
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+        c[i] = (b2 ? b[i + 2] : b[i]) + __shfl_xor_sync(0xffffffffu, b2 ? b[i] : b[i + 2], 4);
+    float d = (b1 ? c[1] : c[0]) + __shfl_xor_sync(0xffffffffu, b1 ? c[0] : c[1], 2);
+    return d + __shfl_xor_sync(0xffffffffu, d, 1);
+}
+
 // bounded wait that gives up at once after an abort
 __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int *abort_flag, int *err,
                                               int code) {
@@ -413,6 +434,18 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
             const bool full = seg_first_unit == ub * nc && seg_last_unit == ub * nc + nc - 1;
             const int tile = ub / nblk, blk = ub - tile * nblk;
             const int f = blk * ROWS + r;
+            if constexpr (OP == Q4Epilogue::RESID) {
+                // the residual rows this thread will update: into L1 while the
+                // partials are exchanged
+#pragma unroll
+                for (int p = 0; p < PIECES; ++p) {
+                    const int cc = p * 64 + tg * 16, m0 = tile * NT + cc;
+                    const int mlim = cc < NT ? max(0, min(16, M - m0)) : 0;
+#pragma unroll
+                    for (int q = 0; q < 16; ++q)
+                        if (q < mlim) asm volatile("prefetch.global.L1 [%0];" ::"l"(ep.out + (size_t)(m0 + q) * ep.ldo + f));
+                }
+            }
             bool bad = *abort_flag != 0;
             if (lane == 0 && !bad)
                 bad = !wait_or_abort(tc::smem_u32(&cs.d_full[ldset]), (lseg / C::DSETS) & 1, abort_flag, ep.err,
@@ -560,6 +593,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                         float sv[16];
 #pragma unroll
                         for (int q = 0; q < 16; ++q) sv[q] = q < mlim ? __ldcg(ep.norm_scale + m0 + q) : 0.f;
+                        float sq[16];
 #pragma unroll
                         for (int q = 0; q < 16; ++q) {
                             const float v = y[q];
@@ -567,9 +601,10 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                                 ep.out[(size_t)(m0 + q) * ep.ldo + f] = v;
                                 ep.xout[xblk(m0 + q, f, ep.ldx_rows)] = __float2half_rn(v * nw * sv[q]);
                             }
-                            const float t2 = warp_sum(v * v);
-                            if (lane == q) cs.wsum2[tg][quarter][q] = t2;
+                            sq[q] = v * v;
                         }
+                        const float t2 = warp_sum16(sq, lane);
+                        if (!(lane & 1)) cs.wsum2[tg][quarter][(lane >> 1) & 15] = t2;
                         named_bar_sync(TAIL_BAR, TAIL_THREADS);
                         if (tid < 64) {
                             const int tg2 = tid >> 4, q = tid & 15, cc2 = p * 64 + tg2 * 16;
@@ -624,11 +659,11 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                     }
                     if (nw) {
                         // per-head sum of squares for each token: warp shuffles + smem
+                        float sq[16];
 #pragma unroll
-                        for (int q = 0; q < 16; ++q) {
-                            const float t2 = warp_sum(y[q] * y[q]);
-                            if (lane == q) cs.wsum2[tg][quarter][q] = t2;
-                        }
+                        for (int q = 0; q < 16; ++q) sq[q] = y[q] * y[q];
+                        const float t2 = warp_sum16(sq, lane);
+                        if (!(lane & 1)) cs.wsum2[tg][quarter][(lane >> 1) & 15] = t2;
                     }
                     named_bar_sync(TAIL_BAR, TAIL_THREADS);
                     if (ep.q_norm || ep.k_norm) {
@@ -896,6 +931,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                             float sv[16];
 #pragma unroll
                             for (int q = 0; q < 16; ++q) sv[q] = q < mlim ? __ldcg(ep.norm_scale + m0 + q) : 0.f;
+                            float sq[16];
 #pragma unroll
                             for (int q = 0; q < 16; ++q) {
                                 const float v = y[q];
@@ -903,9 +939,10 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                                     ep.out[(size_t)(m0 + q) * ep.ldo + f] = v;
                                     ep.xout[xblk(m0 + q, f, ep.ldx_rows)] = __float2half_rn(v * nw * sv[q]);
                                 }
-                                const float t2 = warp_sum(v * v);
-                                if (lane == q) cs.wsum[quarter][q] = t2;
+                                sq[q] = v * v;
                             }
+                            const float t2 = warp_sum16(sq, lane);
+                            if (!(lane & 1)) cs.wsum[quarter][(lane >> 1) & 15] = t2;
                             named_bar_sync(EPI_BAR, EP_THREADS);
                             if (etid < mlim)
                                 ep.norm_part[(size_t)blk * ep.norm_rows + m0 + etid] =
