@@ -24,7 +24,7 @@ namespace mlxcat {
 namespace {
 
 constexpr int KB = 32;       // keys per staged block
-constexpr int KSTAGES = 2;   // cp.async ring depth (blocks in flight)
+constexpr int KSTAGES = 3;   // cp.async ring depth (blocks in flight)
 
 __device__ __forceinline__ void mma16816(float *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
     asm volatile(

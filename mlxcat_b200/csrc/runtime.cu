@@ -28,7 +28,7 @@ namespace {
 
 constexpr int PREFILL_CHUNK = 128;   // prompt tokens per prefill forward
 constexpr int PREFILL_QG = 8;        // prompt tokens per attention group
-constexpr int KEY_CHUNK = 256;       // keys per attention split
+constexpr int KEY_CHUNK = 384;       // keys per attention split (3-deep ring, one wave at the verify shape)
 
 thread_local std::string g_op_err;
 
