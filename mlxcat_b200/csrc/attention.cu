@@ -306,17 +306,39 @@ __global__ void attn_combine_kernel(const float *__restrict__ o_part, const floa
     const size_t it0 = ((size_t)grp * Hkv + h) * P;
     const int KO = Hq * D;
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        float mmax = -INFINITY;
-        for (int p = 0; p < P; ++p) mmax = fmaxf(mmax, ml_part[((it0 + p) * QROWS + qi) * 2]);
-        float num = 0.f, den = 0.f;
-        if (mmax != -INFINITY) {
-            for (int p = 0; p < P; ++p) {
-                const float mp = ml_part[((it0 + p) * QROWS + qi) * 2];
-                if (mp == -INFINITY) continue;
-                const float w = exp2f(mp - mmax);
-                den += w * ml_part[((it0 + p) * QROWS + qi) * 2 + 1];
-                num += w * o_part[((it0 + p) * QROWS + qi) * D + d];
+        // splits in batches of PB whose loads are all issued before any is used
+        // (one L2 round trip per batch); a running max rescales across batches,
+        // and with P <= PB the sums are exactly the two-pass ones
+        constexpr int PB = 8;
+        float num = 0.f, den = 0.f, mrun = -INFINITY;
+        for (int p0 = 0; p0 < P; p0 += PB) {
+            float m[PB], l[PB], v[PB];
+#pragma unroll
+            for (int k = 0; k < PB; ++k) {
+                m[k] = -INFINITY; l[k] = 0.f; v[k] = 0.f;
+                if (p0 + k < P) {
+                    const float2 ml = *reinterpret_cast<const float2 *>(ml_part + ((it0 + p0 + k) * QROWS + qi) * 2);
+                    m[k] = ml.x; l[k] = ml.y;
+                    v[k] = o_part[((it0 + p0 + k) * QROWS + qi) * D + d];
+                }
             }
+            float mb = mrun;
+#pragma unroll
+            for (int k = 0; k < PB; ++k) mb = fmaxf(mb, m[k]);
+            if (mb == -INFINITY) continue;
+            if (mrun != -INFINITY && mrun != mb) {
+                const float a = exp2f(mrun - mb);
+                num *= a;
+                den *= a;
+            }
+#pragma unroll
+            for (int k = 0; k < PB; ++k) {
+                if (m[k] == -INFINITY) continue;
+                const float w = exp2f(m[k] - mb);
+                den += w * l[k];
+                num += w * v[k];
+            }
+            mrun = mb;
         }
         const float r = den > 0.f ? num / den : 0.f;
         const int j = qi / G, gh = qi - j * G;
