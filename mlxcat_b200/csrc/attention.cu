@@ -58,7 +58,8 @@ __global__ void __launch_bounds__(QT * 64, 8 / QT)
 attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
             const __half *__restrict__ vc, int max_len, const int32_t *__restrict__ trow,
             const int32_t *__restrict__ tpos, int M, int qg, int Hq, int Hkv, int key_chunk,
-            int splits, float scale_log2, float *__restrict__ o_part, float *__restrict__ ml_part) {
+            int splits, float scale_log2, float *__restrict__ o_part, float *__restrict__ ml_part,
+            int early_kv) {
     constexpr int QROWS = QT * 16;
     constexpr int PITCH = D + 8;               // halves
     constexpr int NTHREADS = QT * 64;
@@ -70,7 +71,12 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
     constexpr int NU = KPW / 16, NN = KPW / 8;
 
     griddep_launch_dependents();   // the combine pass may be scheduled
-    griddep_wait();                // queries and the new K/V come from the previous kernel
+    // Inside the verify forward (early_kv) token rows and positions are inputs of
+    // the forward and keys below the row's first position in this launch were
+    // written by earlier forwards, so they are read before waiting for the
+    // previous kernel (the QKV projection), which writes only the queries and the
+    // new keys.  Otherwise everything waits for the previous kernel.
+    if (!early_kv) griddep_wait();
     const int grp = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
     const int G = Hq / Hkv;
     const int t0 = grp * qg;
@@ -88,9 +94,15 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
     float *mlp = ml_part + item * QROWS * 2;
 
     if (kb >= ke) {
+        griddep_wait();   // the previous launch's combine may still read this scratch
         for (int i = threadIdx.x; i < QROWS * 2; i += NTHREADS) mlp[i] = (i & 1) ? 0.f : -INFINITY;
         return;
     }
+    // first position of this row written by this launch (prefill puts several
+    // groups of one row in a launch)
+    int new_lo = pos0;
+    for (int gg = 0; gg * qg < M; ++gg)
+        if (trow[gg * qg] == row) new_lo = min(new_lo, tpos[gg * qg]);
 
     const __half *kbase = kc + ((size_t)row * Hkv + h) * max_len * D;
     const __half *vbase = vc + ((size_t)row * Hkv + h) * max_len * D;
@@ -99,13 +111,15 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
     const uint32_t vs_a = (uint32_t)__cvta_generic_to_shared(vs);
 
     // stage Q: row qi = j*G + gh -> token t0+j, head h*G+gh
-    for (int v = threadIdx.x; v < QROWS * (D / 8); v += NTHREADS) {
-        const int qi = v / (D / 8), c8 = v - qi * (D / 8);
-        const int j = qi / G, gh = qi - j * G;
-        const bool ok = qi < NQ;
-        const __half *src = qbuf + ((size_t)(ok ? t0 + j : t0) * Hq + h * G + (ok ? gh : 0)) * D + c8 * 8;
-        cp16(qs_a + (uint32_t)(qi * PITCH + c8 * 8) * 2, src, ok ? 16 : 0);
-    }
+    auto stage_q = [&]() {
+        for (int v = threadIdx.x; v < QROWS * (D / 8); v += NTHREADS) {
+            const int qi = v / (D / 8), c8 = v - qi * (D / 8);
+            const int j = qi / G, gh = qi - j * G;
+            const bool ok = qi < NQ;
+            const __half *src = qbuf + ((size_t)(ok ? t0 + j : t0) * Hq + h * G + (ok ? gh : 0)) * D + c8 * 8;
+            cp16(qs_a + (uint32_t)(qi * PITCH + c8 * 8) * 2, src, ok ? 16 : 0);
+        }
+    };
     auto stage_kv = [&](int blk, int buf) {
         const int key0 = kb + blk * KB;
         for (int v = threadIdx.x; v < KB * (D / 8); v += NTHREADS) {
@@ -119,9 +133,19 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
         }
     };
     const int nblk = (ke - kb + KB - 1) / KB;
+    // prologue: the first blocks, those holding only older keys before the wait
+    // (they join the first cp.async group, with Q and block 0)
+    bool pre[KSTAGES - 1];
 #pragma unroll
-    for (int p = 0; p < KSTAGES - 1; ++p) {   // prologue: the first blocks (Q rides with block 0)
-        if (p < nblk) stage_kv(p, p);
+    for (int p = 0; p < KSTAGES - 1; ++p) {
+        pre[p] = early_kv && p < nblk && kb + (p + 1) * KB <= new_lo;
+        if (pre[p]) stage_kv(p, p);
+    }
+    griddep_wait();                // queries and the new K/V come from the previous kernel
+    stage_q();
+#pragma unroll
+    for (int p = 0; p < KSTAGES - 1; ++p) {
+        if (p < nblk && !pre[p]) stage_kv(p, p);
         cp_commit();
     }
 
@@ -350,7 +374,7 @@ __global__ void attn_combine_kernel(const float *__restrict__ o_part, const floa
 template <int QT, int D>
 cudaError_t launch_attn(const __half *qbuf, KVLayer kv, const int32_t *trow, const int32_t *tpos,
                         int M, int qg, int Hq, int Hkv, int key_chunk, int splits,
-                        AttnScratch sc, __half *out, bool permuted, int out_rows, cudaStream_t st) {
+                        AttnScratch sc, __half *out, bool permuted, int out_rows, bool early_kv, cudaStream_t st) {
     constexpr int PITCH = D + 8;
     const size_t smem = std::max((size_t)(QT * 16 + 2 * KSTAGES * KB) * PITCH * 2,
                                  (size_t)QT * 16 * (D + 2) * 4);   // K/V ring, then the split merge
@@ -367,7 +391,7 @@ cudaError_t launch_attn(const __half *qbuf, KVLayer kv, const int32_t *trow, con
     dim3 grid(groups, Hkv, splits);
     const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
     cudaError_t e = launch_pdl(attn_kernel<QT, D>, grid, dim3(QT * 64), smem, st, qbuf, kv.k, kv.v, kv.max_len,
-                               trow, tpos, M, qg, Hq, Hkv, key_chunk, splits, scale_log2, sc.o, sc.ml);
+                               trow, tpos, M, qg, Hq, Hkv, key_chunk, splits, scale_log2, sc.o, sc.ml, early_kv ? 1 : 0);
     if (e != cudaSuccess) return e;
     dim3 g2(groups, Hkv, QT * 16);
     return launch_pdl(attn_combine_kernel<QT>, g2, dim3(D), 0, st, (const float *)sc.o, (const float *)sc.ml, M, qg,
@@ -390,19 +414,19 @@ size_t attention_scratch_items(int groups, int n_kv, int splits) {
 cudaError_t attention(const __half *qbuf, KVLayer kv, const int32_t *trow, const int32_t *tpos,
                       int M, int qg, int n_heads, int n_kv, int D, int key_chunk, int splits,
                       AttnScratch scratch, __half *out, bool permuted_out, int out_rows,
-                      cudaStream_t st) {
+                      cudaStream_t st, bool early_kv) {
     if (key_chunk % KB || n_heads % n_kv) return cudaErrorInvalidValue;
     const int nq = qg * (n_heads / n_kv);
     const int groups = (M + qg - 1) / qg;
     if (attention_scratch_items(groups, n_kv, splits) > scratch.items) return cudaErrorInvalidValue;
     if (D == 128) {
-        if (nq <= 16) return launch_attn<1, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, st);
-        if (nq <= 32) return launch_attn<2, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, st);
-        if (nq <= 64) return launch_attn<4, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, st);
+        if (nq <= 16) return launch_attn<1, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, early_kv, st);
+        if (nq <= 32) return launch_attn<2, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, early_kv, st);
+        if (nq <= 64) return launch_attn<4, 128>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, early_kv, st);
     } else if (D == 64) {
-        if (nq <= 16) return launch_attn<1, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, st);
-        if (nq <= 32) return launch_attn<2, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, st);
-        if (nq <= 64) return launch_attn<4, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, st);
+        if (nq <= 16) return launch_attn<1, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, early_kv, st);
+        if (nq <= 32) return launch_attn<2, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, early_kv, st);
+        if (nq <= 64) return launch_attn<4, 64>(qbuf, kv, trow, tpos, M, qg, n_heads, n_kv, key_chunk, splits, scratch, out, permuted_out, out_rows, early_kv, st);
     }
     return cudaErrorInvalidValue;
 }

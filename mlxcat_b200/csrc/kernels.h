@@ -157,7 +157,9 @@ int attention_qrows(int qg, int n_heads, int n_kv);
 cudaError_t attention(const __half *qbuf, KVLayer kv, const int32_t *trow, const int32_t *tpos,
                       int M, int qg, int n_heads, int n_kv, int D, int key_chunk, int splits,
                       AttnScratch scratch, __half *out, bool permuted_out, int out_rows,
-                      cudaStream_t st);
+                      cudaStream_t st, bool early_kv = false);
+// early_kv: the launch follows the QKV projection of the same forward, so cached
+// keys older than the launch's tokens may be read before waiting for it
 
 // ---- lm head / sampling ----------------------------------------------------
 // argmax of each row of logits [M][V]; with scratch (part: argmax_scratch_words(M)

@@ -302,7 +302,7 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
         ctx->launches++;  // attention is two kernels
         { ProfScope ps(c, 1);
           LK(ctx, attention(c->qbuf, kv, trow, tpos, M, qg, Hq, Hkv, D, KEY_CHUNK, c->attn_splits,
-                            c->attn, c->xn, true, R, st)); }
+                            c->attn, c->xn, true, R, st, true)); }
         {   // output projection into the residual stream
             Q4Epilogue e = ep;
             e.op = Q4Epilogue::RESID; e.out = c->h; e.ldo = H;
