@@ -54,6 +54,11 @@ typedef struct {
     int32_t qk_norm;              /* Qwen3 per-head q/k RMSNorm             */
     float rms_eps, rope_theta;
     int32_t group_size, bits;     /* must be 64 and 4 (MLX affine q4 g64)   */
+    /* Sparse MoE MLP in every layer (Qwen3-MoE, mlx-swift-lm's SwitchGLU
+     * block) when n_experts > 0: bf16 router [n_experts][hidden], top_k
+     * experts per token, each a q4 SwiGLU of width `intermediate`;
+     * norm_topk renormalises the k routing weights.  0 = dense MLP. */
+    int32_t n_experts, top_k, norm_topk;
 } mlxcat_model_config;
 
 /* SamplingParameters subset on the path (Sampling.swift:139-217). */
@@ -98,13 +103,21 @@ MLXCAT_API int64_t mlxcat_ctx_launch_count(const mlxcat_ctx *ctx);
 /* ---- weights ---------------------------------------------------------------
  * replaces: MLX QuantizedLinear / QuantizedEmbedding parameter loading.
  * tensor ids: layer*16 + {0 q,1 k,2 v,3 o,4 gate,5 up,6 down},
- * 0xFFFF0000 embedding, 0xFFFF0001 lm_head (untied only). */
+ * 0xFFFF0000 embedding, 0xFFFF0001 lm_head (untied only).
+ * MoE models: layer*16 + 7 is the bf16 router [n_experts][hidden]
+ * (mlxcat_weights_set_bf16); expert tensors are
+ * MLXCAT_TENSOR_EXPERT(layer, expert, {0 gate, 1 up, 2 down}) (q4). */
+#define MLXCAT_TENSOR_EXPERT(layer, expert, kind) \
+    (0x40000000u | ((uint32_t)(layer) << 12) | ((uint32_t)(expert) << 2) | (uint32_t)(kind))
 MLXCAT_API int mlxcat_weights_synth(mlxcat_ctx *ctx, uint64_t seed, float stddev);
 MLXCAT_API int mlxcat_weights_set_q4(mlxcat_ctx *ctx, uint32_t tensor_id, const uint32_t *wq,
                           const uint16_t *scales, const uint16_t *biases);
 MLXCAT_API int mlxcat_weights_get_q4(mlxcat_ctx *ctx, uint32_t tensor_id, uint32_t *wq, uint16_t *scales,
                           uint16_t *biases);
 MLXCAT_API int mlxcat_weights_set_table(mlxcat_ctx *ctx, const int32_t *next_token, int32_t vocab);
+/* bf16 tensors (the MoE router, id layer*16 + 7): [n_experts][hidden] */
+MLXCAT_API int mlxcat_weights_set_bf16(mlxcat_ctx *ctx, uint32_t tensor_id, const uint16_t *w);
+MLXCAT_API int mlxcat_weights_get_bf16(mlxcat_ctx *ctx, uint32_t tensor_id, uint16_t *w);
 /* bytes of q4 weights one forward streams (packed words + scales + biases) */
 MLXCAT_API int64_t mlxcat_weights_bytes(const mlxcat_ctx *ctx);
 
@@ -197,6 +210,24 @@ MLXCAT_API int mlxcat_op_attention(const uint16_t *q, const uint16_t *k_cache, c
                         int32_t max_len, const int32_t *trow, const int32_t *tpos, int32_t M,
                         int32_t qg, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                         uint16_t *out, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Sparse MoE MLP: the SwitchGLU block of mlx-swift-lm's Qwen3-MoE model
+ * (un-vendored) that the verify forward (BatchGenerator.swift:900) runs in
+ * every layer of a MoE model, on an already normalised input x [M][hidden]
+ * fp16.  router: bf16 [n_experts][hidden]; wq/scales/biases[0..2]: gate and up
+ * [n_experts][intermediate][hidden/8] and down [n_experts][hidden][intermediate/8]
+ * (the MLX SwitchLinear layout; scales/biases [n_experts][N][K/64]).
+ * Routing: bf16 logits, fp32 softmax, top_k largest (ties to the lower
+ * index), weights renormalised over the k when norm_topk.
+ * y [M][hidden] fp32 = sum_j w_j down_e(silu(gate_e x) * up_e x); ids and
+ * weights [M][top_k] (each may be NULL) receive the routing. */
+MLXCAT_API size_t mlxcat_op_moe_workspace(int32_t M, int32_t hidden, int32_t intermediate, int32_t n_experts,
+                                          int32_t top_k);
+MLXCAT_API int mlxcat_op_moe(const uint16_t *x, int32_t M, int32_t hidden, int32_t intermediate,
+                             int32_t n_experts, int32_t top_k, int32_t norm_topk, const uint16_t *router,
+                             const uint32_t *const wq[3], const uint16_t *const scales[3],
+                             const uint16_t *const biases[3], float *y, int32_t *ids, float *weights,
+                             void *workspace, size_t workspace_bytes, void *stream);
 
 /* No counterpart in the reference: the attention operator above for callers
  * that cannot allocate device memory.  Same arguments and result as

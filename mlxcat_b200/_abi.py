@@ -35,6 +35,7 @@ class ModelConfigC(C.Structure):
         ("intermediate", C.c_int32), ("vocab", C.c_int32), ("tie_embeddings", C.c_int32),
         ("qk_norm", C.c_int32), ("rms_eps", C.c_float), ("rope_theta", C.c_float),
         ("group_size", C.c_int32), ("bits", C.c_int32),
+        ("n_experts", C.c_int32), ("top_k", C.c_int32), ("norm_topk", C.c_int32),
     ]
 
 
@@ -72,6 +73,7 @@ class RowsC(C.Structure):
 
 # name -> (restype, argtypes)
 _vp, _i32, _u32, _u64, _f32, _sz = C.c_void_p, C.c_int32, C.c_uint32, C.c_uint64, C.c_float, C.c_size_t
+_vp3 = C.c_void_p * 3   # const T *const [3]: gate, up, down
 PROTOTYPES = {
     "mlxcat_ctx_create": (C.c_int, [C.POINTER(ModelConfigC), _i32, C.POINTER(_vp)]),
     "mlxcat_ctx_destroy": (C.c_int, [_vp]),
@@ -83,6 +85,8 @@ PROTOTYPES = {
     "mlxcat_weights_set_q4": (C.c_int, [_vp, _u32, _vp, _vp, _vp]),
     "mlxcat_weights_get_q4": (C.c_int, [_vp, _u32, _vp, _vp, _vp]),
     "mlxcat_weights_set_table": (C.c_int, [_vp, _vp, _i32]),
+    "mlxcat_weights_set_bf16": (C.c_int, [_vp, _u32, _vp]),
+    "mlxcat_weights_get_bf16": (C.c_int, [_vp, _u32, _vp]),
     "mlxcat_weights_bytes": (C.c_int64, [_vp]),
     "mlxcat_cache_create": (C.c_int, [_vp, _i32, _i32, C.POINTER(_vp)]),
     "mlxcat_cache_destroy": (C.c_int, [_vp]),
@@ -112,6 +116,9 @@ PROTOTYPES = {
     "mlxcat_op_attention_noalloc": (C.c_int, [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32,
                                               _i32, _vp, _vp]),
     "mlxcat_op_synth_q4": (C.c_int, [_u64, _u32, _f32, _i32, _i32, _vp, _vp, _vp, _vp]),
+    "mlxcat_op_moe_workspace": (_sz, [_i32, _i32, _i32, _i32, _i32]),
+    "mlxcat_op_moe": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp3, _vp3, _vp3,
+                                _vp, _vp, _vp, _vp, _sz, _vp]),
     "mlxcat_op_draft": (C.c_int, [C.POINTER(RowsC), C.POINTER(SpecConfigC), _vp, _vp, _vp, _vp, _vp]),
     "mlxcat_op_accept_workspace": (_sz, [_i32, _i32]),
     "mlxcat_op_accept": (C.c_int, [C.POINTER(RowsC), C.POINTER(SpecConfigC), _vp, _vp, _vp, _i32,

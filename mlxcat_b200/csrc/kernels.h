@@ -5,6 +5,7 @@
 
 #include <utility>
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -142,6 +143,70 @@ cudaError_t qkv_epilogue(const float *part, int splits, int M, int n_heads, int 
                          __half *qbuf, KVLayer kv, cudaStream_t st);
 // xn[m][i] = silu(g) * u from partials [.., 2I] (gate rows first)
 cudaError_t swiglu(const float *part, int splits, int M, int I, __half *xn, cudaStream_t st);
+
+// ---- sparse MoE MLP (moe.cu) -------------------------------------------------
+// router GEMV (bf16 weights) + softmax + top-k; assignment a = m * TK + j of
+// token m's j-th expert is appended to exp_list[expert][slot] (exp_count must
+// start at zero; list_cap >= M).  The operand is the folded-RMSNorm MLP input:
+// the scale rstd/col_prev of each token goes to tok_scale and rstd to col_rstd.
+struct MoERouteArgs {
+    const __half *x = nullptr;      // blocked operand [H/64][ldx_rows][64]
+    int ldx_rows = 0;
+    int M = 0, H = 0, E = 0, TK = 0, norm_topk = 1;
+    const __nv_bfloat16 *wr = nullptr;   // [E][H]
+    const float *col_part = nullptr, *col_prev = nullptr;
+    float *col_rstd = nullptr;
+    int norm_rows = 0;
+    float eps = 0.f;
+    float *tok_scale = nullptr;     // [M]
+    int32_t *topk_id = nullptr;     // [M*TK]
+    float *topk_w = nullptr;        // [M*TK]
+    int *exp_count = nullptr;       // [E]
+    int32_t *exp_list = nullptr;    // [E][list_cap]
+    int list_cap = 0;
+};
+// grouped expert linear over all E experts of one layer: weights [E][N][K/8]
+// (+ scales/biases [E][N][K/64]), the MLX SwitchGLU layout.  epi 0: gate (wq)
+// and up (wq2) projections, act = silu(g)*u in the blocked layout
+// [N/64][act_rows][64] per assignment; epi 1: y[assignment][N] fp32 scaled by
+// the routing weight.  Operand row of assignment a: a / x_div.  A route
+// without col_part treats the operand as already normalised (scale 1).
+struct MoEExpertArgs {
+    const uint32_t *wq = nullptr, *wq2 = nullptr;
+    const __half *scales = nullptr, *biases = nullptr, *scales2 = nullptr, *biases2 = nullptr;
+    int N = 0, K = 0, E = 0;
+    const __half *x = nullptr;
+    int ldx_rows = 0, x_div = 1;
+    const int *exp_count = nullptr;
+    const int32_t *exp_list = nullptr;
+    int list_cap = 0;
+    const float *tok_scale = nullptr;   // epi 0: per operand row
+    const float *topk_w = nullptr;      // epi 1: per assignment
+    __half *act = nullptr;
+    int act_rows = 0;
+    float *y = nullptr;
+};
+// h[m] += sum_j y[m*TK + j] (selection order); with norm_w also the next
+// linear's operand fp16(h * norm_w * norm_scale[m]) and per-128-block sums of
+// squares of h (the residual epilogue of the dense path)
+struct MoECombineArgs {
+    float *h = nullptr;
+    const float *y = nullptr;
+    int M = 0, H = 0, TK = 0;
+    const float *norm_w = nullptr, *norm_scale = nullptr;
+    __half *xout = nullptr;
+    int ldx_rows = 0;
+    float *norm_part = nullptr;
+    int norm_rows = 0;
+};
+size_t moe_route_smem(int H, int E);
+cudaError_t moe_route(const MoERouteArgs &a, cudaStream_t st);
+cudaError_t moe_expert(const MoEExpertArgs &a, int epi, cudaStream_t st);
+cudaError_t moe_combine(const MoECombineArgs &a, cudaStream_t st);
+// bf16 router weights N(0, stddev) from the weight stream (bit-identical with
+// the CPU restatement's orc_router_synth)
+cudaError_t router_synth(uint64_t seed, uint32_t tensor_id, float stddev, int E, int H, void *w,
+                         cudaStream_t st);
 
 // ---- decode attention (split-K over keys, GQA) -----------------------------
 // Tokens come in groups of `qg` consecutive positions of one row (the verify

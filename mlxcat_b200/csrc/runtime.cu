@@ -70,6 +70,14 @@ struct mlxcat_ctx {
     std::vector<void *> allocs;
     DevLin embed, lm_head;
     std::vector<DevLin> qkv, o, gu, down;
+    // sparse MoE MLP per layer: bf16 router [E][H]; gate, up [E][I][H/8] and down
+    // [E][H][I/8] q4 in the MLX SwitchGLU layout (scales/biases [E][N][K/64])
+    struct MoEBank {
+        __nv_bfloat16 *router = nullptr;
+        uint32_t *wq[3] = {};
+        __half *s[3] = {}, *b[3] = {};
+    };
+    std::vector<MoEBank> moe;
     float *norms = nullptr;     // attn[L][H], mlp[L][H], final[H], qn[L][D], kn[L][D]
     float *inv_freq = nullptr;
     int32_t *table = nullptr;
@@ -115,6 +123,12 @@ struct mlxcat_cache {
     // folded RMSNorm: per-block sums of squares of h [H/128][rows], and the rstd of
     // the attention-norm and MLP-norm inputs of each token row (pre-scales)
     float *norm_part = nullptr, *r_attn = nullptr, *r_mlp = nullptr;
+    // sparse MoE: routing, per-expert assignment lists (counts per layer, zeroed
+    // once per forward), SwiGLU activations per assignment, scaled expert outputs
+    int32_t *moe_id = nullptr, *moe_list = nullptr;
+    int *moe_count = nullptr;
+    float *moe_w = nullptr, *moe_scale = nullptr, *moe_y = nullptr;
+    __half *moe_act = nullptr;
     size_t part_floats = 0;
     unsigned *counters = nullptr;     // split-K tickets of the q4 linear (self-resetting)
     unsigned long long *amax_part = nullptr;   // split argmax partial keys
@@ -221,6 +235,12 @@ bool valid_config(const mlxcat_model_config *c, std::string &why) {
     }
     if (c->n_heads % c->n_kv_heads) { why = "n_heads must be a multiple of n_kv_heads"; return false; }
     if (c->head_dim != 64 && c->head_dim != 128) { why = "head_dim must be 64 or 128"; return false; }
+    if (c->n_experts < 0) { why = "n_experts must be >= 0"; return false; }
+    if (c->n_experts > 0) {
+        if (c->n_experts % 32 || c->n_experts > 256) { why = "n_experts must be a multiple of 32, at most 256"; return false; }
+        if (c->top_k < 1 || c->top_k > 8 || c->top_k > c->n_experts) { why = "top_k must be in 1..min(8, n_experts)"; return false; }
+        if (c->hidden % 256) { why = "MoE models need hidden a multiple of 256"; return false; }
+    }
     const int qkv = (c->n_heads + 2 * c->n_kv_heads) * c->head_dim;
     const int dims[] = {c->hidden, c->intermediate, c->n_heads * c->head_dim, qkv, 2 * c->intermediate, c->vocab};
     for (int d : dims)
@@ -278,6 +298,7 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
     // sums of squares of h; the next linear scales its accumulators by rstd / s.
     // Layer 0's input is normalised exactly here.
     LK(ctx, embed_norm(ctx->embed.view(), tok, M, ctx->attn_norm(0), eps, c->h, c->xn, R, st, c->r_attn));
+    if (cf.n_experts) CK(ctx, cudaMemsetAsync(c->moe_count, 0, sizeof(int) * (size_t)L * cf.n_experts, st));
     Q4Epilogue ep;
     ep.part = c->part;
     ep.counters = c->counters;
@@ -312,6 +333,37 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
             e.norm_part = c->norm_part; e.norm_rows = R;
             ProfScope ps(c, 0);
             LK(ctx, q4_tc(ctx->o[l].tc(), c->xn, R, 0, M, ctx->sm_count, e, st));
+        }
+        if (cf.n_experts) {   // sparse MoE MLP: route, experts, combine into the residual
+            const int E = cf.n_experts, TK = cf.top_k;
+            int *cnt = c->moe_count + (size_t)l * E;
+            MoERouteArgs ra;
+            ra.x = c->xg; ra.ldx_rows = R; ra.M = M; ra.H = H; ra.E = E; ra.TK = TK; ra.norm_topk = cf.norm_topk;
+            ra.wr = ctx->moe[l].router;
+            ra.col_part = c->norm_part; ra.col_prev = c->r_attn; ra.col_rstd = c->r_mlp; ra.norm_rows = R;
+            ra.eps = eps; ra.tok_scale = c->moe_scale; ra.topk_id = c->moe_id; ra.topk_w = c->moe_w;
+            ra.exp_count = cnt; ra.exp_list = c->moe_list; ra.list_cap = c->m_cap;
+            LK(ctx, moe_route(ra, st));
+            const auto &mb = ctx->moe[l];
+            MoEExpertArgs xa;
+            xa.wq = mb.wq[0]; xa.scales = mb.s[0]; xa.biases = mb.b[0];
+            xa.wq2 = mb.wq[1]; xa.scales2 = mb.s[1]; xa.biases2 = mb.b[1];
+            xa.N = I; xa.K = H; xa.E = E; xa.x = c->xg; xa.ldx_rows = R; xa.x_div = TK;
+            xa.exp_count = cnt; xa.exp_list = c->moe_list; xa.list_cap = c->m_cap;
+            xa.tok_scale = c->moe_scale; xa.act = c->moe_act; xa.act_rows = c->m_cap * TK;
+            { ProfScope ps(c, 0); LK(ctx, moe_expert(xa, 0, st)); }
+            MoEExpertArgs da;
+            da.wq = mb.wq[2]; da.scales = mb.s[2]; da.biases = mb.b[2];
+            da.N = H; da.K = I; da.E = E; da.x = c->moe_act; da.ldx_rows = c->m_cap * TK; da.x_div = 1;
+            da.exp_count = cnt; da.exp_list = c->moe_list; da.list_cap = c->m_cap;
+            da.topk_w = c->moe_w; da.y = c->moe_y;
+            { ProfScope ps(c, 0); LK(ctx, moe_expert(da, 1, st)); }
+            MoECombineArgs ca;
+            ca.h = c->h; ca.y = c->moe_y; ca.M = M; ca.H = H; ca.TK = TK;
+            ca.norm_w = l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(); ca.norm_scale = c->r_mlp;
+            ca.xout = c->xn; ca.ldx_rows = R; ca.norm_part = c->norm_part; ca.norm_rows = R;
+            LK(ctx, moe_combine(ca, st));
+            continue;
         }
         {   // gate/up + SwiGLU
             Q4Epilogue e = ep;
@@ -499,12 +551,25 @@ int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx
         const int H = c.hidden, D = c.head_dim, L = c.n_layers;
         alloc_lin(ctx->embed, c.vocab, H);
         if (!c.tie_embeddings) alloc_lin(ctx->lm_head, c.vocab, H);
-        ctx->qkv.resize(L); ctx->o.resize(L); ctx->gu.resize(L); ctx->down.resize(L);
+        ctx->qkv.resize(L); ctx->o.resize(L);
+        if (c.n_experts) ctx->moe.resize(L);
+        else { ctx->gu.resize(L); ctx->down.resize(L); }
         for (int l = 0; l < L && rc == MLXCAT_OK; ++l) {
             alloc_lin(ctx->qkv[l], (c.n_heads + 2 * c.n_kv_heads) * D, H);
             alloc_lin(ctx->o[l], H, c.n_heads * D);
-            alloc_lin(ctx->gu[l], 2 * c.intermediate, H);
-            alloc_lin(ctx->down[l], H, c.intermediate);
+            if (c.n_experts) {
+                auto &mb = ctx->moe[l];
+                const size_t n = (size_t)c.n_experts * c.intermediate * H;   // weights per projection
+                bool ok = dalloc(ctx->allocs, &mb.router, (size_t)c.n_experts * H) == cudaSuccess;
+                for (int p = 0; p < 3 && ok; ++p)
+                    ok = dalloc(ctx->allocs, &mb.wq[p], n / 8) == cudaSuccess &&
+                         dalloc(ctx->allocs, &mb.s[p], n / 64) == cudaSuccess &&
+                         dalloc(ctx->allocs, &mb.b[p], n / 64) == cudaSuccess;
+                if (!ok) rc = set_err(ctx, MLXCAT_E_OOM, "expert weight allocation failed (layer %d)", l);
+            } else {
+                alloc_lin(ctx->gu[l], 2 * c.intermediate, H);
+                alloc_lin(ctx->down[l], H, c.intermediate);
+            }
         }
         const size_t nn = (size_t)(2 * L + 1) * H + (size_t)2 * L * D;
         if (rc == MLXCAT_OK && dalloc(ctx->allocs, &ctx->norms, nn) != cudaSuccess)
@@ -551,9 +616,30 @@ int mlxcat_ctx_synchronize(mlxcat_ctx *ctx) {
 
 int64_t mlxcat_ctx_launch_count(const mlxcat_ctx *ctx) { return ctx ? ctx->launches : -1; }
 
+// A MoE expert tensor (MLXCAT_TENSOR_EXPERT ids) as a non-owning view into its
+// layer's expert bank.
+static bool expert_view(mlxcat_ctx *ctx, uint32_t id, DevLin *v, RowMap *rm) {
+    const mlxcat_model_config &c = ctx->cfg;
+    if (c.kind != MLXCAT_MODEL_TRANSFORMER || !c.n_experts || (id & 0xC0000000u) != 0x40000000u) return false;
+    const int l = (int)((id >> 12) & 0x3FFFFu), e = (int)((id >> 2) & 0x3FFu), kind = (int)(id & 3u);
+    if (l >= c.n_layers || e >= c.n_experts || kind > 2) return false;
+    const auto &mb = ctx->moe[l];
+    const size_t per = (size_t)c.intermediate * c.hidden;   // weights of one expert projection
+    *rm = RowMap();
+    *v = DevLin();
+    v->wq = mb.wq[kind] + (size_t)e * per / 8;
+    v->s = mb.s[kind] + (size_t)e * per / 64;
+    v->b = mb.b[kind] + (size_t)e * per / 64;
+    v->N = kind < 2 ? c.intermediate : c.hidden;
+    v->K = kind < 2 ? c.hidden : c.intermediate;
+    rm->rows = v->N;
+    return true;
+}
+
 static DevLin *lin_for(mlxcat_ctx *ctx, uint32_t id, RowMap *rm) {
     const mlxcat_model_config &c = ctx->cfg;
     if (c.kind != MLXCAT_MODEL_TRANSFORMER) return nullptr;
+    if ((id & 0xC0000000u) == 0x40000000u) return nullptr;
     *rm = RowMap();
     if (id == 0xFFFF0000u) { rm->rows = c.vocab; return &ctx->embed; }
     if (id == 0xFFFF0001u) {
@@ -568,6 +654,9 @@ static DevLin *lin_for(mlxcat_ctx *ctx, uint32_t id, RowMap *rm) {
     case 1: rm->offset = qd; rm->rows = kvd; return &ctx->qkv[l];
     case 2: rm->offset = qd + kvd; rm->rows = kvd; return &ctx->qkv[l];
     case 3: rm->rows = c.hidden; return &ctx->o[l];
+    }
+    if (c.n_experts) return nullptr;   // MoE layers have no dense MLP
+    switch (kind) {
     case 4: rm->group = 64; rm->stride = 128; rm->rows = c.intermediate; return &ctx->gu[l];
     case 5: rm->group = 64; rm->stride = 128; rm->offset = 64; rm->rows = c.intermediate; return &ctx->gu[l];
     case 6: rm->rows = c.hidden; return &ctx->down[l];
@@ -608,7 +697,20 @@ int mlxcat_weights_synth(mlxcat_ctx *ctx, uint64_t seed, float stddev) {
     std::vector<uint32_t> ids = {0xFFFF0000u};
     if (!c.tie_embeddings) ids.push_back(0xFFFF0001u);
     for (int l = 0; l < c.n_layers; ++l)
-        for (int k = 0; k < 7; ++k) ids.push_back((uint32_t)l * 16u + (uint32_t)k);
+        for (int k = 0; k < (c.n_experts ? 4 : 7); ++k) ids.push_back((uint32_t)l * 16u + (uint32_t)k);
+    for (int l = 0; l < c.n_layers && c.n_experts; ++l) {
+        LK(ctx, router_synth(seed, (uint32_t)l * 16u + 7u, stddev, c.n_experts, c.hidden, ctx->moe[l].router,
+                             ctx->stream));
+        for (int e = 0; e < c.n_experts; ++e)
+            for (int kind = 0; kind < 3; ++kind) {
+                const uint32_t id = MLXCAT_TENSOR_EXPERT(l, e, kind);
+                DevLin v;
+                RowMap rm;
+                expert_view(ctx, id, &v, &rm);
+                LK(ctx, synth_q4(seed, id, stddev, rm.rows, v.K, v.wq, v.s, v.b, rm.offset, ctx->stream,
+                                 rm.group, rm.stride));
+            }
+    }
     for (uint32_t id : ids) {
         RowMap rm;
         DevLin *w = lin_for(ctx, id, &rm);
@@ -629,6 +731,14 @@ int mlxcat_weights_set_q4(mlxcat_ctx *ctx, uint32_t id, const uint32_t *wq, cons
                           const uint16_t *biases) {
     if (!ctx || !wq || !scales || !biases) return MLXCAT_E_INVALID;
     RowMap rm;
+    DevLin ev;
+    if (expert_view(ctx, id, &ev, &rm)) {
+        CK(ctx, cudaSetDevice(ctx->device));
+        CK(ctx, copy_rows(&ev, rm, const_cast<uint32_t *>(wq), const_cast<uint16_t *>(scales),
+                          const_cast<uint16_t *>(biases), true));
+        ctx->have_weights = true;
+        return MLXCAT_OK;
+    }
     DevLin *w = lin_for(ctx, id, &rm);
     if (!w) return set_err(ctx, MLXCAT_E_INVALID, "unknown tensor id 0x%x", id);
     CK(ctx, cudaSetDevice(ctx->device));
@@ -643,11 +753,41 @@ int mlxcat_weights_set_q4(mlxcat_ctx *ctx, uint32_t id, const uint32_t *wq, cons
 int mlxcat_weights_get_q4(mlxcat_ctx *ctx, uint32_t id, uint32_t *wq, uint16_t *scales, uint16_t *biases) {
     if (!ctx) return MLXCAT_E_INVALID;
     RowMap rm;
-    DevLin *w = lin_for(ctx, id, &rm);
+    DevLin ev;
+    DevLin *w = expert_view(ctx, id, &ev, &rm) ? &ev : lin_for(ctx, id, &rm);
     if (!w) return set_err(ctx, MLXCAT_E_INVALID, "unknown tensor id 0x%x", id);
     CK(ctx, cudaSetDevice(ctx->device));
     CK(ctx, cudaStreamSynchronize(ctx->stream));
     CK(ctx, copy_rows(w, rm, wq, scales, biases, false));
+    return MLXCAT_OK;
+}
+
+static __nv_bfloat16 *bf16_for(mlxcat_ctx *ctx, uint32_t id, size_t *n) {
+    const mlxcat_model_config &c = ctx->cfg;
+    if (c.kind != MLXCAT_MODEL_TRANSFORMER || !c.n_experts || id % 16u != 7u || (int)(id / 16u) >= c.n_layers)
+        return nullptr;
+    *n = (size_t)c.n_experts * c.hidden;
+    return ctx->moe[id / 16u].router;
+}
+
+int mlxcat_weights_set_bf16(mlxcat_ctx *ctx, uint32_t id, const uint16_t *w) {
+    if (!ctx || !w) return MLXCAT_E_INVALID;
+    size_t n = 0;
+    __nv_bfloat16 *d = bf16_for(ctx, id, &n);
+    if (!d) return set_err(ctx, MLXCAT_E_INVALID, "unknown bf16 tensor id 0x%x", id);
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaMemcpy(d, w, n * 2, cudaMemcpyHostToDevice));
+    return MLXCAT_OK;
+}
+
+int mlxcat_weights_get_bf16(mlxcat_ctx *ctx, uint32_t id, uint16_t *w) {
+    if (!ctx || !w) return MLXCAT_E_INVALID;
+    size_t n = 0;
+    __nv_bfloat16 *d = bf16_for(ctx, id, &n);
+    if (!d) return set_err(ctx, MLXCAT_E_INVALID, "unknown bf16 tensor id 0x%x", id);
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    CK(ctx, cudaMemcpy(w, d, n * 2, cudaMemcpyDeviceToHost));
     return MLXCAT_OK;
 }
 
@@ -666,8 +806,16 @@ int mlxcat_weights_set_table(mlxcat_ctx *ctx, const int32_t *next, int32_t vocab
 int64_t mlxcat_weights_bytes(const mlxcat_ctx *ctx) {
     if (!ctx || ctx->cfg.kind != MLXCAT_MODEL_TRANSFORMER) return 0;
     size_t b = ctx->cfg.tie_embeddings ? ctx->embed.bytes() : ctx->lm_head.bytes();
-    for (int l = 0; l < ctx->cfg.n_layers; ++l)
-        b += ctx->qkv[l].bytes() + ctx->o[l].bytes() + ctx->gu[l].bytes() + ctx->down[l].bytes();
+    const mlxcat_model_config &c = ctx->cfg;
+    for (int l = 0; l < c.n_layers; ++l) {
+        b += ctx->qkv[l].bytes() + ctx->o[l].bytes();
+        if (c.n_experts)   // every expert is touched by a verify step's assignments
+            b += (size_t)c.n_experts * (3 * ((size_t)c.intermediate * c.hidden / 2 +
+                                             (size_t)c.intermediate * c.hidden / 64 * 4) +
+                                        (size_t)c.hidden * 2);
+        else
+            b += ctx->gu[l].bytes() + ctx->down[l].bytes();
+    }
     return (int64_t)b;
 }
 
@@ -727,6 +875,16 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
         chk(dalloc(A, &c->r_attn, (size_t)Mc));
         chk(dalloc(A, &c->r_mlp, (size_t)Mc));
         chk(dalloc(A, &c->qbuf, (size_t)Mc * Hq * D));
+        if (cf.n_experts) {
+            const size_t asg = (size_t)Mc * cf.top_k;
+            chk(dalloc(A, &c->moe_id, asg));
+            chk(dalloc(A, &c->moe_w, asg));
+            chk(dalloc(A, &c->moe_scale, (size_t)Mc));
+            chk(dalloc(A, &c->moe_list, (size_t)cf.n_experts * Mc));
+            chk(dalloc(A, &c->moe_count, (size_t)cf.n_layers * cf.n_experts));
+            chk(dalloc(A, &c->moe_act, asg * I));
+            chk(dalloc(A, &c->moe_y, asg * H));
+        }
         chk(dalloc(A, &c->rope, (size_t)max_len * (D / 2)));
         if (rc == MLXCAT_OK) chk(rope_table(ctx->inv_freq, D / 2, max_len, c->rope, ctx->stream));
         if (rc == MLXCAT_OK) chk(cudaStreamSynchronize(ctx->stream));
@@ -1149,6 +1307,76 @@ int mlxcat_op_q4_linear(const uint32_t *wq, const uint16_t *scales, const uint16
         e = pack_q4_sb(w.scales, w.biases, N, K, reinterpret_cast<uint32_t *>(w8 + off_sbp), st);
     if (e == cudaSuccess) e = q4_tc(w, xp, M, 0, M, op_sm_count(), ep, st);
     if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "q4_linear: %s", cudaGetErrorString(e));
+    return MLXCAT_OK;
+}
+
+// ---- sparse MoE MLP operator ------------------------------------------------
+static void moe_ws_layout(int32_t M, int32_t H, int32_t I, int32_t E, int32_t TK, size_t off[8]) {
+    const size_t sz[8] = {(size_t)M * H * 2, (size_t)M * 4, (size_t)M * TK * 4, (size_t)M * TK * 4,
+                          (size_t)E * 4, (size_t)E * M * 4, (size_t)M * TK * I * 2, (size_t)M * TK * H * 4};
+    size_t o = 0;
+    for (int i = 0; i < 8; ++i) {
+        off[i] = o;
+        o += (sz[i] + 255) & ~(size_t)255;
+    }
+}
+
+size_t mlxcat_op_moe_workspace(int32_t M, int32_t hidden, int32_t intermediate, int32_t n_experts, int32_t top_k) {
+    if (M <= 0 || hidden <= 0 || intermediate <= 0 || n_experts <= 0 || top_k <= 0) return 0;
+    size_t off[8];
+    moe_ws_layout(M, hidden, intermediate, n_experts, top_k, off);
+    return off[7] + (size_t)M * top_k * hidden * 4;
+}
+
+int mlxcat_op_moe(const uint16_t *x, int32_t M, int32_t hidden, int32_t intermediate, int32_t n_experts,
+                  int32_t top_k, int32_t norm_topk, const uint16_t *router, const uint32_t *const wq[3],
+                  const uint16_t *const scales[3], const uint16_t *const biases[3], float *y, int32_t *ids,
+                  float *weights, void *ws, size_t ws_bytes, void *stream) {
+    if (!x || !router || !wq || !scales || !biases || !y || M <= 0)
+        return op_err(MLXCAT_E_INVALID, "bad moe arguments");
+    for (int p = 0; p < 3; ++p)
+        if (!wq[p] || !scales[p] || !biases[p]) return op_err(MLXCAT_E_INVALID, "bad moe weight pointers");
+    const int H = hidden, I = intermediate, E = n_experts, TK = top_k;
+    if (H % 256 || I % 128 || E % 32 || E > 256 || TK < 1 || TK > 8 || TK > E)
+        return op_err(MLXCAT_E_INVALID, "moe shape: hidden %% 256, intermediate %% 128, n_experts %% 32 (<= 256), "
+                                        "1 <= top_k <= min(8, n_experts)");
+    const size_t need = mlxcat_op_moe_workspace(M, H, I, E, TK);
+    if (!ws || ws_bytes < need) return op_err(MLXCAT_E_INVALID, "workspace of %zu bytes required", need);
+    size_t off[8];
+    moe_ws_layout(M, H, I, E, TK, off);
+    char *w8 = static_cast<char *>(ws);
+    cudaStream_t st = (cudaStream_t)stream;
+    __half *xb = reinterpret_cast<__half *>(w8 + off[0]);
+    float *tsc = reinterpret_cast<float *>(w8 + off[1]);
+    int32_t *tid = ids ? ids : reinterpret_cast<int32_t *>(w8 + off[2]);
+    float *tw = weights ? weights : reinterpret_cast<float *>(w8 + off[3]);
+    int *cnt = reinterpret_cast<int *>(w8 + off[4]);
+    int32_t *list = reinterpret_cast<int32_t *>(w8 + off[5]);
+    __half *act = reinterpret_cast<__half *>(w8 + off[6]);
+    float *yt = reinterpret_cast<float *>(w8 + off[7]);
+    cudaError_t e = permute_activations(reinterpret_cast<const __half *>(x), xb, M, H, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(cnt, 0, sizeof(int) * E, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)M * H, st);
+    MoERouteArgs ra;
+    ra.x = xb; ra.ldx_rows = M; ra.M = M; ra.H = H; ra.E = E; ra.TK = TK; ra.norm_topk = norm_topk;
+    ra.wr = reinterpret_cast<const __nv_bfloat16 *>(router);
+    ra.tok_scale = tsc; ra.topk_id = tid; ra.topk_w = tw; ra.exp_count = cnt; ra.exp_list = list; ra.list_cap = M;
+    if (e == cudaSuccess) e = moe_route(ra, st);
+    MoEExpertArgs ga;
+    ga.wq = wq[0]; ga.scales = reinterpret_cast<const __half *>(scales[0]); ga.biases = reinterpret_cast<const __half *>(biases[0]);
+    ga.wq2 = wq[1]; ga.scales2 = reinterpret_cast<const __half *>(scales[1]); ga.biases2 = reinterpret_cast<const __half *>(biases[1]);
+    ga.N = I; ga.K = H; ga.E = E; ga.x = xb; ga.ldx_rows = M; ga.x_div = TK;
+    ga.exp_count = cnt; ga.exp_list = list; ga.list_cap = M; ga.tok_scale = tsc; ga.act = act; ga.act_rows = M * TK;
+    if (e == cudaSuccess) e = moe_expert(ga, 0, st);
+    MoEExpertArgs da;
+    da.wq = wq[2]; da.scales = reinterpret_cast<const __half *>(scales[2]); da.biases = reinterpret_cast<const __half *>(biases[2]);
+    da.N = H; da.K = I; da.E = E; da.x = act; da.ldx_rows = M * TK; da.x_div = 1;
+    da.exp_count = cnt; da.exp_list = list; da.list_cap = M; da.topk_w = tw; da.y = yt;
+    if (e == cudaSuccess) e = moe_expert(da, 1, st);
+    MoECombineArgs ca;
+    ca.h = y; ca.y = yt; ca.M = M; ca.H = H; ca.TK = TK;
+    if (e == cudaSuccess) e = moe_combine(ca, st);
+    if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "moe: %s", cudaGetErrorString(e));
     return MLXCAT_OK;
 }
 

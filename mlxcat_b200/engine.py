@@ -45,11 +45,17 @@ class ModelConfig:
     rope_theta: float = 10000.0
     kind: int = A.MODEL_TRANSFORMER
     name: str = "custom"
+    # sparse MoE MLP (Qwen3-MoE): experts per layer, experts per token,
+    # renormalised routing weights; `intermediate` is then the expert width
+    n_experts: int = 0
+    top_k: int = 0
+    norm_topk: bool = True
 
     def to_c(self) -> A.ModelConfigC:
         return A.ModelConfigC(self.kind, self.n_layers, self.hidden, self.n_heads, self.n_kv_heads,
                               self.head_dim, self.intermediate, self.vocab, int(self.tie_embeddings),
-                              int(self.qk_norm), self.rms_eps, self.rope_theta, 64, 4)
+                              int(self.qk_norm), self.rms_eps, self.rope_theta, 64, 4,
+                              self.n_experts, self.top_k, int(self.norm_topk))
 
     @staticmethod
     def table(vocab: int) -> "ModelConfig":
@@ -61,7 +67,9 @@ TINY = ModelConfig(4, 512, 8, 2, 64, 1408, 32000, True, False, 1e-5, 500000.0, n
 QWEN3_4B = ModelConfig(36, 2560, 32, 8, 128, 9728, 151936, True, True, 1e-6, 1e6, name="qwen3-4b")
 LLAMA3_8B = ModelConfig(32, 4096, 32, 8, 128, 14336, 128256, False, False, 1e-5, 500000.0,
                         name="llama3-8b")
-CONFIGS = {c.name: c for c in (TINY, QWEN3_4B, LLAMA3_8B)}
+QWEN3_30B_A3B = ModelConfig(48, 2048, 32, 4, 128, 768, 151936, False, True, 1e-6, 1e6,
+                            name="qwen3-30b-a3b", n_experts=128, top_k=8, norm_topk=True)
+CONFIGS = {c.name: c for c in (TINY, QWEN3_4B, LLAMA3_8B, QWEN3_30B_A3B)}
 
 
 @dataclasses.dataclass
@@ -176,6 +184,15 @@ class Context:
         b = np.ascontiguousarray(biases, dtype=np.uint16)
         self.check(self.L.mlxcat_weights_set_q4(self.h, tensor_id, wq.ctypes.data, s.ctypes.data,
                                                 b.ctypes.data))
+
+    def set_bf16(self, tensor_id: int, w):
+        w = np.ascontiguousarray(w, dtype=np.uint16)
+        self.check(self.L.mlxcat_weights_set_bf16(self.h, tensor_id, w.ctypes.data))
+
+    def get_bf16(self, tensor_id: int, shape):
+        w = np.zeros(shape, np.uint16)
+        self.check(self.L.mlxcat_weights_get_bf16(self.h, tensor_id, w.ctypes.data))
+        return w
 
     def get_q4(self, tensor_id: int, N: int, K: int):
         wq = np.zeros((N, K // 8), np.uint32)

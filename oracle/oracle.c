@@ -96,6 +96,16 @@ float orc_f16_to_f32(uint16_t u) {
     _Float16 h; memcpy(&h, &u, 2); return (float)h;
 }
 
+/* bf16: the upper half of the fp32 pattern, rounded to nearest even */
+uint16_t orc_f32_to_bf16(float x) {
+    uint32_t u; memcpy(&u, &x, 4);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+float orc_bf16_to_f32(uint16_t h) {
+    uint32_t u = (uint32_t)h << 16; float f; memcpy(&f, &u, 4); return f;
+}
+
 /* Marsaglia polar method over the Philox stream keyed by the weight seed. */
 float orc_normal(uint64_t seed, uint32_t tensor_id, uint64_t index) {
     const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
@@ -443,6 +453,8 @@ struct orc_model {
     int32_t *table_next;
     q4_t embed, lm_head;
     q4_t *lin;                   /* n_layers * 7 */
+    uint16_t *router;            /* MoE: bf16 [n_layers][n_experts][hidden] */
+    q4_t *experts;               /* MoE: [n_layers][n_experts][3] gate, up, down */
     float *ones;                 /* norm weights (all ones) */
     float *inv_freq;
 };
@@ -479,9 +491,17 @@ static void tensor_shape(const orc_config *c, int kind, int *N, int *K) {
 
 static q4_t *find_tensor(orc_model *m, uint32_t id) {
     if (id == ORC_TENSOR_EMBED) return &m->embed;
+    if ((id & 0xC0000000u) == 0x40000000u) {
+        const int layer = (int)((id >> 12) & 0x3FFFFu), e = (int)((id >> 2) & 0x3FFu),
+                  kind = (int)(id & 3u);
+        if (!m->cfg.n_experts || layer >= m->cfg.n_layers || e >= m->cfg.n_experts || kind > 2)
+            return NULL;
+        return &m->experts[((size_t)layer * m->cfg.n_experts + e) * 3 + kind];
+    }
     if (id == ORC_TENSOR_LM_HEAD) return m->cfg.tie_embeddings ? NULL : &m->lm_head;
     int layer = (int)(id / 16u), kind = (int)(id % 16u);
     if (layer >= m->cfg.n_layers || kind > ORC_T_DOWN) return NULL;
+    if (m->cfg.n_experts && kind >= ORC_T_GATE) return NULL;
     return &m->lin[layer * 7 + kind];
 }
 
@@ -491,12 +511,23 @@ orc_model *orc_model_empty(const orc_config *cfg) {
     q4_alloc(&m->embed, cfg->vocab, cfg->hidden);
     if (!cfg->tie_embeddings) q4_alloc(&m->lm_head, cfg->vocab, cfg->hidden);
     m->lin = (q4_t *)calloc((size_t)cfg->n_layers * 7, sizeof(q4_t));
+    const int dense_kinds = cfg->n_experts ? ORC_T_GATE : 7;   /* MoE: no dense MLP */
     for (int l = 0; l < cfg->n_layers; ++l)
-        for (int k = 0; k < 7; ++k) {
+        for (int k = 0; k < dense_kinds; ++k) {
             int N, K;
             tensor_shape(cfg, k, &N, &K);
             q4_alloc(&m->lin[l * 7 + k], N, K);
         }
+    if (cfg->n_experts) {
+        const size_t E = (size_t)cfg->n_experts, L = (size_t)cfg->n_layers;
+        m->router = (uint16_t *)calloc(L * E * (size_t)cfg->hidden, 2);
+        m->experts = (q4_t *)calloc(L * E * 3, sizeof(q4_t));
+        for (size_t i = 0; i < L * E; ++i) {
+            q4_alloc(&m->experts[i * 3 + 0], cfg->intermediate, cfg->hidden);
+            q4_alloc(&m->experts[i * 3 + 1], cfg->intermediate, cfg->hidden);
+            q4_alloc(&m->experts[i * 3 + 2], cfg->hidden, cfg->intermediate);
+        }
+    }
     int big = cfg->hidden > cfg->head_dim ? cfg->hidden : cfg->head_dim;
     m->ones = (float *)malloc(sizeof(float) * (size_t)big);
     for (int i = 0; i < big; ++i) m->ones[i] = 1.0f;
@@ -516,10 +547,24 @@ orc_model *orc_model_synth(const orc_config *cfg, uint64_t seed, float stddev) {
         orc_q4_synth(seed, ORC_TENSOR_LM_HEAD, stddev, h->N, h->K, h->wq, h->s, h->b);
     }
     for (int l = 0; l < cfg->n_layers; ++l)
-        for (int k = 0; k < 7; ++k) {
+        for (int k = 0; k < (cfg->n_experts ? ORC_T_GATE : 7); ++k) {
             q4_t *t = &m->lin[l * 7 + k];
             orc_q4_synth(seed, orc_tensor_id(l, k), stddev, t->N, t->K, t->wq, t->s, t->b);
         }
+    if (cfg->n_experts) {
+        const int E = cfg->n_experts, H = cfg->hidden;
+        for (int l = 0; l < cfg->n_layers; ++l) {
+            orc_router_synth(seed, orc_tensor_id(l, ORC_T_ROUTER), stddev, E, H,
+                             m->router + (size_t)l * E * H);
+#pragma omp parallel for schedule(dynamic)
+            for (int i = 0; i < E * 3; ++i) {
+                const int e = i / 3, kind = i % 3;
+                q4_t *t = &m->experts[((size_t)l * E + e) * 3 + kind];
+                orc_q4_synth(seed, ORC_TENSOR_EXPERT(l, e, kind), stddev, t->N, t->K, t->wq, t->s,
+                             t->b);
+            }
+        }
+    }
     return m;
 }
 
@@ -549,6 +594,71 @@ void orc_model_get_q4(const orc_model *m, uint32_t tensor_id, const uint32_t **w
     *wq = t->wq; *scales = t->s; *biases = t->b; *N = t->N; *K = t->K;
 }
 
+/* Router weights of a Qwen3-MoE layer: bf16, synthesised from the same
+ * Philox normal stream as the q4 tensors (element e*H + k). */
+void orc_router_synth(uint64_t seed, uint32_t tensor_id, float stddev, int E, int H,
+                      uint16_t *w) {
+#pragma omp parallel for schedule(static)
+    for (int e = 0; e < E; ++e)
+        for (int k = 0; k < H; ++k) {
+            const uint64_t idx = (uint64_t)e * (uint64_t)H + (uint64_t)k;
+            w[(size_t)e * H + k] = orc_f32_to_bf16(orc_normal(seed, tensor_id, idx) * stddev);
+        }
+}
+
+int orc_model_set_router(orc_model *m, int layer, const uint16_t *w) {
+    if (!m->cfg.n_experts || layer < 0 || layer >= m->cfg.n_layers) return -1;
+    const size_t n = (size_t)m->cfg.n_experts * m->cfg.hidden;
+    memcpy(m->router + (size_t)layer * n, w, n * 2);
+    return 0;
+}
+
+/* Routing of the sparse MoE block (Qwen3-MoE in mlx-swift-lm dcfa3aa1,
+ * un-vendored; called from the verify forward at BatchGenerator.swift:900):
+ * logits = x . Wr^T kept bf16, p = softmax(logits) in fp32, the top_k largest
+ * (ties to the lower expert index), weights p_j / sum of the selected p when
+ * norm_topk.  Returns logit[k-th] - logit[(k+1)-th] (0 when k == E). */
+float orc_moe_route(const orc_model *m, int layer, const float *x, int32_t *ids, float *weights) {
+    const orc_config *c = &m->cfg;
+    const int E = c->n_experts, H = c->hidden, TK = c->top_k;
+    float *lg = (float *)malloc(sizeof(float) * (size_t)E);
+    float *p = (float *)malloc(sizeof(float) * (size_t)E);
+    uint8_t *used = (uint8_t *)calloc((size_t)E, 1);
+    const uint16_t *W = m->router + (size_t)layer * E * H;
+    for (int e = 0; e < E; ++e) {
+        float acc = 0.0f;
+        for (int k = 0; k < H; ++k) acc += x[k] * orc_bf16_to_f32(W[(size_t)e * H + k]);
+        lg[e] = orc_bf16_to_f32(orc_f32_to_bf16(acc));
+    }
+    float mx = lg[0];
+    for (int e = 1; e < E; ++e) if (lg[e] > mx) mx = lg[e];
+    float den = 0.0f;
+    for (int e = 0; e < E; ++e) { p[e] = expf(lg[e] - mx); den += p[e]; }
+    for (int e = 0; e < E; ++e) p[e] = p[e] / den;
+    float sel = 0.0f, last = 0.0f;
+    for (int j = 0; j < TK; ++j) {
+        int best = -1;
+        for (int e = 0; e < E; ++e)
+            if (!used[e] && (best < 0 || lg[e] > lg[best])) best = e;
+        used[best] = 1;
+        ids[j] = best;
+        weights[j] = p[best];
+        sel += p[best];
+        last = lg[best];
+    }
+    float margin = 0.0f;
+    if (TK < E) {
+        int nxt = -1;
+        for (int e = 0; e < E; ++e)
+            if (!used[e] && (nxt < 0 || lg[e] > lg[nxt])) nxt = e;
+        margin = last - lg[nxt];
+    }
+    if (c->norm_topk)
+        for (int j = 0; j < TK; ++j) weights[j] = weights[j] / sel;
+    free(lg); free(p); free(used);
+    return margin;
+}
+
 void orc_model_free(orc_model *m) {
     if (!m) return;
     if (!m->is_table) {
@@ -556,6 +666,12 @@ void orc_model_free(orc_model *m) {
         if (!m->cfg.tie_embeddings) q4_free(&m->lm_head);
         for (int i = 0; i < m->cfg.n_layers * 7; ++i) q4_free(&m->lin[i]);
         free(m->lin);
+        if (m->cfg.n_experts) {
+            for (size_t i = 0; i < (size_t)m->cfg.n_layers * m->cfg.n_experts * 3; ++i)
+                q4_free(&m->experts[i]);
+            free(m->experts);
+            free(m->router);
+        }
         free(m->ones);
         free(m->inv_freq);
     }
@@ -631,6 +747,58 @@ static void rope(float *x, int D, int pos, const float *inv_freq) {
 static void lin(const q4_t *t, const float *x, int M, float *y) {
     orc_q4_linear(t->wq, t->s, t->b, t->N, t->K, x, M, y);
 }
+
+/* Sparse MoE MLP (Qwen3-MoE): per token, route (orc_moe_route), then
+ * h += sum_j w_j * down_e(silu(gate_e(x)) * up_e(x)) over the selected
+ * experts in selection order.  x: [M][H] normalised MLP input. */
+static float orc_last_route_margin = 1e30f;   /* smallest selection margin seen */
+float orc_moe_min_margin(int reset) {
+    float v = orc_last_route_margin;
+    if (reset) orc_last_route_margin = 1e30f;
+    return v;
+}
+/* the MoE MLP alone on given inputs: y[M][H] (accumulated onto, start it at
+ * zero), ids/weights [M][top_k], margins [M] (each may be NULL) */
+void orc_moe_mlp(const orc_model *m, int layer, const float *x, int M, float *y, int32_t *ids_out,
+                 float *w_out, float *margins) {
+    const orc_config *c = &m->cfg;
+    const int H = c->hidden, I = c->intermediate, E = c->n_experts, TK = c->top_k;
+    int32_t *ids = (int32_t *)malloc(sizeof(int32_t) * (size_t)M * TK);
+    float *wts = (float *)malloc(sizeof(float) * (size_t)M * TK);
+    for (int i = 0; i < M; ++i) {
+        float mg = orc_moe_route(m, layer, x + (size_t)i * H, ids + (size_t)i * TK, wts + (size_t)i * TK);
+        if (margins) margins[i] = mg;
+        if (TK < E && mg < orc_last_route_margin) orc_last_route_margin = mg;
+    }
+#pragma omp parallel
+    {
+        float *g = (float *)malloc(sizeof(float) * (size_t)I);
+        float *u = (float *)malloc(sizeof(float) * (size_t)I);
+        float *yy = (float *)malloc(sizeof(float) * (size_t)H);
+#pragma omp for schedule(dynamic)
+        for (int i = 0; i < M; ++i) {
+            float *hi = y + (size_t)i * H;
+            for (int j = 0; j < TK; ++j) {
+                const q4_t *X = &m->experts[((size_t)layer * E + ids[(size_t)i * TK + j]) * 3];
+                orc_q4_linear(X[0].wq, X[0].s, X[0].b, I, H, x + (size_t)i * H, 1, g);
+                orc_q4_linear(X[1].wq, X[1].s, X[1].b, I, H, x + (size_t)i * H, 1, u);
+                for (int n = 0; n < I; ++n) g[n] = g[n] / (1.0f + expf(-g[n])) * u[n];
+                orc_q4_linear(X[2].wq, X[2].s, X[2].b, H, I, g, 1, yy);
+                const float w = wts[(size_t)i * TK + j];
+                for (int n = 0; n < H; ++n) hi[n] += w * yy[n];
+            }
+        }
+        free(g); free(u); free(yy);
+    }
+    if (ids_out) memcpy(ids_out, ids, sizeof(int32_t) * (size_t)M * TK);
+    if (w_out) memcpy(w_out, wts, sizeof(float) * (size_t)M * TK);
+    free(ids); free(wts);
+}
+
+static void moe_block(const orc_model *m, int layer, const float *x, int M, float *h) {
+    orc_moe_mlp(m, layer, x, M, h, NULL, NULL, NULL);
+}
+
 
 void orc_forward(const orc_model *m, orc_kv *kv, int M, const int32_t *tokens,
                  const int32_t *rows, const int32_t *pos, float *logits) {
@@ -712,6 +880,10 @@ void orc_forward(const orc_model *m, orc_kv *kv, int M, const int32_t *tokens,
         lin(&W[ORC_T_O], att, M, o);
         for (size_t i = 0; i < (size_t)M * H; ++i) h[i] += o[i];
         for (int i = 0; i < M; ++i) rmsnorm(h + (size_t)i * H, m->ones, H, c->rms_eps, x + (size_t)i * H);
+        if (c->n_experts) {
+            moe_block(m, l, x, M, h);
+            continue;
+        }
         lin(&W[ORC_T_GATE], x, M, g);
         lin(&W[ORC_T_UP], x, M, u);
         for (size_t i = 0; i < (size_t)M * I; ++i) {

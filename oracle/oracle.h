@@ -92,15 +92,44 @@ typedef struct {
     int n_layers, hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab;
     int tie_embeddings, qk_norm;
     float rms_eps, rope_theta;
+    /* sparse MoE MLP in every layer when n_experts > 0 (Qwen3-MoE): a bf16
+     * router [n_experts][hidden], top_k experts per token, each expert a q4
+     * SwiGLU of width `intermediate`; norm_topk renormalises the k weights */
+    int n_experts, top_k, norm_topk;
 } orc_config;
 
 typedef struct orc_model orc_model;
 typedef struct orc_kv orc_kv;
 
-enum { ORC_T_Q = 0, ORC_T_K, ORC_T_V, ORC_T_O, ORC_T_GATE, ORC_T_UP, ORC_T_DOWN };
+enum { ORC_T_Q = 0, ORC_T_K, ORC_T_V, ORC_T_O, ORC_T_GATE, ORC_T_UP, ORC_T_DOWN, ORC_T_ROUTER };
 #define ORC_TENSOR_EMBED 0xFFFF0000u
 #define ORC_TENSOR_LM_HEAD 0xFFFF0001u
 uint32_t orc_tensor_id(int layer, int kind);
+/* expert tensors: kind 0 gate, 1 up, 2 down */
+#define ORC_TENSOR_EXPERT(layer, expert, kind) \
+    (0x40000000u | ((uint32_t)(layer) << 12) | ((uint32_t)(expert) << 2) | (uint32_t)(kind))
+
+/* bf16 round-to-nearest-even (NaN not produced by the callers) */
+uint16_t orc_f32_to_bf16(float x);
+float orc_bf16_to_f32(uint16_t h);
+/* router weights: bf16(N(0, stddev)) from the weight stream of tensor
+ * orc_tensor_id(layer, ORC_T_ROUTER), element index e*hidden + k */
+void orc_router_synth(uint64_t seed, uint32_t tensor_id, float stddev, int E, int H,
+                      uint16_t *w);
+int orc_model_set_router(orc_model *m, int layer, const uint16_t *w);
+/* MoE routing of one token (x: normalised MLP input, fp32): bf16 router
+ * logits, fp32 softmax, top-k (ties to the lower expert index), optional
+ * renormalisation.  Writes ids[k], weights[k]; returns the gap between the
+ * k-th and (k+1)-th largest logit (the margin of the selection). */
+float orc_moe_route(const orc_model *m, int layer, const float *x, int32_t *ids, float *weights);
+/* smallest routing margin over all tokens routed since the last reset: a
+ * parity test on a MoE model skips inputs whose expert choice is a near tie */
+float orc_moe_min_margin(int reset);
+/* the MoE MLP of `layer` alone on given normalised inputs x[M][hidden]:
+ * y[M][hidden] += sum_j w_j expert_j(x); ids/weights [M][top_k] and routing
+ * margins [M] (each may be NULL) */
+void orc_moe_mlp(const orc_model *m, int layer, const float *x, int M, float *y, int32_t *ids,
+                 float *weights, float *margins);
 
 orc_model *orc_model_synth(const orc_config *cfg, uint64_t seed, float stddev);
 /* table model: logits +20 at next[token], -20 elsewhere (the reference test doubles) */

@@ -17,9 +17,14 @@ _LIB_PATH = os.path.join(_HERE, "liboracle.so")
 
 MODE_COMPAT = 0
 MODE_PREFIX = 1
-T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN = range(7)
+T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN, T_ROUTER = range(8)
 TENSOR_EMBED = 0xFFFF0000
 TENSOR_LM_HEAD = 0xFFFF0001
+
+
+def tensor_expert(layer: int, expert: int, kind: int) -> int:
+    """id of a MoE expert tensor (kind 0 gate, 1 up, 2 down)"""
+    return 0x40000000 | (layer << 12) | (expert << 2) | kind
 
 
 def build() -> str:
@@ -34,6 +39,7 @@ class Config(C.Structure):
         ("n_kv_heads", C.c_int), ("head_dim", C.c_int), ("intermediate", C.c_int),
         ("vocab", C.c_int), ("tie_embeddings", C.c_int), ("qk_norm", C.c_int),
         ("rms_eps", C.c_float), ("rope_theta", C.c_float),
+        ("n_experts", C.c_int), ("top_k", C.c_int), ("norm_topk", C.c_int),
     ]
 
 
@@ -126,6 +132,15 @@ def lib():
                                 C.POINTER(SpecConfig), i32p, i32p, C.POINTER(Stats)]
     L.orc_admit.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(Row), C.c_int, i32p, C.c_int, C.c_int]
     L.orc_admit.restype = C.c_int
+    L.orc_router_synth.argtypes = [C.c_uint64, C.c_uint32, C.c_float, C.c_int, C.c_int, u16p]
+    L.orc_model_set_router.argtypes = [C.c_void_p, C.c_int, u16p]
+    L.orc_model_set_router.restype = C.c_int
+    L.orc_moe_route.argtypes = [C.c_void_p, C.c_int, f32p, i32p, f32p]
+    L.orc_moe_route.restype = C.c_float
+    L.orc_moe_min_margin.argtypes = [C.c_int]
+    L.orc_moe_min_margin.restype = C.c_float
+    L.orc_f32_to_bf16.argtypes = [C.c_float]; L.orc_f32_to_bf16.restype = C.c_uint16
+    L.orc_moe_mlp.argtypes = [C.c_void_p, C.c_int, f32p, C.c_int, f32p, i32p, f32p, f32p]
     _lib = L
     return L
 
@@ -262,9 +277,21 @@ def accept_row(mode, logits, drafts, sp: Sampling, gen_index: int):
 # model / cache / generator
 # --------------------------------------------------------------------------- #
 def make_config(n_layers, hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab,
-                tie_embeddings=True, qk_norm=False, rms_eps=1e-5, rope_theta=10000.0) -> Config:
+                tie_embeddings=True, qk_norm=False, rms_eps=1e-5, rope_theta=10000.0,
+                n_experts=0, top_k=0, norm_topk=True) -> Config:
     return Config(n_layers, hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab,
-                  int(tie_embeddings), int(qk_norm), rms_eps, rope_theta)
+                  int(tie_embeddings), int(qk_norm), rms_eps, rope_theta, n_experts, top_k,
+                  int(norm_topk))
+
+
+def router_synth(seed: int, tensor_id: int, stddev: float, E: int, H: int):
+    w = np.zeros((E, H), np.uint16)
+    lib().orc_router_synth(seed, tensor_id, stddev, E, H, _ptr(w, C.c_uint16))
+    return w
+
+
+def moe_min_margin(reset=True) -> float:
+    return float(lib().orc_moe_min_margin(int(reset)))
 
 
 class Model:
@@ -292,6 +319,32 @@ class Model:
                                     _ptr(np.ascontiguousarray(b), C.c_uint16))
         if rc != 0:
             raise KeyError(tensor_id)
+
+    def set_router(self, layer: int, w):
+        if lib().orc_model_set_router(self.h, layer, _ptr(np.ascontiguousarray(w, np.uint16), C.c_uint16)):
+            raise KeyError(layer)
+
+    def route(self, layer: int, x):
+        """(expert ids, weights, margin) of one token's normalised MLP input"""
+        k = self.cfg.top_k
+        ids = np.zeros(k, np.int32)
+        w = np.zeros(k, np.float32)
+        xv = np.ascontiguousarray(x, np.float32)
+        mg = lib().orc_moe_route(self.h, layer, _ptr(xv, C.c_float), _ptr(ids, C.c_int32), _ptr(w, C.c_float))
+        return ids, w, float(mg)
+
+    def moe_mlp(self, layer: int, x):
+        """(y, ids, weights, margins) of the MoE MLP of `layer` on x [M][hidden]"""
+        xv = np.ascontiguousarray(x, np.float32)
+        M = xv.shape[0]
+        k = self.cfg.top_k
+        y = np.zeros((M, self.cfg.hidden), np.float32)
+        ids = np.zeros((M, k), np.int32)
+        w = np.zeros((M, k), np.float32)
+        mg = np.zeros(M, np.float32)
+        lib().orc_moe_mlp(self.h, layer, _ptr(xv, C.c_float), M, _ptr(y, C.c_float), _ptr(ids, C.c_int32),
+                          _ptr(w, C.c_float), _ptr(mg, C.c_float))
+        return y, ids, w, mg
 
     def get_q4(self, tensor_id: int):
         wq, s, b = C.POINTER(C.c_uint32)(), C.POINTER(C.c_uint16)(), C.POINTER(C.c_uint16)()
