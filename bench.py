@@ -427,6 +427,32 @@ def run_kernel_case(args):
             A.check(L.mlxcat_op_q4_linear(p(W[j]), p(S[j]), p(B[j]), N, K, p(x), M, p(y), p(ws),
                                           ws_bytes, None))
         shape = {"N": N, "K": K, "M": M, "copies": copies}
+    elif args.kernel_case == "moe":
+        # one layer's sparse MoE MLP (router, gate/up + SwiGLU, down, combine);
+        # the experts of one layer (E x 3 q4 matrices) are larger than L2
+        H, I, E, TK = cfg.hidden, cfg.intermediate, cfg.n_experts, cfg.top_k
+        if not E:
+            raise SystemExit("--kernel-case moe needs a MoE workload")
+        copies = 2
+        shapes = ((I, H), (I, H), (H, I))
+        Wt = [[(torch.randint(-2**31, 2**31 - 1, (E, n, k // 8), dtype=torch.int32, device="cuda"),
+                (torch.rand((E, n, k // 64), device="cuda") * 1e-2).half(),
+                (torch.rand((E, n, k // 64), device="cuda") * -1e-2).half()) for (n, k) in shapes]
+              for _ in range(copies)]
+        router = (torch.randn((E, H), device="cuda") * 0.02).to(torch.bfloat16)
+        x = torch.randn((M, H), device="cuda").half()
+        y = torch.empty((M, H), dtype=torch.float32, device="cuda")
+        ws_bytes = L.mlxcat_op_moe_workspace(M, H, I, E, TK)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+        ptrs = [tuple(A._vp3(*[Wt[j][kind][f].data_ptr() for kind in range(3)]) for f in range(3))
+                for j in range(copies)]
+        algo = E * 3 * (I * H // 2 + I * (H // 64) * 4) + E * H * 2 + M * H * 2 + M * H * 4
+
+        def launch(i):
+            wq, sc, bi = ptrs[i % copies]
+            A.check(L.mlxcat_op_moe(p(x), M, H, I, E, TK, 1, p(router), wq, sc, bi, p(y), None, None,
+                                    p(ws), ws_bytes, None))
+        shape = {"M": M, "hidden": H, "intermediate": I, "experts": E, "top_k": TK, "copies": copies}
     else:
         Hq, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         ctx_len = wl["prompt"] + wl["max_new"] // 2
@@ -472,7 +498,7 @@ def main():
     ap.add_argument("--config", default="qwen3-4b", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="mlxcat", choices=["mlxcat", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-case", choices=["q4_linear", "attention"])
+    ap.add_argument("--kernel-case", choices=["q4_linear", "attention", "moe"])
     ap.add_argument("--kernel-reps", type=int, default=50)
     args = ap.parse_args()
     if args.kernel_case:

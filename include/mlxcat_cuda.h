@@ -59,6 +59,14 @@ typedef struct {
      * experts per token, each a q4 SwiGLU of width `intermediate`;
      * norm_topk renormalises the k routing weights.  0 = dense MLP. */
     int32_t n_experts, top_k, norm_topk;
+    /* Tensor parallelism over tp_size GPUs (0 or 1: off), this context being
+     * rank tp_rank: q/k/v heads and gate/up rows split by rank (column-split),
+     * o/down inputs split (row-split), one allreduce after the attention and
+     * one after the MLP block of every layer (NCCL, see mlxcat_ctx_tp_connect).
+     * Embedding, lm_head and norms are replicated; every rank runs the same
+     * rows.  Weight and KV-cache calls on such a context address the rank's
+     * slice (n_heads/tp_size heads, intermediate/tp_size MLP rows). */
+    int32_t tp_size, tp_rank;
 } mlxcat_model_config;
 
 /* SamplingParameters subset on the path (Sampling.swift:139-217). */
@@ -93,6 +101,13 @@ typedef struct mlxcat_cache mlxcat_cache;
  * replaces: model construction + MLX device stream (NativeModelEngine.swift:44-54) */
 MLXCAT_API int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx **out);
 MLXCAT_API int mlxcat_ctx_destroy(mlxcat_ctx *ctx);
+/* Tensor parallelism: one rank creates an id (ncclGetUniqueId), the host
+ * hands the 128 bytes to every rank, each rank connects its context
+ * (ncclCommInitRank; collective: all ranks call it).  NCCL is loaded at run
+ * time (libnccl.so.2); without it these return MLXCAT_E_STATE.  Must precede
+ * the first forward on a context with tp_size > 1. */
+MLXCAT_API int mlxcat_tp_unique_id(uint8_t id[128]);
+MLXCAT_API int mlxcat_ctx_tp_connect(mlxcat_ctx *ctx, const uint8_t id[128]);
 MLXCAT_API const char *mlxcat_last_error(const mlxcat_ctx *ctx);
 /* the context's CUDA stream (cudaStream_t), for callers that time or order work */
 MLXCAT_API int mlxcat_ctx_stream(mlxcat_ctx *ctx, void **stream);

@@ -36,6 +36,7 @@ class ModelConfigC(C.Structure):
         ("qk_norm", C.c_int32), ("rms_eps", C.c_float), ("rope_theta", C.c_float),
         ("group_size", C.c_int32), ("bits", C.c_int32),
         ("n_experts", C.c_int32), ("top_k", C.c_int32), ("norm_topk", C.c_int32),
+        ("tp_size", C.c_int32), ("tp_rank", C.c_int32),
     ]
 
 
@@ -77,6 +78,8 @@ _vp3 = C.c_void_p * 3   # const T *const [3]: gate, up, down
 PROTOTYPES = {
     "mlxcat_ctx_create": (C.c_int, [C.POINTER(ModelConfigC), _i32, C.POINTER(_vp)]),
     "mlxcat_ctx_destroy": (C.c_int, [_vp]),
+    "mlxcat_tp_unique_id": (C.c_int, [_vp]),
+    "mlxcat_ctx_tp_connect": (C.c_int, [_vp, _vp]),
     "mlxcat_last_error": (C.c_char_p, [_vp]),
     "mlxcat_ctx_stream": (C.c_int, [_vp, C.POINTER(_vp)]),
     "mlxcat_ctx_synchronize": (C.c_int, [_vp]),

@@ -42,9 +42,12 @@ struct Q4Weight {
 
 // ---- weight synthesis (seeded N(0, std) then affine q4, bit-exact with the
 //      CPU restatement) ------------------------------------------------------
+// row_base / col_base / k_total: the slice [row_base.., col_base..] of a tensor
+// with k_total columns (tensor-parallel shards); defaults give the whole tensor
 cudaError_t synth_q4(uint64_t seed, uint32_t tensor_id, float stddev, int N, int K,
                      uint32_t *wq, __half *scales, __half *biases, int row_offset,
-                     cudaStream_t st, int rgroup = 0, int rstride = 0);
+                     cudaStream_t st, int rgroup = 0, int rstride = 0, int row_base = 0,
+                     int col_base = 0, int k_total = 0);
 
 // ---- q4 linear (small-M path): out[s][M][N] fp32 partials over split s ----
 int q4_linear_splits(int N, int K, int M, int sm_count);
@@ -164,6 +167,7 @@ struct MoERouteArgs {
     int *exp_count = nullptr;       // [E]
     int32_t *exp_list = nullptr;    // [E][list_cap]
     int list_cap = 0;
+    float *logits = nullptr;        // scratch [M][E]
 };
 // grouped expert linear over all E experts of one layer: weights [E][N][K/8]
 // (+ scales/biases [E][N][K/64]), the MLX SwitchGLU layout.  epi 0: gate (wq)
@@ -199,7 +203,6 @@ struct MoECombineArgs {
     float *norm_part = nullptr;
     int norm_rows = 0;
 };
-size_t moe_route_smem(int H, int E);
 cudaError_t moe_route(const MoERouteArgs &a, cudaStream_t st);
 cudaError_t moe_expert(const MoEExpertArgs &a, int epi, cudaStream_t st);
 cudaError_t moe_combine(const MoECombineArgs &a, cudaStream_t st);
@@ -207,6 +210,13 @@ cudaError_t moe_combine(const MoECombineArgs &a, cudaStream_t st);
 // the CPU restatement's orc_router_synth)
 cudaError_t router_synth(uint64_t seed, uint32_t tensor_id, float stddev, int E, int H, void *w,
                          cudaStream_t st);
+
+// ---- tensor parallelism (tp.cu): NCCL opened at run time; error strings or nullptr
+bool tp_available();
+const char *tp_unique_id(uint8_t *out128);
+const char *tp_connect(void **comm, const uint8_t *id128, int nranks, int rank);
+const char *tp_allreduce_sum(void *comm, float *buf, size_t n, cudaStream_t st);
+void tp_destroy(void *comm);
 
 // ---- decode attention (split-K over keys, GQA) -----------------------------
 // Tokens come in groups of `qg` consecutive positions of one row (the verify

@@ -9,14 +9,16 @@
 //
 // Kernels (one verify step touches every expert, so the experts' q4 weights
 // stream from HBM once per layer like a dense MLP's):
-//   moe_route_kernel    bf16 router GEMV + softmax + top-k for RT tokens per CTA;
-//                       appends each (token, slot) assignment to its expert's
-//                       list (atomic slot, fixed capacity = token rows).
+//   moe_logits_kernel   bf16 router GEMV, 4 tokens x 4 experts per warp, logits
+//                       rounded to bf16;
+//   moe_topk_kernel     softmax + top-k, one warp per token; appends each
+//                       (token, slot) assignment to its expert's list (atomic
+//                       slot, fixed capacity = token rows).
 //   moe_expert_kernel   grouped q4 linear: CTA = (128-row tile, expert); the
 //                       expert's assignments are the columns.  Weights stay in
 //                       the MLX SwitchGLU layout, [E][out][in/8] per projection,
-//                       and are the A operand of mma.m16n8k16 (dequantised in registers from
-//                       coalesced 16-byte loads), tokens the B operand in groups
+//                       and are the A operand of mma.m16n8k16 (dequantised in
+//                       registers from coalesced 16-byte loads), tokens the B operand in groups
 //                       of 8 -- a ~20-token expert wastes at most 7 columns.
 //                       GATEUP: one tile = 64 gate rows + the matching 64 up
 //                       rows, SwiGLU epilogue into the down projection's
@@ -72,13 +74,11 @@ __device__ __forceinline__ float bf16_round(float x) {
 }
 
 // ---------------------------------------------------------------------------
-// router + top-k
+// router logits: warp = 4 tokens x 4 experts, lanes split k in 8-wide blocks;
+// CTA = 8 warps = 32 experts of 4 tokens (grid: token groups x E/32)
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(ROUTE_THREADS)
-moe_route_kernel(MoERouteArgs a) {
-    extern __shared__ float rsm[];
-    float *xs = rsm;                       // [RT][H]
-    float *ls = rsm + (size_t)RT * a.H;    // [RT][E]
+moe_logits_kernel(MoERouteArgs a) {
     __shared__ float sc[RT];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int m0 = blockIdx.x * RT;
@@ -88,31 +88,44 @@ moe_route_kernel(MoERouteArgs a) {
         float s = 0.f;
         if (m < a.M && !a.col_part) {
             s = 1.f;   // operand already normalised
-            a.tok_scale[m] = s;
         } else if (m < a.M) {
             // folded RMSNorm of the operand: rstd from the producer's block sums
             float ss = 0.f;
             for (int b = 0; b < H / 128; ++b) ss += __ldcg(a.col_part + (size_t)b * a.norm_rows + m);
             const float r = 1.0f / sqrtf(ss / (float)H + a.eps);
-            a.col_rstd[m] = r;
+            if (blockIdx.y == 0) a.col_rstd[m] = r;
             s = r / __ldcg(a.col_prev + m);
-            a.tok_scale[m] = s;
         }
+        if (m < a.M && blockIdx.y == 0) a.tok_scale[m] = s;
         sc[tid] = s;
     }
-    for (int i = tid; i < RT * H; i += ROUTE_THREADS) {
-        const int t = i / H, k = i - t * H, m = m0 + t;
-        xs[i] = m < a.M ? __half2float(a.x[xblk(m, k, a.ldx_rows)]) : 0.f;
-    }
     __syncthreads();
-    // logits: warp w takes experts w, w+8, ...; lanes split k in 8-wide slices
-    for (int e = warp; e < E; e += ROUTE_THREADS / 32) {
-        float acc[RT];
+    const int e0 = (blockIdx.y * (ROUTE_THREADS / 32) + warp) * 4;
+    float acc[RT][4];
 #pragma unroll
-        for (int t = 0; t < RT; ++t) acc[t] = 0.f;
-        const __nv_bfloat16 *wr = a.wr + (size_t)e * H;
-        for (int k0 = lane * 8; k0 < H; k0 += 256) {
-            const uint4 wv = *reinterpret_cast<const uint4 *>(wr + k0);
+    for (int t = 0; t < RT; ++t)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[t][q] = 0.f;
+    for (int b = lane; b < H / 8; b += 32) {
+        // operand 8-block b of each token, perm8 order (k0, k0+4, k0+1, k0+5, ...)
+        float xv[RT][8];
+#pragma unroll
+        for (int t = 0; t < RT; ++t) {
+            const int m = m0 + t;
+            uint4 u = make_uint4(0, 0, 0, 0);
+            if (m < a.M)
+                u = *reinterpret_cast<const uint4 *>(a.x + ((size_t)(b >> 3) * a.ldx_rows + m) * 64 + (b & 7) * 8);
+            const __half2 *h2 = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(h2[i]);
+                xv[t][2 * i] = f.x;       // natural k0 + i
+                xv[t][2 * i + 1] = f.y;   // natural k0 + i + 4
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint4 wv = *reinterpret_cast<const uint4 *>(a.wr + (size_t)(e0 + q) * H + 8 * b);
             const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&wv);
             float w[8];
 #pragma unroll
@@ -123,73 +136,80 @@ moe_route_kernel(MoERouteArgs a) {
             }
 #pragma unroll
             for (int t = 0; t < RT; ++t) {
-                const float4 x0 = *reinterpret_cast<const float4 *>(xs + t * H + k0);
-                const float4 x1 = *reinterpret_cast<const float4 *>(xs + t * H + k0 + 4);
-                acc[t] += x0.x * w[0] + x0.y * w[1] + x0.z * w[2] + x0.w * w[3] +
-                          x1.x * w[4] + x1.y * w[5] + x1.z * w[6] + x1.w * w[7];
-            }
-        }
+                float d = 0.f;
 #pragma unroll
-        for (int t = 0; t < RT; ++t) {
-            const float v = warp_sum(acc[t]);
-            if (lane == 0) ls[t * E + e] = bf16_round(v * sc[t]);
+                for (int i = 0; i < 4; ++i) d += xv[t][2 * i] * w[i] + xv[t][2 * i + 1] * w[i + 4];
+                acc[t][q] += d;
+            }
         }
     }
-    __syncthreads();
-    // softmax + top-k: warp t routes token m0 + t; lane holds experts lane + 32 i
-    if (warp < RT && m0 + warp < a.M) {
-        const int m = m0 + warp;
-        const int per = E / 32;
-        float l[8], p[8];
-        bool used[8];
-        float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            l[i] = i < per ? ls[warp * E + lane + 32 * i] : -INFINITY;
-            used[i] = i >= per;
-            mx = fmaxf(mx, l[i]);
+    for (int t = 0; t < RT; ++t)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float v = warp_sum(acc[t][q]);
+            if (lane == 0 && m0 + t < a.M) a.logits[(size_t)(m0 + t) * E + e0 + q] = bf16_round(v * sc[t]);
         }
-        mx = warp_max(mx);
-        float den = 0.f;
+}
+
+// ---------------------------------------------------------------------------
+// softmax + top-k: one warp per token; lane holds experts lane + 32 i
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(ROUTE_THREADS)
+moe_topk_kernel(MoERouteArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int m = blockIdx.x * (ROUTE_THREADS / 32) + (threadIdx.x >> 5);
+    if (m >= a.M) return;
+    const int E = a.E, per = E / 32;
+    float l[8], p[8];
+    bool used[8];
+    float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            p[i] = i < per ? expf(l[i] - mx) : 0.f;
-            den += p[i];
+    for (int i = 0; i < 8; ++i) {
+        l[i] = i < per ? __ldcg(a.logits + (size_t)m * E + lane + 32 * i) : -INFINITY;
+        used[i] = i >= per;
+        mx = fmaxf(mx, l[i]);
+    }
+    mx = warp_max(mx);
+    float den = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        p[i] = i < per ? expf(l[i] - mx) : 0.f;
+        den += p[i];
+    }
+    den = warp_sum(den);
+    float sel = 0.f;
+    float wsel = 0.f;   // lane j keeps the weight of pick j
+    int isel = 0;
+    for (int j = 0; j < a.TK; ++j) {
+        // lane's best unused (largest logit, then lowest index)
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (!used[i] && (l[i] > bv || (l[i] == bv && lane + 32 * i < bi))) { bv = l[i]; bi = lane + 32 * i; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
-        den = warp_sum(den);
-        float sel = 0.f;
-        float wsel = 0.f;   // lane j keeps the weight of pick j
-        int isel = 0;
-        for (int j = 0; j < a.TK; ++j) {
-            // lane's best unused (largest logit, then lowest index)
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
+        const int owner = bi & 31, slot = bi >> 5;
+        float pw = 0.f;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (!used[i] && (l[i] > bv || (l[i] == bv && lane + 32 * i < bi))) { bv = l[i]; bi = lane + 32 * i; }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-            }
-            const int owner = bi & 31, slot = bi >> 5;
-            float pw = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (lane == owner && i == slot) { used[i] = true; pw = p[i] / den; }
-            pw = __shfl_sync(0xffffffffu, pw, owner);
-            sel += pw;
-            if (lane == j) { wsel = pw; isel = bi; }
-        }
-        if (lane < a.TK) {
-            const float w = a.norm_topk ? wsel / sel : wsel;
-            const int asg = m * a.TK + lane;
-            a.topk_w[asg] = w;
-            a.topk_id[asg] = isel;
-            const int s = atomicAdd(a.exp_count + isel, 1);
-            a.exp_list[(size_t)isel * a.list_cap + s] = asg;
-        }
+        for (int i = 0; i < 8; ++i)
+            if (lane == owner && i == slot) { used[i] = true; pw = p[i] / den; }
+        pw = __shfl_sync(0xffffffffu, pw, owner);
+        sel += pw;
+        if (lane == j) { wsel = pw; isel = bi; }
+    }
+    if (lane < a.TK) {
+        const float w = a.norm_topk ? wsel / sel : wsel;
+        const int asg = m * a.TK + lane;
+        a.topk_w[asg] = w;
+        a.topk_id[asg] = isel;
+        const int s = atomicAdd(a.exp_count + isel, 1);
+        a.exp_list[(size_t)isel * a.list_cap + s] = asg;
     }
 }
 
@@ -363,35 +383,54 @@ moe_expert_kernel(MoEExpertArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// combine + folded RMSNorm producer
+// combine + folded RMSNorm producer: thread = 8 consecutive features (two
+// 16-byte loads per source row), 16 threads = one 128-feature norm block
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(COMBINE_THREADS)
 moe_combine_kernel(MoECombineArgs a) {
-    __shared__ float wsum[64];   // per 32-feature slice (H <= 2048 per pass of 256 x 8)
     const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
-    const int H = a.H;
+    const int H = a.H, tk = a.TK;
     const float s = a.norm_w ? __ldcg(a.norm_scale + m) : 0.f;
-    for (int base = 0; base < H; base += 2048) {
-        const int span = min(2048, H - base);
-        for (int i = tid; i < span; i += COMBINE_THREADS) {
-            const int f = base + i;
-            float v = a.h[(size_t)m * H + f];
-            for (int j = 0; j < a.TK; ++j) v += __ldcg(a.y + ((size_t)m * a.TK + j) * H + f);
-            a.h[(size_t)m * H + f] = v;
-            if (a.norm_w) {
-                a.xout[xblk(m, f, a.ldx_rows)] = __float2half_rn(v * a.norm_w[f] * s);
-                const float q = warp_sum(v * v);
-                if (lane == 0) wsum[i >> 5] = q;
-            }
+    for (int base = 0; base < H; base += 8 * COMBINE_THREADS) {
+        const int f0 = base + 8 * tid;
+        const bool on = f0 < H;
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (on) {
+            float4 *hp = reinterpret_cast<float4 *>(a.h + (size_t)m * H + f0);
+            float4 y[16];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (j < tk) {
+                    const float4 *yp = reinterpret_cast<const float4 *>(a.y + ((size_t)m * tk + j) * H + f0);
+                    y[2 * j] = __ldcg(yp);
+                    y[2 * j + 1] = __ldcg(yp + 1);
+                }
+            const float4 h0 = hp[0], h1 = hp[1];
+            v[0] = h0.x; v[1] = h0.y; v[2] = h0.z; v[3] = h0.w;
+            v[4] = h1.x; v[5] = h1.y; v[6] = h1.z; v[7] = h1.w;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (j < tk) {   // selection order
+                    v[0] += y[2 * j].x; v[1] += y[2 * j].y; v[2] += y[2 * j].z; v[3] += y[2 * j].w;
+                    v[4] += y[2 * j + 1].x; v[5] += y[2 * j + 1].y; v[6] += y[2 * j + 1].z; v[7] += y[2 * j + 1].w;
+                }
+            hp[0] = make_float4(v[0], v[1], v[2], v[3]);
+            hp[1] = make_float4(v[4], v[5], v[6], v[7]);
         }
         if (a.norm_w) {
-            __syncthreads();
-            if (tid < span / 128) {
-                const int b = tid;
-                a.norm_part[(size_t)(base / 128 + b) * a.norm_rows + m] =
-                    wsum[4 * b] + wsum[4 * b + 1] + wsum[4 * b + 2] + wsum[4 * b + 3];
+            float sq = 0.f;
+            if (on) {
+                __align__(16) __half o[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    o[perm8(i)] = __float2half_rn(v[i] * a.norm_w[f0 + i] * s);
+                    sq += v[i] * v[i];
+                }
+                *reinterpret_cast<uint4 *>(a.xout + xblk(m, f0, a.ldx_rows)) = *reinterpret_cast<const uint4 *>(o);
             }
-            __syncthreads();
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            if (on && (lane & 15) == 0) a.norm_part[(size_t)(f0 / 128) * a.norm_rows + m] = sq;
         }
     }
 }
@@ -405,17 +444,13 @@ __global__ void router_synth_kernel(uint64_t seed, uint32_t tensor_id, float std
 
 }  // namespace
 
-size_t moe_route_smem(int H, int E) { return sizeof(float) * (size_t)RT * (H + E); }
-
 cudaError_t moe_route(const MoERouteArgs &a, cudaStream_t st) {
-    if (a.E % 32 || a.E > 256 || a.TK < 1 || a.TK > 8 || a.TK > a.E || a.H % 256 || a.M <= 0)
+    if (a.E % 32 || a.E > 256 || a.TK < 1 || a.TK > 8 || a.TK > a.E || a.H % 256 || a.M <= 0 || !a.logits)
         return cudaErrorInvalidValue;
-    const size_t sm = moe_route_smem(a.H, a.E);
-    if (sm > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        if (e != cudaSuccess) return e;
-    }
-    moe_route_kernel<<<(a.M + RT - 1) / RT, ROUTE_THREADS, sm, st>>>(a);
+    moe_logits_kernel<<<dim3((a.M + RT - 1) / RT, a.E / 32), ROUTE_THREADS, 0, st>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    moe_topk_kernel<<<(a.M + ROUTE_THREADS / 32 - 1) / (ROUTE_THREADS / 32), ROUTE_THREADS, 0, st>>>(a);
     return cudaGetLastError();
 }
 
@@ -428,7 +463,7 @@ cudaError_t moe_expert(const MoEExpertArgs &a, int epi, cudaStream_t st) {
 }
 
 cudaError_t moe_combine(const MoECombineArgs &a, cudaStream_t st) {
-    if (a.H % 128 || a.M <= 0) return cudaErrorInvalidValue;
+    if (a.H % 128 || a.M <= 0 || a.TK < 1 || a.TK > 8) return cudaErrorInvalidValue;
     moe_combine_kernel<<<a.M, COMBINE_THREADS, 0, st>>>(a);
     return cudaGetLastError();
 }

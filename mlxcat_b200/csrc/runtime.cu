@@ -63,7 +63,11 @@ struct RowMap {
 }  // namespace
 
 struct mlxcat_ctx {
-    mlxcat_model_config cfg{};
+    // cfg: this rank's view (per-rank head / MLP widths when tensor-parallel);
+    // gcfg: the model as configured by the caller
+    mlxcat_model_config cfg{}, gcfg{};
+    int tp = 1, tp_rank = 0;
+    void *nccl = nullptr;   // ncclComm_t of the tensor-parallel group
     int device = 0, sm_count = 148;
     cudaStream_t stream = nullptr;
     std::string err;
@@ -123,11 +127,12 @@ struct mlxcat_cache {
     // folded RMSNorm: per-block sums of squares of h [H/128][rows], and the rstd of
     // the attention-norm and MLP-norm inputs of each token row (pre-scales)
     float *norm_part = nullptr, *r_attn = nullptr, *r_mlp = nullptr;
+    float *tp_part = nullptr;          // tensor parallel: this rank's O / down partial sums [rows][H]
     // sparse MoE: routing, per-expert assignment lists (counts per layer, zeroed
     // once per forward), SwiGLU activations per assignment, scaled expert outputs
     int32_t *moe_id = nullptr, *moe_list = nullptr;
     int *moe_count = nullptr;
-    float *moe_w = nullptr, *moe_scale = nullptr, *moe_y = nullptr;
+    float *moe_w = nullptr, *moe_scale = nullptr, *moe_y = nullptr, *moe_logits = nullptr;
     __half *moe_act = nullptr;
     size_t part_floats = 0;
     unsigned *counters = nullptr;     // split-K tickets of the q4 linear (self-resetting)
@@ -235,6 +240,16 @@ bool valid_config(const mlxcat_model_config *c, std::string &why) {
     }
     if (c->n_heads % c->n_kv_heads) { why = "n_heads must be a multiple of n_kv_heads"; return false; }
     if (c->head_dim != 64 && c->head_dim != 128) { why = "head_dim must be 64 or 128"; return false; }
+    if (c->tp_size > 1) {
+        const int T = c->tp_size;
+        if (c->tp_rank < 0 || c->tp_rank >= T) { why = "tp_rank must be in [0, tp_size)"; return false; }
+        if (c->n_kv_heads % T) { why = "n_kv_heads must be a multiple of tp_size"; return false; }
+        if (c->intermediate % T || (c->intermediate / T) % 128) {
+            why = "intermediate / tp_size must be a multiple of 128";
+            return false;
+        }
+        if (c->n_experts > 0) { why = "tensor parallelism is for dense models"; return false; }
+    }
     if (c->n_experts < 0) { why = "n_experts must be >= 0"; return false; }
     if (c->n_experts > 0) {
         if (c->n_experts % 32 || c->n_experts > 256) { why = "n_experts must be a multiple of 32, at most 256"; return false; }
@@ -275,6 +290,29 @@ struct ProfScope {
         if (e1) cudaEventRecordWithFlags(e1, c->ctx->stream, cudaEventRecordExternal);
     }
 };
+
+// Tensor-parallel residual step: this rank's slice of a row-split projection
+// (O or down) as fp32 partial sums, one allreduce (sum) over the group, then
+// h += y with the next linear's folded-norm operand fp16(h * norm_w * s) and
+// per-block sums of squares -- what the RESID epilogue does on one GPU.
+int tp_residual(mlxcat_cache *c, const DevLin &w, const __half *x, int M, const float *norm_w,
+                const float *norm_scale, __half *xout) {
+    mlxcat_ctx *ctx = c->ctx;
+    const int H = ctx->cfg.hidden, R = c->m_cap;
+    cudaStream_t st = ctx->stream;
+    Q4Epilogue e;
+    e.part = c->part; e.counters = c->counters; e.err = c->err; e.pdl = 1;
+    e.op = Q4Epilogue::STORE; e.out = c->tp_part; e.ldo = H;
+    { ProfScope ps(c, 0); LK(ctx, q4_tc(w.tc(), x, R, 0, M, ctx->sm_count, e, st)); }
+    if (const char *er = tp_allreduce_sum(ctx->nccl, c->tp_part, (size_t)M * H, st))
+        return set_err(ctx, MLXCAT_E_CUDA, "allreduce: %s", er);
+    MoECombineArgs ca;
+    ca.h = c->h; ca.y = c->tp_part; ca.M = M; ca.H = H; ca.TK = 1;
+    ca.norm_w = norm_w; ca.norm_scale = norm_scale; ca.xout = xout; ca.ldx_rows = R;
+    ca.norm_part = c->norm_part; ca.norm_rows = R;
+    LK(ctx, moe_combine(ca, st));
+    return MLXCAT_OK;
+}
 
 // ---------------------------------------------------------------------------
 // forward over M tokens (tok/trow/tpos on device); logits for tokens
@@ -324,7 +362,10 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
         { ProfScope ps(c, 1);
           LK(ctx, attention(c->qbuf, kv, trow, tpos, M, qg, Hq, Hkv, D, KEY_CHUNK, c->attn_splits,
                             c->attn, c->xn, true, R, st, true)); }
-        {   // output projection into the residual stream
+        if (ctx->tp > 1) {   // row-split output projection: partial sums, allreduce, residual
+            int rc = tp_residual(c, ctx->o[l], c->xn, M, ctx->mlp_norm(l), c->r_attn, c->xg);
+            if (rc) return rc;
+        } else {   // output projection into the residual stream
             Q4Epilogue e = ep;
             e.op = Q4Epilogue::RESID; e.out = c->h; e.ldo = H;
             // + the MLP input fp16(h * mlp_norm * r_attn) (not into xn: other CTAs
@@ -342,7 +383,8 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
             ra.wr = ctx->moe[l].router;
             ra.col_part = c->norm_part; ra.col_prev = c->r_attn; ra.col_rstd = c->r_mlp; ra.norm_rows = R;
             ra.eps = eps; ra.tok_scale = c->moe_scale; ra.topk_id = c->moe_id; ra.topk_w = c->moe_w;
-            ra.exp_count = cnt; ra.exp_list = c->moe_list; ra.list_cap = c->m_cap;
+            ra.exp_count = cnt; ra.exp_list = c->moe_list; ra.list_cap = c->m_cap; ra.logits = c->moe_logits;
+            ctx->launches++;   // logits + top-k
             LK(ctx, moe_route(ra, st));
             const auto &mb = ctx->moe[l];
             MoEExpertArgs xa;
@@ -373,6 +415,12 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
             ProfScope ps(c, 0);
             LK(ctx, q4_tc(ctx->gu[l].tc(), c->xg, R, 0, M, ctx->sm_count, e, st));
         }
+        if (ctx->tp > 1) {   // row-split down projection
+            int rc = tp_residual(c, ctx->down[l], c->xa, M, l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(),
+                                 c->r_mlp, c->xn);
+            if (rc) return rc;
+            continue;
+        }
         {   // down projection into the residual stream
             Q4Epilogue e = ep;
             e.op = Q4Epilogue::RESID; e.out = c->h; e.ldo = H;
@@ -397,6 +445,7 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
 
 int check_weights(mlxcat_ctx *ctx) {
     if (!ctx->have_weights) return set_err(ctx, MLXCAT_E_STATE, "weights not loaded");
+    if (ctx->tp > 1 && !ctx->nccl) return set_err(ctx, MLXCAT_E_STATE, "tensor-parallel context not connected");
     return MLXCAT_OK;
 }
 
@@ -520,7 +569,24 @@ int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx
     if (device < 0 || device >= ndev) return op_err(MLXCAT_E_INVALID, "device %d out of range", device);
     mlxcat_ctx *ctx = new mlxcat_ctx();
     ctx->cfg = *cfg;
+    ctx->gcfg = *cfg;
     ctx->device = device;
+    if (cfg->kind == MLXCAT_MODEL_TRANSFORMER && cfg->tp_size > 1) {
+        // this rank's slice: whole KV heads with their query-head groups, a
+        // contiguous block of MLP rows
+        ctx->tp = cfg->tp_size;
+        ctx->tp_rank = cfg->tp_rank;
+        ctx->cfg.n_heads = cfg->n_heads / ctx->tp;
+        ctx->cfg.n_kv_heads = cfg->n_kv_heads / ctx->tp;
+        ctx->cfg.intermediate = cfg->intermediate / ctx->tp;
+        ctx->cfg.tp_size = 1;
+        ctx->cfg.tp_rank = 0;
+        std::string lwhy;
+        if (!valid_config(&ctx->cfg, lwhy)) {
+            delete ctx;
+            return op_err(MLXCAT_E_INVALID, "per-rank slice: %s", lwhy.c_str());
+        }
+    }
     auto fail = [&](int code) {
         g_op_err = ctx->err;
         mlxcat_ctx_destroy(ctx);
@@ -592,10 +658,27 @@ int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx
     return MLXCAT_OK;
 }
 
+int mlxcat_tp_unique_id(uint8_t id[128]) {
+    if (!id) return op_err(MLXCAT_E_INVALID, "null id buffer");
+    if (const char *e = tp_unique_id(id)) return op_err(MLXCAT_E_STATE, "tensor parallel id: %s", e);
+    return MLXCAT_OK;
+}
+
+int mlxcat_ctx_tp_connect(mlxcat_ctx *ctx, const uint8_t id[128]) {
+    if (!ctx || !id) return MLXCAT_E_INVALID;
+    if (ctx->tp <= 1) return set_err(ctx, MLXCAT_E_STATE, "context is not tensor-parallel (tp_size <= 1)");
+    if (ctx->nccl) return set_err(ctx, MLXCAT_E_STATE, "context already connected");
+    CK(ctx, cudaSetDevice(ctx->device));
+    if (const char *e = tp_connect(&ctx->nccl, id, ctx->tp, ctx->tp_rank))
+        return set_err(ctx, MLXCAT_E_STATE, "tensor parallel connect: %s", e);
+    return MLXCAT_OK;
+}
+
 int mlxcat_ctx_destroy(mlxcat_ctx *ctx) {
     if (!ctx) return MLXCAT_OK;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    tp_destroy(ctx->nccl);
     for (void *p : ctx->allocs) cudaFree(p);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -714,8 +797,22 @@ int mlxcat_weights_synth(mlxcat_ctx *ctx, uint64_t seed, float stddev) {
     for (uint32_t id : ids) {
         RowMap rm;
         DevLin *w = lin_for(ctx, id, &rm);
+        // tensor parallel: this rank's rows (q, k, v, gate, up) or columns (o, down)
+        // of the full tensor, drawn from the full tensor's weight stream
+        int row_base = 0, col_base = 0, k_total = 0;
+        if (ctx->tp > 1 && id < 0xFFFF0000u) {
+            const int kind = (int)(id % 16u), r = ctx->tp_rank, D = c.head_dim;
+            switch (kind) {
+            case 0: row_base = r * c.n_heads * D; break;
+            case 1: case 2: row_base = r * c.n_kv_heads * D; break;
+            case 3: col_base = r * c.n_heads * D; k_total = ctx->gcfg.n_heads * D; break;
+            case 4: case 5: row_base = r * c.intermediate; break;
+            case 6: col_base = r * c.intermediate; k_total = ctx->gcfg.intermediate; break;
+            default: break;
+            }
+        }
         LK(ctx, synth_q4(seed, id, stddev, rm.rows, w->K, w->wq, w->s, w->b, rm.offset, ctx->stream,
-                         rm.group, rm.stride));
+                         rm.group, rm.stride, row_base, col_base, k_total));
     }
     for (uint32_t id : ids) {   // fused matrices are packed once per distinct buffer (repeats are harmless)
         RowMap rm;
@@ -875,6 +972,7 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
         chk(dalloc(A, &c->r_attn, (size_t)Mc));
         chk(dalloc(A, &c->r_mlp, (size_t)Mc));
         chk(dalloc(A, &c->qbuf, (size_t)Mc * Hq * D));
+        if (ctx->tp > 1) chk(dalloc(A, &c->tp_part, (size_t)Mc * H));
         if (cf.n_experts) {
             const size_t asg = (size_t)Mc * cf.top_k;
             chk(dalloc(A, &c->moe_id, asg));
@@ -884,6 +982,7 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
             chk(dalloc(A, &c->moe_count, (size_t)cf.n_layers * cf.n_experts));
             chk(dalloc(A, &c->moe_act, asg * I));
             chk(dalloc(A, &c->moe_y, asg * H));
+            chk(dalloc(A, &c->moe_logits, (size_t)Mc * cf.n_experts));
         }
         chk(dalloc(A, &c->rope, (size_t)max_len * (D / 2)));
         if (rc == MLXCAT_OK) chk(rope_table(ctx->inv_freq, D / 2, max_len, c->rope, ctx->stream));
@@ -1311,11 +1410,12 @@ int mlxcat_op_q4_linear(const uint32_t *wq, const uint16_t *scales, const uint16
 }
 
 // ---- sparse MoE MLP operator ------------------------------------------------
-static void moe_ws_layout(int32_t M, int32_t H, int32_t I, int32_t E, int32_t TK, size_t off[8]) {
-    const size_t sz[8] = {(size_t)M * H * 2, (size_t)M * 4, (size_t)M * TK * 4, (size_t)M * TK * 4,
-                          (size_t)E * 4, (size_t)E * M * 4, (size_t)M * TK * I * 2, (size_t)M * TK * H * 4};
+static void moe_ws_layout(int32_t M, int32_t H, int32_t I, int32_t E, int32_t TK, size_t off[9]) {
+    const size_t sz[9] = {(size_t)M * H * 2, (size_t)M * 4, (size_t)M * TK * 4, (size_t)M * TK * 4,
+                          (size_t)E * 4, (size_t)E * M * 4, (size_t)M * TK * I * 2, (size_t)M * E * 4,
+                          (size_t)M * TK * H * 4};
     size_t o = 0;
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 9; ++i) {
         off[i] = o;
         o += (sz[i] + 255) & ~(size_t)255;
     }
@@ -1323,9 +1423,9 @@ static void moe_ws_layout(int32_t M, int32_t H, int32_t I, int32_t E, int32_t TK
 
 size_t mlxcat_op_moe_workspace(int32_t M, int32_t hidden, int32_t intermediate, int32_t n_experts, int32_t top_k) {
     if (M <= 0 || hidden <= 0 || intermediate <= 0 || n_experts <= 0 || top_k <= 0) return 0;
-    size_t off[8];
+    size_t off[9];
     moe_ws_layout(M, hidden, intermediate, n_experts, top_k, off);
-    return off[7] + (size_t)M * top_k * hidden * 4;
+    return off[8] + (size_t)M * top_k * hidden * 4;
 }
 
 int mlxcat_op_moe(const uint16_t *x, int32_t M, int32_t hidden, int32_t intermediate, int32_t n_experts,
@@ -1342,7 +1442,7 @@ int mlxcat_op_moe(const uint16_t *x, int32_t M, int32_t hidden, int32_t intermed
                                         "1 <= top_k <= min(8, n_experts)");
     const size_t need = mlxcat_op_moe_workspace(M, H, I, E, TK);
     if (!ws || ws_bytes < need) return op_err(MLXCAT_E_INVALID, "workspace of %zu bytes required", need);
-    size_t off[8];
+    size_t off[9];
     moe_ws_layout(M, H, I, E, TK, off);
     char *w8 = static_cast<char *>(ws);
     cudaStream_t st = (cudaStream_t)stream;
@@ -1353,7 +1453,8 @@ int mlxcat_op_moe(const uint16_t *x, int32_t M, int32_t hidden, int32_t intermed
     int *cnt = reinterpret_cast<int *>(w8 + off[4]);
     int32_t *list = reinterpret_cast<int32_t *>(w8 + off[5]);
     __half *act = reinterpret_cast<__half *>(w8 + off[6]);
-    float *yt = reinterpret_cast<float *>(w8 + off[7]);
+    float *lg = reinterpret_cast<float *>(w8 + off[7]);
+    float *yt = reinterpret_cast<float *>(w8 + off[8]);
     cudaError_t e = permute_activations(reinterpret_cast<const __half *>(x), xb, M, H, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(cnt, 0, sizeof(int) * E, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)M * H, st);
@@ -1361,6 +1462,7 @@ int mlxcat_op_moe(const uint16_t *x, int32_t M, int32_t hidden, int32_t intermed
     ra.x = xb; ra.ldx_rows = M; ra.M = M; ra.H = H; ra.E = E; ra.TK = TK; ra.norm_topk = norm_topk;
     ra.wr = reinterpret_cast<const __nv_bfloat16 *>(router);
     ra.tok_scale = tsc; ra.topk_id = tid; ra.topk_w = tw; ra.exp_count = cnt; ra.exp_list = list; ra.list_cap = M;
+    ra.logits = lg;
     if (e == cudaSuccess) e = moe_route(ra, st);
     MoEExpertArgs ga;
     ga.wq = wq[0]; ga.scales = reinterpret_cast<const __half *>(scales[0]); ga.biases = reinterpret_cast<const __half *>(biases[0]);

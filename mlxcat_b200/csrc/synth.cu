@@ -7,6 +7,9 @@
 // Bit-identical with the CPU restatement (orc_q4_synth).  Logical row n is
 // written to row (n / rgroup) * rstride + n % rgroup + row_offset of the
 // destination (fused matrices: contiguous q|k|v, gate/up interleaved per 64).
+// A tensor-parallel slice (rows row_base.., columns col_base.. of a tensor with
+// k_total columns) draws the same stream elements as the full tensor, so each
+// rank's slice is bit-identical with that part of the full tensor.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -15,7 +18,7 @@ namespace mlxcat {
 __global__ void synth_q4_kernel(uint64_t seed, uint32_t tensor_id, float stddev, int N, int K,
                                 uint32_t *__restrict__ wq, __half *__restrict__ scales,
                                 __half *__restrict__ biases, int row_offset, int rgroup,
-                                int rstride) {
+                                int rstride, int row_base, int col_base, int k_total) {
     const int G = K / MLXCAT_GS;
     const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (long long)N * G) return;
@@ -23,7 +26,8 @@ __global__ void synth_q4_kernel(uint64_t seed, uint32_t tensor_id, float stddev,
     float w[MLXCAT_GS];
     float mn = 0.f, mx = 0.f;
     for (int i = 0; i < MLXCAT_GS; ++i) {
-        const uint64_t idx = (uint64_t)n * (uint64_t)K + (uint64_t)(grp * MLXCAT_GS + i);
+        const uint64_t idx = (uint64_t)(row_base + n) * (uint64_t)k_total +
+                             (uint64_t)(col_base + grp * MLXCAT_GS + i);
         w[i] = __fmul_rn(det_normal(seed, tensor_id, idx), stddev);
         if (i == 0 || w[i] < mn) mn = w[i];
         if (i == 0 || w[i] > mx) mx = w[i];
@@ -53,13 +57,16 @@ __global__ void synth_q4_kernel(uint64_t seed, uint32_t tensor_id, float stddev,
 
 cudaError_t synth_q4(uint64_t seed, uint32_t tensor_id, float stddev, int N, int K,
                      uint32_t *wq, __half *scales, __half *biases, int row_offset,
-                     cudaStream_t st, int rgroup, int rstride) {
+                     cudaStream_t st, int rgroup, int rstride, int row_base, int col_base, int k_total) {
     if (rgroup <= 0) { rgroup = N; rstride = 0; }
+    if (k_total <= 0) k_total = K;
+    if (col_base % MLXCAT_GS || col_base + K > k_total) return cudaErrorInvalidValue;
     const long long groups = (long long)N * (K / MLXCAT_GS);
     const int threads = 128;
     const long long blocks = (groups + threads - 1) / threads;
     synth_q4_kernel<<<(unsigned)blocks, threads, 0, st>>>(seed, tensor_id, stddev, N, K, wq,
-                                                          scales, biases, row_offset, rgroup, rstride);
+                                                          scales, biases, row_offset, rgroup, rstride,
+                                                          row_base, col_base, k_total);
     return cudaGetLastError();
 }
 

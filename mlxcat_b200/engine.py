@@ -50,12 +50,15 @@ class ModelConfig:
     n_experts: int = 0
     top_k: int = 0
     norm_topk: bool = True
+    # tensor parallelism: this context is rank tp_rank of tp_size (1 = off)
+    tp_size: int = 1
+    tp_rank: int = 0
 
     def to_c(self) -> A.ModelConfigC:
         return A.ModelConfigC(self.kind, self.n_layers, self.hidden, self.n_heads, self.n_kv_heads,
                               self.head_dim, self.intermediate, self.vocab, int(self.tie_embeddings),
                               int(self.qk_norm), self.rms_eps, self.rope_theta, 64, 4,
-                              self.n_experts, self.top_k, int(self.norm_topk))
+                              self.n_experts, self.top_k, int(self.norm_topk), self.tp_size, self.tp_rank)
 
     @staticmethod
     def table(vocab: int) -> "ModelConfig":
@@ -67,9 +70,11 @@ TINY = ModelConfig(4, 512, 8, 2, 64, 1408, 32000, True, False, 1e-5, 500000.0, n
 QWEN3_4B = ModelConfig(36, 2560, 32, 8, 128, 9728, 151936, True, True, 1e-6, 1e6, name="qwen3-4b")
 LLAMA3_8B = ModelConfig(32, 4096, 32, 8, 128, 14336, 128256, False, False, 1e-5, 500000.0,
                         name="llama3-8b")
+LLAMA3_70B = ModelConfig(80, 8192, 64, 8, 128, 28672, 128256, False, False, 1e-5, 500000.0,
+                         name="llama3-70b")
 QWEN3_30B_A3B = ModelConfig(48, 2048, 32, 4, 128, 768, 151936, False, True, 1e-6, 1e6,
                             name="qwen3-30b-a3b", n_experts=128, top_k=8, norm_topk=True)
-CONFIGS = {c.name: c for c in (TINY, QWEN3_4B, LLAMA3_8B, QWEN3_30B_A3B)}
+CONFIGS = {c.name: c for c in (TINY, QWEN3_4B, LLAMA3_8B, QWEN3_30B_A3B, LLAMA3_70B)}
 
 
 @dataclasses.dataclass
@@ -170,6 +175,18 @@ class Context:
 
     def check(self, rc):
         return A.check(rc, self.h)
+
+    @staticmethod
+    def tp_unique_id() -> bytes:
+        """a fresh NCCL id for a tensor-parallel group (create on one rank)"""
+        buf = (C.c_uint8 * 128)()
+        A.check(A.lib().mlxcat_tp_unique_id(buf))
+        return bytes(buf)
+
+    def tp_connect(self, uid: bytes):
+        """join the tensor-parallel group (collective over its tp_size ranks)"""
+        buf = (C.c_uint8 * 128).from_buffer_copy(uid)
+        self.check(self.L.mlxcat_ctx_tp_connect(self.h, buf))
 
     def synth_weights(self, seed: int, stddev: float = 0.02):
         self.check(self.L.mlxcat_weights_synth(self.h, seed, stddev))
