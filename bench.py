@@ -45,6 +45,9 @@ WORKLOADS = {
                       temperature=0.7, top_p=0.9, max_new=256),
     "qwen3-30b-a3b": dict(model="qwen3-30b-a3b", rows=64, prompt=8192, seg_pool=64, seg_len=64, n=3, k=4,
                           temperature=0.0, top_p=0.0, max_new=256),
+    # tensor-parallel over all ranks of the run (does not fit one GPU at 64 rows)
+    "llama3-70b": dict(model="llama3-70b", rows=64, prompt=8192, seg_pool=64, seg_len=64, n=4, k=6,
+                       temperature=0.0, top_p=0.0, max_new=256, tp=True),
 }
 WEIGHT_SEED = 20261201
 MIN_CONTEXT = 8
@@ -147,18 +150,29 @@ def run_ours(args, wl, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     cfg = model_config(wl["model"])
+    tp = bool(wl.get("tp")) and world > 1
+    if tp:   # every rank runs the same rows on its slice of the model
+        import dataclasses
+        cfg = dataclasses.replace(cfg, tp_size=world, tp_rank=rank)
     ctx = M.Context(cfg, local_rank)
+    if tp:
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(M.Context.tp_unique_id()), dtype=torch.uint8))
+        torch.distributed.broadcast(uid, 0)
+        ctx.tp_connect(bytes(uid.cpu().numpy().tobytes()))
     ctx.synth_weights(WEIGHT_SEED, 0.02)
+    prank = 0 if tp else rank   # prompt / seed stream of this rank's rows
     rows, k1 = wl["rows"], wl["k"] + 1
     max_len = wl["prompt"] + wl["max_new"] + 16
     cache = M.BatchKVCache(ctx, rows, max_len)
     spec = M.SpeculativeDecodingConfiguration(True, wl["k"], wl["n"], MIN_CONTEXT, A.ACCEPT_PREFIX)
     prompts = [segment_prompt(cfg.vocab, wl["seg_pool"], wl["seg_len"], wl["prompt"],
-                              1000 * rank + r) for r in range(rows)]
+                              1000 * prank + r) for r in range(rows)]
     t0 = time.perf_counter()
     for r, p in enumerate(prompts):
         sp = M.SamplingParameters(temperature=wl["temperature"], top_p=wl["top_p"],
-                                  seed=WEIGHT_SEED + 1000 * rank + r)
+                                  seed=WEIGHT_SEED + 1000 * prank + r)
         cache.insert_row(r, p, wl["max_new"], sp)
     ctx.synchronize()
     prefill_s = time.perf_counter() - t0
@@ -218,8 +232,9 @@ def run_ours(args, wl, rank, world, local_rank):
             prof.append(cache.profile())
     cache.set_profiling(False)
 
-    # ---- aggregate over ranks ----
-    dev_ms_max, wall_max, tokens_all = reduce_over_ranks(dev_ms, wall, tokens, world, "cuda")
+    # ---- aggregate over ranks (tensor parallel: the ranks emit the same tokens) ----
+    dev_ms_max, wall_max, tokens_all = reduce_over_ranks(dev_ms, wall, 0 if tp and rank else tokens, world,
+                                                         "cuda")
 
     result = None
     if rank == 0:
@@ -263,14 +278,16 @@ def run_ours(args, wl, rank, world, local_rank):
         result = {
             "metric": "accepted tok/s", "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+            "dtype": "f16",
             "data": "synthetic (seeded segment-pool prompts, random-init N(0,0.02) q4 weights)",
             "config": {"workload": args.config, "model": wl["model"], "rows_per_gpu": wl["rows"],
-                       "global_batch": wl["rows"] * world, "prompt_tokens": wl["prompt"],
+                       "global_batch": wl["rows"] * (1 if tp else world), "prompt_tokens": wl["prompt"],
                        "ngram_n": wl["n"], "k": wl["k"], "temperature": wl["temperature"],
                        "top_p": wl["top_p"], "max_new_tokens": wl["max_new"],
                        "acceptance": "prefix match (greedy) / single-draft rejection sampling",
-                       "parallelism": f"request-parallel x{world}",
+                       "parallelism": (f"tensor-parallel x{world} (NCCL allreduce per block)" if tp
+                                       else f"request-parallel x{world}"),
                        "l2": "inputs larger than L2: %.2f GB q4 weights + KV per step" % (ctx.weights_bytes() / 1e9)},
             "verify_step_us": verify_ms / args.steps * 1e3,
             "acceptance_rate": (accepted / proposed if proposed else None),

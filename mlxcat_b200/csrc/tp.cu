@@ -68,13 +68,19 @@ const char *tp_connect(void **comm, const uint8_t *id, int nranks, int rank) {
     ncclComm_t c = nullptr;
     const ncclResult_t r = api().comm_init_rank(&c, nranks, uid, rank);
     if (r != ncclSuccess) return err_str(r);
+    // NCCL handles the CUDA errors of its own probing internally, but they stay
+    // in the runtime's last-error slot, where the next kernel launch's
+    // cudaGetLastError would report them as its own: clear it.
+    (void)cudaGetLastError();
     *comm = c;
     return nullptr;
 }
 
 const char *tp_allreduce_sum(void *comm, float *buf, size_t n, cudaStream_t st) {
     const ncclResult_t r = api().all_reduce(buf, buf, n, ncclFloat32, ncclSum, static_cast<ncclComm_t>(comm), st);
-    return r == ncclSuccess ? nullptr : err_str(r);
+    if (r != ncclSuccess) return err_str(r);
+    (void)cudaGetLastError();   // as after ncclCommInitRank
+    return nullptr;
 }
 
 void tp_destroy(void *comm) {
