@@ -143,6 +143,23 @@ def reduce_over_ranks(dev_ms, wall, tokens, world, device):
     return float(t[0]), float(t[1]), float(n[0])
 
 
+def share_tp_id(uid, rank, device):
+    """The tensor-parallel group's 128-byte NCCL id, created on rank 0 (uid) and
+    broadcast over the job's process group to every rank."""
+    import torch
+    t = torch.zeros(128, dtype=torch.uint8, device=device)
+    if rank == 0:
+        t.copy_(torch.frombuffer(bytearray(uid), dtype=torch.uint8))
+    torch.distributed.broadcast(t, 0)
+    return bytes(t.cpu().numpy().tobytes())
+
+
+def job_tokens(tokens, rank, tp):
+    """Tokens a rank contributes to the job total: tensor-parallel ranks all
+    emit the same rows' tokens, so only rank 0 counts them."""
+    return 0 if tp and rank else tokens
+
+
 def run_ours(args, wl, rank, world, local_rank):
     import torch
     import mlxcat_b200 as M
@@ -156,11 +173,7 @@ def run_ours(args, wl, rank, world, local_rank):
         cfg = dataclasses.replace(cfg, tp_size=world, tp_rank=rank)
     ctx = M.Context(cfg, local_rank)
     if tp:
-        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
-        if rank == 0:
-            uid.copy_(torch.frombuffer(bytearray(M.Context.tp_unique_id()), dtype=torch.uint8))
-        torch.distributed.broadcast(uid, 0)
-        ctx.tp_connect(bytes(uid.cpu().numpy().tobytes()))
+        ctx.tp_connect(share_tp_id(M.Context.tp_unique_id() if rank == 0 else None, rank, "cuda"))
     ctx.synth_weights(WEIGHT_SEED, 0.02)
     prank = 0 if tp else rank   # prompt / seed stream of this rank's rows
     rows, k1 = wl["rows"], wl["k"] + 1
@@ -233,7 +246,7 @@ def run_ours(args, wl, rank, world, local_rank):
     cache.set_profiling(False)
 
     # ---- aggregate over ranks (tensor parallel: the ranks emit the same tokens) ----
-    dev_ms_max, wall_max, tokens_all = reduce_over_ranks(dev_ms, wall, 0 if tp and rank else tokens, world,
+    dev_ms_max, wall_max, tokens_all = reduce_over_ranks(dev_ms, wall, job_tokens(tokens, rank, tp), world,
                                                          "cuda")
 
     result = None
