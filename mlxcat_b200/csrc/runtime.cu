@@ -598,7 +598,7 @@ int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx
         set_err(ctx, MLXCAT_E_CUDA, "stream creation failed");
         return fail(MLXCAT_E_CUDA);
     }
-    const mlxcat_model_config &c = *cfg;
+    const mlxcat_model_config &c = ctx->cfg;   // this rank's view (the slice when tensor-parallel)
     int rc = MLXCAT_OK;
     auto alloc_lin = [&](DevLin &w, int N, int K) {
         w.N = N; w.K = K;
