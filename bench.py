@@ -45,6 +45,9 @@ WORKLOADS = {
                       temperature=0.7, top_p=0.9, max_new=256),
     "qwen3-30b-a3b": dict(model="qwen3-30b-a3b", rows=64, prompt=8192, seg_pool=64, seg_len=64, n=3, k=4,
                           temperature=0.0, top_p=0.0, max_new=256),
+    # expert parallel over the run's ranks: the 64 rows split across ranks, experts 128/N per GPU
+    "qwen3-30b-a3b-ep": dict(model="qwen3-30b-a3b", rows=64, prompt=8192, seg_pool=64, seg_len=64, n=3, k=4,
+                             temperature=0.0, top_p=0.0, max_new=256, ep=True),
     # tensor-parallel over all ranks of the run (does not fit one GPU at 64 rows)
     "llama3-70b": dict(model="llama3-70b", rows=64, prompt=8192, seg_pool=64, seg_len=64, n=4, k=6,
                        temperature=0.0, top_p=0.0, max_new=256, tp=True),
@@ -168,15 +171,18 @@ def run_ours(args, wl, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     cfg = model_config(wl["model"])
     tp = bool(wl.get("tp")) and world > 1
+    ep = bool(wl.get("ep")) and world > 1
+    import dataclasses
     if tp:   # every rank runs the same rows on its slice of the model
-        import dataclasses
         cfg = dataclasses.replace(cfg, tp_size=world, tp_rank=rank)
+    if ep:   # every rank runs its share of the rows with 1/world of the experts
+        cfg = dataclasses.replace(cfg, ep_size=world, ep_rank=rank)
     ctx = M.Context(cfg, local_rank)
-    if tp:
+    if tp or ep:
         ctx.tp_connect(share_tp_id(M.Context.tp_unique_id() if rank == 0 else None, rank, "cuda"))
     ctx.synth_weights(WEIGHT_SEED, 0.02)
     prank = 0 if tp else rank   # prompt / seed stream of this rank's rows
-    rows, k1 = wl["rows"], wl["k"] + 1
+    rows, k1 = (wl["rows"] // world if ep else wl["rows"]), wl["k"] + 1
     max_len = wl["prompt"] + wl["max_new"] + 16
     cache = M.BatchKVCache(ctx, rows, max_len)
     spec = M.SpeculativeDecodingConfiguration(True, wl["k"], wl["n"], MIN_CONTEXT, A.ACCEPT_PREFIX)
@@ -291,20 +297,21 @@ def run_ours(args, wl, rank, world, local_rank):
         result = {
             "metric": "accepted tok/s", "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps,
-            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if tp or ep else "weak", "vs_baseline": None,
             "dtype": "f16",
             "data": "synthetic (seeded segment-pool prompts, random-init N(0,0.02) q4 weights)",
-            "config": {"workload": args.config, "model": wl["model"], "rows_per_gpu": wl["rows"],
-                       "global_batch": wl["rows"] * (1 if tp else world), "prompt_tokens": wl["prompt"],
+            "config": {"workload": args.config, "model": wl["model"], "rows_per_gpu": rows,
+                       "global_batch": rows * (1 if tp else world), "prompt_tokens": wl["prompt"],
                        "ngram_n": wl["n"], "k": wl["k"], "temperature": wl["temperature"],
                        "top_p": wl["top_p"], "max_new_tokens": wl["max_new"],
                        "acceptance": "prefix match (greedy) / single-draft rejection sampling",
-                       "parallelism": (f"tensor-parallel x{world} (NCCL allreduce per block)" if tp
-                                       else f"request-parallel x{world}"),
+                       "parallelism": (f"tensor-parallel x{world} (NCCL allreduce per block)" if tp else
+                                       f"expert-parallel x{world} (NCCL all-to-all per MoE layer)" if ep else
+                                       f"request-parallel x{world}"),
                        "l2": "inputs larger than L2: %.2f GB q4 weights + KV per step" % (ctx.weights_bytes() / 1e9)},
             "verify_step_us": verify_ms / args.steps * 1e3,
             "acceptance_rate": (accepted / proposed if proposed else None),
-            "tokens_per_row_step": tokens / (args.steps * wl["rows"]),
+            "tokens_per_row_step": tokens / (args.steps * rows),
             "roofline": roof, "kernels": extra,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 4 * (rows * k1 + 2 * rows) + 32,

@@ -67,6 +67,14 @@ typedef struct {
      * rows.  Weight and KV-cache calls on such a context address the rank's
      * slice (n_heads/tp_size heads, intermediate/tp_size MLP rows). */
     int32_t tp_size, tp_rank;
+    /* Expert parallelism for MoE models over ep_size GPUs (0 or 1: off): rank
+     * ep_rank holds experts [ep_rank*E/ep_size, (ep_rank+1)*E/ep_size) and runs
+     * its own rows; every MoE layer exchanges the routed operand rows with the
+     * experts' owners and the results back (two NCCL all-to-alls of fixed-size
+     * per-peer blocks).  The other weights are replicated.  All ranks must
+     * call the forward entry points with the same shapes in the same order.
+     * Connect with mlxcat_ctx_tp_connect.  Not combinable with tp_size > 1. */
+    int32_t ep_size, ep_rank;
 } mlxcat_model_config;
 
 /* SamplingParameters subset on the path (Sampling.swift:139-217). */
@@ -101,11 +109,11 @@ typedef struct mlxcat_cache mlxcat_cache;
  * replaces: model construction + MLX device stream (NativeModelEngine.swift:44-54) */
 MLXCAT_API int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx **out);
 MLXCAT_API int mlxcat_ctx_destroy(mlxcat_ctx *ctx);
-/* Tensor parallelism: one rank creates an id (ncclGetUniqueId), the host
- * hands the 128 bytes to every rank, each rank connects its context
+/* Tensor or expert parallelism: one rank creates an id (ncclGetUniqueId), the
+ * host hands the 128 bytes to every rank, each rank connects its context
  * (ncclCommInitRank; collective: all ranks call it).  NCCL is loaded at run
  * time (libnccl.so.2); without it these return MLXCAT_E_STATE.  Must precede
- * the first forward on a context with tp_size > 1. */
+ * the first forward on a context with tp_size > 1 or ep_size > 1. */
 MLXCAT_API int mlxcat_tp_unique_id(uint8_t id[128]);
 MLXCAT_API int mlxcat_ctx_tp_connect(mlxcat_ctx *ctx, const uint8_t id[128]);
 MLXCAT_API const char *mlxcat_last_error(const mlxcat_ctx *ctx);

@@ -37,6 +37,7 @@ class ModelConfigC(C.Structure):
         ("group_size", C.c_int32), ("bits", C.c_int32),
         ("n_experts", C.c_int32), ("top_k", C.c_int32), ("norm_topk", C.c_int32),
         ("tp_size", C.c_int32), ("tp_rank", C.c_int32),
+        ("ep_size", C.c_int32), ("ep_rank", C.c_int32),
     ]
 
 

@@ -217,6 +217,34 @@ const char *tp_unique_id(uint8_t *out128);
 const char *tp_connect(void **comm, const uint8_t *id128, int nranks, int rank);
 const char *tp_allreduce_sum(void *comm, float *buf, size_t n, cudaStream_t st);
 void tp_destroy(void *comm);
+// expert parallel: all-to-all of fixed-size per-peer blocks (one NCCL group)
+struct TpBlock {
+    const void *send;
+    void *recv;
+    size_t bytes;    // per peer
+    size_t stride;   // bytes between consecutive peers' blocks
+};
+const char *ep_exchange(void *comm, int nranks, const TpBlock *blocks, int nblocks, cudaStream_t st);
+
+// ---- expert parallel MoE (moe.cu) -------------------------------------------
+// Per-peer slabs of cap rows: the source packs each assignment's operand row
+// (natural order, fp16, unscaled) and meta {local expert, scale, routing
+// weight} into the slab of the rank owning its expert; back[a] = dest*cap + slot.
+struct EpMeta {
+    int expert;      // the owner's local expert index
+    float scale;     // folded-norm scale of the token
+    float weight;    // routing weight
+    int pad;
+};
+cudaError_t ep_pack(const int32_t *topk_id, const float *topk_w, const float *tok_scale, const __half *x_blk,
+                    int ldx_rows, int M, int TK, int H, int experts_per_rank, int cap, __half *send_x,
+                    EpMeta *send_meta, int *send_count, int32_t *back, cudaStream_t st);
+// owner side: per-local-expert lists over the received rows (row = src*cap + slot),
+// each row's scale and routing weight
+cudaError_t ep_lists(const int *recv_count, const EpMeta *recv_meta, int nranks, int cap, int *exp_count,
+                     int32_t *exp_list, float *row_scale, float *row_weight, cudaStream_t st);
+// source side: y[a] = yr[back[a]] for the M*TK assignments (fp32 rows of H)
+cudaError_t ep_gather(const float *yr, const int32_t *back, int n, int H, float *y, cudaStream_t st);
 
 // ---- decode attention (split-K over keys, GQA) -----------------------------
 // Tokens come in groups of `qg` consecutive positions of one row (the verify

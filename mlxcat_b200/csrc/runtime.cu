@@ -67,7 +67,8 @@ struct mlxcat_ctx {
     // gcfg: the model as configured by the caller
     mlxcat_model_config cfg{}, gcfg{};
     int tp = 1, tp_rank = 0;
-    void *nccl = nullptr;   // ncclComm_t of the tensor-parallel group
+    int ep = 1, ep_rank = 0, epr = 0;   // expert parallel: ranks, this rank, experts per rank
+    void *nccl = nullptr;   // ncclComm_t of the tensor- or expert-parallel group
     int device = 0, sm_count = 148;
     cudaStream_t stream = nullptr;
     std::string err;
@@ -128,6 +129,14 @@ struct mlxcat_cache {
     // the attention-norm and MLP-norm inputs of each token row (pre-scales)
     float *norm_part = nullptr, *r_attn = nullptr, *r_mlp = nullptr;
     float *tp_part = nullptr;          // tensor parallel: this rank's O / down partial sums [rows][H]
+    // expert parallel: per-peer slabs of routed operand rows and metadata, the
+    // received rows in the expert kernels' layout, results and their return
+    __half *ep_send_x = nullptr, *ep_recv_x = nullptr, *ep_xe = nullptr, *ep_act = nullptr;
+    EpMeta *ep_send_meta = nullptr, *ep_recv_meta = nullptr;
+    int *ep_counts = nullptr;          // [layer][send N | recv N]
+    int *ep_exp_count = nullptr;       // [layer][local experts]
+    int32_t *ep_exp_list = nullptr, *ep_back = nullptr;
+    float *ep_scale = nullptr, *ep_w = nullptr, *ep_ys = nullptr, *ep_yr = nullptr;
     // sparse MoE: routing, per-expert assignment lists (counts per layer, zeroed
     // once per forward), SwiGLU activations per assignment, scaled expert outputs
     int32_t *moe_id = nullptr, *moe_list = nullptr;
@@ -250,6 +259,11 @@ bool valid_config(const mlxcat_model_config *c, std::string &why) {
         }
         if (c->n_experts > 0) { why = "tensor parallelism is for dense models"; return false; }
     }
+    if (c->ep_size > 1) {
+        if (c->n_experts <= 0 || c->n_experts % c->ep_size) { why = "ep_size must divide n_experts (MoE models)"; return false; }
+        if (c->ep_rank < 0 || c->ep_rank >= c->ep_size) { why = "ep_rank must be in [0, ep_size)"; return false; }
+        if (c->tp_size > 1) { why = "tensor and expert parallelism are not combined"; return false; }
+    }
     if (c->n_experts < 0) { why = "n_experts must be >= 0"; return false; }
     if (c->n_experts > 0) {
         if (c->n_experts % 32 || c->n_experts > 256) { why = "n_experts must be a multiple of 32, at most 256"; return false; }
@@ -290,6 +304,52 @@ struct ProfScope {
         if (e1) cudaEventRecordWithFlags(e1, c->ctx->stream, cudaEventRecordExternal);
     }
 };
+
+// Expert-parallel MoE MLP of layer l (after the route): every assignment's
+// operand row goes to the rank owning its expert (fixed-size per-peer blocks
+// of M * top_k rows, one NCCL group with the counts and metadata), the owner
+// runs the grouped expert kernels over all received rows, the scaled outputs
+// go back the same way, and the source gathers them into the combine's order.
+int ep_moe(mlxcat_cache *c, int l, int M) {
+    mlxcat_ctx *ctx = c->ctx;
+    const mlxcat_model_config &cf = ctx->cfg;
+    const int H = cf.hidden, I = cf.intermediate, TK = cf.top_k, N = ctx->ep, epr = ctx->epr, R = c->m_cap;
+    const int cap = M * TK, rows = N * cap;
+    cudaStream_t st = ctx->stream;
+    int *scnt = c->ep_counts + (size_t)l * 2 * N, *rcnt = scnt + N;
+    LK(ctx, ep_pack(c->moe_id, c->moe_w, c->moe_scale, c->xg, R, M, TK, H, epr, cap, c->ep_send_x,
+                    c->ep_send_meta, scnt, c->ep_back, st));
+    const TpBlock out[3] = {{scnt, rcnt, sizeof(int), sizeof(int)},
+                            {c->ep_send_meta, c->ep_recv_meta, (size_t)cap * sizeof(EpMeta), (size_t)cap * sizeof(EpMeta)},
+                            {c->ep_send_x, c->ep_recv_x, (size_t)cap * H * 2, (size_t)cap * H * 2}};
+    if (const char *er = ep_exchange(ctx->nccl, N, out, 3, st)) return set_err(ctx, MLXCAT_E_CUDA, "dispatch: %s", er);
+    int *ecnt = c->ep_exp_count + (size_t)l * epr;
+    LK(ctx, ep_lists(rcnt, c->ep_recv_meta, N, cap, ecnt, c->ep_exp_list, c->ep_scale, c->ep_w, st));
+    LK(ctx, permute_activations(c->ep_recv_x, c->ep_xe, rows, H, st));
+    const auto &mb = ctx->moe[l];
+    MoEExpertArgs xa;
+    xa.wq = mb.wq[0]; xa.scales = mb.s[0]; xa.biases = mb.b[0];
+    xa.wq2 = mb.wq[1]; xa.scales2 = mb.s[1]; xa.biases2 = mb.b[1];
+    xa.N = I; xa.K = H; xa.E = epr; xa.x = c->ep_xe; xa.ldx_rows = rows; xa.x_div = 1;
+    xa.exp_count = ecnt; xa.exp_list = c->ep_exp_list; xa.list_cap = rows;
+    xa.tok_scale = c->ep_scale; xa.act = c->ep_act; xa.act_rows = rows;
+    { ProfScope ps(c, 0); LK(ctx, moe_expert(xa, 0, st)); }
+    MoEExpertArgs da;
+    da.wq = mb.wq[2]; da.scales = mb.s[2]; da.biases = mb.b[2];
+    da.N = H; da.K = I; da.E = epr; da.x = c->ep_act; da.ldx_rows = rows; da.x_div = 1;
+    da.exp_count = ecnt; da.exp_list = c->ep_exp_list; da.list_cap = rows;
+    da.topk_w = c->ep_w; da.y = c->ep_ys;
+    { ProfScope ps(c, 0); LK(ctx, moe_expert(da, 1, st)); }
+    const TpBlock back = {c->ep_ys, c->ep_yr, (size_t)cap * H * 4, (size_t)cap * H * 4};
+    if (const char *er = ep_exchange(ctx->nccl, N, &back, 1, st)) return set_err(ctx, MLXCAT_E_CUDA, "combine: %s", er);
+    LK(ctx, ep_gather(c->ep_yr, c->ep_back, cap, H, c->moe_y, st));
+    MoECombineArgs ca;
+    ca.h = c->h; ca.y = c->moe_y; ca.M = M; ca.H = H; ca.TK = TK;
+    ca.norm_w = l + 1 < cf.n_layers ? ctx->attn_norm(l + 1) : ctx->final_norm(); ca.norm_scale = c->r_mlp;
+    ca.xout = c->xn; ca.ldx_rows = R; ca.norm_part = c->norm_part; ca.norm_rows = R;
+    LK(ctx, moe_combine(ca, st));
+    return MLXCAT_OK;
+}
 
 // Tensor-parallel residual step: this rank's slice of a row-split projection
 // (O or down) as fp32 partial sums, one allreduce (sum) over the group, then
@@ -337,6 +397,10 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
     // Layer 0's input is normalised exactly here.
     LK(ctx, embed_norm(ctx->embed.view(), tok, M, ctx->attn_norm(0), eps, c->h, c->xn, R, st, c->r_attn));
     if (cf.n_experts) CK(ctx, cudaMemsetAsync(c->moe_count, 0, sizeof(int) * (size_t)L * cf.n_experts, st));
+    if (cf.n_experts && ctx->ep > 1) {
+        CK(ctx, cudaMemsetAsync(c->ep_counts, 0, sizeof(int) * (size_t)L * 2 * ctx->ep, st));
+        CK(ctx, cudaMemsetAsync(c->ep_exp_count, 0, sizeof(int) * (size_t)L * ctx->epr, st));
+    }
     Q4Epilogue ep;
     ep.part = c->part;
     ep.counters = c->counters;
@@ -387,6 +451,11 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
             ctx->launches++;   // logits + top-k
             LK(ctx, moe_route(ra, st));
             const auto &mb = ctx->moe[l];
+            if (ctx->ep > 1) {
+                int rc = ep_moe(c, l, M);
+                if (rc) return rc;
+                continue;
+            }
             MoEExpertArgs xa;
             xa.wq = mb.wq[0]; xa.scales = mb.s[0]; xa.biases = mb.b[0];
             xa.wq2 = mb.wq[1]; xa.scales2 = mb.s[1]; xa.biases2 = mb.b[1];
@@ -445,7 +514,8 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
 
 int check_weights(mlxcat_ctx *ctx) {
     if (!ctx->have_weights) return set_err(ctx, MLXCAT_E_STATE, "weights not loaded");
-    if (ctx->tp > 1 && !ctx->nccl) return set_err(ctx, MLXCAT_E_STATE, "tensor-parallel context not connected");
+    if ((ctx->tp > 1 || ctx->ep > 1) && !ctx->nccl)
+        return set_err(ctx, MLXCAT_E_STATE, "tensor- or expert-parallel context not connected");
     return MLXCAT_OK;
 }
 
@@ -571,6 +641,11 @@ int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx
     ctx->cfg = *cfg;
     ctx->gcfg = *cfg;
     ctx->device = device;
+    if (cfg->kind == MLXCAT_MODEL_TRANSFORMER && cfg->n_experts > 0) {
+        ctx->ep = cfg->ep_size > 1 ? cfg->ep_size : 1;
+        ctx->ep_rank = ctx->ep > 1 ? cfg->ep_rank : 0;
+        ctx->epr = cfg->n_experts / ctx->ep;
+    }
     if (cfg->kind == MLXCAT_MODEL_TRANSFORMER && cfg->tp_size > 1) {
         // this rank's slice: whole KV heads with their query-head groups, a
         // contiguous block of MLP rows
@@ -625,7 +700,7 @@ int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx
             alloc_lin(ctx->o[l], H, c.n_heads * D);
             if (c.n_experts) {
                 auto &mb = ctx->moe[l];
-                const size_t n = (size_t)c.n_experts * c.intermediate * H;   // weights per projection
+                const size_t n = (size_t)ctx->epr * c.intermediate * H;   // this rank's experts, per projection
                 bool ok = dalloc(ctx->allocs, &mb.router, (size_t)c.n_experts * H) == cudaSuccess;
                 for (int p = 0; p < 3 && ok; ++p)
                     ok = dalloc(ctx->allocs, &mb.wq[p], n / 8) == cudaSuccess &&
@@ -666,10 +741,12 @@ int mlxcat_tp_unique_id(uint8_t id[128]) {
 
 int mlxcat_ctx_tp_connect(mlxcat_ctx *ctx, const uint8_t id[128]) {
     if (!ctx || !id) return MLXCAT_E_INVALID;
-    if (ctx->tp <= 1) return set_err(ctx, MLXCAT_E_STATE, "context is not tensor-parallel (tp_size <= 1)");
+    if (ctx->tp <= 1 && ctx->ep <= 1)
+        return set_err(ctx, MLXCAT_E_STATE, "context is neither tensor- nor expert-parallel");
     if (ctx->nccl) return set_err(ctx, MLXCAT_E_STATE, "context already connected");
     CK(ctx, cudaSetDevice(ctx->device));
-    if (const char *e = tp_connect(&ctx->nccl, id, ctx->tp, ctx->tp_rank))
+    const int group = ctx->tp > 1 ? ctx->tp : ctx->ep, grank = ctx->tp > 1 ? ctx->tp_rank : ctx->ep_rank;
+    if (const char *e = tp_connect(&ctx->nccl, id, group, grank))
         return set_err(ctx, MLXCAT_E_STATE, "tensor parallel connect: %s", e);
     return MLXCAT_OK;
 }
@@ -704,8 +781,10 @@ int64_t mlxcat_ctx_launch_count(const mlxcat_ctx *ctx) { return ctx ? ctx->launc
 static bool expert_view(mlxcat_ctx *ctx, uint32_t id, DevLin *v, RowMap *rm) {
     const mlxcat_model_config &c = ctx->cfg;
     if (c.kind != MLXCAT_MODEL_TRANSFORMER || !c.n_experts || (id & 0xC0000000u) != 0x40000000u) return false;
-    const int l = (int)((id >> 12) & 0x3FFFFu), e = (int)((id >> 2) & 0x3FFu), kind = (int)(id & 3u);
-    if (l >= c.n_layers || e >= c.n_experts || kind > 2) return false;
+    const int l = (int)((id >> 12) & 0x3FFFFu), eg = (int)((id >> 2) & 0x3FFu), kind = (int)(id & 3u);
+    if (l >= c.n_layers || eg >= c.n_experts || kind > 2) return false;
+    const int e = eg - ctx->ep_rank * ctx->epr;   // this rank's bank holds experts [ep_rank*epr, +epr)
+    if (e < 0 || e >= ctx->epr) return false;
     const auto &mb = ctx->moe[l];
     const size_t per = (size_t)c.intermediate * c.hidden;   // weights of one expert projection
     *rm = RowMap();
@@ -784,7 +863,7 @@ int mlxcat_weights_synth(mlxcat_ctx *ctx, uint64_t seed, float stddev) {
     for (int l = 0; l < c.n_layers && c.n_experts; ++l) {
         LK(ctx, router_synth(seed, (uint32_t)l * 16u + 7u, stddev, c.n_experts, c.hidden, ctx->moe[l].router,
                              ctx->stream));
-        for (int e = 0; e < c.n_experts; ++e)
+        for (int e = ctx->ep_rank * ctx->epr; e < (ctx->ep_rank + 1) * ctx->epr; ++e)
             for (int kind = 0; kind < 3; ++kind) {
                 const uint32_t id = MLXCAT_TENSOR_EXPERT(l, e, kind);
                 DevLin v;
@@ -906,10 +985,10 @@ int64_t mlxcat_weights_bytes(const mlxcat_ctx *ctx) {
     const mlxcat_model_config &c = ctx->cfg;
     for (int l = 0; l < c.n_layers; ++l) {
         b += ctx->qkv[l].bytes() + ctx->o[l].bytes();
-        if (c.n_experts)   // every expert is touched by a verify step's assignments
-            b += (size_t)c.n_experts * (3 * ((size_t)c.intermediate * c.hidden / 2 +
-                                             (size_t)c.intermediate * c.hidden / 64 * 4) +
-                                        (size_t)c.hidden * 2);
+        if (c.n_experts)   // every (local) expert is touched by a verify step's assignments; router replicated
+            b += (size_t)ctx->epr * 3 * ((size_t)c.intermediate * c.hidden / 2 +
+                                         (size_t)c.intermediate * c.hidden / 64 * 4) +
+                 (size_t)c.n_experts * c.hidden * 2;
         else
             b += ctx->gu[l].bytes() + ctx->down[l].bytes();
     }
@@ -983,6 +1062,23 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
             chk(dalloc(A, &c->moe_act, asg * I));
             chk(dalloc(A, &c->moe_y, asg * H));
             chk(dalloc(A, &c->moe_logits, (size_t)Mc * cf.n_experts));
+            if (ctx->ep > 1) {
+                const size_t N = (size_t)ctx->ep, rows = N * asg;   // per-peer capacity: all of a rank's assignments
+                chk(dalloc(A, &c->ep_send_x, rows * H));
+                chk(dalloc(A, &c->ep_recv_x, rows * H));
+                chk(dalloc(A, &c->ep_xe, rows * H));
+                chk(dalloc(A, &c->ep_act, rows * I));
+                chk(dalloc(A, &c->ep_send_meta, rows));
+                chk(dalloc(A, &c->ep_recv_meta, rows));
+                chk(dalloc(A, &c->ep_counts, (size_t)cf.n_layers * 2 * N));
+                chk(dalloc(A, &c->ep_exp_count, (size_t)cf.n_layers * ctx->epr));
+                chk(dalloc(A, &c->ep_exp_list, (size_t)ctx->epr * rows));
+                chk(dalloc(A, &c->ep_back, asg));
+                chk(dalloc(A, &c->ep_scale, rows));
+                chk(dalloc(A, &c->ep_w, rows));
+                chk(dalloc(A, &c->ep_ys, rows * H));
+                chk(dalloc(A, &c->ep_yr, rows * H));
+            }
         }
         chk(dalloc(A, &c->rope, (size_t)max_len * (D / 2)));
         if (rc == MLXCAT_OK) chk(rope_table(ctx->inv_freq, D / 2, max_len, c->rope, ctx->stream));

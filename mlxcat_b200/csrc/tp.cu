@@ -3,8 +3,8 @@
 // The library does not link NCCL: libnccl.so.2 is opened on first use (an
 // already-loaded copy, e.g. the one a host framework brought in, is reused),
 // so single-GPU users need no NCCL and a host's own NCCL is not duplicated.
-// Only the five entry points below are used; their signatures are NCCL's
-// public API (nccl.h).
+// Only the entry points below are used; their signatures are NCCL's public
+// API (nccl.h).
 #include <dlfcn.h>
 #include <nccl.h>
 
@@ -25,6 +25,10 @@ struct NcclApi {
                                cudaStream_t) = nullptr;
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
     const char *(*error_string)(ncclResult_t) = nullptr;
+    ncclResult_t (*group_start)() = nullptr;
+    ncclResult_t (*group_end)() = nullptr;
+    ncclResult_t (*send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
 };
 
 NcclApi &api() {
@@ -40,7 +44,12 @@ NcclApi &api() {
         a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
         a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
         a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
-        a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.comm_destroy && a.error_string;
+        a.group_start = reinterpret_cast<decltype(a.group_start)>(dlsym(h, "ncclGroupStart"));
+        a.group_end = reinterpret_cast<decltype(a.group_end)>(dlsym(h, "ncclGroupEnd"));
+        a.send = reinterpret_cast<decltype(a.send)>(dlsym(h, "ncclSend"));
+        a.recv = reinterpret_cast<decltype(a.recv)>(dlsym(h, "ncclRecv"));
+        a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.comm_destroy && a.error_string &&
+               a.group_start && a.group_end && a.send && a.recv;
     });
     return a;
 }
@@ -80,6 +89,27 @@ const char *tp_allreduce_sum(void *comm, float *buf, size_t n, cudaStream_t st) 
     const ncclResult_t r = api().all_reduce(buf, buf, n, ncclFloat32, ncclSum, static_cast<ncclComm_t>(comm), st);
     if (r != ncclSuccess) return err_str(r);
     (void)cudaGetLastError();   // as after ncclCommInitRank
+    return nullptr;
+}
+
+const char *ep_exchange(void *comm, int nranks, const TpBlock *blocks, int nblocks, cudaStream_t st) {
+    // one NCCL group: for every block and every peer p, send block.bytes from
+    // send + p * stride and receive as many into recv + p * stride
+    ncclResult_t r = api().group_start();
+    if (r != ncclSuccess) return err_str(r);
+    for (int b = 0; b < nblocks && r == ncclSuccess; ++b)
+        for (int p = 0; p < nranks && r == ncclSuccess; ++p) {
+            const TpBlock &k = blocks[b];
+            r = api().send(static_cast<const char *>(k.send) + (size_t)p * k.stride, k.bytes, ncclUint8, p,
+                           static_cast<ncclComm_t>(comm), st);
+            if (r == ncclSuccess)
+                r = api().recv(static_cast<char *>(k.recv) + (size_t)p * k.stride, k.bytes, ncclUint8, p,
+                               static_cast<ncclComm_t>(comm), st);
+        }
+    const ncclResult_t e = api().group_end();
+    if (r != ncclSuccess) return err_str(r);
+    if (e != ncclSuccess) return err_str(e);
+    (void)cudaGetLastError();
     return nullptr;
 }
 

@@ -53,12 +53,16 @@ class ModelConfig:
     # tensor parallelism: this context is rank tp_rank of tp_size (1 = off)
     tp_size: int = 1
     tp_rank: int = 0
+    # expert parallelism (MoE): rank ep_rank of ep_size holds 1/ep_size of the experts
+    ep_size: int = 1
+    ep_rank: int = 0
 
     def to_c(self) -> A.ModelConfigC:
         return A.ModelConfigC(self.kind, self.n_layers, self.hidden, self.n_heads, self.n_kv_heads,
                               self.head_dim, self.intermediate, self.vocab, int(self.tie_embeddings),
                               int(self.qk_norm), self.rms_eps, self.rope_theta, 64, 4,
-                              self.n_experts, self.top_k, int(self.norm_topk), self.tp_size, self.tp_rank)
+                              self.n_experts, self.top_k, int(self.norm_topk), self.tp_size, self.tp_rank,
+                              self.ep_size, self.ep_rank)
 
     @staticmethod
     def table(vocab: int) -> "ModelConfig":

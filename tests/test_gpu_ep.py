@@ -1,0 +1,105 @@
+"""Expert-parallel MoE verify forward (the partitioning of the Qwen3-30B-A3B
+configuration) on two GPUs, one process per GPU, against the CPU oracle of the
+whole model.
+
+Each rank holds half of every layer's experts and runs its own rows; every MoE
+layer sends each routed operand row to the rank owning its expert and brings
+the scaled expert output back (NCCL send/recv in one group per direction).
+Each rank's verify logits are compared with the oracle's for its rows, with
+the MoE tolerance rule of tests/test_gpu_moe.py (a bf16 near-tie in the
+routing may flip one expert of a token).  Needs two GPUs (skipped otherwise)."""
+import multiprocessing as mp
+import os
+import queue
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+    pytest.skip("needs two CUDA devices", allow_module_level=True)
+
+import mlxcat_b200 as M  # noqa: E402
+from mlxcat_b200 import _abi as A  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+
+TOL = 2e-2
+MOE = dict(n_layers=2, hidden=512, n_heads=8, n_kv_heads=2, head_dim=64, intermediate=256, vocab=4096,
+           tie_embeddings=False, qk_norm=True, rms_eps=1e-6, rope_theta=1e6, n_experts=32, top_k=4,
+           norm_topk=True)
+SEED = 17
+K = 4
+
+
+def prompts(rank):
+    return [[int(t) for t in np.random.default_rng(100 * rank + r).integers(0, 4096, n)]
+            for r, n in enumerate((48, 33))]
+
+
+def rank_main(rank, world, ids, results):
+    try:
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        ctx = M.Context(M.ModelConfig(**MOE, name="ep-small", ep_size=world, ep_rank=rank), rank)
+        if rank == 0:
+            uid = M.Context.tp_unique_id()
+            for _ in range(world - 1):
+                ids.put(uid)
+        else:
+            uid = ids.get(timeout=60)
+        ctx.tp_connect(uid)
+        ctx.synth_weights(SEED)
+        spec = M.SpeculativeDecodingConfiguration(True, K, 3, 8, A.ACCEPT_PREFIX)
+        ps = prompts(rank)
+        cache = M.BatchKVCache(ctx, len(ps), 128)
+        # the same prompt lengths on every rank: each forward has the same shape
+        firsts = [cache.insert_row(r, p, 16, M.SamplingParameters()) for r, p in enumerate(ps)]
+        drafts = cache.draft(spec)
+        logits = cache.verify_forward(spec)
+        cache.accept(spec)
+        cache.close()
+        ctx.close()
+        results.put((rank, firsts, drafts, logits))
+    except Exception as e:  # reported to the parent
+        results.put((rank, "error", repr(e), None))
+
+
+def test_expert_parallel_verify_matches_oracle():
+    world = 2
+    ctx_mp = mp.get_context("spawn")
+    ids, results = ctx_mp.Queue(), ctx_mp.Queue()
+    procs = [ctx_mp.Process(target=rank_main, args=(r, world, ids, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    try:
+        for _ in range(world):
+            r = results.get(timeout=240)
+            out[r[0]] = r
+            if r[1] == "error":   # the other ranks would wait in a collective
+                break
+    except queue.Empty:
+        pass
+    for p in procs:
+        p.join(timeout=5 if any(v[1] == "error" for v in out.values()) else 30)
+        if p.is_alive():
+            p.kill()
+    for r in out.values():
+        assert r[1] != "error", f"rank {r[0]}: {r[2]}"
+    assert len(out) == world, f"ranks reported: {sorted(out)}"
+    om = O.Model.synth(O.make_config(**MOE), SEED, 0.02)
+    close = total = 0
+    for rank in range(world):
+        _, firsts, drafts, logits = out[rank]
+        ps = prompts(rank)
+        gen = O.Generator(om, len(ps), 128, O.SpecConfig(A.ACCEPT_PREFIX, 1, K, 3, 8))
+        for r, p in enumerate(ps):
+            gen.admit(r, p, 16, O.sampling())
+        for r, p in enumerate(ps):
+            toks = [firsts[r]] + drafts[r]
+            ol = O.forward(om, gen.kv, toks, [r] * len(toks), list(range(len(p), len(p) + len(toks))))
+            for j in range(len(toks)):
+                total += 1
+                close += bool(np.all(np.abs(logits[r, j] - ol[j]) <= TOL + TOL * np.abs(ol[j])))
+    assert close >= 0.75 * total, f"{close}/{total} verify rows within tolerance"
