@@ -83,3 +83,54 @@ def test_baseline_configs_are_valid_shapes():
         for d in (c.hidden, c.intermediate, c.n_heads * c.head_dim, c.vocab):
             assert d % 128 == 0
         assert c.n_heads % c.n_kv_heads == 0
+
+
+def test_ctypes_structs_match_the_header_layout(tmp_path):
+    """Size and field offsets of every struct of the header, as the C compiler
+    lays them out, equal the Python mirrors' (a Swift or ctypes binding reads
+    the same bytes)."""
+    structs = {"mlxcat_model_config": A.ModelConfigC, "mlxcat_sampling": A.SamplingC,
+               "mlxcat_spec_config": A.SpecConfigC, "mlxcat_stats": A.StatsC, "mlxcat_rows": A.RowsC}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "mlxcat_cuda.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = {}
+    for ln in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        cname, key, val = ln.split()
+        got[(cname, key)] = int(val)
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == C.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, (cname, fname)
+
+
+def test_oracle_structs_match_their_header(tmp_path):
+    """The checker's own ctypes mirrors (oracle/oracle.py) against oracle.h."""
+    from oracle import oracle as O
+    structs = {"orc_config": O.Config, "orc_sampling": O.Sampling, "orc_spec_config": O.SpecConfig,
+               "orc_stats": O.Stats, "orc_row": O.Row}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "oracle.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines.append("return 0; }")
+    src = tmp_path / "olayout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "olayout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "oracle"), str(src), "-o", str(exe)], check=True)
+    got = {}
+    for ln in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        cname, key, val = ln.split()
+        got[(cname, key)] = int(val)
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == C.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, (cname, fname)
