@@ -163,6 +163,15 @@ MLXCAT_API int mlxcat_cache_remove_row(mlxcat_cache *cache, int32_t row);
 /* BatchKVCache.trim(n) (BatchCache.swift:403-424): every row loses
  * min(n, its length); *trimmed = min(n, longest row) */
 MLXCAT_API int mlxcat_cache_trim(mlxcat_cache *cache, int32_t n, int32_t *trimmed);
+/* BatchKVCache.filter(keeping:) (BatchCache.swift:217-245): every row not
+ * listed in keep[0..n) is removed as by mlxcat_cache_remove_row; listed rows
+ * stay active in their slot (the device batch is addressed by slot, so no KV
+ * moves and the caller's row-to-slot map is unchanged).  n = 0 removes all. */
+MLXCAT_API int mlxcat_cache_filter(mlxcat_cache *cache, const int32_t *keep, int32_t n);
+/* trim(n) for one row: the right-ragged form of BatchCache.swift:403-424 --
+ * the row's KV loses min(n, its length) positions; *trimmed (may be NULL)
+ * receives that count.  Like mlxcat_cache_trim it changes KV lengths only. */
+MLXCAT_API int mlxcat_cache_trim_row(mlxcat_cache *cache, int32_t row, int32_t n, int32_t *trimmed);
 /* per-row KV lengths (BatchKVCache.offset / ropeOffset) */
 MLXCAT_API int mlxcat_cache_lengths(mlxcat_cache *cache, int32_t *out_rows);
 /* speculativeTokenHistory[row] (BatchGenerator.swift:452-456, 1012-1014) */

@@ -97,6 +97,8 @@ PROTOTYPES = {
     "mlxcat_cache_insert_row": (C.c_int, [_vp, _i32, _vp, _i32, _i32, C.POINTER(SamplingC),
                                           C.POINTER(_i32)]),
     "mlxcat_cache_remove_row": (C.c_int, [_vp, _i32]),
+    "mlxcat_cache_filter": (C.c_int, [_vp, _vp, _i32]),
+    "mlxcat_cache_trim_row": (C.c_int, [_vp, _i32, _i32, C.POINTER(_i32)]),
     "mlxcat_cache_trim": (C.c_int, [_vp, _i32, C.POINTER(_i32)]),
     "mlxcat_cache_lengths": (C.c_int, [_vp, _vp]),
     "mlxcat_cache_history": (C.c_int, [_vp, _i32, _vp, _i32, C.POINTER(_i32)]),

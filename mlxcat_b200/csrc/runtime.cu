@@ -1249,6 +1249,36 @@ int mlxcat_cache_trim(mlxcat_cache *c, int32_t n, int32_t *trimmed) {
     return MLXCAT_OK;
 }
 
+int mlxcat_cache_filter(mlxcat_cache *c, const int32_t *keep, int32_t n) {
+    if (!c || n < 0 || (n > 0 && !keep)) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    std::vector<char> kept(c->rows, 0);
+    for (int i = 0; i < n; ++i) {
+        if (keep[i] < 0 || keep[i] >= c->rows) return set_err(ctx, MLXCAT_E_INVALID, "filter: row %d out of range", keep[i]);
+        kept[keep[i]] = 1;
+    }
+    for (int r = 0; r < c->rows; ++r)
+        if (!kept[r]) {
+            const int rc = mlxcat_cache_remove_row(c, r);
+            if (rc) return rc;
+        }
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_trim_row(mlxcat_cache *c, int32_t row, int32_t n, int32_t *trimmed) {
+    if (!c || row < 0 || row >= c->rows || n < 0) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    int32_t len = 0;
+    CK(ctx, cudaMemcpy(&len, c->kv_len + row, 4, cudaMemcpyDeviceToHost));
+    const int32_t t = std::min(n, len);
+    len -= t;
+    CK(ctx, cudaMemcpy(c->kv_len + row, &len, 4, cudaMemcpyHostToDevice));
+    if (trimmed) *trimmed = t;
+    return MLXCAT_OK;
+}
+
 int mlxcat_cache_lengths(mlxcat_cache *c, int32_t *out) {
     if (!c || !out) return MLXCAT_E_INVALID;
     mlxcat_ctx *ctx = c->ctx;

@@ -273,6 +273,16 @@ class BatchKVCache:
     def remove_row(self, row: int):
         self.ctx.check(self.L.mlxcat_cache_remove_row(self.h, row))
 
+    def filter(self, keep):
+        """BatchKVCache.filter(keeping:): rows not in keep are removed (slots are kept)"""
+        k = np.ascontiguousarray(list(keep), dtype=np.int32)
+        self.ctx.check(self.L.mlxcat_cache_filter(self.h, k.ctypes.data if len(k) else None, len(k)))
+
+    def trim_row(self, row: int, n: int) -> int:
+        t = C.c_int32()
+        self.ctx.check(self.L.mlxcat_cache_trim_row(self.h, row, n, C.byref(t)))
+        return t.value
+
     def trim(self, n: int) -> int:
         t = C.c_int32()
         self.ctx.check(self.L.mlxcat_cache_trim(self.h, n, C.byref(t)))

@@ -64,6 +64,20 @@ def test_operator_argument_validation():
     assert L.mlxcat_op_q4_linear_workspace(128, 256, 4) >= 4 * 256 * 2
     assert L.mlxcat_op_attention_workspace(5, 5, 8, 2, 64, 600) > 0
     assert L.mlxcat_op_accept_workspace(8, 5) > 0
+    # cache calls reject a null cache before any device work
+    assert L.mlxcat_cache_filter(None, None, 0) == A.E_INVALID
+    assert L.mlxcat_cache_trim_row(None, 0, 1, None) == A.E_INVALID
+    # MoE operator: shapes outside the kernels' contract are refused up front
+    assert L.mlxcat_op_moe_workspace(0, 2048, 768, 128, 8) == 0
+    assert L.mlxcat_op_moe_workspace(320, 2048, 768, 128, 8) > 320 * 8 * 2048 * 4
+    # tensor / expert parallel configurations are validated on the host
+    h = C.c_void_p()
+    bad = M.ModelConfig(2, 512, 8, 3, 64, 512, 4096, tp_size=2).to_c()      # 3 KV heads over 2 ranks
+    assert L.mlxcat_ctx_create(C.byref(bad), 0, C.byref(h)) == A.E_INVALID
+    bad = M.ModelConfig(2, 512, 8, 2, 64, 256, 4096, n_experts=32, top_k=4, ep_size=3).to_c()   # 32 % 3
+    assert L.mlxcat_ctx_create(C.byref(bad), 0, C.byref(h)) == A.E_INVALID
+    bad = M.ModelConfig(2, 512, 8, 2, 64, 256, 4096, n_experts=48, top_k=4).to_c()   # experts % 32
+    assert L.mlxcat_ctx_create(C.byref(bad), 0, C.byref(h)) == A.E_INVALID
 
 
 def test_spec_config_clamps_like_reference():
