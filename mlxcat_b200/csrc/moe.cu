@@ -51,13 +51,23 @@ __device__ __forceinline__ uint4 ldg_stream16(const void *p) {
     return r;
 }
 
-__device__ __forceinline__ uint32_t dq2(uint32_t w, int shift, __half2 s2, __half2 b2) {
-    // nibbles (shift/4, shift/4 + 4) as fp16 1024 + q, then q * scale + bias
-    uint32_t v = ((w >> shift) & 0x000f000fu) | 0x64006400u;
-    __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&v),
-                        __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400)));
-    __half2 r = __hfma2(q, s2, b2);
-    return *reinterpret_cast<uint32_t *>(&r);
+// The four nibble pairs (i, i + 4) of one packed word with one shift: the pairs
+// at bits 0-3 / 16-19 take the 0x6400 magic (fp16 1024 + q); the pairs at bits
+// 4-7 / 20-23 take the 0x5400 magic (fp16 64.0, whose unit in the last place is
+// 1/16, so mantissa bits 4-7 hold exactly 64 + q); the other two pairs the same
+// from w >> 8.  Each pair then becomes q * scale + bias.
+__device__ __forceinline__ void dq_word(uint32_t w, __half2 s2, __half2 b2, uint32_t out[4]) {
+    const uint32_t hi = w >> 8;
+    uint32_t v[4] = {(w & 0x000f000fu) | 0x64006400u, (w & 0x00f000f0u) | 0x54005400u,
+                     (hi & 0x000f000fu) | 0x64006400u, (hi & 0x00f000f0u) | 0x54005400u};
+    const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+    const __half2 k64 = __halves2half2(__ushort_as_half(0x5400), __ushort_as_half(0x5400));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&v[i]), (i & 1) ? k64 : k1024);
+        const __half2 r = __hfma2(q, s2, b2);
+        out[i] = *reinterpret_cast<const uint32_t *>(&r);
+    }
 }
 
 __device__ __forceinline__ void mma16816(float *c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -310,10 +320,7 @@ moe_expert_kernel(MoEExpertArgs a) {
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const uint32_t w = (&wcur[mt][h].x)[s];
-                        p[mt][h][0] = dq2(w, 0, s2[mt][h], b2[mt][h]);
-                        p[mt][h][1] = dq2(w, 4, s2[mt][h], b2[mt][h]);
-                        p[mt][h][2] = dq2(w, 8, s2[mt][h], b2[mt][h]);
-                        p[mt][h][3] = dq2(w, 12, s2[mt][h], b2[mt][h]);
+                        dq_word(w, s2[mt][h], b2[mt][h], p[mt][h]);
                     }
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
