@@ -20,6 +20,10 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
     pytest.skip("needs two CUDA devices", allow_module_level=True)
+if os.environ.get("MLXCAT_TEST_EP") != "1":
+    # opt-in until this path has passed on two GPUs once: a failure here would
+    # stop a `-x` run before the verified GPU tests that sort after it
+    pytest.skip("expert-parallel path not yet run on GPUs; set MLXCAT_TEST_EP=1", allow_module_level=True)
 
 import mlxcat_b200 as M  # noqa: E402
 from mlxcat_b200 import _abi as A  # noqa: E402
