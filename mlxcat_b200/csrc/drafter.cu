@@ -21,7 +21,7 @@ namespace mlxcat {
 namespace {
 
 constexpr int DTPB = 256;
-constexpr int MAX_N = 64;
+constexpr int MAX_N = 64;   // tail tokens staged in shared memory
 
 __global__ void draft_kernel(RowState rs, SpecParams sp, int32_t *__restrict__ vtok,
                              int32_t *__restrict__ count, int32_t *__restrict__ trow,
@@ -47,18 +47,18 @@ __global__ void draft_kernel(RowState rs, SpecParams sp, int32_t *__restrict__ v
     if (sp.mode == 0)  // compat: width 1, greedy, no per-request seed (:959-972)
         gate = gate && n_active_sh == 1 && rs.temperature[r] == 0.0f && !rs.has_seed[r];
     const int limit = min(sp.k, remaining - 1);
-    const int S = min(min(sp.n, MAX_N), L - 1);
+    const int S = min(sp.n, L - 1);   // any n: tail positions past MAX_N come from global memory
     gate = gate && limit > 0 && S > 0;
 
     unsigned long long best = 0;
     if (gate) {
-        for (int i = threadIdx.x; i < S; i += blockDim.x) tail[i] = hist[L - 1 - i];
+        for (int i = threadIdx.x; i < min(S, MAX_N); i += blockDim.x) tail[i] = hist[L - 1 - i];
         __syncthreads();
         const int32_t last = tail[0];
         for (int e = threadIdx.x; e <= L - 2; e += blockDim.x) {
             if (hist[e] != last) continue;
             int l = 1;
-            while (l < S && e - l >= 0 && hist[e - l] == tail[l]) ++l;
+            while (l < S && e - l >= 0 && hist[e - l] == (l < MAX_N ? tail[l] : hist[L - 1 - l])) ++l;
             const int smax = min(l, L - 1 - e);
             if (smax >= 1) {
                 const unsigned long long key = ((unsigned long long)smax << 32) | (unsigned)e;

@@ -1,7 +1,8 @@
-// fused.cu -- per-token kernels between the q4 linears of the verify forward:
-// embedding + RMSNorm, split-K reduction + residual + RMSNorm, q/k/v epilogue
-// (per-head q/k RMSNorm, RoPE, KV append), SwiGLU, argmax, and the table
-// model used as the reference's fake LanguageModel.
+// fused.cu -- per-token kernels around the q4 linears of the verify forward:
+// embedding + first RMSNorm, the blocked activation layout, the RoPE table,
+// argmax, and the table model used as the reference's fake LanguageModel.
+// (The norms, q/k/v epilogue and SwiGLU between the linears are fused into
+// the q4 linear's epilogues, q4_tc.cu.)
 //
 // Model math follows mlx-swift-lm's Llama / Qwen3 blocks as used on the
 // verify forward (BatchGenerator.swift:900-904): pre-norm residual blocks,
@@ -56,140 +57,6 @@ __global__ void embed_norm_kernel(const uint32_t *__restrict__ wq, const __half 
             const int k = w * 8 + i;
             xn[xblk(m, k, ldx_rows)] = __float2half_rn(hm[k] * r * nw[k]);
         }
-}
-
-// xn = rmsnorm(h) * w for one token per CTA (perm8 layout for the q4 linear)
-__global__ void rmsnorm_kernel(const float *__restrict__ h, int H, const float *__restrict__ nw,
-                               float eps, __half *__restrict__ xn, int ldx_rows) {
-    griddep_launch_dependents();   // the next linear may start prefetching its weights
-    griddep_wait();                // h is the previous kernel's output
-    __shared__ float sh[32];
-    const int m = blockIdx.x;
-    const float *hm = h + (size_t)m * H;
-    float ss = 0.f;
-    for (int k = threadIdx.x; k < H; k += blockDim.x) ss += hm[k] * hm[k];
-    ss = block_sum(ss, sh);
-    const float r = 1.0f / sqrtf(ss / (float)H + eps);
-    for (int k = threadIdx.x; k < H; k += blockDim.x)
-        xn[xblk(m, k, ldx_rows)] = __float2half_rn(hm[k] * r * nw[k]);
-}
-
-__global__ void residual_norm_kernel(const float *__restrict__ part, int splits, int M, int H,
-                                     const float *__restrict__ nw, float eps,
-                                     float *__restrict__ h, __half *__restrict__ xn) {
-    __shared__ float sh[32];
-    const int m = blockIdx.x;
-    float *hm = h + (size_t)m * H;
-    float ss = 0.f;
-    for (int k = threadIdx.x; k < H; k += blockDim.x) {
-        float v = hm[k];
-        float a = 0.f;
-        for (int s = 0; s < splits; ++s) a += part[((size_t)s * M + m) * H + k];
-        v += a;
-        hm[k] = v;
-        ss += v * v;
-    }
-    if (!xn) return;
-    ss = block_sum(ss, sh);
-    const float r = 1.0f / sqrtf(ss / (float)H + eps);
-    for (int k = threadIdx.x; k < H; k += blockDim.x)
-        xn[(size_t)m * H + perm8(k)] = __float2half_rn(hm[k] * r * nw[k]);
-}
-
-// one warp per head; lanes own rotate-half pairs (i, i + D/2)
-__global__ void qkv_epilogue_kernel(const float *__restrict__ part, int splits, int M,
-                                    int n_heads, int n_kv, int D, const float *__restrict__ q_norm,
-                                    const float *__restrict__ k_norm, float eps,
-                                    const float *__restrict__ inv_freq, const int32_t *trow,
-                                    const int32_t *tpos, __half *__restrict__ qbuf,
-                                    __half *__restrict__ kc, __half *__restrict__ vc,
-                                    int max_len) {
-    const int m = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    const int N = (n_heads + 2 * n_kv) * D;
-    const int row = trow[m], pos = tpos[m];
-    const int half = D / 2;
-    const int PP = 4;  // pairs per lane (D <= 256)
-    for (int hh = warp; hh < n_heads + 2 * n_kv; hh += nwarps) {
-        const bool is_q = hh < n_heads, is_k = !is_q && hh < n_heads + n_kv;
-        const int base = hh * D;
-        float a[PP], b[PP];
-        float ss = 0.f;
-#pragma unroll
-        for (int p = 0; p < PP; ++p) {
-            const int i = lane + 32 * p;
-            a[p] = b[p] = 0.f;
-            if (i < half) {
-                for (int s = 0; s < splits; ++s) {
-                    a[p] += part[((size_t)s * M + m) * N + base + i];
-                    b[p] += part[((size_t)s * M + m) * N + base + i + half];
-                }
-                ss += a[p] * a[p] + b[p] * b[p];
-            }
-        }
-        if (is_q || is_k) {
-            const float *nw = is_q ? q_norm : k_norm;
-            float r = 1.f;
-            if (nw) {
-                ss = warp_sum(ss);
-                r = 1.0f / sqrtf(ss / (float)D + eps);
-            }
-#pragma unroll
-            for (int p = 0; p < PP; ++p) {
-                const int i = lane + 32 * p;
-                if (i < half) {
-                    float x0 = a[p], x1 = b[p];
-                    if (nw) { x0 = x0 * r * nw[i]; x1 = x1 * r * nw[i + half]; }
-                    const float ang = __fmul_rn((float)pos, inv_freq[i]);
-                    float sn, cs;
-                    sincosf(ang, &sn, &cs);
-                    a[p] = x0 * cs - x1 * sn;
-                    b[p] = x0 * sn + x1 * cs;
-                }
-            }
-        }
-        __half *dst;
-        if (is_q) {
-            dst = qbuf + ((size_t)m * n_heads + hh) * D;
-        } else {
-            const int kvh = is_k ? hh - n_heads : hh - n_heads - n_kv;
-            __half *cache = is_k ? kc : vc;
-            dst = cache + (((size_t)row * n_kv + kvh) * max_len + pos) * D;
-        }
-#pragma unroll
-        for (int p = 0; p < PP; ++p) {
-            const int i = lane + 32 * p;
-            if (i < half) {
-                dst[i] = __float2half_rn(a[p]);
-                dst[i + half] = __float2half_rn(b[p]);
-            }
-        }
-    }
-}
-
-__global__ void swiglu_kernel(const float *__restrict__ part, int splits, int M, int I,
-                              __half *__restrict__ xn) {
-    const int m = blockIdx.y;
-    const int N = 2 * I;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < I; i += gridDim.x * blockDim.x) {
-        float gg = 0.f, uu = 0.f;
-        for (int s = 0; s < splits; ++s) {
-            gg += part[((size_t)s * M + m) * N + i];
-            uu += part[((size_t)s * M + m) * N + I + i];
-        }
-        const float a = gg / (1.0f + expf(-gg)) * uu;
-        xn[(size_t)m * I + xperm(i)] = __float2half_rn(a);
-    }
-}
-
-__global__ void reduce_splits_kernel(const float *__restrict__ part, int splits, size_t n,
-                                     float *__restrict__ y) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-         i += (size_t)gridDim.x * blockDim.x) {
-        float a = 0.f;
-        for (int s = 0; s < splits; ++s) a += part[(size_t)s * n + i];
-        y[i] = a;
-    }
 }
 
 __global__ void permute_kernel(const __half *__restrict__ x, __half *__restrict__ y, int M, int K) {
@@ -314,44 +181,11 @@ cudaError_t embed_norm(const Q4Weight &embed, const int32_t *tok, int M, const f
     return cudaGetLastError();
 }
 
-cudaError_t rmsnorm(const float *h, int M, int H, const float *norm_w, float eps, __half *xn,
-                    int ldx_rows, cudaStream_t st) {
-    return launch_pdl(rmsnorm_kernel, dim3(M), dim3(TPB), 0, st, h, H, norm_w, eps, xn, ldx_rows);
-}
-
-cudaError_t residual_norm(const float *part, int splits, int M, int H, const float *norm_w,
-                          float eps, float *h, __half *xn, cudaStream_t st) {
-    residual_norm_kernel<<<M, TPB, 0, st>>>(part, splits, M, H, norm_w, eps, h, xn);
-    return cudaGetLastError();
-}
-
-cudaError_t qkv_epilogue(const float *part, int splits, int M, int n_heads, int n_kv, int D,
-                         const float *q_norm, const float *k_norm, float eps,
-                         const float *inv_freq, const int32_t *trow, const int32_t *tpos,
-                         __half *qbuf, KVLayer kv, cudaStream_t st) {
-    if (D > 256 || (D & 1)) return cudaErrorInvalidValue;
-    qkv_epilogue_kernel<<<M, TPB, 0, st>>>(part, splits, M, n_heads, n_kv, D, q_norm, k_norm, eps,
-                                           inv_freq, trow, tpos, qbuf, kv.k, kv.v, kv.max_len);
-    return cudaGetLastError();
-}
-
-cudaError_t swiglu(const float *part, int splits, int M, int I, __half *xn, cudaStream_t st) {
-    dim3 grid((I + TPB - 1) / TPB, M);
-    swiglu_kernel<<<grid, TPB, 0, st>>>(part, splits, M, I, xn);
-    return cudaGetLastError();
-}
-
 cudaError_t permute_activations(const __half *x, __half *x_perm, int M, int K, cudaStream_t st) {
     if (K % 64) return cudaErrorInvalidValue;
     const size_t n = (size_t)M * K;
     const int blocks = (int)((n + TPB - 1) / TPB < 4096 ? (n + TPB - 1) / TPB : 4096);
     permute_kernel<<<blocks > 0 ? blocks : 1, TPB, 0, st>>>(x, x_perm, M, K);
-    return cudaGetLastError();
-}
-
-cudaError_t reduce_splits(const float *part, int splits, size_t n, float *y, cudaStream_t st) {
-    const size_t b = (n + TPB - 1) / TPB;
-    reduce_splits_kernel<<<(unsigned)(b < 4096 ? (b ? b : 1) : 4096), TPB, 0, st>>>(part, splits, n, y);
     return cudaGetLastError();
 }
 

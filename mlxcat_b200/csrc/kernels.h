@@ -49,12 +49,6 @@ cudaError_t synth_q4(uint64_t seed, uint32_t tensor_id, float stddev, int N, int
                      cudaStream_t st, int rgroup = 0, int rstride = 0, int row_base = 0,
                      int col_base = 0, int k_total = 0);
 
-// ---- q4 linear (small-M path): out[s][M][N] fp32 partials over split s ----
-int q4_linear_splits(int N, int K, int M, int sm_count);
-int q4_linear_real_splits(int K, int splits);
-cudaError_t q4_linear(const Q4Weight &w, const __half *x_perm, int M, int ldx, int splits,
-                      float *out, cudaStream_t st);
-
 // ---- q4 linear on tcgen05 (TMA + TMEM) with fused split-K and epilogue ------
 }  // namespace mlxcat
 #include <cuda.h>
@@ -119,8 +113,6 @@ cudaError_t q4_tc(const Q4WeightTC &w, const __half *x_blk, int ldx_rows, int to
 // ---- activation layout helpers --------------------------------------------
 // natural [M][K] fp16 -> blocked token layout with M rows
 cudaError_t permute_activations(const __half *x, __half *x_blk, int M, int K, cudaStream_t st);
-// y[i] = sum_s part[s][i] for i < n (fixed split order)
-cudaError_t reduce_splits(const float *part, int splits, size_t n, float *y, cudaStream_t st);
 
 // ---- per-token fused kernels ------------------------------------------------
 // h = dequant(embed[tok]);  xn = rmsnorm(h) * w   (xn permuted fp16)
@@ -128,25 +120,11 @@ cudaError_t reduce_splits(const float *part, int splits, size_t n, float *y, cud
 cudaError_t embed_norm(const Q4Weight &embed, const int32_t *tok, int M, const float *norm_w,
                        float eps, float *h, __half *xn, int ldx_rows, cudaStream_t st,
                        float *rstd_out = nullptr);
-// xn = rmsnorm(h) * w  (perm8 layout)
-cudaError_t rmsnorm(const float *h, int M, int H, const float *norm_w, float eps, __half *xn,
-                    int ldx_rows, cudaStream_t st);
-// h += sum_s part[s];  xn = rmsnorm(h) * w
-cudaError_t residual_norm(const float *part, int splits, int M, int H, const float *norm_w,
-                          float eps, float *h, __half *xn, cudaStream_t st);
-// q/k/v from partials; optional per-head q/k RMSNorm; RoPE; q -> qbuf,
-// k/v -> cache at (row, pos)
+// one layer of the KV cache
 struct KVLayer {
     __half *k = nullptr, *v = nullptr;   // [rows][n_kv][max_len][D]
     int max_len = 0;
 };
-cudaError_t qkv_epilogue(const float *part, int splits, int M, int n_heads, int n_kv, int D,
-                         const float *q_norm, const float *k_norm, float eps,
-                         const float *inv_freq, const int32_t *trow, const int32_t *tpos,
-                         __half *qbuf, KVLayer kv, cudaStream_t st);
-// xn[m][i] = silu(g) * u from partials [.., 2I] (gate rows first)
-cudaError_t swiglu(const float *part, int splits, int M, int I, __half *xn, cudaStream_t st);
-
 // ---- sparse MoE MLP (moe.cu) -------------------------------------------------
 // router GEMV (bf16 weights) + softmax + top-k; assignment a = m * TK + j of
 // token m's j-th expert is appended to exp_list[expert][slot] (exp_count must

@@ -277,10 +277,6 @@ bool valid_config(const mlxcat_model_config *c, std::string &why) {
     return true;
 }
 
-int splits_for(const mlxcat_ctx *ctx, int N, int K, int M) {
-    return q4_linear_real_splits(K, q4_linear_splits(N, K, M, ctx->sm_count));
-}
-
 // bracket one launch with a pair of events when the step is being profiled
 struct ProfScope {
     mlxcat_cache *c;

@@ -466,7 +466,9 @@ class Scheduler:
             return FinishReason.LENGTH
         return None
 
-    def step(self) -> List[Response]:
+    def admit_waiting(self) -> List[Response]:
+        """Admit waiting requests into free rows (Scheduler.admitWaiting /
+        completeAdmission, Scheduler.swift:478, 599-668): prefill, first token."""
         out: List[Response] = []
         while self.waiting and self.generator.free:
             req = self.waiting.popleft()
@@ -481,6 +483,12 @@ class Scheduler:
                 self.generator.remove(req.uid)
             else:
                 self.running[req.uid] = {"req": req, "count": 1}
+        return out
+
+    def step(self) -> List[Response]:
+        """One scheduler step: admissions, then one (speculative) decode step
+        over every running row."""
+        out = self.admit_waiting()
         if not self.running:
             return out
         finished = []

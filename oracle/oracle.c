@@ -23,6 +23,12 @@
 /* Philox4x32-10 (Salmon, Moraes, Dror, Shaw: "Parallel random numbers: as     */
 /* easy as 1, 2, 3", SC'11).                                                  */
 /* ========================================================================== */
+int orc_set_threads(int n) {
+    if (n < 1) n = omp_get_num_procs();
+    omp_set_num_threads(n);
+    return omp_get_max_threads();
+}
+
 void orc_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]) {
     uint32_t c0 = ctr[0], c1 = ctr[1], c2 = ctr[2], c3 = ctr[3];
     uint32_t k0 = key[0], k1 = key[1];

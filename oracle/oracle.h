@@ -35,6 +35,10 @@ extern "C" {
 #endif
 
 /* ---- deterministic arithmetic (bit-identical with the device versions) --- */
+/* OpenMP threads of the parallel loops below (n < 1: every host core);
+ * returns the count in effect.  Hosts launched by torchrun inherit
+ * OMP_NUM_THREADS=1, which would serialise the CPU baseline. */
+int orc_set_threads(int n);
 void orc_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);
 float orc_exp_neg(float x);          /* e^x for x <= 0 (0 below -87)          */
 float orc_log(float x);              /* natural log, x > 0 normal             */

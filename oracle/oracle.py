@@ -90,6 +90,7 @@ def lib():
     u32p, u16p, f32p, i32p = (C.POINTER(C.c_uint32), C.POINTER(C.c_uint16),
                               C.POINTER(C.c_float), C.POINTER(C.c_int32))
     L.orc_philox4x32_10.argtypes = [u32p, u32p, u32p]
+    L.orc_set_threads.argtypes = [C.c_int]; L.orc_set_threads.restype = C.c_int
     L.orc_exp_neg.argtypes = [C.c_float]; L.orc_exp_neg.restype = C.c_float
     L.orc_log.argtypes = [C.c_float]; L.orc_log.restype = C.c_float
     L.orc_normal.argtypes = [C.c_uint64, C.c_uint32, C.c_uint64]; L.orc_normal.restype = C.c_float
@@ -148,6 +149,11 @@ def lib():
 # --------------------------------------------------------------------------- #
 # thin numpy helpers
 # --------------------------------------------------------------------------- #
+def set_threads(n: int = 0) -> int:
+    """OpenMP threads for the oracle's loops (0: every host core)"""
+    return int(lib().orc_set_threads(n))
+
+
 def philox(ctr, key):
     c = np.asarray(ctr, dtype=np.uint32)
     k = np.asarray(key, dtype=np.uint32)

@@ -195,6 +195,24 @@ def test_drafter_bit_exact(trial):
                                                                            len(hists[r]) + k))
 
 
+@pytest.mark.parametrize("n", [64, 65, 100, 300])
+def test_drafter_long_suffix_bit_exact(n):
+    """Suffix lengths past the 64 tail tokens staged in shared memory: an older
+    occurrence of the row's last 100 tokens (match length 100) must beat a more
+    recent one that matches only 70, exactly as proposeSuffixTokens scans
+    L = min(n, |ctx| - 1) down to 1 (BatchGenerator.swift:987-1008)."""
+    rnd = random.Random(n)
+    T = [rnd.randrange(1000, 30000) for _ in range(100)]
+    d1, d2 = [11, 12, 13, 14], [21, 22, 23, 24]
+    hist = [5] * 20 + T + d1 + [7] * 9 + [3] + T[30:] + d2 + [8] * 13 + T
+    rows = DeviceRows([hist, hist[:-1]], [500, 500])
+    vtok, cnt, _, _ = run_draft(rows, A.ACCEPT_PREFIX, 1, 4, n, 8)
+    for r, h in enumerate([hist, hist[:-1]]):
+        want = O.propose_suffix(h, n, 8, 4) or []
+        assert vtok[r, 1:1 + cnt[r]].tolist() == want, (n, r, want)
+    assert O.propose_suffix(hist, n, 8, 4) == (d1 if n >= 71 else d2)
+
+
 def test_drafter_compat_gate_width_one():
     """COMPAT speculates only at width 1, greedy, unseeded (BatchGenerator.swift:957-975)."""
     h = [1, 2, 3, 1, 2, 3, 1, 2, 3]
