@@ -158,6 +158,19 @@ MLXCAT_API int mlxcat_cache_destroy(mlxcat_cache *cache);
 MLXCAT_API int mlxcat_cache_insert_row(mlxcat_cache *cache, int32_t row, const int32_t *prompt, int32_t len,
                             int32_t max_new_tokens, const mlxcat_sampling *sampling,
                             int32_t *first_token);
+/* Admission on a prefix-cache hit: the reference installs the KV its prefix
+ * cache reconstructed for the first `prefix_len` prompt tokens and prefills
+ * only positions [prefix_len, len) (Scheduler.swift:931-985 prepareHitRow,
+ * TrackA/BlockAwarePrefixCache.swift:57-87 reconstructCache).  k_prefix and
+ * v_prefix: host fp16 [n_layers][n_kv_heads][prefix_len][head_dim] (the
+ * rank's heads when tensor-parallel), copied into the row's cache slots; then
+ * the rest of the prompt is prefilled and the first token sampled as in
+ * mlxcat_cache_insert_row.  0 <= prefix_len < len (a full match is shortened
+ * by the caller, as the reference does, so one position produces logits). */
+MLXCAT_API int mlxcat_cache_insert_row_prefix(mlxcat_cache *cache, int32_t row, const int32_t *prompt,
+                                              int32_t len, int32_t prefix_len, const uint16_t *k_prefix,
+                                              const uint16_t *v_prefix, int32_t max_new_tokens,
+                                              const mlxcat_sampling *sampling, int32_t *first_token);
 /* generator.remove(uid:) */
 MLXCAT_API int mlxcat_cache_remove_row(mlxcat_cache *cache, int32_t row);
 /* BatchKVCache.trim(n) (BatchCache.swift:403-424): every row loses
@@ -181,6 +194,14 @@ MLXCAT_API int mlxcat_cache_history(mlxcat_cache *cache, int32_t row, int32_t *o
 MLXCAT_API int mlxcat_cache_extract_row(mlxcat_cache *cache, int32_t row, int32_t layer, uint16_t *k_out,
                              uint16_t *v_out);
 MLXCAT_API int mlxcat_cache_active(mlxcat_cache *cache, int32_t *out_rows);
+/* Expert routing of the last forward on a MoE model (the SwitchGLU gate's
+ * top-k choice, un-vendored mlx-swift-lm Qwen3-MoE): ids and renormalised
+ * weights [M][top_k] of `layer`, M = the last forward's token count (rows x
+ * (k+1) after a verify forward), returned in *m.  Inspection for tests and
+ * hosts that log routing; either output may be NULL. */
+MLXCAT_API int mlxcat_cache_moe_routing(mlxcat_cache *cache, int32_t layer, int32_t *ids, float *weights,
+                                        int32_t *m);
+
 
 /* ---- hot path ----------------------------------------------------------------
  * mlxcat_draft: proposeSuffixTokens for every row (BatchGenerator.swift:982-1010)
@@ -266,12 +287,15 @@ MLXCAT_API int mlxcat_op_moe(const uint16_t *x, int32_t M, int32_t hidden, int32
  * mlxcat_op_attention, but its scratch lives in a fixed device array of
  * MLXCAT_NOALLOC_ATTN_SCRATCH_BYTES inside the library (held on every GPU that
  * loads it until exit); a shape whose mlxcat_op_attention_workspace exceeds
- * that size is rejected with MLXCAT_E_INVALID.  It allocates nothing.  The
- * first call on a device resolves the array's address with
- * cudaGetSymbolAddress (this can load the library's device code on that
- * device): make that first call before any stream capture.  All calls share
- * the one array, so calls whose kernels overlap on the GPU (different streams
- * without ordering) race on it. */
+ * that size is rejected with MLXCAT_E_INVALID.  It allocates nothing.  Each
+ * call made outside a stream capture resolves the array's address on the
+ * current device with cudaGetSymbolAddress (the first such call can load the
+ * library's device code on that device; after a device reset it picks up the
+ * new address); a call inside a capture uses the address found by the
+ * device's last uncaptured call, so make one call on each device before any
+ * stream capture (a first call inside a capture returns MLXCAT_E_STATE).  All
+ * calls share the one array, so calls whose kernels overlap on the GPU
+ * (different streams without ordering) race on it. */
 #define MLXCAT_NOALLOC_ATTN_SCRATCH_BYTES (16u << 20)
 MLXCAT_API int mlxcat_op_attention_noalloc(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
                         int32_t max_len, const int32_t *trow, const int32_t *tpos, int32_t M,

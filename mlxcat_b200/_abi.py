@@ -96,6 +96,9 @@ PROTOTYPES = {
     "mlxcat_cache_destroy": (C.c_int, [_vp]),
     "mlxcat_cache_insert_row": (C.c_int, [_vp, _i32, _vp, _i32, _i32, C.POINTER(SamplingC),
                                           C.POINTER(_i32)]),
+    "mlxcat_cache_moe_routing": (C.c_int, [_vp, _i32, _vp, _vp, C.POINTER(_i32)]),
+    "mlxcat_cache_insert_row_prefix": (C.c_int, [_vp, _i32, _vp, _i32, _i32, _vp, _vp, _i32,
+                                                 C.POINTER(SamplingC), C.POINTER(_i32)]),
     "mlxcat_cache_remove_row": (C.c_int, [_vp, _i32]),
     "mlxcat_cache_filter": (C.c_int, [_vp, _vp, _i32]),
     "mlxcat_cache_trim_row": (C.c_int, [_vp, _i32, _i32, C.POINTER(_i32)]),

@@ -144,12 +144,17 @@ moe_logits_kernel(MoERouteArgs a) {
                 w[2 * i] = f.x;
                 w[2 * i + 1] = f.y;
             }
+            // pinned arithmetic (no contraction): d = sum_i (x[k0+i] w[k0+i] + x[k0+i+4] w[k0+i+4]),
+            // lane accumulator += d; lanes then summed by the xor butterfly 16, 8, 4, 2, 1.
+            // The CPU restatement repeats exactly this order, so the bf16 logits are
+            // bit-identical for the same operand.
 #pragma unroll
             for (int t = 0; t < RT; ++t) {
                 float d = 0.f;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) d += xv[t][2 * i] * w[i] + xv[t][2 * i + 1] * w[i + 4];
-                acc[t][q] += d;
+                for (int i = 0; i < 4; ++i)
+                    d = __fadd_rn(d, __fadd_rn(__fmul_rn(xv[t][2 * i], w[i]), __fmul_rn(xv[t][2 * i + 1], w[i + 4])));
+                acc[t][q] = __fadd_rn(acc[t][q], d);
             }
         }
     }
@@ -158,7 +163,7 @@ moe_logits_kernel(MoERouteArgs a) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const float v = warp_sum(acc[t][q]);
-            if (lane == 0 && m0 + t < a.M) a.logits[(size_t)(m0 + t) * E + e0 + q] = bf16_round(v * sc[t]);
+            if (lane == 0 && m0 + t < a.M) a.logits[(size_t)(m0 + t) * E + e0 + q] = bf16_round(__fmul_rn(v, sc[t]));
         }
 }
 

@@ -117,6 +117,7 @@ struct mlxcat_cache {
     std::vector<float> host_temp;
     // step buffers
     int m_cap = 0;
+    int last_m = 0;                    // tokens of the last forward
     int32_t *vtok = nullptr, *count = nullptr, *trow = nullptr, *tpos = nullptr, *amax = nullptr,
             *out_tok = nullptr, *out_n = nullptr, *out_fin = nullptr, *first_tok = nullptr,
             *ptok = nullptr;
@@ -313,7 +314,8 @@ int ep_moe(mlxcat_cache *c, int l, int M) {
     const int cap = M * TK, rows = N * cap;
     cudaStream_t st = ctx->stream;
     int *scnt = c->ep_counts + (size_t)l * 2 * N, *rcnt = scnt + N;
-    LK(ctx, ep_pack(c->moe_id, c->moe_w, c->moe_scale, c->xg, R, M, TK, H, epr, cap, c->ep_send_x,
+    const size_t asg = (size_t)c->m_cap * TK;
+    LK(ctx, ep_pack(c->moe_id + l * asg, c->moe_w + l * asg, c->moe_scale, c->xg, R, M, TK, H, epr, cap, c->ep_send_x,
                     c->ep_send_meta, scnt, c->ep_back, st));
     const TpBlock out[3] = {{scnt, rcnt, sizeof(int), sizeof(int)},
                             {c->ep_send_meta, c->ep_recv_meta, (size_t)cap * sizeof(EpMeta), (size_t)cap * sizeof(EpMeta)},
@@ -387,6 +389,7 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
               I = cf.intermediate, L = cf.n_layers;
     const float eps = cf.rms_eps;
     const int R = c->m_cap;   // token rows of the blocked activation buffers
+    c->last_m = M;
     // The RMSNorms between the linears are folded into them: a residual linear
     // writes fp16(h * w * s) with s an earlier rstd of the row and the per-block
     // sums of squares of h; the next linear scales its accumulators by rstd / s.
@@ -442,7 +445,8 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
             ra.x = c->xg; ra.ldx_rows = R; ra.M = M; ra.H = H; ra.E = E; ra.TK = TK; ra.norm_topk = cf.norm_topk;
             ra.wr = ctx->moe[l].router;
             ra.col_part = c->norm_part; ra.col_prev = c->r_attn; ra.col_rstd = c->r_mlp; ra.norm_rows = R;
-            ra.eps = eps; ra.tok_scale = c->moe_scale; ra.topk_id = c->moe_id; ra.topk_w = c->moe_w;
+            const size_t asg = (size_t)c->m_cap * TK;   // routing kept per layer (inspection)
+            ra.eps = eps; ra.tok_scale = c->moe_scale; ra.topk_id = c->moe_id + l * asg; ra.topk_w = c->moe_w + l * asg;
             ra.exp_count = cnt; ra.exp_list = c->moe_list; ra.list_cap = c->m_cap; ra.logits = c->moe_logits;
             ctx->launches++;   // logits + top-k
             LK(ctx, moe_route(ra, st));
@@ -463,7 +467,7 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
             da.wq = mb.wq[2]; da.scales = mb.s[2]; da.biases = mb.b[2];
             da.N = H; da.K = I; da.E = E; da.x = c->moe_act; da.ldx_rows = c->m_cap * TK; da.x_div = 1;
             da.exp_count = cnt; da.exp_list = c->moe_list; da.list_cap = c->m_cap;
-            da.topk_w = c->moe_w; da.y = c->moe_y;
+            da.topk_w = c->moe_w + l * asg; da.y = c->moe_y;
             { ProfScope ps(c, 0); LK(ctx, moe_expert(da, 1, st)); }
             MoECombineArgs ca;
             ca.h = c->h; ca.y = c->moe_y; ca.M = M; ca.H = H; ca.TK = TK;
@@ -613,6 +617,69 @@ void drop_graph(mlxcat_cache *c) {
     c->graph = nullptr;
 }
 
+}  // namespace
+
+namespace {
+// Admission of `row`: row state, then prefill of prompt positions [start, len)
+// (positions below `start` are already in the cache: a prefix-cache import)
+// and the first token from the last position's logits.
+int admit_row(mlxcat_cache *c, int32_t row, const int32_t *prompt, int32_t len, int32_t start,
+              int32_t max_new_tokens, const mlxcat_sampling *sp, int32_t *first_token) {
+    mlxcat_ctx *ctx = c->ctx;
+    if (row < 0 || row >= c->rows || !prompt || len < 1 || max_new_tokens < 1 || !sp)
+        return set_err(ctx, MLXCAT_E_INVALID, "bad insert arguments");
+    if ((int64_t)len + max_new_tokens + MLXCAT_MAX_PROPOSAL + 1 > c->max_len)
+        return set_err(ctx, MLXCAT_E_INVALID, "prompt %d + max_new %d exceeds cache length %d", len,
+                       max_new_tokens, c->max_len);
+    if (sp->n_eos < 0 || sp->n_eos > MLXCAT_MAX_EOS) return set_err(ctx, MLXCAT_E_INVALID, "too many EOS ids");
+    if (sp->temperature < 0.0f) return set_err(ctx, MLXCAT_E_INVALID, "negative temperature");
+    for (int i = 0; i < len; ++i)
+        if (prompt[i] < 0 || prompt[i] >= ctx->cfg.vocab) return set_err(ctx, MLXCAT_E_INVALID, "prompt token out of range");
+    int rc = check_weights(ctx);
+    if (rc) return rc;
+    CK(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    CK(ctx, cudaStreamSynchronize(st));
+    // row state (host -> device)
+    const int32_t zero = 0, one = 1;
+    const int32_t eos_pad[MLXCAT_MAX_EOS] = {sp->eos[0], sp->eos[1], sp->eos[2], sp->eos[3],
+                                             sp->eos[4], sp->eos[5], sp->eos[6], sp->eos[7]};
+    CK(ctx, cudaMemcpy(c->hist + (size_t)row * c->hist_cap, prompt, sizeof(int32_t) * len, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->hist_len + row, &len, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->kv_len + row, &len, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->n_gen + row, &zero, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->max_new + row, &max_new_tokens, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->active + row, &one, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->temperature + row, &sp->temperature, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->top_p + row, &sp->top_p, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->seed + row, &sp->seed, 8, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->has_seed + row, &sp->has_seed, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->eos + (size_t)row * MLXCAT_MAX_EOS, eos_pad, sizeof eos_pad, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->n_eos + row, &sp->n_eos, 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(c->trigger + row, &sp->trigger, 4, cudaMemcpyHostToDevice));
+    c->host_temp[row] = sp->temperature;
+    // prefill in chunks; logits only for the last prompt token
+    std::vector<int32_t> rr(PREFILL_CHUNK, row), pp(PREFILL_CHUNK);
+    for (int s0 = start; s0 < len; s0 += PREFILL_CHUNK) {
+        const int n = std::min(PREFILL_CHUNK, len - s0);
+        for (int i = 0; i < n; ++i) pp[i] = s0 + i;
+        CK(ctx, cudaMemcpyAsync(c->ptok, prompt + s0, 4 * n, cudaMemcpyHostToDevice, st));
+        CK(ctx, cudaMemcpyAsync(c->trow, rr.data(), 4 * n, cudaMemcpyHostToDevice, st));
+        CK(ctx, cudaMemcpyAsync(c->tpos, pp.data(), 4 * n, cudaMemcpyHostToDevice, st));
+        const bool last = s0 + n == len;
+        rc = forward(c, n, PREFILL_QG, c->ptok, c->trow, c->tpos, last ? n - 1 : n);
+        if (rc) return rc;
+        CK(ctx, cudaStreamSynchronize(st));   // host staging vectors are reused
+    }
+    LK(ctx, argmax_rows(c->logits, 1, ctx->cfg.vocab, c->amax, st, c->amax_part, c->amax_ctr));
+    LK(ctx, sample_first(c->rs(), row, c->logits, ctx->cfg.vocab, c->amax, c->samp, c->first_tok, st));
+    int32_t t0 = 0;
+    CK(ctx, cudaMemcpyAsync(&t0, c->first_tok, 4, cudaMemcpyDeviceToHost, st));
+    CK(ctx, cudaStreamSynchronize(st));
+    if ((rc = device_err(c, false))) return rc;
+    if (first_token) *first_token = t0;
+    return MLXCAT_OK;
+}
 }  // namespace
 
 // ===========================================================================
@@ -1050,8 +1117,8 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
         if (ctx->tp > 1) chk(dalloc(A, &c->tp_part, (size_t)Mc * H));
         if (cf.n_experts) {
             const size_t asg = (size_t)Mc * cf.top_k;
-            chk(dalloc(A, &c->moe_id, asg));
-            chk(dalloc(A, &c->moe_w, asg));
+            chk(dalloc(A, &c->moe_id, asg * cf.n_layers));
+            chk(dalloc(A, &c->moe_w, asg * cf.n_layers));
             chk(dalloc(A, &c->moe_scale, (size_t)Mc));
             chk(dalloc(A, &c->moe_list, (size_t)cf.n_experts * Mc));
             chk(dalloc(A, &c->moe_count, (size_t)cf.n_layers * cf.n_experts));
@@ -1160,61 +1227,39 @@ int mlxcat_cache_destroy(mlxcat_cache *c) {
 int mlxcat_cache_insert_row(mlxcat_cache *c, int32_t row, const int32_t *prompt, int32_t len,
                             int32_t max_new_tokens, const mlxcat_sampling *sp, int32_t *first_token) {
     if (!c) return MLXCAT_E_INVALID;
-    mlxcat_ctx *ctx = c->ctx;
-    if (row < 0 || row >= c->rows || !prompt || len < 1 || max_new_tokens < 1 || !sp)
-        return set_err(ctx, MLXCAT_E_INVALID, "bad insert arguments");
-    if ((int64_t)len + max_new_tokens + MLXCAT_MAX_PROPOSAL + 1 > c->max_len)
-        return set_err(ctx, MLXCAT_E_INVALID, "prompt %d + max_new %d exceeds cache length %d", len,
-                       max_new_tokens, c->max_len);
-    if (sp->n_eos < 0 || sp->n_eos > MLXCAT_MAX_EOS) return set_err(ctx, MLXCAT_E_INVALID, "too many EOS ids");
-    if (sp->temperature < 0.0f) return set_err(ctx, MLXCAT_E_INVALID, "negative temperature");
-    for (int i = 0; i < len; ++i)
-        if (prompt[i] < 0 || prompt[i] >= ctx->cfg.vocab) return set_err(ctx, MLXCAT_E_INVALID, "prompt token out of range");
-    int rc = check_weights(ctx);
-    if (rc) return rc;
-    CK(ctx, cudaSetDevice(ctx->device));
-    cudaStream_t st = ctx->stream;
-    CK(ctx, cudaStreamSynchronize(st));
-    // row state (host -> device)
-    const int32_t zero = 0, one = 1;
-    const int32_t eos_pad[MLXCAT_MAX_EOS] = {sp->eos[0], sp->eos[1], sp->eos[2], sp->eos[3],
-                                             sp->eos[4], sp->eos[5], sp->eos[6], sp->eos[7]};
-    CK(ctx, cudaMemcpy(c->hist + (size_t)row * c->hist_cap, prompt, sizeof(int32_t) * len, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(c->hist_len + row, &len, 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(c->kv_len + row, &len, 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(c->n_gen + row, &zero, 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(c->max_new + row, &max_new_tokens, 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(c->active + row, &one, 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(c->temperature + row, &sp->temperature, 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(c->top_p + row, &sp->top_p, 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(c->seed + row, &sp->seed, 8, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(c->has_seed + row, &sp->has_seed, 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(c->eos + (size_t)row * MLXCAT_MAX_EOS, eos_pad, sizeof eos_pad, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(c->n_eos + row, &sp->n_eos, 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(c->trigger + row, &sp->trigger, 4, cudaMemcpyHostToDevice));
-    c->host_temp[row] = sp->temperature;
-    // prefill in chunks; logits only for the last prompt token
-    std::vector<int32_t> rr(PREFILL_CHUNK, row), pp(PREFILL_CHUNK);
-    for (int s0 = 0; s0 < len; s0 += PREFILL_CHUNK) {
-        const int n = std::min(PREFILL_CHUNK, len - s0);
-        for (int i = 0; i < n; ++i) pp[i] = s0 + i;
-        CK(ctx, cudaMemcpyAsync(c->ptok, prompt + s0, 4 * n, cudaMemcpyHostToDevice, st));
-        CK(ctx, cudaMemcpyAsync(c->trow, rr.data(), 4 * n, cudaMemcpyHostToDevice, st));
-        CK(ctx, cudaMemcpyAsync(c->tpos, pp.data(), 4 * n, cudaMemcpyHostToDevice, st));
-        const bool last = s0 + n == len;
-        rc = forward(c, n, PREFILL_QG, c->ptok, c->trow, c->tpos, last ? n - 1 : n);
-        if (rc) return rc;
-        CK(ctx, cudaStreamSynchronize(st));   // host staging vectors are reused
-    }
-    LK(ctx, argmax_rows(c->logits, 1, ctx->cfg.vocab, c->amax, st, c->amax_part, c->amax_ctr));
-    LK(ctx, sample_first(c->rs(), row, c->logits, ctx->cfg.vocab, c->amax, c->samp, c->first_tok, st));
-    int32_t t0 = 0;
-    CK(ctx, cudaMemcpyAsync(&t0, c->first_tok, 4, cudaMemcpyDeviceToHost, st));
-    CK(ctx, cudaStreamSynchronize(st));
-    if ((rc = device_err(c, false))) return rc;
-    if (first_token) *first_token = t0;
-    return MLXCAT_OK;
+    return admit_row(c, row, prompt, len, 0, max_new_tokens, sp, first_token);
 }
+
+int mlxcat_cache_insert_row_prefix(mlxcat_cache *c, int32_t row, const int32_t *prompt, int32_t len,
+                                   int32_t prefix_len, const uint16_t *k_prefix, const uint16_t *v_prefix,
+                                   int32_t max_new_tokens, const mlxcat_sampling *sp, int32_t *first_token) {
+    if (!c) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    if (ctx->cfg.kind != MLXCAT_MODEL_TRANSFORMER)
+        return set_err(ctx, MLXCAT_E_INVALID, "prefix import needs a transformer model");
+    if (prefix_len < 0 || prefix_len >= len || (prefix_len > 0 && (!k_prefix || !v_prefix)))
+        return set_err(ctx, MLXCAT_E_INVALID, "prefix_len must be in [0, len) with K and V given");
+    if (row < 0 || row >= c->rows || (int64_t)len + max_new_tokens + MLXCAT_MAX_PROPOSAL + 1 > c->max_len)
+        return set_err(ctx, MLXCAT_E_INVALID, "bad insert arguments");
+    if (prefix_len > 0) {
+        CK(ctx, cudaSetDevice(ctx->device));
+        CK(ctx, cudaStreamSynchronize(ctx->stream));
+        const mlxcat_model_config &cf = ctx->cfg;
+        const size_t D = cf.head_dim, Hkv = cf.n_kv_heads;
+        const size_t host_pitch = (size_t)prefix_len * D * 2, dev_pitch = (size_t)c->max_len * D * 2;
+        for (int l = 0; l < cf.n_layers; ++l) {
+            const KVLayer kv = c->layer(l);
+            const size_t host_off = (size_t)l * Hkv * prefix_len * D;
+            const size_t dev_off = (size_t)row * Hkv * c->max_len * D;
+            CK(ctx, cudaMemcpy2DAsync(kv.k + dev_off, dev_pitch, k_prefix + host_off, host_pitch, host_pitch, Hkv,
+                                      cudaMemcpyHostToDevice, ctx->stream));
+            CK(ctx, cudaMemcpy2DAsync(kv.v + dev_off, dev_pitch, v_prefix + host_off, host_pitch, host_pitch, Hkv,
+                                      cudaMemcpyHostToDevice, ctx->stream));
+        }
+    }
+    return admit_row(c, row, prompt, len, prefix_len, max_new_tokens, sp, first_token);
+}
+
 
 int mlxcat_cache_remove_row(mlxcat_cache *c, int32_t row) {
     if (!c || row < 0 || row >= c->rows) return MLXCAT_E_INVALID;
@@ -1281,6 +1326,21 @@ int mlxcat_cache_lengths(mlxcat_cache *c, int32_t *out) {
     CK(ctx, cudaSetDevice(ctx->device));
     CK(ctx, cudaStreamSynchronize(ctx->stream));
     CK(ctx, cudaMemcpy(out, c->kv_len, 4 * c->rows, cudaMemcpyDeviceToHost));
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_moe_routing(mlxcat_cache *c, int32_t layer, int32_t *ids, float *weights, int32_t *m) {
+    if (!c) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    const mlxcat_model_config &cf = ctx->cfg;
+    if (!cf.n_experts || layer < 0 || layer >= cf.n_layers)
+        return set_err(ctx, MLXCAT_E_INVALID, "no MoE layer %d", layer);
+    if (m) *m = c->last_m;
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    const size_t asg = (size_t)c->m_cap * cf.top_k, n = (size_t)c->last_m * cf.top_k;
+    if (ids && n) CK(ctx, cudaMemcpy(ids, c->moe_id + layer * asg, n * 4, cudaMemcpyDeviceToHost));
+    if (weights && n) CK(ctx, cudaMemcpy(weights, c->moe_w + layer * asg, n * 4, cudaMemcpyDeviceToHost));
     return MLXCAT_OK;
 }
 
@@ -1655,8 +1715,11 @@ int mlxcat_op_attention(const uint16_t *q, const uint16_t *k_cache, const uint16
 // GPU that loads this library holds that array until the process exits.
 //
 // In host code `g_attn_noalloc_scratch` is only a stand-in for the device
-// symbol; its device address is fetched once per device with
-// cudaGetSymbolAddress and cached.
+// symbol; its device address comes from cudaGetSymbolAddress on the current
+// device.  It is fetched again on every call made outside a stream capture (a
+// device reset reloads the module, after which an old address would be
+// stale); inside a capture, where that query is not allowed, the address
+// cached by the device's last uncaptured call is used.
 static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[MLXCAT_NOALLOC_ATTN_SCRATCH_BYTES];
 
 namespace {
@@ -1683,14 +1746,22 @@ int mlxcat_op_attention_noalloc(const uint16_t *q, const uint16_t *k_cache, cons
     if (dev < 0 || dev >= 64) return op_err(MLXCAT_E_INVALID, "attention_noalloc: device ordinal %d >= 64", dev);
     char *base = nullptr;
     {
-        // first call on this device (the current one): resolve the array's address
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        e = cudaStreamIsCapturing((cudaStream_t)stream, &cap);
+        if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "attention_noalloc: %s", cudaGetErrorString(e));
         std::lock_guard<std::mutex> lock(g_noalloc_mu);
-        if (!g_noalloc_base[dev]) {
+        if (cap == cudaStreamCaptureStatusNone) {
+            // resolve the array's address on the current device
             void *p = nullptr;
             e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
             if (e != cudaSuccess)
                 return op_err(MLXCAT_E_CUDA, "attention_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
             g_noalloc_base[dev] = p;
+        } else if (!g_noalloc_base[dev]) {
+            return op_err(MLXCAT_E_STATE,
+                          "attention_noalloc: first call on device %d inside a stream capture; call it once "
+                          "outside a capture first",
+                          dev);
         }
         base = static_cast<char *>(g_noalloc_base[dev]);
     }

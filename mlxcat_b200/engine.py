@@ -270,6 +270,23 @@ class BatchKVCache:
                                                       C.byref(sp), C.byref(first)))
         return first.value
 
+    def insert_row_prefix(self, row: int, prompt, k_prefix, v_prefix, max_new_tokens: int,
+                          sampling: SamplingParameters, default_seed: int = 0) -> int:
+        """Admission on a prefix-cache hit (Scheduler.prepareHitRow): k_prefix,
+        v_prefix fp16 [n_layers][n_kv_heads][prefix_len][head_dim] hold the KV of
+        the first prefix_len prompt tokens; the rest of the prompt is prefilled."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        k = np.ascontiguousarray(k_prefix, dtype=np.float16)
+        v = np.ascontiguousarray(v_prefix, dtype=np.float16)
+        if k.shape != v.shape or k.ndim != 4:
+            raise ValueError("k_prefix / v_prefix must both be [n_layers][n_kv_heads][prefix_len][head_dim]")
+        sp = sampling.to_c(default_seed)
+        first = C.c_int32()
+        self.ctx.check(self.L.mlxcat_cache_insert_row_prefix(self.h, row, p.ctypes.data, len(p), k.shape[2],
+                                                             k.ctypes.data, v.ctypes.data, max_new_tokens,
+                                                             C.byref(sp), C.byref(first)))
+        return first.value
+
     def remove_row(self, row: int):
         self.ctx.check(self.L.mlxcat_cache_remove_row(self.h, row))
 
@@ -312,6 +329,17 @@ class BatchKVCache:
         v = np.zeros_like(k)
         self.ctx.check(self.L.mlxcat_cache_extract_row(self.h, row, layer, k.ctypes.data, v.ctypes.data))
         return k, v
+
+    def moe_routing(self, layer: int):
+        """(expert ids, weights) [M][top_k] of `layer` in the last forward (MoE models)"""
+        tk = self.ctx.cfg.top_k
+        m = C.c_int32()
+        self.ctx.check(self.L.mlxcat_cache_moe_routing(self.h, layer, None, None, C.byref(m)))
+        ids = np.zeros((m.value, tk), np.int32)
+        w = np.zeros((m.value, tk), np.float32)
+        self.ctx.check(self.L.mlxcat_cache_moe_routing(self.h, layer, ids.ctypes.data, w.ctypes.data,
+                                                       C.byref(m)))
+        return ids, w
 
     def draft(self, spec: SpeculativeDecodingConfiguration):
         k = spec.max_proposal_tokens if spec.enabled else 0

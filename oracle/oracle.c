@@ -624,6 +624,35 @@ int orc_model_set_router(orc_model *m, int layer, const uint16_t *w) {
  * logits = x . Wr^T kept bf16, p = softmax(logits) in fp32, the top_k largest
  * (ties to the lower expert index), weights p_j / sum of the selected p when
  * norm_topk.  Returns logit[k-th] - logit[(k+1)-th] (0 when k == E). */
+/* One bf16 router logit: fp32 accumulation in a fixed order, rounded once.
+ * The order is the device kernel's (moe.cu moe_logits_kernel): 32 lane sums,
+ * lane l taking the 8-wide k blocks b = l, l + 32, ...; inside a block
+ * d = sum over i = 0..3 of (x[8b+i] w[8b+i] + x[8b+i+4] w[8b+i+4]); then the
+ * lane sums are combined by an xor butterfly over offsets 16, 8, 4, 2, 1.  Every
+ * product and sum is rounded separately (no fused multiply-add), so the same
+ * fp16 operand gives the same bf16 logit on both sides. */
+static float router_logit(const float *x, const uint16_t *w, int H) {
+    float lane[32];
+    const int nb = H / 8;
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int b = l; b < nb; b += 32) {
+            const int k0 = 8 * b;
+            float d = 0.0f;
+            for (int i = 0; i < 4; ++i) {
+                const float p0 = x[k0 + i] * orc_bf16_to_f32(w[k0 + i]);
+                const float p1 = x[k0 + i + 4] * orc_bf16_to_f32(w[k0 + i + 4]);
+                d = d + (p0 + p1);
+            }
+            acc = acc + d;
+        }
+        lane[l] = acc;
+    }
+    for (int o = 16; o > 0; o >>= 1)
+        for (int l = 0; l < o; ++l) lane[l] = lane[l] + lane[l + o];
+    return orc_bf16_to_f32(orc_f32_to_bf16(lane[0]));
+}
+
 float orc_moe_route(const orc_model *m, int layer, const float *x, int32_t *ids, float *weights) {
     const orc_config *c = &m->cfg;
     const int E = c->n_experts, H = c->hidden, TK = c->top_k;
@@ -631,11 +660,7 @@ float orc_moe_route(const orc_model *m, int layer, const float *x, int32_t *ids,
     float *p = (float *)malloc(sizeof(float) * (size_t)E);
     uint8_t *used = (uint8_t *)calloc((size_t)E, 1);
     const uint16_t *W = m->router + (size_t)layer * E * H;
-    for (int e = 0; e < E; ++e) {
-        float acc = 0.0f;
-        for (int k = 0; k < H; ++k) acc += x[k] * orc_bf16_to_f32(W[(size_t)e * H + k]);
-        lg[e] = orc_bf16_to_f32(orc_f32_to_bf16(acc));
-    }
+    for (int e = 0; e < E; ++e) lg[e] = router_logit(x, W + (size_t)e * H, H);
     float mx = lg[0];
     for (int e = 1; e < E; ++e) if (lg[e] > mx) mx = lg[e];
     float den = 0.0f;
@@ -765,13 +790,97 @@ float orc_moe_min_margin(int reset) {
 }
 /* the MoE MLP alone on given inputs: y[M][H] (accumulated onto, start it at
  * zero), ids/weights [M][top_k], margins [M] (each may be NULL) */
+/* Test hook: expert choices forced from outside (the device's routing of the
+ * same forward), [n_layers][M][top_k]; NULL clears.  A forced choice replaces
+ * the oracle's own selection; the oracle keeps its own softmax for the weights
+ * and records how far the forced set is from its own: the largest logit it
+ * selected but was not forced, minus the smallest forced logit it did not
+ * select, in bf16 steps of those logits (0 when the sets agree).  The device
+ * and the oracle disagree on a choice only when that distance is about one
+ * step (a bf16 near tie), which the parity tests assert. */
+static int32_t *orc_forced = NULL;
+static int orc_forced_layers = 0, orc_forced_m = 0;
+static float orc_forced_dev = 0.0f;
+
+void orc_moe_force(int n_layers, int M, int top_k, const int32_t *ids) {
+    free(orc_forced);
+    orc_forced = NULL;
+    orc_forced_layers = orc_forced_m = 0;
+    if (!ids || n_layers <= 0 || M <= 0) return;
+    orc_forced = (int32_t *)malloc(sizeof(int32_t) * (size_t)n_layers * M * top_k);
+    memcpy(orc_forced, ids, sizeof(int32_t) * (size_t)n_layers * M * top_k);
+    orc_forced_layers = n_layers;
+    orc_forced_m = M;
+}
+
+float orc_moe_force_deviation(int reset) {
+    float v = orc_forced_dev;
+    if (reset) orc_forced_dev = 0.0f;
+    return v;
+}
+
+static float bf16_step(float v) {
+    int e;
+    frexpf(fabsf(v) > 1e-30f ? fabsf(v) : 1e-30f, &e);   /* |v| in [2^(e-1), 2^e) */
+    return ldexpf(1.0f, e - 8);                          /* 8 significant bits */
+}
+
+/* token i of layer `layer` with forced ids f[0..TK): weights from the oracle's
+ * softmax, renormalised over the forced set; returns the distance above */
+static float route_forced(const orc_model *m, int layer, const float *x, const int32_t *f, int32_t *ids,
+                          float *weights) {
+    const orc_config *c = &m->cfg;
+    const int E = c->n_experts, H = c->hidden, TK = c->top_k;
+    float *lg = (float *)malloc(sizeof(float) * (size_t)E);
+    int32_t *own = (int32_t *)malloc(sizeof(int32_t) * (size_t)TK);
+    float *ow = (float *)malloc(sizeof(float) * (size_t)TK);
+    const uint16_t *W = m->router + (size_t)layer * E * H;
+    for (int e = 0; e < E; ++e) lg[e] = router_logit(x, W + (size_t)e * H, H);
+    float mx = lg[0];
+    for (int e = 1; e < E; ++e) if (lg[e] > mx) mx = lg[e];
+    float den = 0.0f;
+    for (int e = 0; e < E; ++e) den += expf(lg[e] - mx);
+    orc_moe_route(m, layer, x, own, ow);
+    float sel = 0.0f;
+    for (int j = 0; j < TK; ++j) {
+        ids[j] = f[j];
+        weights[j] = expf(lg[f[j]] - mx) / den;
+        sel += weights[j];
+    }
+    if (c->norm_topk)
+        for (int j = 0; j < TK; ++j) weights[j] = weights[j] / sel;
+    float hi = -INFINITY, lo = INFINITY;   /* own-not-forced max, forced-not-own min */
+    for (int j = 0; j < TK; ++j) {
+        int inf_ = 0, ino = 0;
+        for (int q = 0; q < TK; ++q) { inf_ |= f[q] == own[j]; ino |= own[q] == f[j]; }
+        if (!inf_ && lg[own[j]] > hi) hi = lg[own[j]];
+        if (!ino && lg[f[j]] < lo) lo = lg[f[j]];
+    }
+    float dist = 0.0f;
+    if (hi > -INFINITY) {
+        const float step = bf16_step(fabsf(hi) > fabsf(lo) ? hi : lo);
+        dist = (hi - lo) / step;
+    }
+    free(lg); free(own); free(ow);
+    return dist;
+}
+
 void orc_moe_mlp(const orc_model *m, int layer, const float *x, int M, float *y, int32_t *ids_out,
                  float *w_out, float *margins) {
     const orc_config *c = &m->cfg;
     const int H = c->hidden, I = c->intermediate, E = c->n_experts, TK = c->top_k;
     int32_t *ids = (int32_t *)malloc(sizeof(int32_t) * (size_t)M * TK);
     float *wts = (float *)malloc(sizeof(float) * (size_t)M * TK);
+    const int forced = orc_forced && layer < orc_forced_layers && M <= orc_forced_m;
     for (int i = 0; i < M; ++i) {
+        if (forced) {
+            const float d = route_forced(m, layer, x + (size_t)i * H,
+                                         orc_forced + ((size_t)layer * orc_forced_m + i) * TK,
+                                         ids + (size_t)i * TK, wts + (size_t)i * TK);
+            if (d > orc_forced_dev) orc_forced_dev = d;
+            if (margins) margins[i] = 0.0f;
+            continue;
+        }
         float mg = orc_moe_route(m, layer, x + (size_t)i * H, ids + (size_t)i * TK, wts + (size_t)i * TK);
         if (margins) margins[i] = mg;
         if (TK < E && mg < orc_last_route_margin) orc_last_route_margin = mg;

@@ -141,6 +141,9 @@ def lib():
     L.orc_moe_min_margin.argtypes = [C.c_int]
     L.orc_moe_min_margin.restype = C.c_float
     L.orc_f32_to_bf16.argtypes = [C.c_float]; L.orc_f32_to_bf16.restype = C.c_uint16
+    L.orc_moe_force.argtypes = [C.c_int, C.c_int, C.c_int, i32p]
+    L.orc_moe_force_deviation.argtypes = [C.c_int]
+    L.orc_moe_force_deviation.restype = C.c_float
     L.orc_moe_mlp.argtypes = [C.c_void_p, C.c_int, f32p, C.c_int, f32p, i32p, f32p, f32p]
     _lib = L
     return L
@@ -294,6 +297,21 @@ def router_synth(seed: int, tensor_id: int, stddev: float, E: int, H: int):
     w = np.zeros((E, H), np.uint16)
     lib().orc_router_synth(seed, tensor_id, stddev, E, H, _ptr(w, C.c_uint16))
     return w
+
+
+def moe_force(ids):
+    """Force the expert choices of the next forwards: ids [n_layers][M][top_k]
+    (e.g. the device's routing of the same verify forward); None clears."""
+    if ids is None:
+        lib().orc_moe_force(0, 0, 0, None)
+        return
+    a = np.ascontiguousarray(ids, dtype=np.int32)
+    lib().orc_moe_force(a.shape[0], a.shape[1], a.shape[2], _ptr(a, C.c_int32))
+
+
+def moe_force_deviation(reset=True) -> float:
+    """largest distance (bf16 steps) between a forced choice and the oracle's own"""
+    return float(lib().orc_moe_force_deviation(int(reset)))
 
 
 def moe_min_margin(reset=True) -> float:
