@@ -108,6 +108,7 @@ typedef struct mlxcat_cache mlxcat_cache;
 /* ---- context -------------------------------------------------------------
  * replaces: model construction + MLX device stream (NativeModelEngine.swift:44-54) */
 MLXCAT_API int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx **out);
+/* also destroys every cache still open on the context (their handles become invalid) */
 MLXCAT_API int mlxcat_ctx_destroy(mlxcat_ctx *ctx);
 /* Tensor or expert parallelism: one rank creates an id (ncclGetUniqueId), the
  * host hands the 128 bytes to every rank, each rank connects its context
@@ -301,6 +302,27 @@ MLXCAT_API int mlxcat_op_attention_noalloc(const uint16_t *q, const uint16_t *k_
                         int32_t max_len, const int32_t *trow, const int32_t *tpos, int32_t M,
                         int32_t qg, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                         uint16_t *out, void *stream);
+
+/* The prefill path's linears (Scheduler.swift:670-1016 admission prefill, which
+ * runs mlx-swift's quantizedMatmul at M = prompt length): at hundreds to
+ * thousands of tokens the contraction is dense, so the q4 weight is
+ * dequantised once into fp16 and multiplied on the tensor cores.
+ * mlxcat_op_dequant_q4: w_out fp16 [N][K] = scale * q + bias (fp16 FMA, as
+ * the q4 linear dequantises).  mlxcat_op_gemm_f16: y[m][n] = sum_k x[m][k]
+ * w[n][k], w fp16 [N][K] (N % 128 == 0), x fp16 [M][K] row-major (K % 64 ==
+ * 0), fp32 accumulation; MLXCAT_GEMM_STORE: out fp32 [M][ldo] = y;
+ * MLXCAT_GEMM_ADD: out fp32 [M][ldo] += y (residual stream);
+ * MLXCAT_GEMM_SWIGLU: w is a fused gate/up matrix (per 128-row block 64 gate
+ * rows then the matching 64 up rows), out fp16 [M][ldo] = silu(g) * u for
+ * the N/2 outputs.  err_flag (device int, may be NULL) becomes non-zero if a
+ * pipeline wait timed out. */
+#define MLXCAT_GEMM_STORE 0
+#define MLXCAT_GEMM_ADD 1
+#define MLXCAT_GEMM_SWIGLU 2
+MLXCAT_API int mlxcat_op_dequant_q4(const uint32_t *wq, const uint16_t *scales, const uint16_t *biases, int32_t N,
+                                    int32_t K, uint16_t *w_out, void *stream);
+MLXCAT_API int mlxcat_op_gemm_f16(const uint16_t *w, int32_t N, int32_t K, const uint16_t *x, int32_t M,
+                                  int32_t epilogue, void *out, int32_t ldo, int32_t *err_flag, void *stream);
 
 /* Seeded N(0, stddev) weights quantised to MLX affine q4 g64 (bit-identical
  * with the CPU restatement). */

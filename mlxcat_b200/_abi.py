@@ -24,6 +24,7 @@ ACCEPT_COMPAT = 0
 ACCEPT_PREFIX = 1
 MAX_PROPOSAL = 8
 MAX_EOS = 8
+GEMM_STORE, GEMM_ADD, GEMM_SWIGLU = 0, 1, 2
 TENSOR_EMBED = 0xFFFF0000
 TENSOR_LM_HEAD = 0xFFFF0001
 
@@ -96,6 +97,8 @@ PROTOTYPES = {
     "mlxcat_cache_destroy": (C.c_int, [_vp]),
     "mlxcat_cache_insert_row": (C.c_int, [_vp, _i32, _vp, _i32, _i32, C.POINTER(SamplingC),
                                           C.POINTER(_i32)]),
+    "mlxcat_op_dequant_q4": (C.c_int, [_vp, _vp, _vp, _i32, _i32, _vp, _vp]),
+    "mlxcat_op_gemm_f16": (C.c_int, [_vp, _i32, _i32, _vp, _i32, _i32, _vp, _i32, _vp, _vp]),
     "mlxcat_cache_moe_routing": (C.c_int, [_vp, _i32, _vp, _vp, C.POINTER(_i32)]),
     "mlxcat_cache_insert_row_prefix": (C.c_int, [_vp, _i32, _vp, _i32, _i32, _vp, _vp, _i32,
                                                  C.POINTER(SamplingC), C.POINTER(_i32)]),

@@ -110,6 +110,19 @@ size_t q4_tc_counters(int N, int M);
 cudaError_t q4_tc(const Q4WeightTC &w, const __half *x_blk, int ldx_rows, int tok_base, int M,
                   int sm_count, const Q4Epilogue &ep, cudaStream_t st);
 
+// ---- dense fp16 GEMM on tcgen05 (gemm_tc.cu): the prefill path's linears ----
+// out[m][n] from y[m][n] = sum_k x[m][k] w[n][k]; w fp16 [N][K], x fp16 [M][K]
+// (row-major, K % 64 == 0, N % 128 == 0).  GEMM_STORE: fp32 out[m*ldo + n];
+// GEMM_ADD: fp32 out[m*ldo + n] += y; GEMM_SWIGLU: w is the fused gate/up
+// matrix (64 gate rows then the matching 64 up rows per 128-row block), fp16
+// out[m*ldo + i] = silu(g_i) * u_i.  err: device flag set when a wait timed out.
+enum GemmEpi { GEMM_STORE = 0, GEMM_ADD = 1, GEMM_SWIGLU = 2 };
+cudaError_t gemm_tc(const __half *w, int N, int K, const __half *x, int M, int epi, void *out, int ldo,
+                    int sm_count, int *err, cudaStream_t st);
+// fp16 [N][K] = scale * q + bias of an MLX affine q4 matrix (hfma in fp16, as
+// the q4 kernels dequantise)
+cudaError_t dequant_q4(const Q4Weight &w, __half *out, cudaStream_t st);
+
 // ---- activation layout helpers --------------------------------------------
 // natural [M][K] fp16 -> blocked token layout with M rows
 cudaError_t permute_activations(const __half *x, __half *x_blk, int M, int K, cudaStream_t st);
@@ -125,6 +138,21 @@ struct KVLayer {
     __half *k = nullptr, *v = nullptr;   // [rows][n_kv][max_len][D]
     int max_len = 0;
 };
+
+// ---- dense prefill path (prefill.cu): row-major activations around gemm_tc ----
+// h[m] = dequantised embedding row of tok[m]
+cudaError_t prefill_embed(const Q4Weight &embed, const int32_t *tok, int n, float *h, cudaStream_t st);
+// x[m] = fp16(h[m] * rstd(h[m]) * w)
+cudaError_t prefill_rmsnorm(const float *h, int n, int H, const float *w, float eps, __half *x, cudaStream_t st);
+// y [n][(Hq + 2 Hkv) D] fp32 -> q/k norm (optional), RoPE from the (cos, sin)
+// table; q to qbuf [n][Hq][D], k/v to the cache of `row` at tpos[m]
+cudaError_t prefill_qkv(const float *y, int n, int n_heads, int n_kv, int D, const float *q_norm,
+                        const float *k_norm, float eps, const float2 *rope, int row, const int32_t *tpos,
+                        __half *qbuf, KVLayer kv, cudaStream_t st);
+// trow[i] = row, tpos[i] = s0 + i for i < n
+cudaError_t prefill_rows(int32_t *trow, int32_t *tpos, int row, int s0, int n, cudaStream_t st);
+// row-major fp16 features of one token -> row 0 of the blocked operand layout
+cudaError_t prefill_to_blocked(const __half *x, int K, __half *xb, int ldx_rows, cudaStream_t st);
 // ---- sparse MoE MLP (moe.cu) -------------------------------------------------
 // router GEMV (bf16 weights) + softmax + top-k; assignment a = m * TK + j of
 // token m's j-th expert is appended to exp_list[expert][slot] (exp_count must

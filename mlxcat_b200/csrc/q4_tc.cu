@@ -69,6 +69,19 @@ namespace mlxcat {
 
 int q4_tc_pmax(int U, int G, int nc);
 
+// the driver's tensor-map encoder, fetched once through the runtime
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void *p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
 namespace {
 
 constexpr int ROWS = 128;              // weight rows per block (MMA M)
@@ -1064,17 +1077,6 @@ __global__ void pack_sb_kernel(const __half *__restrict__ scales, const __half *
 // ---------------------------------------------------------------------------
 // host side: tensor maps and launch
 // ---------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
-        cudaDriverEntryPointQueryResult q;
-        void *p = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }
-    return fn;
-}
 
 constexpr size_t SMEM_LIMIT = 227 * 1024;
 

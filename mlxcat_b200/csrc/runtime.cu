@@ -26,8 +26,10 @@ using namespace mlxcat;
 
 namespace {
 
-constexpr int PREFILL_CHUNK = 128;   // prompt tokens per prefill forward
+constexpr int PREFILL_CHUNK = 128;   // prompt tokens per prefill forward (q4 kernels)
 constexpr int PREFILL_QG = 8;        // prompt tokens per attention group
+constexpr int DENSE_CHUNK = 2048;    // prompt tokens per dense prefill forward (fp16 GEMMs)
+constexpr int DENSE_MIN = 256;       // prompts at least this long take the dense prefill
 constexpr int KEY_CHUNK = 384;       // keys per attention split (3-deep ring, one wave at the verify shape)
 
 thread_local std::string g_op_err;
@@ -88,6 +90,7 @@ struct mlxcat_ctx {
     int32_t *table = nullptr;
     bool have_weights = false;
     int64_t launches = 0;
+    std::vector<mlxcat_cache *> caches;   // live caches; destroyed with the context
 
     const float *attn_norm(int l) const { return norms + (size_t)l * cfg.hidden; }
     const float *mlp_norm(int l) const { return norms + (size_t)(cfg.n_layers + l) * cfg.hidden; }
@@ -153,6 +156,16 @@ struct mlxcat_cache {
     AttnScratch attn;
     int attn_splits = 1;
     SampleScratch samp{};
+    // dense prefill: fp16 weights of one linear, row-major activations of one
+    // chunk of DENSE_CHUNK prompt tokens, attention scratch (one key split)
+    struct Prefill {
+        bool ready = false;
+        int qg = 0, key_chunk = 0;
+        __half *wdq = nullptr, *x = nullptr, *act = nullptr, *q = nullptr;
+        float *h = nullptr, *y = nullptr;
+        int32_t *tok = nullptr, *trow = nullptr, *tpos = nullptr;
+        AttnScratch attn;
+    } pf;
     // pinned host mirrors
     int32_t *h_tok = nullptr, *h_n = nullptr, *h_fin = nullptr;
     unsigned long long *h_stats = nullptr;
@@ -620,6 +633,94 @@ void drop_graph(mlxcat_cache *c) {
 }  // namespace
 
 namespace {
+// The dense prefill path needs a dense (non-MoE) model on one GPU.
+bool dense_prefill_ok(const mlxcat_ctx *ctx) {
+    const mlxcat_model_config &cf = ctx->cfg;
+    return cf.kind == MLXCAT_MODEL_TRANSFORMER && !cf.n_experts && ctx->tp == 1 && ctx->ep == 1 &&
+           cf.hidden % 128 == 0 && cf.intermediate % 128 == 0 && (cf.n_heads * cf.head_dim) % 128 == 0;
+}
+
+int ensure_prefill(mlxcat_cache *c) {
+    auto &pf = c->pf;
+    if (pf.ready) return MLXCAT_OK;
+    mlxcat_ctx *ctx = c->ctx;
+    const mlxcat_model_config &cf = ctx->cfg;
+    const int H = cf.hidden, I = cf.intermediate, D = cf.head_dim, Hq = cf.n_heads, Hkv = cf.n_kv_heads;
+    const size_t P = DENSE_CHUNK, Nqkv = (size_t)(Hq + 2 * Hkv) * D;
+    const size_t xw = std::max<size_t>(std::max(H, I), (size_t)Hq * D);
+    const size_t wmax = std::max(std::max(Nqkv * H, (size_t)H * Hq * D), (size_t)2 * I * H);
+    auto &A = c->allocs;
+    CK(ctx, dalloc(A, &pf.wdq, wmax));
+    CK(ctx, dalloc(A, &pf.x, P * xw));
+    CK(ctx, dalloc(A, &pf.act, P * I));
+    CK(ctx, dalloc(A, &pf.q, P * Hq * D));
+    CK(ctx, dalloc(A, &pf.h, P * H));
+    CK(ctx, dalloc(A, &pf.y, P * Nqkv));
+    CK(ctx, dalloc(A, &pf.tok, P));
+    CK(ctx, dalloc(A, &pf.trow, P));
+    CK(ctx, dalloc(A, &pf.tpos, P));
+    // attention: the longest query group whose heads fit one CTA's 64 query rows;
+    // every key of a group in one split (prefill has many groups to spread)
+    pf.qg = std::max(1, std::min(16, 64 / (Hq / Hkv)));
+    pf.key_chunk = (c->max_len + 31) / 32 * 32;
+    const int groups = (int)((P + pf.qg - 1) / pf.qg);
+    const int qrows = attention_qrows(pf.qg, Hq, Hkv);
+    pf.attn.items = attention_scratch_items(groups, Hkv, 1);
+    CK(ctx, dalloc(A, &pf.attn.o, pf.attn.items * qrows * D));
+    CK(ctx, dalloc(A, &pf.attn.ml, pf.attn.items * qrows * 2));
+    pf.ready = true;
+    return MLXCAT_OK;
+}
+
+// Prompt positions [s0, s0 + n) of `row` (tokens tok, on the device) through
+// every layer with fp16 GEMMs on tcgen05 (gemm_tc.cu): each q4 weight is
+// dequantised once per chunk, activations are row-major, the norms are exact
+// (x = fp16(h * rstd * w)).  K/V of the positions land in the row's cache; with
+// `logits` the last position's logits go to row 0 of c->logits.
+int prefill_dense(mlxcat_cache *c, int row, const int32_t *tok, int s0, int n, bool logits) {
+    mlxcat_ctx *ctx = c->ctx;
+    const mlxcat_model_config &cf = ctx->cfg;
+    auto &pf = c->pf;
+    cudaStream_t st = ctx->stream;
+    const int H = cf.hidden, I = cf.intermediate, D = cf.head_dim, Hq = cf.n_heads, Hkv = cf.n_kv_heads,
+              L = cf.n_layers, sm = ctx->sm_count;
+    const int Nqkv = (Hq + 2 * Hkv) * D;
+    const float eps = cf.rms_eps;
+    LK(ctx, prefill_rows(pf.trow, pf.tpos, row, s0, n, st));
+    LK(ctx, prefill_embed(ctx->embed.view(), tok, n, pf.h, st));
+    LK(ctx, prefill_rmsnorm(pf.h, n, H, ctx->attn_norm(0), eps, pf.x, st));
+    for (int l = 0; l < L; ++l) {
+        const KVLayer kv = c->layer(l);
+        LK(ctx, dequant_q4(ctx->qkv[l].view(), pf.wdq, st));
+        LK(ctx, gemm_tc(pf.wdq, Nqkv, H, pf.x, n, GEMM_STORE, pf.y, Nqkv, sm, c->err, st));
+        LK(ctx, prefill_qkv(pf.y, n, Hq, Hkv, D, ctx->q_norm(l), ctx->k_norm(l), eps, c->rope, row, pf.tpos, pf.q,
+                            kv, st));
+        ctx->launches++;   // attention is two kernels; its output reuses x (row-major [n][Hq*D])
+        LK(ctx, attention(pf.q, kv, pf.trow, pf.tpos, n, pf.qg, Hq, Hkv, D, pf.key_chunk, 1, pf.attn, pf.x, false,
+                          n, st, false));
+        LK(ctx, dequant_q4(ctx->o[l].view(), pf.wdq, st));
+        LK(ctx, gemm_tc(pf.wdq, H, Hq * D, pf.x, n, GEMM_ADD, pf.h, H, sm, c->err, st));
+        LK(ctx, prefill_rmsnorm(pf.h, n, H, ctx->mlp_norm(l), eps, pf.x, st));
+        LK(ctx, dequant_q4(ctx->gu[l].view(), pf.wdq, st));
+        LK(ctx, gemm_tc(pf.wdq, 2 * I, H, pf.x, n, GEMM_SWIGLU, pf.act, I, sm, c->err, st));
+        LK(ctx, dequant_q4(ctx->down[l].view(), pf.wdq, st));
+        LK(ctx, gemm_tc(pf.wdq, H, I, pf.act, n, GEMM_ADD, pf.h, H, sm, c->err, st));
+        LK(ctx, prefill_rmsnorm(pf.h, n, H, l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(), eps, pf.x,
+                                st));
+    }
+    if (logits) {   // the last position through the q4 head (one token: the GEMV-shaped kernel)
+        LK(ctx, prefill_to_blocked(pf.x + (size_t)(n - 1) * H, H, c->xn, c->m_cap, st));
+        const DevLin &head = cf.tie_embeddings ? ctx->embed : ctx->lm_head;
+        Q4Epilogue e;
+        e.part = c->part; e.counters = c->counters; e.err = c->err;
+        e.op = Q4Epilogue::STORE; e.out = c->logits; e.ldo = cf.vocab;
+        LK(ctx, q4_tc(head.tc(), c->xn, c->m_cap, 0, 1, sm, e, st));
+    }
+    return MLXCAT_OK;
+}
+}  // namespace
+
+namespace {
 // Admission of `row`: row state, then prefill of prompt positions [start, len)
 // (positions below `start` are already in the cache: a prefix-cache import)
 // and the first token from the last position's logits.
@@ -659,8 +760,18 @@ int admit_row(mlxcat_cache *c, int32_t row, const int32_t *prompt, int32_t len, 
     CK(ctx, cudaMemcpy(c->trigger + row, &sp->trigger, 4, cudaMemcpyHostToDevice));
     c->host_temp[row] = sp->temperature;
     // prefill in chunks; logits only for the last prompt token
+    const bool dense = len - start >= DENSE_MIN && dense_prefill_ok(ctx);
+    if (dense) {
+        if ((rc = ensure_prefill(c))) return rc;
+        for (int s0 = start; s0 < len; s0 += DENSE_CHUNK) {
+            const int n = std::min(DENSE_CHUNK, len - s0);
+            // stream-ordered after the previous chunk's kernels, which read the same buffer
+            CK(ctx, cudaMemcpyAsync(c->pf.tok, prompt + s0, 4 * n, cudaMemcpyHostToDevice, st));
+            if ((rc = prefill_dense(c, row, c->pf.tok, s0, n, s0 + n == len))) return rc;
+        }
+    }
     std::vector<int32_t> rr(PREFILL_CHUNK, row), pp(PREFILL_CHUNK);
-    for (int s0 = start; s0 < len; s0 += PREFILL_CHUNK) {
+    for (int s0 = dense ? len : start; s0 < len; s0 += PREFILL_CHUNK) {
         const int n = std::min(PREFILL_CHUNK, len - s0);
         for (int i = 0; i < n; ++i) pp[i] = s0 + i;
         CK(ctx, cudaMemcpyAsync(c->ptok, prompt + s0, 4 * n, cudaMemcpyHostToDevice, st));
@@ -816,6 +927,8 @@ int mlxcat_ctx_tp_connect(mlxcat_ctx *ctx, const uint8_t id[128]) {
 
 int mlxcat_ctx_destroy(mlxcat_ctx *ctx) {
     if (!ctx) return MLXCAT_OK;
+    // caches hold the context's stream and buffers: they go first
+    while (!ctx->caches.empty()) mlxcat_cache_destroy(ctx->caches.back());
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     tp_destroy(ctx->nccl);
@@ -1200,12 +1313,15 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
         mlxcat_cache_destroy(c);
         return rc;
     }
+    ctx->caches.push_back(c);
     *out = c;
     return MLXCAT_OK;
 }
 
 int mlxcat_cache_destroy(mlxcat_cache *c) {
     if (!c) return MLXCAT_OK;
+    auto &live = c->ctx->caches;
+    live.erase(std::remove(live.begin(), live.end(), c), live.end());
     cudaSetDevice(c->ctx->device);
     cudaStreamSynchronize(c->ctx->stream);
     drop_graph(c);
@@ -1782,6 +1898,29 @@ int mlxcat_op_attention_noalloc(const uint16_t *q, const uint16_t *k_cache, cons
     e = attention(reinterpret_cast<const __half *>(q), kv, trow, tpos, M, qg, n_heads, n_kv, D, KEY_CHUNK,
                   splits, sc, reinterpret_cast<__half *>(out), false, M, (cudaStream_t)stream);
     if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "attention_noalloc: %s", cudaGetErrorString(e));
+    return MLXCAT_OK;
+}
+
+int mlxcat_op_dequant_q4(const uint32_t *wq, const uint16_t *scales, const uint16_t *biases, int32_t N, int32_t K,
+                         uint16_t *w_out, void *stream) {
+    if (!wq || !scales || !biases || !w_out || N <= 0 || K <= 0 || K % 64)
+        return op_err(MLXCAT_E_INVALID, "dequant_q4: bad arguments");
+    Q4Weight w;
+    w.wq = wq; w.scales = reinterpret_cast<const __half *>(scales); w.biases = reinterpret_cast<const __half *>(biases);
+    w.N = N; w.K = K;
+    cudaError_t e = dequant_q4(w, reinterpret_cast<__half *>(w_out), (cudaStream_t)stream);
+    if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "dequant_q4: %s", cudaGetErrorString(e));
+    return MLXCAT_OK;
+}
+
+int mlxcat_op_gemm_f16(const uint16_t *w, int32_t N, int32_t K, const uint16_t *x, int32_t M, int32_t epilogue,
+                       void *out, int32_t ldo, int32_t *err_flag, void *stream) {
+    if (!w || !x || !out || N <= 0 || K <= 0 || M <= 0 || N % 128 || K % 64 || epilogue < 0 || epilogue > 2)
+        return op_err(MLXCAT_E_INVALID, "gemm_f16: bad arguments (N %% 128, K %% 64)");
+    if (ldo < (epilogue == MLXCAT_GEMM_SWIGLU ? N / 2 : N)) return op_err(MLXCAT_E_INVALID, "gemm_f16: ldo too small");
+    cudaError_t e = gemm_tc(reinterpret_cast<const __half *>(w), N, K, reinterpret_cast<const __half *>(x), M,
+                            epilogue, out, ldo, op_sm_count(), err_flag, (cudaStream_t)stream);
+    if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "gemm_f16: %s", cudaGetErrorString(e));
     return MLXCAT_OK;
 }
 

@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import ctypes as C
 import dataclasses
+import weakref
 from collections import OrderedDict, deque
 from typing import Dict, List, Optional
 
@@ -172,6 +173,7 @@ class Context:
     def __init__(self, cfg: ModelConfig, device: int = 0):
         self.L = A.lib()
         self.cfg = cfg
+        self._caches = weakref.WeakSet()   # mlxcat_ctx_destroy frees them too
         h = C.c_void_p()
         c = cfg.to_c()
         A.check(self.L.mlxcat_ctx_create(C.byref(c), device, C.byref(h)))
@@ -239,6 +241,8 @@ class Context:
 
     def close(self):
         if getattr(self, "h", None):
+            for c in list(getattr(self, "_caches", ())):
+                c.close()   # before the context: a cache uses its stream and buffers
             self.L.mlxcat_ctx_destroy(self.h)
             self.h = None
 
@@ -260,6 +264,7 @@ class BatchKVCache:
         h = C.c_void_p()
         ctx.check(self.L.mlxcat_cache_create(ctx.h, max_rows, max_len, C.byref(h)))
         self.h = h
+        ctx._caches.add(self)
 
     def insert_row(self, row: int, prompt, max_new_tokens: int, sampling: SamplingParameters,
                    default_seed: int = 0) -> int:
@@ -398,9 +403,10 @@ class BatchKVCache:
         return ms.value
 
     def close(self):
-        if getattr(self, "h", None):
+        # a context that was closed first has destroyed this cache already
+        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
             self.L.mlxcat_cache_destroy(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:

@@ -799,16 +799,25 @@ float orc_moe_min_margin(int reset) {
  * and the oracle disagree on a choice only when that distance is about one
  * step (a bf16 near tie), which the parity tests assert. */
 static int32_t *orc_forced = NULL;
+static float *orc_forced_w = NULL;   /* optional: the weights forced too */
 static int orc_forced_layers = 0, orc_forced_m = 0;
 static float orc_forced_dev = 0.0f;
+static float orc_forced_wdev = 0.0f;   /* largest |forced w - own w| / own w */
 
-void orc_moe_force(int n_layers, int M, int top_k, const int32_t *ids) {
+void orc_moe_force(int n_layers, int M, int top_k, const int32_t *ids, const float *weights) {
     free(orc_forced);
+    free(orc_forced_w);
     orc_forced = NULL;
+    orc_forced_w = NULL;
     orc_forced_layers = orc_forced_m = 0;
     if (!ids || n_layers <= 0 || M <= 0) return;
-    orc_forced = (int32_t *)malloc(sizeof(int32_t) * (size_t)n_layers * M * top_k);
-    memcpy(orc_forced, ids, sizeof(int32_t) * (size_t)n_layers * M * top_k);
+    const size_t n = (size_t)n_layers * M * top_k;
+    orc_forced = (int32_t *)malloc(sizeof(int32_t) * n);
+    memcpy(orc_forced, ids, sizeof(int32_t) * n);
+    if (weights) {
+        orc_forced_w = (float *)malloc(sizeof(float) * n);
+        memcpy(orc_forced_w, weights, sizeof(float) * n);
+    }
     orc_forced_layers = n_layers;
     orc_forced_m = M;
 }
@@ -816,6 +825,12 @@ void orc_moe_force(int n_layers, int M, int top_k, const int32_t *ids) {
 float orc_moe_force_deviation(int reset) {
     float v = orc_forced_dev;
     if (reset) orc_forced_dev = 0.0f;
+    return v;
+}
+
+float orc_moe_force_weight_deviation(int reset) {
+    float v = orc_forced_wdev;
+    if (reset) orc_forced_wdev = 0.0f;
     return v;
 }
 
@@ -874,9 +889,17 @@ void orc_moe_mlp(const orc_model *m, int layer, const float *x, int M, float *y,
     const int forced = orc_forced && layer < orc_forced_layers && M <= orc_forced_m;
     for (int i = 0; i < M; ++i) {
         if (forced) {
-            const float d = route_forced(m, layer, x + (size_t)i * H,
-                                         orc_forced + ((size_t)layer * orc_forced_m + i) * TK,
-                                         ids + (size_t)i * TK, wts + (size_t)i * TK);
+            const size_t f0 = ((size_t)layer * orc_forced_m + i) * TK;
+            const float d = route_forced(m, layer, x + (size_t)i * H, orc_forced + f0, ids + (size_t)i * TK,
+                                         wts + (size_t)i * TK);
+            if (orc_forced_w) {
+                for (int j = 0; j < TK; ++j) {
+                    const float own = wts[(size_t)i * TK + j], fw = orc_forced_w[f0 + j];
+                    const float rel = fabsf(fw - own) / (own > 1e-30f ? own : 1e-30f);
+                    if (rel > orc_forced_wdev) orc_forced_wdev = rel;
+                }
+                memcpy(wts + (size_t)i * TK, orc_forced_w + f0, sizeof(float) * TK);
+            }
             if (d > orc_forced_dev) orc_forced_dev = d;
             if (margins) margins[i] = 0.0f;
             continue;

@@ -133,10 +133,13 @@ float orc_moe_min_margin(int reset);
  * y[M][hidden] += sum_j w_j expert_j(x); ids/weights [M][top_k] and routing
  * margins [M] (each may be NULL) */
 /* test hook: force the expert choices of the next forwards, ids
- * [n_layers][M][top_k] (token i of a forward of M tokens); NULL clears */
-void orc_moe_force(int n_layers, int M, int top_k, const int32_t *ids);
+ * [n_layers][M][top_k] (token i of a forward of M tokens), and with weights
+ * (may be NULL) their routing weights too; ids NULL clears */
+void orc_moe_force(int n_layers, int M, int top_k, const int32_t *ids, const float *weights);
 /* largest distance, in bf16 steps, between a forced choice and the oracle's own */
 float orc_moe_force_deviation(int reset);
+/* largest relative difference between a forced routing weight and the oracle's own */
+float orc_moe_force_weight_deviation(int reset);
 void orc_moe_mlp(const orc_model *m, int layer, const float *x, int M, float *y, int32_t *ids,
                  float *weights, float *margins);
 

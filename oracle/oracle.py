@@ -141,9 +141,11 @@ def lib():
     L.orc_moe_min_margin.argtypes = [C.c_int]
     L.orc_moe_min_margin.restype = C.c_float
     L.orc_f32_to_bf16.argtypes = [C.c_float]; L.orc_f32_to_bf16.restype = C.c_uint16
-    L.orc_moe_force.argtypes = [C.c_int, C.c_int, C.c_int, i32p]
+    L.orc_moe_force.argtypes = [C.c_int, C.c_int, C.c_int, i32p, f32p]
     L.orc_moe_force_deviation.argtypes = [C.c_int]
     L.orc_moe_force_deviation.restype = C.c_float
+    L.orc_moe_force_weight_deviation.argtypes = [C.c_int]
+    L.orc_moe_force_weight_deviation.restype = C.c_float
     L.orc_moe_mlp.argtypes = [C.c_void_p, C.c_int, f32p, C.c_int, f32p, i32p, f32p, f32p]
     _lib = L
     return L
@@ -299,19 +301,27 @@ def router_synth(seed: int, tensor_id: int, stddev: float, E: int, H: int):
     return w
 
 
-def moe_force(ids):
+def moe_force(ids, weights=None):
     """Force the expert choices of the next forwards: ids [n_layers][M][top_k]
-    (e.g. the device's routing of the same verify forward); None clears."""
+    (e.g. the device's routing of the same verify forward), and optionally their
+    weights; None clears."""
     if ids is None:
-        lib().orc_moe_force(0, 0, 0, None)
+        lib().orc_moe_force(0, 0, 0, None, None)
         return
     a = np.ascontiguousarray(ids, dtype=np.int32)
-    lib().orc_moe_force(a.shape[0], a.shape[1], a.shape[2], _ptr(a, C.c_int32))
+    w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float32)
+    lib().orc_moe_force(a.shape[0], a.shape[1], a.shape[2], _ptr(a, C.c_int32),
+                        None if w is None else _ptr(w, C.c_float))
 
 
 def moe_force_deviation(reset=True) -> float:
     """largest distance (bf16 steps) between a forced choice and the oracle's own"""
     return float(lib().orc_moe_force_deviation(int(reset)))
+
+
+def moe_force_weight_deviation(reset=True) -> float:
+    """largest relative difference between a forced routing weight and the oracle's own"""
+    return float(lib().orc_moe_force_weight_deviation(int(reset)))
 
 
 def moe_min_margin(reset=True) -> float:

@@ -59,7 +59,7 @@ def verify_at_shape(cfg, rows, ctx_len, k, n, temperature, top_p, seed):
     ctx.synth_weights(seed)
     om = oracle_model(cfg, seed)
     K1, Ly = k + 1, cfg.n_layers
-    max_len = ctx_len + 64
+    max_len = ctx_len + 128   # prompt + 64 new tokens + the verify window
     # segment-pool prompts (64 segments of 48 tokens) so the drafter proposes tokens
     prompts = [segment_prompt(cfg.vocab, 64, 48, ctx_len - (r % 5), 1000 + r) for r in range(rows)]
     sps = [M.SamplingParameters(temperature=temperature, top_p=top_p, seed=7000 + r) for r in range(rows)]
@@ -83,7 +83,8 @@ def verify_at_shape(cfg, rows, ctx_len, k, n, temperature, top_p, seed):
     hist = [cache.history(r) for r in range(rows)]
     drafts = cache.draft(spec)
     logits = cache.verify_forward(spec)
-    assert sum(len(d) for d in drafts) > 0, "the segment-pool prompts should yield drafts"
+    if temperature == 0.0:   # (a sampled first token rarely occurs in the prompt: rows may not draft)
+        assert sum(len(d) for d in drafts) > 0, "the segment-pool prompts should yield drafts"
     toks, trow, tpos = [], [], []
     for r in range(rows):
         assert drafts[r] == (O.propose_suffix(hist[r], n, 8, k) or [])
@@ -92,9 +93,9 @@ def verify_at_shape(cfg, rows, ctx_len, k, n, temperature, top_p, seed):
         trow += [r] * K1
         tpos += list(range(len(prompts[r]), len(prompts[r]) + K1))
     ol = O.forward(om, kv, toks, trow, tpos)
+    # every verify position, the padding too (the oracle ran the same padded tokens)
     for r in range(rows):
-        m = len(drafts[r]) + 1
-        np.testing.assert_allclose(logits[r, :m], ol[r * K1:r * K1 + m], rtol=TOL, atol=TOL)
+        np.testing.assert_allclose(logits[r], ol[r * K1:(r + 1) * K1], rtol=TOL, atol=TOL)
     tok, cnt, fin, stats = cache.accept(spec)
     for r in range(rows):
         m = len(drafts[r]) + 1

@@ -312,7 +312,8 @@ def test_top_p_threshold_matches_oracle_on_hard_cases():
         st = rows.struct()
         sc = A.SpecConfigC(A.ACCEPT_PREFIX, 1, 0, 3, 8)
         dl = dev(logits.astype(np.float32))
-        A.check(L.mlxcat_op_accept(C.byref(st), C.byref(sc), ptr(dev(vt)), ptr(dev(np.zeros(1, np.int32))),
+        dvt, dcnt = dev(vt), dev(np.zeros(1, np.int32))   # alive across the call
+        A.check(L.mlxcat_op_accept(C.byref(st), C.byref(sc), ptr(dvt), ptr(dcnt),
                                    ptr(dl), V, ptr(tokens), ptr(n), ptr(fin), ptr(stats), ptr(ws),
                                    ws_bytes, None))
         torch.cuda.synchronize()

@@ -7,10 +7,13 @@
   within 1e-5, outputs within 2e-2 of the output scale -- at a small shape
   and at the Qwen3-30B-A3B shape (128 experts, top-8, hidden 2048, M = 320);
 * the verify forward of a MoE model against the oracle's forward on every
-  row: the oracle takes the device's expert choices (its inputs differ from
-  the device's in the last fp16 bits, so a bf16 near tie can resolve the
-  other way) and the test asserts that each forced choice is within a bf16
-  step of the oracle's own;
+  row and verify position: the router's logits are bf16 by spec and the
+  device's router input is fp16, so a logit can round to the neighbouring
+  bf16 value -- which moves its routing weight by up to a bf16 step of the
+  logit and can resolve a near tie the other way.  The oracle therefore takes
+  the device's expert choices and weights, and the test bounds both against
+  the oracle's own: every forced choice within NEAR_TIE_STEPS bf16 steps,
+  every forced weight within WEIGHT_RTOL; the logits then agree within 2e-2;
 * batch invariance (the reference's own MoE gate,
   Tests/MLXCatTests/MoEBatchIntegrationTests.swift:37: batched greedy tokens
   equal single-row tokens)."""
@@ -31,6 +34,7 @@ from tests.gpu_util import dev, ptr  # noqa: E402
 L = A.lib()
 TOL = 2e-2
 NEAR_TIE_STEPS = 2.0   # a forced choice may differ from the oracle's only within this many bf16 steps
+WEIGHT_RTOL = 2e-2     # two bf16 steps of a logit of magnitude <= 2.5 move exp(logit) by at most ~2 %
 
 MOE_SMALL = M.ModelConfig(2, 512, 8, 2, 64, 256, 4096, False, True, 1e-6, 1e6, name="moe-small",
                           n_experts=32, top_k=4, norm_topk=True)
@@ -117,11 +121,13 @@ def test_op_moe_matches_oracle(cfg, M_tok):
 
 def moe_verify_against_oracle(cfg, rows, ctx_len, k, seed):
     """Device verify forward of every row vs the oracle's forward over the same
-    padded verify tokens, with the oracle's expert choices forced to the
-    device's (admission and verify forwards); returns the largest distance, in
-    bf16 steps, between a forced choice and the oracle's own.  Prompt KV comes
-    from a prefix-cache import of random fp16 keys/values, so each admission
-    computes one position (the last prompt token) on both sides."""
+    padded verify tokens, with the oracle's expert choices and weights forced
+    to the device's (admission and verify forwards); returns the largest
+    distance, in bf16 steps, between a forced choice and the oracle's own, and
+    the largest relative difference between a forced weight and the oracle's
+    own.  Prompt KV comes from a prefix-cache import of random fp16
+    keys/values, so each admission computes one position (the last prompt
+    token) on both sides."""
     ctx = M.Context(cfg)
     ctx.synth_weights(seed)
     om = oracle_model(cfg, seed)
@@ -132,8 +138,8 @@ def moe_verify_against_oracle(cfg, rows, ctx_len, k, seed):
     cache = M.BatchKVCache(ctx, rows, max_len)
     kv = O.KV(om, rows, max_len)
     rng = np.random.default_rng(seed)
-    dist = 0.0
     O.moe_force_deviation(reset=True)
+    O.moe_force_weight_deviation(reset=True)
     for r, p in enumerate(prompts):
         shape = (L, cfg.n_kv_heads, len(p) - 1, cfg.head_dim)
         kp = rng.standard_normal(shape).astype(np.float16)
@@ -142,14 +148,16 @@ def moe_verify_against_oracle(cfg, rows, ctx_len, k, seed):
         for l in range(L):
             kv.k(r, l, cfg.n_kv_heads, cfg.head_dim)[:, :len(p) - 1] = kp[l].astype(np.float32)
             kv.v(r, l, cfg.n_kv_heads, cfg.head_dim)[:, :len(p) - 1] = vp[l].astype(np.float32)
-        O.moe_force(np.stack([cache.moe_routing(l)[0] for l in range(L)]))
+        rt = [cache.moe_routing(l) for l in range(L)]
+        O.moe_force(np.stack([x[0] for x in rt]), np.stack([x[1] for x in rt]))
         ol = O.forward(om, kv, [p[-1]], [r], [len(p) - 1])[0]
         top2 = np.sort(ol)[-2:]
         assert first == int(np.argmax(ol)) or top2[1] - top2[0] < 1e-2, (r, first)
     hist = [cache.history(r) for r in range(rows)]
     drafts = cache.draft(spec)
     logits = cache.verify_forward(spec)
-    routing = np.stack([cache.moe_routing(l)[0] for l in range(L)])
+    rt = [cache.moe_routing(l) for l in range(L)]
+    routing, weights = np.stack([x[0] for x in rt]), np.stack([x[1] for x in rt])
     assert routing.shape[1] == rows * K1
     toks, trow, tpos = [], [], []
     for r in range(rows):
@@ -157,30 +165,32 @@ def moe_verify_against_oracle(cfg, rows, ctx_len, k, seed):
         toks += [hist[r][-1]] + d + [hist[r][-1]] * (k - len(d))   # the device's padded verify tokens
         trow += [r] * K1
         tpos += list(range(len(prompts[r]), len(prompts[r]) + K1))
-    O.moe_force(routing)
+    O.moe_force(routing, weights)
     ol = O.forward(om, kv, toks, trow, tpos)
     dist = O.moe_force_deviation(reset=True)
+    wdev = O.moe_force_weight_deviation(reset=True)
     O.moe_force(None)
-    for r in range(rows):
-        n = len(drafts[r]) + 1
-        np.testing.assert_allclose(logits[r, :n], ol[r * K1:r * K1 + n], rtol=TOL, atol=TOL)
+    for r in range(rows):   # every verify position, the padding too
+        np.testing.assert_allclose(logits[r], ol[r * K1:(r + 1) * K1], rtol=TOL, atol=TOL)
     tok, n, fin, stats = cache.accept(spec)
     lens = cache.lengths()
     for r in range(rows):
         assert lens[r] == len(prompts[r]) + int(n[r])
-    return dist
+    return dist, wdev
 
 
 def test_moe_verify_logits_match_oracle():
-    dist = moe_verify_against_oracle(MOE_SMALL, 2, 72, 4, 7)
+    dist, wdev = moe_verify_against_oracle(MOE_SMALL, 2, 72, 4, 7)
     assert dist <= NEAR_TIE_STEPS, f"a device expert choice is {dist} bf16 steps from the oracle's"
+    assert wdev <= WEIGHT_RTOL, f"a device routing weight is {wdev:.3g} (relative) from the oracle's"
 
 
 def test_moe_30b_shape_verify_matches_oracle():
     """Qwen3-30B-A3B shapes (128 experts, top-8, hidden 2048, vocab 151936) at
     64 rows x (k+1 = 5) = 320 verify tokens over 1024-token contexts."""
-    dist = moe_verify_against_oracle(MOE_30B, 64, 1024, 4, 31)
+    dist, wdev = moe_verify_against_oracle(MOE_30B, 64, 1024, 4, 31)
     assert dist <= NEAR_TIE_STEPS, f"a device expert choice is {dist} bf16 steps from the oracle's"
+    assert wdev <= WEIGHT_RTOL, f"a device routing weight is {wdev:.3g} (relative) from the oracle's"
 
 
 def test_moe_batched_rows_match_single_row_runs():
