@@ -645,6 +645,38 @@ def run_kernel_case(args):
     torch.cuda.set_device(0)
     p = lambda t: C.c_void_p(t.data_ptr())
     reps = args.kernel_reps
+    if args.kernel_case == "prefill":
+        run_prefill_case(args, wl, cfg)
+        return
+    if args.kernel_case == "gemm":
+        # the prefill's fused gate/up GEMM on one 2048-token chunk (fp16 weights, tcgen05)
+        N, K, Mt = 2 * cfg.intermediate, cfg.hidden, 2048
+        w = (torch.randn((N, K), device="cuda") * 0.02).half()
+        x = torch.randn((Mt, K), device="cuda").half()
+        out = torch.empty((Mt, N // 2), dtype=torch.float16, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        flops = 2.0 * Mt * N * K
+
+        def launch(i):
+            A.check(L.mlxcat_op_gemm_f16(p(w), N, K, p(x), Mt, A.GEMM_SWIGLU, p(out), N // 2, p(err), None))
+        for i in range(args.warmup):
+            launch(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            launch(i)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        _, tfl, _ = peaks()
+        burst = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"] \
+            if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
+        print(json.dumps({"kernel_case": "gemm", "config": args.config,
+                          "shape": {"M": Mt, "N": N, "K": K, "epilogue": "swiglu"}, "us_per_launch": ms * 1e3,
+                          "tflops": flops / (ms / 1e3) / 1e12, "frac_of_burst_bf16": flops / (ms / 1e3) / 1e12 / burst,
+                          "timeout_flag": int(err.item())}))
+        return
     if args.kernel_case == "q4_linear":
         N, K = 2 * cfg.intermediate, cfg.hidden          # fused gate/up projection
         copies = max(2, int(4 * 126e6 // (N * K // 2)) + 1)
@@ -726,6 +758,40 @@ def run_kernel_case(args):
                       "note": "time per launch includes the split-K reduction / combine kernel"}))
 
 
+def run_prefill_case(args, wl, cfg):
+    """Admission of one 4096-token prompt (prefill of every position + the
+    first token) on an otherwise idle batch, timed with CUDA events on the
+    context stream; flops = 2 x weights x tokens + causal attention."""
+    import torch
+    import mlxcat_b200 as M
+    from mlxcat_b200 import _abi as A
+    ctx = M.Context(cfg, 0)
+    ctx.synth_weights(WEIGHT_SEED, 0.02)
+    n = wl["prompt"]
+    cache = M.BatchKVCache(ctx, 2, n + 64)
+    ext = torch.cuda.ExternalStream(ctx.stream(), device=torch.device("cuda", 0))
+    times = []
+    for i in range(args.warmup + args.kernel_reps):
+        req = make_request(M, cfg, wl, 0, i)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        cache.insert_row(i % 2, req.tokens, 8, req.sampling)
+        e1.record(ext)
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            times.append(e0.elapsed_time(e1))
+        cache.remove_row(i % 2)
+    ms = statistics.median(times)
+    weights = ctx.weights_bytes() / 0.5625
+    head = cfg.vocab * cfg.hidden
+    lin_flops = 2.0 * (weights - head) * n + 2.0 * head
+    att_flops = 4.0 * cfg.n_layers * cfg.n_heads * cfg.head_dim * n * (n + 1) / 2
+    print(json.dumps({"kernel_case": "prefill", "config": args.config, "prompt_tokens": n,
+                      "ms_per_admission": ms, "ms_all": times, "tokens_per_s": n / (ms / 1e3),
+                      "linear_tflop": lin_flops / 1e12, "attention_tflop": att_flops / 1e12,
+                      "tflops": (lin_flops + att_flops) / (ms / 1e3) / 1e12}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -734,7 +800,7 @@ def main():
     ap.add_argument("--config", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="mlxcat", choices=["mlxcat", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-case", choices=["q4_linear", "attention", "moe"])
+    ap.add_argument("--kernel-case", choices=["q4_linear", "attention", "moe", "gemm", "prefill"])
     ap.add_argument("--kernel-reps", type=int, default=50)
     args = ap.parse_args()
     if args.kernel_case:

@@ -59,7 +59,7 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
             const __half *__restrict__ vc, int max_len, const int32_t *__restrict__ trow,
             const int32_t *__restrict__ tpos, int M, int qg, int Hq, int Hkv, int key_chunk,
             int splits, float scale_log2, float *__restrict__ o_part, float *__restrict__ ml_part,
-            int early_kv) {
+            int early_kv, __half *__restrict__ direct_out) {
     constexpr int QROWS = QT * 16;
     constexpr int PITCH = D + 8;               // halves
     constexpr int NTHREADS = QT * 64;
@@ -77,7 +77,9 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
     // previous kernel (the QKV projection), which writes only the queries and the
     // new keys.  Otherwise everything waits for the previous kernel.
     if (!early_kv) griddep_wait();
-    const int grp = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+    // direct_out (one key split, prefill): the groups furthest into the prompt
+    // see the most keys, so they are scheduled first
+    const int grp = direct_out ? gridDim.x - 1 - blockIdx.x : blockIdx.x, h = blockIdx.y, s = blockIdx.z;
     const int G = Hq / Hkv;
     const int t0 = grp * qg;
     const int ntok = min(qg, M - t0);
@@ -285,7 +287,32 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
         }
     }
     __syncthreads();
-    if (kh == 0) {
+    if (kh == 0 && direct_out) {
+        // one split: this CTA holds every key of the group, so it writes the
+        // normalised output itself (natural layout [M][Hq*D]); no combine pass
+        const int rws[2] = {qrow0, qrow1};
+        const int KO = Hq * D;
+#pragma unroll
+        for (int rI = 0; rI < 2; ++rI) {
+            const int qi = rws[rI];
+            if (qi >= NQ) continue;
+            const float m1 = ml_s[qi * 2], l1 = ml_s[qi * 2 + 1];
+            const float mm = fmaxf(m_r[rI], m1);
+            const float a0 = m_r[rI] == -INFINITY ? 0.f : exp2f(m_r[rI] - mm);
+            const float a1 = m1 == -INFINITY ? 0.f : exp2f(m1 - mm);
+            const float den = a0 * l_r[rI] + a1 * l1;
+            const float inv = den > 0.f ? 1.0f / den : 0.f;
+            const int j = qi / G, gh = qi - j * G;
+            __half *dst = direct_out + (size_t)(t0 + j) * KO + (size_t)(h * G + gh) * D;
+#pragma unroll
+            for (int i = 0; i < D / 8; ++i) {
+                const int d = i * 8 + 2 * t;
+                const float2 x = *reinterpret_cast<const float2 *>(o_s + qi * D + d);
+                const float v0 = (a0 * o[i][2 * rI] + a1 * x.x) * inv, v1 = (a0 * o[i][2 * rI + 1] + a1 * x.y) * inv;
+                *reinterpret_cast<__half2 *>(dst + d) = __floats2half2_rn(v0, v1);
+            }
+        }
+    } else if (kh == 0) {
         float a0[2], a1[2];
         const int rws[2] = {qrow0, qrow1};
 #pragma unroll
@@ -390,9 +417,13 @@ cudaError_t launch_attn(const __half *qbuf, KVLayer kv, const int32_t *trow, con
     const int groups = (M + qg - 1) / qg;
     dim3 grid(groups, Hkv, splits);
     const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+    // one key split and a natural-layout output: the split pass normalises and
+    // writes the output itself
+    __half *direct = splits == 1 && !permuted ? out : nullptr;
     cudaError_t e = launch_pdl(attn_kernel<QT, D>, grid, dim3(QT * 64), smem, st, qbuf, kv.k, kv.v, kv.max_len,
-                               trow, tpos, M, qg, Hq, Hkv, key_chunk, splits, scale_log2, sc.o, sc.ml, early_kv ? 1 : 0);
-    if (e != cudaSuccess) return e;
+                               trow, tpos, M, qg, Hq, Hkv, key_chunk, splits, scale_log2, sc.o, sc.ml,
+                               early_kv ? 1 : 0, direct);
+    if (e != cudaSuccess || direct) return e;
     dim3 g2(groups, Hkv, QT * 16);
     return launch_pdl(attn_combine_kernel<QT>, g2, dim3(D), 0, st, (const float *)sc.o, (const float *)sc.ml, M, qg,
                       Hq, Hkv, D, splits, out, permuted ? 1 : 0, out_rows);

@@ -28,7 +28,7 @@ namespace {
 
 constexpr int PREFILL_CHUNK = 128;   // prompt tokens per prefill forward (q4 kernels)
 constexpr int PREFILL_QG = 8;        // prompt tokens per attention group
-constexpr int DENSE_CHUNK = 2048;    // prompt tokens per dense prefill forward (fp16 GEMMs)
+constexpr int DENSE_CHUNK = 4096;    // prompt tokens per dense prefill forward (fp16 GEMMs)
 constexpr int DENSE_MIN = 256;       // prompts at least this long take the dense prefill
 constexpr int KEY_CHUNK = 384;       // keys per attention split (3-deep ring, one wave at the verify shape)
 

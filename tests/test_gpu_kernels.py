@@ -118,12 +118,13 @@ def attention_ref(q, kc, vc, trow, tpos, Hq, Hkv, D):
 
 @pytest.mark.parametrize("Hq,Hkv,D", [(8, 2, 64), (32, 8, 128), (16, 2, 128)])
 @pytest.mark.parametrize("qg", [1, 5, 8])
-def test_attention_matches_reference(Hq, Hkv, D, qg):
+@pytest.mark.parametrize("max_len", [700, 340])   # several key splits + combine / one split, direct output
+def test_attention_matches_reference(Hq, Hkv, D, qg, max_len):
     rng = np.random.default_rng(Hq + qg)
-    rows, max_len = 3, 700
+    rows = 3
     if qg * Hq // Hkv > 64:
         pytest.skip("query tile limit")
-    lens = [37, 300, 650]
+    lens = [37, 300, 650] if max_len == 700 else [5, 170, 330]
     kc = rng.normal(size=(rows, Hkv, max_len, D)).astype(np.float16)
     vc = rng.normal(size=(rows, Hkv, max_len, D)).astype(np.float16)
     trow, tpos = [], []
@@ -144,6 +145,8 @@ def test_attention_matches_reference(Hq, Hkv, D, qg):
     torch.cuda.synchronize()
     got = out.cpu().numpy().view(np.float16).astype(np.float32)
     np.testing.assert_allclose(got, ref, rtol=RTOL, atol=ATOL)
+    # fp16 P and output rounding only: much tighter relative to the output scale
+    assert np.abs(got - ref).max() < 5e-3 * np.abs(ref).max()
 
 
 # --------------------------------------------------------------------------- #

@@ -9,7 +9,7 @@ more: Scheduler.completeAdmission, Scheduler.swift:599-668).
 * whole-prompt admissions against the CPU oracle: the KV of every prompt
   position within rtol/atol 2e-2, the first token equal except at top-2 gaps
   under 1e-2, and the next verify step's logits within 2e-2 -- at prompt
-  lengths that take one and several 2048-token chunks, with and without the
+  lengths that take one and two 4096-token chunks, with and without the
   Qwen3 q/k norm, and at the Llama-3-8B layer widths.
 """
 import numpy as np
@@ -102,7 +102,7 @@ def segment_prompt(vocab, n_seg, seg_len, length, seed):
     return pool[picks].reshape(-1)[:length].tolist()
 
 
-@pytest.mark.parametrize("cfg,lens", [(TINY2, [2300, 256]), (QWEN_SMALL, [700, 300]), (LLAMA8B_LAYER, [600])],
+@pytest.mark.parametrize("cfg,lens", [(TINY2, [4500, 256]), (QWEN_SMALL, [700, 300]), (LLAMA8B_LAYER, [600])],
                          ids=lambda v: getattr(v, "name", str(v)))
 def test_dense_prefill_matches_oracle(cfg, lens):
     seed, k = 19, 4
