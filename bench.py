@@ -103,7 +103,7 @@ def workload_config(name, wl, world):
          "acceptance": ("single-draft rejection sampling, per-request seeds" if wl["temperature"] > 0
                         else "greedy prefix match"),
          "parallelism": (f"tensor-parallel x{world} (NCCL allreduce per block)" if tp else
-                         f"expert-parallel x{world} (NCCL exchange per MoE layer)" if ep else
+                         f"expert-parallel x{world} (NVLink peer-memory exchange per MoE layer)" if ep else
                          f"request-parallel x{world} (replicas, no collective)"),
          "l2": wl.get("l2", "inputs larger than L2 (q4 weights + KV read every step)")}
     if wl.get("arrivals"):
@@ -201,6 +201,16 @@ def share_tp_id(uid, rank, device):
         t.copy_(torch.frombuffer(bytearray(uid), dtype=torch.uint8))
     torch.distributed.broadcast(t, 0)
     return bytes(t.cpu().numpy().tobytes())
+
+
+def gather_handles(handle, world, device):
+    """Every rank's 128-byte expert-parallel cache handle, in rank order (one
+    all-gather over the job's process group)."""
+    import torch
+    t = torch.frombuffer(bytearray(handle), dtype=torch.uint8).to(device)
+    out = [torch.empty_like(t) for _ in range(world)]
+    torch.distributed.all_gather(out, t)
+    return [bytes(o.cpu().numpy().tobytes()) for o in out]
 
 
 def job_tokens(tokens, rank, tp):
@@ -422,7 +432,7 @@ def run_ours(args, wl, rank, world, local_rank):
     if ep:   # every rank runs its share of the rows with 1/world of the experts
         cfg = dataclasses.replace(cfg, ep_size=world, ep_rank=rank)
     ctx = M.Context(cfg, local_rank)
-    if tp or ep:
+    if tp:
         ctx.tp_connect(share_tp_id(M.Context.tp_unique_id() if rank == 0 else None, rank, "cuda"))
     ctx.synth_weights(WEIGHT_SEED, 0.02)
     if wl.get("arrivals"):
@@ -432,6 +442,8 @@ def run_ours(args, wl, rank, world, local_rank):
     rows, k1 = (wl["rows"] // world if ep else wl["rows"]), wl["k"] + 1
     max_len = wl["prompt"] + wl["max_new"] + 16
     cache = M.BatchKVCache(ctx, rows, max_len)
+    if ep:   # map every rank's exchange region (NVLink peer memory)
+        cache.ep_connect(gather_handles(cache.ep_handle(), world, "cuda"))
     spec = M.SpeculativeDecodingConfiguration(True, wl["k"], wl["n"], MIN_CONTEXT, A.ACCEPT_PREFIX)
     t0 = time.perf_counter()
     for r in range(rows):

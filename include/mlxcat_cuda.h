@@ -69,11 +69,14 @@ typedef struct {
     int32_t tp_size, tp_rank;
     /* Expert parallelism for MoE models over ep_size GPUs (0 or 1: off): rank
      * ep_rank holds experts [ep_rank*E/ep_size, (ep_rank+1)*E/ep_size) and runs
-     * its own rows; every MoE layer exchanges the routed operand rows with the
-     * experts' owners and the results back (two NCCL all-to-alls of fixed-size
-     * per-peer blocks).  The other weights are replicated.  All ranks must
-     * call the forward entry points with the same shapes in the same order.
-     * Connect with mlxcat_ctx_tp_connect.  Not combinable with tp_size > 1. */
+     * its own rows; every MoE layer stores each routed operand row straight
+     * into its expert owner's memory and the owner stores the result back
+     * (NVLink peer memory, see mlxcat_cache_ep_connect).  The other weights
+     * are replicated.  Every rank must run the same NUMBER of forwards in the
+     * same order (each inserted prompt chunk and each verify is one); their
+     * token counts may differ.  A rank that stops participating makes the
+     * others' next forward fail with MLXCAT_E_CUDA ("exchange timed out")
+     * after about 10 s.  Not combinable with tp_size > 1. */
     int32_t ep_size, ep_rank;
 } mlxcat_model_config;
 
@@ -110,11 +113,12 @@ typedef struct mlxcat_cache mlxcat_cache;
 MLXCAT_API int mlxcat_ctx_create(const mlxcat_model_config *cfg, int32_t device, mlxcat_ctx **out);
 /* also destroys every cache still open on the context (their handles become invalid) */
 MLXCAT_API int mlxcat_ctx_destroy(mlxcat_ctx *ctx);
-/* Tensor or expert parallelism: one rank creates an id (ncclGetUniqueId), the
- * host hands the 128 bytes to every rank, each rank connects its context
+/* Tensor parallelism: one rank creates an id (ncclGetUniqueId), the host
+ * hands the 128 bytes to every rank, each rank connects its context
  * (ncclCommInitRank; collective: all ranks call it).  NCCL is loaded at run
  * time (libnccl.so.2); without it these return MLXCAT_E_STATE.  Must precede
- * the first forward on a context with tp_size > 1 or ep_size > 1. */
+ * the first forward on a context with tp_size > 1.  (Expert-parallel
+ * contexts use no NCCL: their caches connect, mlxcat_cache_ep_connect.) */
 MLXCAT_API int mlxcat_tp_unique_id(uint8_t id[128]);
 MLXCAT_API int mlxcat_ctx_tp_connect(mlxcat_ctx *ctx, const uint8_t id[128]);
 MLXCAT_API const char *mlxcat_last_error(const mlxcat_ctx *ctx);
@@ -152,6 +156,16 @@ MLXCAT_API int64_t mlxcat_weights_bytes(const mlxcat_ctx *ctx);
  * with one length per row. */
 MLXCAT_API int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxcat_cache **out);
 MLXCAT_API int mlxcat_cache_destroy(mlxcat_cache *cache);
+/* Expert parallelism (ep_size > 1): each rank's cache owns one device region
+ * (receive slabs, return rows, flags) that every other rank maps.  Each rank
+ * writes its cache's handle (a CUDA IPC handle plus the region's shape), the
+ * host gathers the ep_size handles in rank order and hands all of them to
+ * every rank's mlxcat_cache_ep_connect.  Caches of different shape (max_rows)
+ * are rejected with MLXCAT_E_INVALID.  Connect before the first insert_row.
+ * No counterpart in the reference (the MLX path runs on one device). */
+#define MLXCAT_EP_HANDLE_BYTES 128
+MLXCAT_API int mlxcat_cache_ep_handle(mlxcat_cache *cache, uint8_t handle[MLXCAT_EP_HANDLE_BYTES]);
+MLXCAT_API int mlxcat_cache_ep_connect(mlxcat_cache *cache, const uint8_t *handles /* [ep_size][128] */);
 /* admission: prefill prompt into `row`, sample the first token (generation
  * index 0).  Scheduler.completeAdmission + generator.insert
  * (Scheduler.swift:599-668, BatchGenerator.swift:380-460).  Requires
@@ -222,6 +236,21 @@ MLXCAT_API int mlxcat_draft(mlxcat_cache *cache, const mlxcat_spec_config *spec,
 MLXCAT_API int mlxcat_verify_forward(mlxcat_cache *cache, const mlxcat_spec_config *spec, float *logits);
 MLXCAT_API int mlxcat_accept(mlxcat_cache *cache, const mlxcat_spec_config *spec, int32_t *out_tokens,
                   int32_t *out_counts, int32_t *out_finished, mlxcat_stats *stats);
+/* Grammar-constrained speculation (the device side of the allow masks of
+ * Sampling.swift:557-590, which today keep a grammar row out of speculation,
+ * BatchGenerator.swift:957-975).  A grammar's allowed set at verify position p
+ * depends on drafts 0..p-1, so the host runs mlxcat_draft, advances its matcher
+ * along each row's drafts, and sets one allowed-token bitset per row and
+ * position: bits [max_rows][k+1][ceil(vocab/32)] (bit v of word v/32 = token v
+ * allowed), enabled [max_rows][k+1] (0 = that position is unconstrained).  The
+ * next mlxcat_accept sets every disallowed logit to -inf before it samples or
+ * takes the argmax; a position whose set holds no valid token id is left
+ * unchanged (as applyAllowedTokenMask does).  The masks are consumed by that
+ * acceptance; enabled == NULL clears pending masks.  While masks are pending,
+ * mlxcat_spec_step returns MLXCAT_E_STATE (its drafts are not known on the
+ * host before it runs). */
+MLXCAT_API int mlxcat_cache_set_token_masks(mlxcat_cache *cache, int32_t k, const uint32_t *bits,
+                                            const uint8_t *enabled);
 MLXCAT_API int mlxcat_spec_step(mlxcat_cache *cache, const mlxcat_spec_config *spec, int32_t *out_tokens,
                      int32_t *out_counts, int32_t *out_finished, mlxcat_stats *stats);
 /* device time (ms) of the verify forward inside the last mlxcat_spec_step */

@@ -361,6 +361,31 @@ sample_first_kernel(RowState rs, int r, const float *logits, int V, const int32_
 
 }  // namespace
 
+// Allowed-token masks of grammar-constrained rows (the device side of
+// applyAllowedTokenMask, Sampling.swift:557-569): per verify token i with
+// on[i] set, logits outside the allowed set become -inf; ids >= V are not
+// tokens, and a set with no valid id leaves the row unchanged.
+__global__ void token_mask_kernel(float *__restrict__ logits, int V, int W, const uint32_t *__restrict__ bits,
+                                  const uint8_t *__restrict__ on) {
+    const int i = blockIdx.x;
+    if (!on[i]) return;
+    const uint32_t *b = bits + (size_t)i * W;
+    const uint32_t tail = (V & 31) ? (1u << (V & 31)) - 1u : 0xffffffffu;
+    int any = 0;
+    for (int w = threadIdx.x; w < W; w += blockDim.x) any |= (b[w] & (w == W - 1 ? tail : 0xffffffffu)) != 0u;
+    if (!__syncthreads_or(any)) return;
+    float *l = logits + (size_t)i * V;
+    for (int v = threadIdx.x; v < V; v += blockDim.x)
+        if (!((b[v >> 5] >> (v & 31)) & 1u)) l[v] = -INFINITY;
+}
+
+cudaError_t apply_token_masks(float *logits, int M, int V, const uint32_t *bits, const uint8_t *on,
+                              cudaStream_t st) {
+    if (M <= 0 || V <= 0 || !bits || !on) return cudaErrorInvalidValue;
+    token_mask_kernel<<<M, 256, 0, st>>>(logits, V, (V + 31) / 32, bits, on);
+    return cudaGetLastError();
+}
+
 cudaError_t accept_greedy(const RowState &rs, const SpecParams &sp, const int32_t *vtok,
                           const int32_t *count, const int32_t *amax, StepOut out,
                           cudaStream_t st) {

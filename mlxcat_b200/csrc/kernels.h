@@ -223,34 +223,45 @@ const char *tp_unique_id(uint8_t *out128);
 const char *tp_connect(void **comm, const uint8_t *id128, int nranks, int rank);
 const char *tp_allreduce_sum(void *comm, float *buf, size_t n, cudaStream_t st);
 void tp_destroy(void *comm);
-// expert parallel: all-to-all of fixed-size per-peer blocks (one NCCL group)
-struct TpBlock {
-    const void *send;
-    void *recv;
-    size_t bytes;    // per peer
-    size_t stride;   // bytes between consecutive peers' blocks
-};
-const char *ep_exchange(void *comm, int nranks, const TpBlock *blocks, int nblocks, cudaStream_t st);
 
-// ---- expert parallel MoE (moe.cu) -------------------------------------------
-// Per-peer slabs of cap rows: the source packs each assignment's operand row
-// (natural order, fp16, unscaled) and meta {local expert, scale, routing
-// weight} into the slab of the rank owning its expert; back[a] = dest*cap + slot.
+// ---- expert parallel MoE over NVLink peer memory (ep.cu) ---------------------
+// Per-assignment metadata stored into the owner's receive slab.
 struct EpMeta {
     int expert;      // the owner's local expert index
     float scale;     // folded-norm scale of the token
     float weight;    // routing weight
-    int pad;
+    int pad;         // the source's assignment index (where the result goes back)
 };
-cudaError_t ep_pack(const int32_t *topk_id, const float *topk_w, const float *tok_scale, const __half *x_blk,
-                    int ldx_rows, int M, int TK, int H, int experts_per_rank, int cap, __half *send_x,
-                    EpMeta *send_meta, int *send_count, int32_t *back, cudaStream_t st);
-// owner side: per-local-expert lists over the received rows (row = src*cap + slot),
-// each row's scale and routing weight
-cudaError_t ep_lists(const int *recv_count, const EpMeta *recv_meta, int nranks, int cap, int *exp_count,
-                     int32_t *exp_list, float *row_scale, float *row_weight, cudaStream_t st);
-// source side: y[a] = yr[back[a]] for the M*TK assignments (fp32 rows of H)
-cudaError_t ep_gather(const float *yr, const int32_t *back, int n, int H, float *y, cudaStream_t st);
+// Byte offsets inside each rank's exported region (two buffer sets, by layer parity):
+// recv_x [2][H/64][N*cap][64] fp16, recv_meta [2][N][cap], recv_count [2][N],
+// recv_flag [2][N], ret_y [2][cap][H] fp32, ret_flag [2][N].
+struct EpLayout {
+    size_t recv_x = 0, recv_meta = 0, recv_count = 0, recv_flag = 0, ret_y = 0, ret_flag = 0, total = 0;
+};
+EpLayout ep_layout(int N, int cap, int H);
+struct EpArgs {
+    char *const *peers = nullptr;   // device array [N]: every rank's mapped region (own included)
+    EpLayout layout;
+    int N = 0, me = 0, cap = 0, H = 0, TK = 0, epr = 0, set = 0, layer = 0;
+    const unsigned *epoch = nullptr;  // forwards run so far (device)
+    int *lcount = nullptr;            // [N] rows dispatched per owner (zero between layers)
+    unsigned *done = nullptr;         // CTA arrival counter (zero between kernels)
+    int *err = nullptr;               // device error flag (wait timeouts)
+};
+cudaError_t ep_begin(unsigned *epoch, cudaStream_t st);
+cudaError_t ep_dispatch(const EpArgs &a, const int32_t *topk_id, const float *topk_w, const float *tok_scale,
+                        const __half *x_blk, int ldx_rows, int n, cudaStream_t st);
+cudaError_t ep_wait_dispatch(const EpArgs &a, cudaStream_t st);
+// owner side: per-local-expert lists over the received rows (row = src*cap + slot)
+cudaError_t ep_lists(const EpArgs &a, int *exp_count, int32_t *exp_list, float *row_scale, float *row_weight,
+                     cudaStream_t st);
+cudaError_t ep_return(const EpArgs &a, const float *ys, cudaStream_t st);
+// source side: wait for every owner's returned rows
+cudaError_t ep_wait_return(const EpArgs &a, cudaStream_t st);
+// this layer's buffer set inside this rank's own region: the returned rows
+// [cap][H] fp32 in assignment order, the received operand rows [H/64][N*cap][64]
+const float *ep_returned(const EpArgs &a, const char *own_region);
+const __half *ep_received(const EpArgs &a, const char *own_region);
 
 // ---- decode attention (split-K over keys, GQA) -----------------------------
 // Tokens come in groups of `qg` consecutive positions of one row (the verify
@@ -324,6 +335,10 @@ struct SampleScratch {
     unsigned long long *S;    // [rows*(k+1)]
     unsigned long long *Pd;   // [rows*(k+1)]
 };
+// grammar masks: logits of token i outside its allowed set (bits [M][ceil(V/32)])
+// become -inf where on[i]; an empty set leaves the row unchanged
+cudaError_t apply_token_masks(float *logits, int M, int V, const uint32_t *bits, const uint8_t *on,
+                              cudaStream_t st);
 cudaError_t accept_sampled(const RowState &rs, const SpecParams &sp, const int32_t *vtok,
                            const int32_t *count, const float *logits, int V, SampleScratch sc,
                            StepOut out, cudaStream_t st);

@@ -447,63 +447,6 @@ moe_combine_kernel(MoECombineArgs a) {
     }
 }
 
-// ---------------------------------------------------------------------------
-// expert parallel: pack / per-expert lists / gather
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
-ep_pack_kernel(const int32_t *__restrict__ topk_id, const float *__restrict__ topk_w,
-               const float *__restrict__ tok_scale, const __half *__restrict__ x, int ldx_rows, int n, int TK,
-               int H, int epr, int cap, __half *__restrict__ send_x, EpMeta *__restrict__ meta,
-               int *__restrict__ send_count, int32_t *__restrict__ back) {
-    const int a = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (a >= n) return;
-    const int m = a / TK, e = topk_id[a], d = e / epr;
-    int slot = 0;
-    if (lane == 0) slot = atomicAdd(send_count + d, 1);
-    slot = __shfl_sync(0xffffffffu, slot, 0);
-    const size_t row = (size_t)d * cap + slot;
-    if (lane == 0) {
-        EpMeta mt;
-        mt.expert = e - d * epr;
-        mt.scale = tok_scale[m];
-        mt.weight = topk_w[a];
-        mt.pad = 0;
-        meta[row] = mt;
-        back[a] = (int32_t)row;
-    }
-    // the token's operand row, blocked perm8 order -> natural order
-    for (int b = lane; b < H / 8; b += 32) {
-        const uint4 u = *reinterpret_cast<const uint4 *>(x + ((size_t)(b >> 3) * ldx_rows + m) * 64 + (b & 7) * 8);
-        const __half *in = reinterpret_cast<const __half *>(&u);
-        __align__(16) __half o[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = in[perm8(i)];
-        *reinterpret_cast<uint4 *>(send_x + row * H + 8 * b) = *reinterpret_cast<const uint4 *>(o);
-    }
-}
-
-__global__ void ep_lists_kernel(const int *__restrict__ recv_count, const EpMeta *__restrict__ meta, int nranks,
-                                int cap, int *__restrict__ exp_count, int32_t *__restrict__ exp_list,
-                                float *__restrict__ row_scale, float *__restrict__ row_weight) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= nranks * cap) return;
-    const int src = i / cap, slot = i - src * cap;
-    if (slot >= recv_count[src]) return;
-    const EpMeta mt = meta[i];
-    const int s = atomicAdd(exp_count + mt.expert, 1);
-    exp_list[(size_t)mt.expert * nranks * cap + s] = i;
-    row_scale[i] = mt.scale;
-    row_weight[i] = mt.weight;
-}
-
-__global__ void ep_gather_kernel(const float *__restrict__ yr, const int32_t *__restrict__ back, int H,
-                                 float *__restrict__ y) {
-    const int a = blockIdx.x;
-    const float4 *src = reinterpret_cast<const float4 *>(yr + (size_t)back[a] * H);
-    float4 *dst = reinterpret_cast<float4 *>(y + (size_t)a * H);
-    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) dst[i] = src[i];
-}
-
 __global__ void router_synth_kernel(uint64_t seed, uint32_t tensor_id, float stddev, int E, int H,
                                     __nv_bfloat16 *w) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -534,31 +477,6 @@ cudaError_t moe_expert(const MoEExpertArgs &a, int epi, cudaStream_t st) {
 cudaError_t moe_combine(const MoECombineArgs &a, cudaStream_t st) {
     if (a.H % 128 || a.M <= 0 || a.TK < 1 || a.TK > 8) return cudaErrorInvalidValue;
     moe_combine_kernel<<<a.M, COMBINE_THREADS, 0, st>>>(a);
-    return cudaGetLastError();
-}
-
-cudaError_t ep_pack(const int32_t *topk_id, const float *topk_w, const float *tok_scale, const __half *x_blk,
-                    int ldx_rows, int M, int TK, int H, int experts_per_rank, int cap, __half *send_x,
-                    EpMeta *send_meta, int *send_count, int32_t *back, cudaStream_t st) {
-    const int n = M * TK;
-    if (n <= 0 || H % 64 || experts_per_rank <= 0 || cap < n) return cudaErrorInvalidValue;
-    ep_pack_kernel<<<(n + 7) / 8, 256, 0, st>>>(topk_id, topk_w, tok_scale, x_blk, ldx_rows, n, TK, H,
-                                                 experts_per_rank, cap, send_x, send_meta, send_count, back);
-    return cudaGetLastError();
-}
-
-cudaError_t ep_lists(const int *recv_count, const EpMeta *recv_meta, int nranks, int cap, int *exp_count,
-                     int32_t *exp_list, float *row_scale, float *row_weight, cudaStream_t st) {
-    const int n = nranks * cap;
-    if (n <= 0) return cudaErrorInvalidValue;
-    ep_lists_kernel<<<(n + 255) / 256, 256, 0, st>>>(recv_count, recv_meta, nranks, cap, exp_count, exp_list,
-                                                      row_scale, row_weight);
-    return cudaGetLastError();
-}
-
-cudaError_t ep_gather(const float *yr, const int32_t *back, int n, int H, float *y, cudaStream_t st) {
-    if (n <= 0 || H % 4) return cudaErrorInvalidValue;
-    ep_gather_kernel<<<n, 256, 0, st>>>(yr, back, H, y);
     return cudaGetLastError();
 }
 

@@ -133,14 +133,22 @@ struct mlxcat_cache {
     // the attention-norm and MLP-norm inputs of each token row (pre-scales)
     float *norm_part = nullptr, *r_attn = nullptr, *r_mlp = nullptr;
     float *tp_part = nullptr;          // tensor parallel: this rank's O / down partial sums [rows][H]
-    // expert parallel: per-peer slabs of routed operand rows and metadata, the
-    // received rows in the expert kernels' layout, results and their return
-    __half *ep_send_x = nullptr, *ep_recv_x = nullptr, *ep_xe = nullptr, *ep_act = nullptr;
-    EpMeta *ep_send_meta = nullptr, *ep_recv_meta = nullptr;
-    int *ep_counts = nullptr;          // [layer][send N | recv N]
+    // expert parallel over peer memory (ep.cu): this cache's exported region
+    // (receive slabs, return rows, flags), every rank's mapping of its peers'
+    // regions, and the owner side's per-expert lists, SwiGLU activations and
+    // scaled outputs over the N * cap received rows
+    char *ep_region = nullptr;
+    EpLayout ep_lay;
+    int ep_cap = 0;                    // rows per (source, owner) and buffer set
+    bool ep_connected = false;
+    std::vector<char *> ep_opened;     // IPC mappings of the peers' regions
+    char **ep_peers = nullptr;         // device [N]
+    unsigned *ep_epoch = nullptr, *ep_done = nullptr;
+    int *ep_lcount = nullptr;          // [N]
+    __half *ep_act = nullptr;
     int *ep_exp_count = nullptr;       // [layer][local experts]
-    int32_t *ep_exp_list = nullptr, *ep_back = nullptr;
-    float *ep_scale = nullptr, *ep_w = nullptr, *ep_ys = nullptr, *ep_yr = nullptr;
+    int32_t *ep_exp_list = nullptr;
+    float *ep_scale = nullptr, *ep_w = nullptr, *ep_ys = nullptr;
     // sparse MoE: routing, per-expert assignment lists (counts per layer, zeroed
     // once per forward), SwiGLU activations per assignment, scaled expert outputs
     int32_t *moe_id = nullptr, *moe_list = nullptr;
@@ -166,6 +174,12 @@ struct mlxcat_cache {
         int32_t *tok = nullptr, *trow = nullptr, *tpos = nullptr;
         AttnScratch attn;
     } pf;
+    // grammar masks for the next acceptance: allowed-token bitsets per verify
+    // token [rows*(k+1)][ceil(vocab/32)] and their enable flags (allocated on
+    // first use); mask_k = the k they were set for, -1 = none pending
+    uint32_t *mask_bits = nullptr;
+    uint8_t *mask_on = nullptr;
+    int mask_k = -1;
     // pinned host mirrors
     int32_t *h_tok = nullptr, *h_n = nullptr, *h_fin = nullptr;
     unsigned long long *h_stats = nullptr;
@@ -316,32 +330,30 @@ struct ProfScope {
 };
 
 // Expert-parallel MoE MLP of layer l (after the route): every assignment's
-// operand row goes to the rank owning its expert (fixed-size per-peer blocks
-// of M * top_k rows, one NCCL group with the counts and metadata), the owner
-// runs the grouped expert kernels over all received rows, the scaled outputs
-// go back the same way, and the source gathers them into the combine's order.
+// operand row is stored into the owning rank's receive slab over NVLink, the
+// owner runs the grouped expert kernels over all rows it received, stores the
+// scaled fp32 outputs back into each source's return buffer, and the source's
+// combine reads them in assignment order (ep.cu).
 int ep_moe(mlxcat_cache *c, int l, int M) {
     mlxcat_ctx *ctx = c->ctx;
     const mlxcat_model_config &cf = ctx->cfg;
     const int H = cf.hidden, I = cf.intermediate, TK = cf.top_k, N = ctx->ep, epr = ctx->epr, R = c->m_cap;
-    const int cap = M * TK, rows = N * cap;
+    const int rows = N * c->ep_cap;
     cudaStream_t st = ctx->stream;
-    int *scnt = c->ep_counts + (size_t)l * 2 * N, *rcnt = scnt + N;
+    EpArgs a;
+    a.peers = c->ep_peers; a.layout = c->ep_lay; a.N = N; a.me = ctx->ep_rank; a.cap = c->ep_cap; a.H = H;
+    a.TK = TK; a.epr = epr; a.set = l & 1; a.layer = l;
+    a.epoch = c->ep_epoch; a.lcount = c->ep_lcount; a.done = c->ep_done; a.err = c->err;
     const size_t asg = (size_t)c->m_cap * TK;
-    LK(ctx, ep_pack(c->moe_id + l * asg, c->moe_w + l * asg, c->moe_scale, c->xg, R, M, TK, H, epr, cap, c->ep_send_x,
-                    c->ep_send_meta, scnt, c->ep_back, st));
-    const TpBlock out[3] = {{scnt, rcnt, sizeof(int), sizeof(int)},
-                            {c->ep_send_meta, c->ep_recv_meta, (size_t)cap * sizeof(EpMeta), (size_t)cap * sizeof(EpMeta)},
-                            {c->ep_send_x, c->ep_recv_x, (size_t)cap * H * 2, (size_t)cap * H * 2}};
-    if (const char *er = ep_exchange(ctx->nccl, N, out, 3, st)) return set_err(ctx, MLXCAT_E_CUDA, "dispatch: %s", er);
+    LK(ctx, ep_dispatch(a, c->moe_id + l * asg, c->moe_w + l * asg, c->moe_scale, c->xg, R, M * TK, st));
+    LK(ctx, ep_wait_dispatch(a, st));
     int *ecnt = c->ep_exp_count + (size_t)l * epr;
-    LK(ctx, ep_lists(rcnt, c->ep_recv_meta, N, cap, ecnt, c->ep_exp_list, c->ep_scale, c->ep_w, st));
-    LK(ctx, permute_activations(c->ep_recv_x, c->ep_xe, rows, H, st));
+    LK(ctx, ep_lists(a, ecnt, c->ep_exp_list, c->ep_scale, c->ep_w, st));
     const auto &mb = ctx->moe[l];
     MoEExpertArgs xa;
     xa.wq = mb.wq[0]; xa.scales = mb.s[0]; xa.biases = mb.b[0];
     xa.wq2 = mb.wq[1]; xa.scales2 = mb.s[1]; xa.biases2 = mb.b[1];
-    xa.N = I; xa.K = H; xa.E = epr; xa.x = c->ep_xe; xa.ldx_rows = rows; xa.x_div = 1;
+    xa.N = I; xa.K = H; xa.E = epr; xa.x = ep_received(a, c->ep_region); xa.ldx_rows = rows; xa.x_div = 1;
     xa.exp_count = ecnt; xa.exp_list = c->ep_exp_list; xa.list_cap = rows;
     xa.tok_scale = c->ep_scale; xa.act = c->ep_act; xa.act_rows = rows;
     { ProfScope ps(c, 0); LK(ctx, moe_expert(xa, 0, st)); }
@@ -351,11 +363,10 @@ int ep_moe(mlxcat_cache *c, int l, int M) {
     da.exp_count = ecnt; da.exp_list = c->ep_exp_list; da.list_cap = rows;
     da.topk_w = c->ep_w; da.y = c->ep_ys;
     { ProfScope ps(c, 0); LK(ctx, moe_expert(da, 1, st)); }
-    const TpBlock back = {c->ep_ys, c->ep_yr, (size_t)cap * H * 4, (size_t)cap * H * 4};
-    if (const char *er = ep_exchange(ctx->nccl, N, &back, 1, st)) return set_err(ctx, MLXCAT_E_CUDA, "combine: %s", er);
-    LK(ctx, ep_gather(c->ep_yr, c->ep_back, cap, H, c->moe_y, st));
+    LK(ctx, ep_return(a, c->ep_ys, st));
+    LK(ctx, ep_wait_return(a, st));
     MoECombineArgs ca;
-    ca.h = c->h; ca.y = c->moe_y; ca.M = M; ca.H = H; ca.TK = TK;
+    ca.h = c->h; ca.y = ep_returned(a, c->ep_region); ca.M = M; ca.H = H; ca.TK = TK;
     ca.norm_w = l + 1 < cf.n_layers ? ctx->attn_norm(l + 1) : ctx->final_norm(); ca.norm_scale = c->r_mlp;
     ca.xout = c->xn; ca.ldx_rows = R; ca.norm_part = c->norm_part; ca.norm_rows = R;
     LK(ctx, moe_combine(ca, st));
@@ -410,8 +421,11 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
     LK(ctx, embed_norm(ctx->embed.view(), tok, M, ctx->attn_norm(0), eps, c->h, c->xn, R, st, c->r_attn));
     if (cf.n_experts) CK(ctx, cudaMemsetAsync(c->moe_count, 0, sizeof(int) * (size_t)L * cf.n_experts, st));
     if (cf.n_experts && ctx->ep > 1) {
-        CK(ctx, cudaMemsetAsync(c->ep_counts, 0, sizeof(int) * (size_t)L * 2 * ctx->ep, st));
+        if (!c->ep_connected)
+            return set_err(ctx, MLXCAT_E_STATE, "expert-parallel cache not connected (mlxcat_cache_ep_connect)");
         CK(ctx, cudaMemsetAsync(c->ep_exp_count, 0, sizeof(int) * (size_t)L * ctx->epr, st));
+        ctx->launches++;
+        LK(ctx, ep_begin(c->ep_epoch, st));   // the forward's epoch, part of every exchange flag
     }
     Q4Epilogue ep;
     ep.part = c->part;
@@ -525,10 +539,12 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
     return MLXCAT_OK;
 }
 
-int check_weights(mlxcat_ctx *ctx) {
+int check_weights(mlxcat_cache *c) {
+    mlxcat_ctx *ctx = c->ctx;
     if (!ctx->have_weights) return set_err(ctx, MLXCAT_E_STATE, "weights not loaded");
-    if ((ctx->tp > 1 || ctx->ep > 1) && !ctx->nccl)
-        return set_err(ctx, MLXCAT_E_STATE, "tensor- or expert-parallel context not connected");
+    if (ctx->tp > 1 && !ctx->nccl) return set_err(ctx, MLXCAT_E_STATE, "tensor-parallel context not connected");
+    if (ctx->ep > 1 && ctx->cfg.n_experts && !c->ep_connected)
+        return set_err(ctx, MLXCAT_E_STATE, "expert-parallel cache not connected (mlxcat_cache_ep_connect)");
     return MLXCAT_OK;
 }
 
@@ -736,7 +752,7 @@ int admit_row(mlxcat_cache *c, int32_t row, const int32_t *prompt, int32_t len, 
     if (sp->temperature < 0.0f) return set_err(ctx, MLXCAT_E_INVALID, "negative temperature");
     for (int i = 0; i < len; ++i)
         if (prompt[i] < 0 || prompt[i] >= ctx->cfg.vocab) return set_err(ctx, MLXCAT_E_INVALID, "prompt token out of range");
-    int rc = check_weights(ctx);
+    int rc = check_weights(c);
     if (rc) return rc;
     CK(ctx, cudaSetDevice(ctx->device));
     cudaStream_t st = ctx->stream;
@@ -915,12 +931,12 @@ int mlxcat_tp_unique_id(uint8_t id[128]) {
 
 int mlxcat_ctx_tp_connect(mlxcat_ctx *ctx, const uint8_t id[128]) {
     if (!ctx || !id) return MLXCAT_E_INVALID;
-    if (ctx->tp <= 1 && ctx->ep <= 1)
-        return set_err(ctx, MLXCAT_E_STATE, "context is neither tensor- nor expert-parallel");
+    if (ctx->ep > 1)
+        return set_err(ctx, MLXCAT_E_STATE, "expert-parallel contexts connect their caches (mlxcat_cache_ep_connect)");
+    if (ctx->tp <= 1) return set_err(ctx, MLXCAT_E_STATE, "context is not tensor-parallel");
     if (ctx->nccl) return set_err(ctx, MLXCAT_E_STATE, "context already connected");
     CK(ctx, cudaSetDevice(ctx->device));
-    const int group = ctx->tp > 1 ? ctx->tp : ctx->ep, grank = ctx->tp > 1 ? ctx->tp_rank : ctx->ep_rank;
-    if (const char *e = tp_connect(&ctx->nccl, id, group, grank))
+    if (const char *e = tp_connect(&ctx->nccl, id, ctx->tp, ctx->tp_rank))
         return set_err(ctx, MLXCAT_E_STATE, "tensor parallel connect: %s", e);
     return MLXCAT_OK;
 }
@@ -1239,21 +1255,26 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
             chk(dalloc(A, &c->moe_y, asg * H));
             chk(dalloc(A, &c->moe_logits, (size_t)Mc * cf.n_experts));
             if (ctx->ep > 1) {
-                const size_t N = (size_t)ctx->ep, rows = N * asg;   // per-peer capacity: all of a rank's assignments
-                chk(dalloc(A, &c->ep_send_x, rows * H));
-                chk(dalloc(A, &c->ep_recv_x, rows * H));
-                chk(dalloc(A, &c->ep_xe, rows * H));
+                // per (source, owner) capacity: all of a rank's assignments of one forward
+                const int N = ctx->ep;
+                c->ep_cap = (int)asg;
+                c->ep_lay = ep_layout(N, c->ep_cap, H);
+                const size_t rows = (size_t)N * c->ep_cap;
+                chk(dalloc(A, &c->ep_region, c->ep_lay.total));   // its own allocation: exported whole
+                if (rc == MLXCAT_OK) chk(cudaMemset(c->ep_region, 0, c->ep_lay.total));
+                chk(dalloc(A, &c->ep_peers, (size_t)N));
+                chk(dalloc(A, &c->ep_epoch, 1));
+                chk(dalloc(A, &c->ep_done, 1));
+                chk(dalloc(A, &c->ep_lcount, (size_t)N));
+                if (rc == MLXCAT_OK) chk(cudaMemset(c->ep_epoch, 0, sizeof(unsigned)));
+                if (rc == MLXCAT_OK) chk(cudaMemset(c->ep_done, 0, sizeof(unsigned)));
+                if (rc == MLXCAT_OK) chk(cudaMemset(c->ep_lcount, 0, sizeof(int) * N));
                 chk(dalloc(A, &c->ep_act, rows * I));
-                chk(dalloc(A, &c->ep_send_meta, rows));
-                chk(dalloc(A, &c->ep_recv_meta, rows));
-                chk(dalloc(A, &c->ep_counts, (size_t)cf.n_layers * 2 * N));
                 chk(dalloc(A, &c->ep_exp_count, (size_t)cf.n_layers * ctx->epr));
                 chk(dalloc(A, &c->ep_exp_list, (size_t)ctx->epr * rows));
-                chk(dalloc(A, &c->ep_back, asg));
                 chk(dalloc(A, &c->ep_scale, rows));
                 chk(dalloc(A, &c->ep_w, rows));
                 chk(dalloc(A, &c->ep_ys, rows * H));
-                chk(dalloc(A, &c->ep_yr, rows * H));
             }
         }
         chk(dalloc(A, &c->rope, (size_t)max_len * (D / 2)));
@@ -1325,6 +1346,7 @@ int mlxcat_cache_destroy(mlxcat_cache *c) {
     cudaSetDevice(c->ctx->device);
     cudaStreamSynchronize(c->ctx->stream);
     drop_graph(c);
+    for (char *p : c->ep_opened) cudaIpcCloseMemHandle(p);
     for (void *p : c->allocs) cudaFree(p);
     if (c->h_tok) cudaFreeHost(c->h_tok);
     if (c->h_n) cudaFreeHost(c->h_n);
@@ -1337,6 +1359,102 @@ int mlxcat_cache_destroy(mlxcat_cache *c) {
     if (c->es1) cudaEventDestroy(c->es1);
     for (cudaEvent_t e : c->prof_ev) cudaEventDestroy(e);
     delete c;
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_set_token_masks(mlxcat_cache *c, int32_t k, const uint32_t *bits, const uint8_t *enabled) {
+    if (!c) return MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    if (!enabled) {   // clear
+        c->mask_k = -1;
+        return MLXCAT_OK;
+    }
+    if (k < 0 || k > MLXCAT_MAX_PROPOSAL) return set_err(ctx, MLXCAT_E_INVALID, "k must be in [0, %d]", MLXCAT_MAX_PROPOSAL);
+    if (!bits) return set_err(ctx, MLXCAT_E_INVALID, "null mask bits");
+    CK(ctx, cudaSetDevice(ctx->device));
+    const size_t W = ((size_t)ctx->cfg.vocab + 31) / 32, T = (size_t)c->rows * (MLXCAT_MAX_PROPOSAL + 1);
+    const size_t n = (size_t)c->rows * (k + 1);
+    if (!c->mask_bits) {
+        CK(ctx, dalloc(c->allocs, &c->mask_bits, T * W));
+        CK(ctx, dalloc(c->allocs, &c->mask_on, T));
+    }
+    CK(ctx, cudaMemcpyAsync(c->mask_bits, bits, n * W * sizeof(uint32_t), cudaMemcpyHostToDevice, ctx->stream));
+    CK(ctx, cudaMemcpyAsync(c->mask_on, enabled, n, cudaMemcpyHostToDevice, ctx->stream));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    c->mask_k = k;
+    return MLXCAT_OK;
+}
+
+namespace {
+// The bytes one rank hands to the others for expert parallelism.
+struct EpHandle {
+    char magic[4];              // "MXEP"
+    int32_t version;            // 1
+    int32_t rank, ranks, cap, hidden;
+    uint64_t bytes;             // size of the exported region
+    cudaIpcMemHandle_t ipc;     // the region (its own cudaMalloc allocation)
+};
+static_assert(sizeof(EpHandle) <= MLXCAT_EP_HANDLE_BYTES, "expert-parallel handle too large");
+}  // namespace
+
+int mlxcat_cache_ep_handle(mlxcat_cache *c, uint8_t out[MLXCAT_EP_HANDLE_BYTES]) {
+    if (!c || !out) return c ? set_err(c->ctx, MLXCAT_E_INVALID, "null handle buffer") : MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    if (ctx->ep <= 1 || !c->ep_region) return set_err(ctx, MLXCAT_E_STATE, "cache is not expert-parallel");
+    CK(ctx, cudaSetDevice(ctx->device));
+    EpHandle h;
+    std::memset(&h, 0, sizeof h);
+    std::memcpy(h.magic, "MXEP", 4);
+    h.version = 1;
+    h.rank = ctx->ep_rank; h.ranks = ctx->ep; h.cap = c->ep_cap; h.hidden = ctx->cfg.hidden;
+    h.bytes = c->ep_lay.total;
+    CK(ctx, cudaIpcGetMemHandle(&h.ipc, c->ep_region));
+    std::memset(out, 0, MLXCAT_EP_HANDLE_BYTES);
+    std::memcpy(out, &h, sizeof h);
+    return MLXCAT_OK;
+}
+
+int mlxcat_cache_ep_connect(mlxcat_cache *c, const uint8_t *handles) {
+    if (!c || !handles) return c ? set_err(c->ctx, MLXCAT_E_INVALID, "null handles") : MLXCAT_E_INVALID;
+    mlxcat_ctx *ctx = c->ctx;
+    if (ctx->ep <= 1 || !c->ep_region) return set_err(ctx, MLXCAT_E_STATE, "cache is not expert-parallel");
+    if (c->ep_connected) return set_err(ctx, MLXCAT_E_STATE, "cache already connected");
+    CK(ctx, cudaSetDevice(ctx->device));
+    const int N = ctx->ep;
+    std::vector<EpHandle> hs(N);
+    for (int p = 0; p < N; ++p) {
+        std::memcpy(&hs[p], handles + (size_t)p * MLXCAT_EP_HANDLE_BYTES, sizeof(EpHandle));
+        const EpHandle &h = hs[p];
+        if (std::memcmp(h.magic, "MXEP", 4) || h.version != 1)
+            return set_err(ctx, MLXCAT_E_INVALID, "handle %d is not an expert-parallel cache handle", p);
+        if (h.rank != p || h.ranks != N)
+            return set_err(ctx, MLXCAT_E_INVALID, "handle %d is rank %d of %d (want rank %d of %d, in rank order)", p,
+                           h.rank, h.ranks, p, N);
+        if (h.cap != c->ep_cap || h.hidden != ctx->cfg.hidden || h.bytes != c->ep_lay.total)
+            return set_err(ctx, MLXCAT_E_INVALID,
+                           "rank %d's cache has another shape (capacity %d rows, hidden %d; this rank: %d, %d): "
+                           "every rank's cache needs the same max_rows",
+                           p, h.cap, h.hidden, c->ep_cap, ctx->cfg.hidden);
+    }
+    std::vector<char *> peers(N, nullptr), opened;
+    for (int p = 0; p < N; ++p) {
+        if (p == ctx->ep_rank) { peers[p] = c->ep_region; continue; }
+        void *q = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&q, hs[p].ipc, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (char *o : opened) cudaIpcCloseMemHandle(o);
+            return set_err(ctx, MLXCAT_E_CUDA, "mapping rank %d's region: %s", p, cudaGetErrorString(e));
+        }
+        peers[p] = static_cast<char *>(q);
+        opened.push_back(peers[p]);
+    }
+    const cudaError_t e = cudaMemcpy(c->ep_peers, peers.data(), sizeof(char *) * N, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        for (char *o : opened) cudaIpcCloseMemHandle(o);
+        return set_err(ctx, MLXCAT_E_CUDA, "peer table upload: %s", cudaGetErrorString(e));
+    }
+    c->ep_opened = opened;
+    c->ep_connected = true;
     return MLXCAT_OK;
 }
 
@@ -1530,7 +1648,7 @@ int mlxcat_verify_forward(mlxcat_cache *c, const mlxcat_spec_config *spec, float
     mlxcat_ctx *ctx = c->ctx;
     int rc = validate_spec(ctx, spec);
     if (rc) return rc;
-    if ((rc = check_weights(ctx))) return rc;
+    if ((rc = check_weights(c))) return rc;
     const SpecParams sp = params_of(spec);
     if (c->last_k != sp.k) return set_err(ctx, MLXCAT_E_STATE, "mlxcat_draft with the same config must come first");
     CK(ctx, cudaSetDevice(ctx->device));
@@ -1556,6 +1674,13 @@ int mlxcat_accept(mlxcat_cache *c, const mlxcat_spec_config *spec, int32_t *out_
     CK(ctx, cudaSetDevice(ctx->device));
     cudaStream_t st = ctx->stream;
     const int K1 = sp.k + 1, M = c->rows * K1;
+    if (c->mask_k >= 0) {
+        if (c->mask_k != sp.k)
+            return set_err(ctx, MLXCAT_E_STATE, "token masks were set for k = %d, this step has k = %d", c->mask_k, sp.k);
+        ctx->launches++;
+        LK(ctx, apply_token_masks(c->logits, M, ctx->cfg.vocab, c->mask_bits, c->mask_on, st));
+        c->mask_k = -1;   // consumed by this acceptance
+    }
     LK(ctx, argmax_rows(c->logits, M, ctx->cfg.vocab, c->amax, st, c->amax_part, c->amax_ctr));
     LK(ctx, accept_greedy(c->rs(), sp, c->vtok, c->count, c->amax, step_out(c), st));
     if (any_sampled(c)) {
@@ -1578,7 +1703,11 @@ int mlxcat_spec_step(mlxcat_cache *c, const mlxcat_spec_config *spec, int32_t *o
     mlxcat_ctx *ctx = c->ctx;
     int rc = validate_spec(ctx, spec);
     if (rc) return rc;
-    if ((rc = check_weights(ctx))) return rc;
+    if ((rc = check_weights(c))) return rc;
+    if (c->mask_k >= 0)
+        return set_err(ctx, MLXCAT_E_STATE,
+                       "token masks are pending: they depend on the drafts, so they apply to the split step "
+                       "(mlxcat_draft, mlxcat_verify_forward, mlxcat_accept)");
     CK(ctx, cudaSetDevice(ctx->device));
     const SpecParams sp = params_of(spec);
     const bool sampled = any_sampled(c);

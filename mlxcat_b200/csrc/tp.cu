@@ -92,26 +92,6 @@ const char *tp_allreduce_sum(void *comm, float *buf, size_t n, cudaStream_t st) 
     return nullptr;
 }
 
-const char *ep_exchange(void *comm, int nranks, const TpBlock *blocks, int nblocks, cudaStream_t st) {
-    // one NCCL group: for every block and every peer p, send block.bytes from
-    // send + p * stride and receive as many into recv + p * stride
-    ncclResult_t r = api().group_start();
-    if (r != ncclSuccess) return err_str(r);
-    for (int b = 0; b < nblocks && r == ncclSuccess; ++b)
-        for (int p = 0; p < nranks && r == ncclSuccess; ++p) {
-            const TpBlock &k = blocks[b];
-            r = api().send(static_cast<const char *>(k.send) + (size_t)p * k.stride, k.bytes, ncclUint8, p,
-                           static_cast<ncclComm_t>(comm), st);
-            if (r == ncclSuccess)
-                r = api().recv(static_cast<char *>(k.recv) + (size_t)p * k.stride, k.bytes, ncclUint8, p,
-                               static_cast<ncclComm_t>(comm), st);
-        }
-    const ncclResult_t e = api().group_end();
-    if (r != ncclSuccess) return err_str(r);
-    if (e != ncclSuccess) return err_str(e);
-    (void)cudaGetLastError();
-    return nullptr;
-}
 
 void tp_destroy(void *comm) {
     if (comm && api().ok) api().comm_destroy(static_cast<ncclComm_t>(comm));

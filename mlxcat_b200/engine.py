@@ -167,6 +167,35 @@ class Request:
 # --------------------------------------------------------------------------- #
 # context / cache
 # --------------------------------------------------------------------------- #
+def allowed_next_token_ids(allowed_sequences, generated_tokens) -> Optional[List[int]]:
+    """TokenSampler.allowedNextTokenIDs (Sources/MLXCat/TrackB/Sampling.swift:529-546):
+    the next tokens of every allowed sequence that the generated tokens are a
+    strict prefix of, sorted; None when there are no sequences or none of them
+    continues (no constraint)."""
+    if not allowed_sequences:
+        return None
+    g = list(generated_tokens)
+    allowed = set()
+    for seq in allowed_sequences:
+        if len(g) >= len(seq) or list(seq[:len(g)]) != g:
+            continue
+        allowed.add(int(seq[len(g)]))
+    return sorted(allowed) if allowed else None
+
+
+def speculative_token_masks(row: int, allowed_sequences, generated_tokens, drafts) -> Dict:
+    """The allowed sets of one choice-constrained row at each verify position:
+    position p follows the generated tokens and drafts[:p] (what the row will
+    have generated if the drafts before p are accepted).  The result feeds
+    BatchKVCache.set_token_masks; unconstrained positions are left out."""
+    out = {}
+    for p in range(len(drafts) + 1):
+        ids = allowed_next_token_ids(allowed_sequences, list(generated_tokens) + list(drafts[:p]))
+        if ids is not None:
+            out[(row, p)] = ids
+    return out
+
+
 class Context:
     """One model on one device (mlxcat_ctx)."""
 
@@ -265,6 +294,40 @@ class BatchKVCache:
         ctx.check(self.L.mlxcat_cache_create(ctx.h, max_rows, max_len, C.byref(h)))
         self.h = h
         ctx._caches.add(self)
+
+    EP_HANDLE_BYTES = 128
+
+    def ep_handle(self) -> bytes:
+        """This rank's expert-parallel handle (mlxcat_cache_ep_handle): the
+        bytes every other rank needs to map this cache's exchange region."""
+        buf = (C.c_uint8 * self.EP_HANDLE_BYTES)()
+        self.ctx.check(self.L.mlxcat_cache_ep_handle(self.h, buf))
+        return bytes(buf)
+
+    def ep_connect(self, handles):
+        """Map every rank's region (handles: one per rank, in rank order)."""
+        if any(len(h) != self.EP_HANDLE_BYTES for h in handles):
+            raise ValueError(f"expert-parallel handles are {self.EP_HANDLE_BYTES} bytes each")
+        buf = (C.c_uint8 * (self.EP_HANDLE_BYTES * len(handles))).from_buffer_copy(b"".join(handles))
+        self.ctx.check(self.L.mlxcat_cache_ep_connect(self.h, buf))
+
+    def set_token_masks(self, k: int, allowed):
+        """Grammar masks for the next accept(): allowed maps (row, position) to
+        the token ids the row's grammar allows at that verify position (after
+        the drafts before it); positions not in the map are unconstrained."""
+        V = self.ctx.cfg.vocab
+        W = (V + 31) // 32
+        bits = np.zeros((self.max_rows, k + 1, W), np.uint32)
+        on = np.zeros((self.max_rows, k + 1), np.uint8)
+        for (r, p), ids in allowed.items():
+            on[r, p] = 1
+            for t in ids:
+                if 0 <= t < V:
+                    bits[r, p, t >> 5] |= np.uint32(1 << (t & 31))
+        self.ctx.check(self.L.mlxcat_cache_set_token_masks(self.h, k, bits.ctypes.data, on.ctypes.data))
+
+    def clear_token_masks(self):
+        self.ctx.check(self.L.mlxcat_cache_set_token_masks(self.h, 0, None, None))
 
     def insert_row(self, row: int, prompt, max_new_tokens: int, sampling: SamplingParameters,
                    default_seed: int = 0) -> int:

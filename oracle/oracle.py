@@ -287,6 +287,21 @@ def accept_row(mode, logits, drafts, sp: Sampling, gen_index: int):
 # --------------------------------------------------------------------------- #
 # model / cache / generator
 # --------------------------------------------------------------------------- #
+def apply_allowed_mask(logits, allowed_ids):
+    """applyAllowedTokenMask (Sources/MLXCat/TrackB/Sampling.swift:557-569):
+    ids outside [0, vocab) are dropped; if none is left the logits come back
+    unchanged, else every logit outside the allowed ids becomes -inf (fp32)."""
+    out = np.array(logits, dtype=np.float32, copy=True)
+    V = out.shape[-1]
+    valid = sorted({int(t) for t in allowed_ids if 0 <= int(t) < V})
+    if not valid:
+        return out
+    keep = np.zeros(V, dtype=bool)
+    keep[valid] = True
+    out[..., ~keep] = -np.inf
+    return out
+
+
 def make_config(n_layers, hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab,
                 tie_embeddings=True, qk_norm=False, rms_eps=1e-5, rope_theta=10000.0,
                 n_experts=0, top_k=0, norm_topk=True) -> Config:
