@@ -92,7 +92,7 @@ def model_config(name):
     return CONFIGS[name]
 
 
-def workload_config(name, wl, world):
+def workload_config(name, wl, world, tp_allreduce="peer"):
     """The `config` object both arms print (identical for the same workload)."""
     tp, ep = bool(wl.get("tp")) and world > 1, bool(wl.get("ep")) and world > 1
     rows = wl["rows"] // world if ep else wl["rows"]
@@ -102,7 +102,9 @@ def workload_config(name, wl, world):
          "max_new_tokens": wl["max_new"],
          "acceptance": ("single-draft rejection sampling, per-request seeds" if wl["temperature"] > 0
                         else "greedy prefix match"),
-         "parallelism": (f"tensor-parallel x{world} (NCCL allreduce per block)" if tp else
+         "parallelism": (f"tensor-parallel x{world} (" + ("NCCL allreduce" if tp_allreduce == "nccl" else
+                                                          "allreduce fused into the row-split projections over "
+                                                          "NVLink peer memory") + " per block)" if tp else
                          f"expert-parallel x{world} (NVLink peer-memory exchange per MoE layer)" if ep else
                          f"request-parallel x{world} (replicas, no collective)"),
          "l2": wl.get("l2", "inputs larger than L2 (q4 weights + KV read every step)")}
@@ -400,7 +402,7 @@ def run_serving(args, wl, M, A, ctx, cfg, rank, world, local_rank):
         "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": dev_ms_max / K,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded segment-pool prompts, Poisson arrivals, random-init N(0,0.02) q4 weights)",
-        "config": workload_config(args.config, wl, world),
+        "config": workload_config(args.config, wl, world, args.tp_allreduce),
         "verify_step_us": statistics.mean(verify) * 1e3,
         "acceptance_rate": (accepted / proposed if proposed else None),
         "tokens_per_step": tokens / K, "admitted_in_timed_region": admitted,
@@ -432,7 +434,7 @@ def run_ours(args, wl, rank, world, local_rank):
     if ep:   # every rank runs its share of the rows with 1/world of the experts
         cfg = dataclasses.replace(cfg, ep_size=world, ep_rank=rank)
     ctx = M.Context(cfg, local_rank)
-    if tp:
+    if tp and args.tp_allreduce == "nccl":
         ctx.tp_connect(share_tp_id(M.Context.tp_unique_id() if rank == 0 else None, rank, "cuda"))
     ctx.synth_weights(WEIGHT_SEED, 0.02)
     if wl.get("arrivals"):
@@ -442,8 +444,8 @@ def run_ours(args, wl, rank, world, local_rank):
     rows, k1 = (wl["rows"] // world if ep else wl["rows"]), wl["k"] + 1
     max_len = wl["prompt"] + wl["max_new"] + 16
     cache = M.BatchKVCache(ctx, rows, max_len)
-    if ep:   # map every rank's exchange region (NVLink peer memory)
-        cache.ep_connect(gather_handles(cache.ep_handle(), world, "cuda"))
+    if ep or (tp and args.tp_allreduce == "peer"):   # map every rank's exchange region (NVLink peer memory)
+        cache.peer_connect(gather_handles(cache.peer_handle(), world, "cuda"))
     spec = M.SpeculativeDecodingConfiguration(True, wl["k"], wl["n"], MIN_CONTEXT, A.ACCEPT_PREFIX)
     t0 = time.perf_counter()
     for r in range(rows):
@@ -511,7 +513,7 @@ def run_ours(args, wl, rank, world, local_rank):
         "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
         "dtype": "f16",
         "data": "synthetic (seeded segment-pool prompts, random-init N(0,0.02) q4 weights)",
-        "config": workload_config(args.config, wl, world),
+        "config": workload_config(args.config, wl, world, args.tp_allreduce),
         "verify_step_us": statistics.mean(verify) * 1e3,
         "acceptance_rate": (accepted / proposed if proposed else None),
         "tokens_per_row_step": tokens / (args.steps * rows),
@@ -626,7 +628,7 @@ def run_reference(args, wl, world):
             "n_gpus": 0, "steps": steps, "warmup": warm + 1, "ms_per_step": dt / steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded segment-pool prompts, random-init N(0,0.02) q4 weights)",
-            "config": workload_config(args.config, wl, world),
+            "config": workload_config(args.config, wl, world, args.tp_allreduce),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
                              "sample": f"{steps} speculative steps x {rows} rows of the workload "
                                        f"(weights synthesised on the host in {synth_s:.0f} s, prompt KV "
@@ -814,6 +816,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-case", choices=["q4_linear", "attention", "moe", "gemm", "prefill"])
     ap.add_argument("--kernel-reps", type=int, default=50)
+    ap.add_argument("--tp-allreduce", default="peer", choices=["peer", "nccl"],
+                    help="tensor-parallel allreduce: fused over peer memory, or one NCCL call per block")
     args = ap.parse_args()
     if args.kernel_case:
         run_kernel_case(args)

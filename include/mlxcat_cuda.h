@@ -71,7 +71,7 @@ typedef struct {
      * ep_rank holds experts [ep_rank*E/ep_size, (ep_rank+1)*E/ep_size) and runs
      * its own rows; every MoE layer stores each routed operand row straight
      * into its expert owner's memory and the owner stores the result back
-     * (NVLink peer memory, see mlxcat_cache_ep_connect).  The other weights
+     * (NVLink peer memory, see mlxcat_cache_peer_connect).  The other weights
      * are replicated.  Every rank must run the same NUMBER of forwards in the
      * same order (each inserted prompt chunk and each verify is one); their
      * token counts may differ.  A rank that stops participating makes the
@@ -118,7 +118,8 @@ MLXCAT_API int mlxcat_ctx_destroy(mlxcat_ctx *ctx);
  * (ncclCommInitRank; collective: all ranks call it).  NCCL is loaded at run
  * time (libnccl.so.2); without it these return MLXCAT_E_STATE.  Must precede
  * the first forward on a context with tp_size > 1.  (Expert-parallel
- * contexts use no NCCL: their caches connect, mlxcat_cache_ep_connect.) */
+ * contexts use no NCCL: their caches connect, mlxcat_cache_peer_connect, which also
+ * gives tensor-parallel caches the fused allreduce over peer memory.) */
 MLXCAT_API int mlxcat_tp_unique_id(uint8_t id[128]);
 MLXCAT_API int mlxcat_ctx_tp_connect(mlxcat_ctx *ctx, const uint8_t id[128]);
 MLXCAT_API const char *mlxcat_last_error(const mlxcat_ctx *ctx);
@@ -146,6 +147,13 @@ MLXCAT_API int mlxcat_weights_set_table(mlxcat_ctx *ctx, const int32_t *next_tok
 /* bf16 tensors (the MoE router, id layer*16 + 7): [n_experts][hidden] */
 MLXCAT_API int mlxcat_weights_set_bf16(mlxcat_ctx *ctx, uint32_t tensor_id, const uint16_t *w);
 MLXCAT_API int mlxcat_weights_get_bf16(mlxcat_ctx *ctx, uint32_t tensor_id, uint16_t *w);
+/* RMSNorm weights (fp32; all ones until set): id layer*16 + {8 input_layernorm,
+ * 9 post_attention_layernorm, 10 q_norm, 11 k_norm} ([hidden], q/k: [head_dim],
+ * Qwen3 only), MLXCAT_NORM_FINAL ([hidden]).  Replaces the RMSNorm parameter
+ * loading of the mlx-swift-lm model (un-vendored). */
+#define MLXCAT_NORM_FINAL 0xFFFF0002u
+#define MLXCAT_NORM(layer, kind) ((uint32_t)(layer) * 16u + 8u + (uint32_t)(kind))
+MLXCAT_API int mlxcat_weights_set_norm(mlxcat_ctx *ctx, uint32_t norm_id, const float *w);
 /* bytes of q4 weights one forward streams (packed words + scales + biases) */
 MLXCAT_API int64_t mlxcat_weights_bytes(const mlxcat_ctx *ctx);
 
@@ -156,16 +164,21 @@ MLXCAT_API int64_t mlxcat_weights_bytes(const mlxcat_ctx *ctx);
  * with one length per row. */
 MLXCAT_API int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxcat_cache **out);
 MLXCAT_API int mlxcat_cache_destroy(mlxcat_cache *cache);
-/* Expert parallelism (ep_size > 1): each rank's cache owns one device region
- * (receive slabs, return rows, flags) that every other rank maps.  Each rank
- * writes its cache's handle (a CUDA IPC handle plus the region's shape), the
- * host gathers the ep_size handles in rank order and hands all of them to
- * every rank's mlxcat_cache_ep_connect.  Caches of different shape (max_rows)
- * are rejected with MLXCAT_E_INVALID.  Connect before the first insert_row.
- * No counterpart in the reference (the MLX path runs on one device). */
-#define MLXCAT_EP_HANDLE_BYTES 128
-MLXCAT_API int mlxcat_cache_ep_handle(mlxcat_cache *cache, uint8_t handle[MLXCAT_EP_HANDLE_BYTES]);
-MLXCAT_API int mlxcat_cache_ep_connect(mlxcat_cache *cache, const uint8_t *handles /* [ep_size][128] */);
+/* Expert parallelism (ep_size > 1) and the fused tensor-parallel allreduce
+ * (tp_size > 1): each rank's cache owns one device region (expert parallel:
+ * receive slabs, return rows, flags; tensor parallel: scatter and gather
+ * buffers of the row-split projections, flags) that every other rank maps
+ * and writes over NVLink.  Each rank writes its cache's handle (a CUDA IPC
+ * handle plus the region's shape), the host gathers the group's handles in
+ * rank order and hands all of them to every rank's mlxcat_cache_peer_connect.
+ * Caches of different shape (max_rows) are rejected with MLXCAT_E_INVALID.
+ * Connect before the first insert_row.  Expert parallelism needs it; tensor
+ * parallelism uses NCCL (mlxcat_ctx_tp_connect) instead while the cache is
+ * not peer-connected.  No counterpart in the reference (the MLX path runs on
+ * one device). */
+#define MLXCAT_PEER_HANDLE_BYTES 128
+MLXCAT_API int mlxcat_cache_peer_handle(mlxcat_cache *cache, uint8_t handle[MLXCAT_PEER_HANDLE_BYTES]);
+MLXCAT_API int mlxcat_cache_peer_connect(mlxcat_cache *cache, const uint8_t *handles /* [group][128] */);
 /* admission: prefill prompt into `row`, sample the first token (generation
  * index 0).  Scheduler.completeAdmission + generator.insert
  * (Scheduler.swift:599-668, BatchGenerator.swift:380-460).  Requires

@@ -12,11 +12,12 @@ from ._abi import MlxcatError, lib
 from .engine import (
     CONFIGS, LLAMA3_8B, QWEN3_4B, TINY, BatchKVCache, ContinuousBatchGenerator, Context,
     FinishReason, ModelConfig, Request, Response, SamplingParameters, Scheduler,
-    SpeculativeDecodingConfiguration, SpeculativeDecodingStats,
+    SpeculativeDecodingConfiguration, SpeculativeDecodingStats, allowed_next_token_ids, speculative_token_masks,
 )
 
 __all__ = [
     "BatchKVCache", "CONFIGS", "ContinuousBatchGenerator", "Context", "FinishReason", "LLAMA3_8B",
     "MlxcatError", "ModelConfig", "QWEN3_4B", "Request", "Response", "SamplingParameters",
-    "Scheduler", "SpeculativeDecodingConfiguration", "SpeculativeDecodingStats", "TINY", "lib",
+    "Scheduler", "SpeculativeDecodingConfiguration", "SpeculativeDecodingStats", "TINY", "allowed_next_token_ids",
+    "lib", "speculative_token_masks",
 ]

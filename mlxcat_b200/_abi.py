@@ -92,12 +92,13 @@ PROTOTYPES = {
     "mlxcat_weights_set_table": (C.c_int, [_vp, _vp, _i32]),
     "mlxcat_weights_set_bf16": (C.c_int, [_vp, _u32, _vp]),
     "mlxcat_weights_get_bf16": (C.c_int, [_vp, _u32, _vp]),
+    "mlxcat_weights_set_norm": (C.c_int, [_vp, _u32, _vp]),
     "mlxcat_weights_bytes": (C.c_int64, [_vp]),
     "mlxcat_cache_create": (C.c_int, [_vp, _i32, _i32, C.POINTER(_vp)]),
     "mlxcat_cache_destroy": (C.c_int, [_vp]),
-    "mlxcat_cache_ep_handle": (C.c_int, [_vp, _vp]),
+    "mlxcat_cache_peer_handle": (C.c_int, [_vp, _vp]),
     "mlxcat_cache_set_token_masks": (C.c_int, [_vp, _i32, _vp, _vp]),
-    "mlxcat_cache_ep_connect": (C.c_int, [_vp, _vp]),
+    "mlxcat_cache_peer_connect": (C.c_int, [_vp, _vp]),
     "mlxcat_cache_insert_row": (C.c_int, [_vp, _i32, _vp, _i32, _i32, C.POINTER(SamplingC),
                                           C.POINTER(_i32)]),
     "mlxcat_op_dequant_q4": (C.c_int, [_vp, _vp, _vp, _i32, _i32, _vp, _vp]),

@@ -39,14 +39,8 @@ namespace mlxcat {
 
 namespace {
 
-__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
+using tc::ld_acquire_sys;
+using tc::st_release_sys;
 
 constexpr uint64_t EP_WAIT_NS = 10000000000ull;   // 10 s
 
@@ -107,21 +101,8 @@ __global__ void ep_dispatch_kernel(EpArgs a, const int32_t *__restrict__ topk_id
 // current flag value (bounded)
 __global__ void ep_wait_kernel(EpArgs a, size_t flag_off, int code) {
     const int t = threadIdx.x;
-    if (t < a.N && !*reinterpret_cast<volatile int *>(a.err)) {
-        const unsigned want = ep_flag(a);
-        const unsigned *f = at<unsigned>(a.peers[a.me], flag_off) + a.set * a.N + t;
-        if (ld_acquire_sys(f) != want) {
-            const uint64_t t0 = tc::global_ns();
-            for (;;) {
-                if (ld_acquire_sys(f) == want) break;
-                if (*reinterpret_cast<volatile int *>(a.err) || tc::global_ns() - t0 > EP_WAIT_NS) {
-                    atomicExch(a.err, code);
-                    break;
-                }
-                __nanosleep(200);
-            }
-        }
-    }
+    if (t < a.N) tc::peer_flag_wait(at<unsigned>(a.peers[a.me], flag_off) + a.set * a.N + t, ep_flag(a), a.err, code,
+                                    EP_WAIT_NS);
     __syncthreads();
     __threadfence_system();
 }

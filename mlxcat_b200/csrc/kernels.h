@@ -95,6 +95,15 @@ struct Q4Epilogue {
     const float *col_prev = nullptr;     // [rows] the producer's pre-scale
     float *col_rstd = nullptr;
     float col_eps = 0.f;
+    // STORE into peer memory (the tensor-parallel scatter, tpx.cu): feature f of
+    // token m goes to peers[f / peer_cols] + peer_off + (m * peer_cols + f % peer_cols) * 4
+    // bytes; once every CTA has stored, the last one writes *peer_flag * 512 +
+    // peer_call + 1 to the word at peer_flag_off of every peer's region (release)
+    char *const *peers = nullptr;
+    size_t peer_off = 0, peer_flag_off = 0;
+    int peer_n = 0, peer_cols = 0, peer_call = 0;
+    const unsigned *peer_flag = nullptr;   // the forward's epoch (device)
+    unsigned *peer_ctr = nullptr;          // CTA arrivals (zero between launches)
 };
 // (cos, sin) of p * inv_freq[i] for every position p < max_len and i < half
 cudaError_t rope_table(const float *inv_freq, int half, int max_len, float2 *tab, cudaStream_t st);
@@ -262,6 +271,28 @@ cudaError_t ep_wait_return(const EpArgs &a, cudaStream_t st);
 // [cap][H] fp32 in assignment order, the received operand rows [H/64][N*cap][64]
 const float *ep_returned(const EpArgs &a, const char *own_region);
 const __half *ep_received(const EpArgs &a, const char *own_region);
+
+// ---- tensor-parallel allreduce over peer memory (tpx.cu) --------------------
+// Byte offsets inside each rank's exported region (two buffer sets, by call parity):
+// scat [2][N][mcap][H/N] fp32, scat_flag [2][N], gath [2][mcap][H] fp32, gath_flag [2][N].
+struct TpxLayout {
+    size_t scat = 0, scat_flag = 0, gath = 0, gath_flag = 0, total = 0;
+};
+TpxLayout tpx_layout(int N, int mcap, int H);
+struct TpxArgs {
+    char *const *peers = nullptr;   // device array [N]: every rank's mapped region (own included)
+    TpxLayout layout;
+    int N = 0, me = 0, mcap = 0, H = 0, set = 0, call = 0;
+    const unsigned *epoch = nullptr;  // forwards run so far (device)
+    unsigned *done = nullptr;         // reduce kernel's CTA arrivals (zero between kernels)
+    unsigned *sig = nullptr;          // scatter (q4 kernel) CTA arrivals
+    int *err = nullptr;
+};
+// the STORE epilogue fields that make a row-split projection scatter its partial sums
+void tpx_scatter_epilogue(const TpxArgs &a, Q4Epilogue &e);
+cudaError_t tpx_reduce(const TpxArgs &a, int M, int sm_count, cudaStream_t st);
+cudaError_t tpx_wait(const TpxArgs &a, cudaStream_t st);
+const float *tpx_gathered(const TpxArgs &a, const char *own_region);
 
 // ---- decode attention (split-K over keys, GQA) -----------------------------
 // Tokens come in groups of `qg` consecutive positions of one row (the verify

@@ -283,6 +283,24 @@ __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, vol
     return false;
 }
 
+// STORE epilogue: feature f of tokens m0..m0+mlim-1, into out[m][f] or, when
+// the projection scatters to peers (tensor parallel), into the owner's slot
+__device__ __forceinline__ void store_rows(const Q4Epilogue &ep, int f, int m0, int mlim, const float *y) {
+    float *o;
+    size_t ld;
+    if (ep.peers) {
+        const int d = f / ep.peer_cols;
+        o = reinterpret_cast<float *>(ep.peers[d] + ep.peer_off) + (f - d * ep.peer_cols);
+        ld = (size_t)ep.peer_cols;
+    } else {
+        o = ep.out + f;
+        ld = (size_t)ep.ldo;
+    }
+#pragma unroll
+    for (int q = 0; q < 16; ++q)
+        if (q < mlim) o[(size_t)(m0 + q) * ld] = y[q];
+}
+
 template <int NT, int OP>
 __global__ void __launch_bounds__(THREADS, 1)
 q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
@@ -586,9 +604,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                     for (int q = 0; q < 16; ++q) y[q] *= cs.cscale[cc + q];
                 }
                 if constexpr (OP == Q4Epilogue::STORE) {
-#pragma unroll
-                    for (int q = 0; q < 16; ++q)
-                        if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] = y[q];
+                    store_rows(ep, f, m0, mlim, y);
                 } else if constexpr (OP == Q4Epilogue::RESID) {
                     // every load of the piece is issued before its first store (the
                     // compiler cannot tell the pointers apart, so interleaving would
@@ -926,9 +942,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                         for (int q = 0; q < 16; ++q) y[q] *= cs.xch[p * 16 + q];
                     }
                     if constexpr (OP == Q4Epilogue::STORE) {
-#pragma unroll
-                        for (int q = 0; q < 16; ++q)
-                            if (q < mlim) ep.out[(size_t)(m0 + q) * ep.ldo + f] = y[q];
+                        store_rows(ep, f, m0, mlim, y);
                     } else if constexpr (OP == Q4Epilogue::RESID) {
                         // loads of the piece before its stores (see the tail epilogue)
 #pragma unroll
@@ -1046,11 +1060,20 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
             if (++dset == C::DSETS) dset = 0;
         }
     }
+    if (OP == Q4Epilogue::STORE && ep.peers) __threadfence_system();   // this thread's peer stores
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 0) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, 512);
+    }
+    if (OP == Q4Epilogue::STORE && ep.peers && tid == 0 && atomicAdd(ep.peer_ctr, 1u) == (unsigned)G - 1) {
+        // every CTA's partial sums are stored: flag every owner
+        *ep.peer_ctr = 0u;
+        __threadfence_system();
+        const unsigned flag = *ep.peer_flag * 512u + (unsigned)ep.peer_call + 1u;
+        for (int d = 0; d < ep.peer_n; ++d)
+            tc::st_release_sys(reinterpret_cast<unsigned *>(ep.peers[d] + ep.peer_flag_off), flag);
     }
 }
 
@@ -1171,9 +1194,13 @@ cudaError_t pack_q4_sb(const __half *scales, const __half *biases, int N, int K,
     return cudaGetLastError();
 }
 
+// token tile: the fewest tiles of at most 128 tokens, split evenly (M = 160 ->
+// two tiles of 80, not 128 + 32 padded to 128: the MMAs of a sub-chunk and its
+// token-operand loads scale with the tile width)
 int q4_tc_tile(int M) {
-    const int nt = ((M + 15) / 16) * 16;
-    return nt > 128 ? 128 : nt;
+    const int tiles = (M + 127) / 128;
+    const int per = (M + tiles - 1) / tiles;
+    return ((per + 15) / 16) * 16;
 }
 
 // most CTAs that share one row block (stream-K contributors)

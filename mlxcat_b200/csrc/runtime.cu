@@ -133,17 +133,21 @@ struct mlxcat_cache {
     // the attention-norm and MLP-norm inputs of each token row (pre-scales)
     float *norm_part = nullptr, *r_attn = nullptr, *r_mlp = nullptr;
     float *tp_part = nullptr;          // tensor parallel: this rank's O / down partial sums [rows][H]
-    // expert parallel over peer memory (ep.cu): this cache's exported region
-    // (receive slabs, return rows, flags), every rank's mapping of its peers'
-    // regions, and the owner side's per-expert lists, SwiGLU activations and
-    // scaled outputs over the N * cap received rows
-    char *ep_region = nullptr;
+    // expert / tensor parallel over peer memory (ep.cu, tpx.cu): this cache's
+    // exported region (receive slabs or scatter/gather buffers, flags), every
+    // rank's mapping of its peers' regions, and for experts the owner side's
+    // per-expert lists, SwiGLU activations and scaled outputs over the N * cap
+    // received rows
+    char *peer_region = nullptr;
+    size_t peer_bytes = 0;
+    int peer_kind = 0;                 // 1 = expert parallel, 2 = tensor parallel
+    int peer_cap = 0;                  // rows per (source, owner) / token rows of the buffers
     EpLayout ep_lay;
-    int ep_cap = 0;                    // rows per (source, owner) and buffer set
-    bool ep_connected = false;
-    std::vector<char *> ep_opened;     // IPC mappings of the peers' regions
-    char **ep_peers = nullptr;         // device [N]
-    unsigned *ep_epoch = nullptr, *ep_done = nullptr;
+    TpxLayout tpx_lay;
+    bool peer_connected = false;
+    std::vector<char *> peer_opened;   // IPC mappings of the peers' regions
+    char **peer_tab = nullptr;         // device [N]
+    unsigned *peer_epoch = nullptr, *peer_done = nullptr, *peer_sig = nullptr;
     int *ep_lcount = nullptr;          // [N]
     __half *ep_act = nullptr;
     int *ep_exp_count = nullptr;       // [layer][local experts]
@@ -338,12 +342,12 @@ int ep_moe(mlxcat_cache *c, int l, int M) {
     mlxcat_ctx *ctx = c->ctx;
     const mlxcat_model_config &cf = ctx->cfg;
     const int H = cf.hidden, I = cf.intermediate, TK = cf.top_k, N = ctx->ep, epr = ctx->epr, R = c->m_cap;
-    const int rows = N * c->ep_cap;
+    const int rows = N * c->peer_cap;
     cudaStream_t st = ctx->stream;
     EpArgs a;
-    a.peers = c->ep_peers; a.layout = c->ep_lay; a.N = N; a.me = ctx->ep_rank; a.cap = c->ep_cap; a.H = H;
+    a.peers = c->peer_tab; a.layout = c->ep_lay; a.N = N; a.me = ctx->ep_rank; a.cap = c->peer_cap; a.H = H;
     a.TK = TK; a.epr = epr; a.set = l & 1; a.layer = l;
-    a.epoch = c->ep_epoch; a.lcount = c->ep_lcount; a.done = c->ep_done; a.err = c->err;
+    a.epoch = c->peer_epoch; a.lcount = c->ep_lcount; a.done = c->peer_done; a.err = c->err;
     const size_t asg = (size_t)c->m_cap * TK;
     LK(ctx, ep_dispatch(a, c->moe_id + l * asg, c->moe_w + l * asg, c->moe_scale, c->xg, R, M * TK, st));
     LK(ctx, ep_wait_dispatch(a, st));
@@ -353,7 +357,7 @@ int ep_moe(mlxcat_cache *c, int l, int M) {
     MoEExpertArgs xa;
     xa.wq = mb.wq[0]; xa.scales = mb.s[0]; xa.biases = mb.b[0];
     xa.wq2 = mb.wq[1]; xa.scales2 = mb.s[1]; xa.biases2 = mb.b[1];
-    xa.N = I; xa.K = H; xa.E = epr; xa.x = ep_received(a, c->ep_region); xa.ldx_rows = rows; xa.x_div = 1;
+    xa.N = I; xa.K = H; xa.E = epr; xa.x = ep_received(a, c->peer_region); xa.ldx_rows = rows; xa.x_div = 1;
     xa.exp_count = ecnt; xa.exp_list = c->ep_exp_list; xa.list_cap = rows;
     xa.tok_scale = c->ep_scale; xa.act = c->ep_act; xa.act_rows = rows;
     { ProfScope ps(c, 0); LK(ctx, moe_expert(xa, 0, st)); }
@@ -366,7 +370,7 @@ int ep_moe(mlxcat_cache *c, int l, int M) {
     LK(ctx, ep_return(a, c->ep_ys, st));
     LK(ctx, ep_wait_return(a, st));
     MoECombineArgs ca;
-    ca.h = c->h; ca.y = ep_returned(a, c->ep_region); ca.M = M; ca.H = H; ca.TK = TK;
+    ca.h = c->h; ca.y = ep_returned(a, c->peer_region); ca.M = M; ca.H = H; ca.TK = TK;
     ca.norm_w = l + 1 < cf.n_layers ? ctx->attn_norm(l + 1) : ctx->final_norm(); ca.norm_scale = c->r_mlp;
     ca.xout = c->xn; ca.ldx_rows = R; ca.norm_part = c->norm_part; ca.norm_rows = R;
     LK(ctx, moe_combine(ca, st));
@@ -374,22 +378,38 @@ int ep_moe(mlxcat_cache *c, int l, int M) {
 }
 
 // Tensor-parallel residual step: this rank's slice of a row-split projection
-// (O or down) as fp32 partial sums, one allreduce (sum) over the group, then
-// h += y with the next linear's folded-norm operand fp16(h * norm_w * s) and
-// per-block sums of squares -- what the RESID epilogue does on one GPU.
+// (O or down) as fp32 partial sums, summed over the group, then h += y with the
+// next linear's folded-norm operand fp16(h * norm_w * s) and per-block sums of
+// squares -- what the RESID epilogue does on one GPU.  With the cache's peer
+// regions connected the sum is the fused scatter / reduce / gather of tpx.cu
+// (call = 2 * layer + {0: O, 1: down}); otherwise one NCCL allreduce.
 int tp_residual(mlxcat_cache *c, const DevLin &w, const __half *x, int M, const float *norm_w,
-                const float *norm_scale, __half *xout) {
+                const float *norm_scale, __half *xout, int call) {
     mlxcat_ctx *ctx = c->ctx;
     const int H = ctx->cfg.hidden, R = c->m_cap;
     cudaStream_t st = ctx->stream;
     Q4Epilogue e;
     e.part = c->part; e.counters = c->counters; e.err = c->err; e.pdl = 1;
     e.op = Q4Epilogue::STORE; e.out = c->tp_part; e.ldo = H;
-    { ProfScope ps(c, 0); LK(ctx, q4_tc(w.tc(), x, R, 0, M, ctx->sm_count, e, st)); }
-    if (const char *er = tp_allreduce_sum(ctx->nccl, c->tp_part, (size_t)M * H, st))
-        return set_err(ctx, MLXCAT_E_CUDA, "allreduce: %s", er);
+    const float *y = c->tp_part;
+    if (c->peer_connected) {
+        TpxArgs a;
+        a.peers = c->peer_tab; a.layout = c->tpx_lay; a.N = ctx->tp; a.me = ctx->tp_rank; a.mcap = c->peer_cap;
+        a.H = H; a.set = call & 1; a.call = call;
+        a.epoch = c->peer_epoch; a.done = c->peer_done; a.sig = c->peer_sig; a.err = c->err;
+        tpx_scatter_epilogue(a, e);
+        { ProfScope ps(c, 0); LK(ctx, q4_tc(w.tc(), x, R, 0, M, ctx->sm_count, e, st)); }
+        ctx->launches += 2;
+        LK(ctx, tpx_reduce(a, M, ctx->sm_count, st));
+        LK(ctx, tpx_wait(a, st));
+        y = tpx_gathered(a, c->peer_region);
+    } else {
+        { ProfScope ps(c, 0); LK(ctx, q4_tc(w.tc(), x, R, 0, M, ctx->sm_count, e, st)); }
+        if (const char *er = tp_allreduce_sum(ctx->nccl, c->tp_part, (size_t)M * H, st))
+            return set_err(ctx, MLXCAT_E_CUDA, "allreduce: %s", er);
+    }
     MoECombineArgs ca;
-    ca.h = c->h; ca.y = c->tp_part; ca.M = M; ca.H = H; ca.TK = 1;
+    ca.h = c->h; ca.y = y; ca.M = M; ca.H = H; ca.TK = 1;
     ca.norm_w = norm_w; ca.norm_scale = norm_scale; ca.xout = xout; ca.ldx_rows = R;
     ca.norm_part = c->norm_part; ca.norm_rows = R;
     LK(ctx, moe_combine(ca, st));
@@ -421,11 +441,13 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
     LK(ctx, embed_norm(ctx->embed.view(), tok, M, ctx->attn_norm(0), eps, c->h, c->xn, R, st, c->r_attn));
     if (cf.n_experts) CK(ctx, cudaMemsetAsync(c->moe_count, 0, sizeof(int) * (size_t)L * cf.n_experts, st));
     if (cf.n_experts && ctx->ep > 1) {
-        if (!c->ep_connected)
-            return set_err(ctx, MLXCAT_E_STATE, "expert-parallel cache not connected (mlxcat_cache_ep_connect)");
+        if (!c->peer_connected)
+            return set_err(ctx, MLXCAT_E_STATE, "expert-parallel cache not connected (mlxcat_cache_peer_connect)");
         CK(ctx, cudaMemsetAsync(c->ep_exp_count, 0, sizeof(int) * (size_t)L * ctx->epr, st));
+    }
+    if (c->peer_connected) {
         ctx->launches++;
-        LK(ctx, ep_begin(c->ep_epoch, st));   // the forward's epoch, part of every exchange flag
+        LK(ctx, ep_begin(c->peer_epoch, st));   // the forward's epoch, part of every exchange flag
     }
     Q4Epilogue ep;
     ep.part = c->part;
@@ -453,7 +475,7 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
           LK(ctx, attention(c->qbuf, kv, trow, tpos, M, qg, Hq, Hkv, D, KEY_CHUNK, c->attn_splits,
                             c->attn, c->xn, true, R, st, true)); }
         if (ctx->tp > 1) {   // row-split output projection: partial sums, allreduce, residual
-            int rc = tp_residual(c, ctx->o[l], c->xn, M, ctx->mlp_norm(l), c->r_attn, c->xg);
+            int rc = tp_residual(c, ctx->o[l], c->xn, M, ctx->mlp_norm(l), c->r_attn, c->xg, 2 * l);
             if (rc) return rc;
         } else {   // output projection into the residual stream
             Q4Epilogue e = ep;
@@ -513,7 +535,7 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
         }
         if (ctx->tp > 1) {   // row-split down projection
             int rc = tp_residual(c, ctx->down[l], c->xa, M, l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(),
-                                 c->r_mlp, c->xn);
+                                 c->r_mlp, c->xn, 2 * l + 1);
             if (rc) return rc;
             continue;
         }
@@ -542,9 +564,11 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
 int check_weights(mlxcat_cache *c) {
     mlxcat_ctx *ctx = c->ctx;
     if (!ctx->have_weights) return set_err(ctx, MLXCAT_E_STATE, "weights not loaded");
-    if (ctx->tp > 1 && !ctx->nccl) return set_err(ctx, MLXCAT_E_STATE, "tensor-parallel context not connected");
-    if (ctx->ep > 1 && ctx->cfg.n_experts && !c->ep_connected)
-        return set_err(ctx, MLXCAT_E_STATE, "expert-parallel cache not connected (mlxcat_cache_ep_connect)");
+    if (ctx->tp > 1 && !ctx->nccl && !c->peer_connected)
+        return set_err(ctx, MLXCAT_E_STATE,
+                       "tensor-parallel cache not connected (mlxcat_cache_peer_connect or mlxcat_ctx_tp_connect)");
+    if (ctx->ep > 1 && ctx->cfg.n_experts && !c->peer_connected)
+        return set_err(ctx, MLXCAT_E_STATE, "expert-parallel cache not connected (mlxcat_cache_peer_connect)");
     return MLXCAT_OK;
 }
 
@@ -1159,6 +1183,26 @@ int mlxcat_weights_get_bf16(mlxcat_ctx *ctx, uint32_t id, uint16_t *w) {
     return MLXCAT_OK;
 }
 
+int mlxcat_weights_set_norm(mlxcat_ctx *ctx, uint32_t id, const float *w) {
+    if (!ctx || !w) return MLXCAT_E_INVALID;
+    const mlxcat_model_config &c = ctx->cfg;
+    if (c.kind != MLXCAT_MODEL_TRANSFORMER || !ctx->norms) return set_err(ctx, MLXCAT_E_STATE, "model has no norms");
+    const float *dst = nullptr;
+    int n = c.hidden;
+    const int l = (int)(id / 16u), kind = (int)(id % 16u);
+    if (id == MLXCAT_NORM_FINAL) dst = ctx->final_norm();
+    else if (id < 0x40000000u && l < c.n_layers && kind == 8) dst = ctx->attn_norm(l);
+    else if (id < 0x40000000u && l < c.n_layers && kind == 9) dst = ctx->mlp_norm(l);
+    else if (id < 0x40000000u && l < c.n_layers && kind == 10 && c.qk_norm) { dst = ctx->q_norm(l); n = c.head_dim; }
+    else if (id < 0x40000000u && l < c.n_layers && kind == 11 && c.qk_norm) { dst = ctx->k_norm(l); n = c.head_dim; }
+    if (!dst) return set_err(ctx, MLXCAT_E_INVALID, "unknown norm id 0x%x", id);
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    CK(ctx, cudaMemcpy(const_cast<float *>(dst), w, sizeof(float) * n, cudaMemcpyHostToDevice));
+    for (mlxcat_cache *cc : ctx->caches) drop_graph(cc);
+    return MLXCAT_OK;
+}
+
 int mlxcat_weights_set_table(mlxcat_ctx *ctx, const int32_t *next, int32_t vocab) {
     if (!ctx || !next) return MLXCAT_E_INVALID;
     if (ctx->cfg.kind != MLXCAT_MODEL_TABLE || vocab != ctx->cfg.vocab)
@@ -1243,7 +1287,13 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
         chk(dalloc(A, &c->r_attn, (size_t)Mc));
         chk(dalloc(A, &c->r_mlp, (size_t)Mc));
         chk(dalloc(A, &c->qbuf, (size_t)Mc * Hq * D));
-        if (ctx->tp > 1) chk(dalloc(A, &c->tp_part, (size_t)Mc * H));
+        if (ctx->tp > 1) {
+            chk(dalloc(A, &c->tp_part, (size_t)Mc * H));
+            c->peer_kind = 2;
+            c->peer_cap = Mc;
+            c->tpx_lay = tpx_layout(ctx->tp, Mc, H);
+            c->peer_bytes = c->tpx_lay.total;
+        }
         if (cf.n_experts) {
             const size_t asg = (size_t)Mc * cf.top_k;
             chk(dalloc(A, &c->moe_id, asg * cf.n_layers));
@@ -1257,17 +1307,12 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
             if (ctx->ep > 1) {
                 // per (source, owner) capacity: all of a rank's assignments of one forward
                 const int N = ctx->ep;
-                c->ep_cap = (int)asg;
-                c->ep_lay = ep_layout(N, c->ep_cap, H);
-                const size_t rows = (size_t)N * c->ep_cap;
-                chk(dalloc(A, &c->ep_region, c->ep_lay.total));   // its own allocation: exported whole
-                if (rc == MLXCAT_OK) chk(cudaMemset(c->ep_region, 0, c->ep_lay.total));
-                chk(dalloc(A, &c->ep_peers, (size_t)N));
-                chk(dalloc(A, &c->ep_epoch, 1));
-                chk(dalloc(A, &c->ep_done, 1));
+                c->peer_kind = 1;
+                c->peer_cap = (int)asg;
+                c->ep_lay = ep_layout(N, c->peer_cap, H);
+                c->peer_bytes = c->ep_lay.total;
+                const size_t rows = (size_t)N * c->peer_cap;
                 chk(dalloc(A, &c->ep_lcount, (size_t)N));
-                if (rc == MLXCAT_OK) chk(cudaMemset(c->ep_epoch, 0, sizeof(unsigned)));
-                if (rc == MLXCAT_OK) chk(cudaMemset(c->ep_done, 0, sizeof(unsigned)));
                 if (rc == MLXCAT_OK) chk(cudaMemset(c->ep_lcount, 0, sizeof(int) * N));
                 chk(dalloc(A, &c->ep_act, rows * I));
                 chk(dalloc(A, &c->ep_exp_count, (size_t)cf.n_layers * ctx->epr));
@@ -1276,6 +1321,18 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
                 chk(dalloc(A, &c->ep_w, rows));
                 chk(dalloc(A, &c->ep_ys, rows * H));
             }
+        }
+        if (c->peer_kind) {   // the exported region is its own allocation (mapped whole by the peers)
+            const int N = c->peer_kind == 1 ? ctx->ep : ctx->tp;
+            chk(dalloc(A, &c->peer_region, c->peer_bytes));
+            if (rc == MLXCAT_OK) chk(cudaMemset(c->peer_region, 0, c->peer_bytes));
+            chk(dalloc(A, &c->peer_tab, (size_t)N));
+            chk(dalloc(A, &c->peer_epoch, 1));
+            chk(dalloc(A, &c->peer_done, 1));
+            chk(dalloc(A, &c->peer_sig, 1));
+            if (rc == MLXCAT_OK) chk(cudaMemset(c->peer_epoch, 0, sizeof(unsigned)));
+            if (rc == MLXCAT_OK) chk(cudaMemset(c->peer_done, 0, sizeof(unsigned)));
+            if (rc == MLXCAT_OK) chk(cudaMemset(c->peer_sig, 0, sizeof(unsigned)));
         }
         chk(dalloc(A, &c->rope, (size_t)max_len * (D / 2)));
         if (rc == MLXCAT_OK) chk(rope_table(ctx->inv_freq, D / 2, max_len, c->rope, ctx->stream));
@@ -1346,7 +1403,7 @@ int mlxcat_cache_destroy(mlxcat_cache *c) {
     cudaSetDevice(c->ctx->device);
     cudaStreamSynchronize(c->ctx->stream);
     drop_graph(c);
-    for (char *p : c->ep_opened) cudaIpcCloseMemHandle(p);
+    for (char *p : c->peer_opened) cudaIpcCloseMemHandle(p);
     for (void *p : c->allocs) cudaFree(p);
     if (c->h_tok) cudaFreeHost(c->h_tok);
     if (c->h_n) cudaFreeHost(c->h_n);
@@ -1386,59 +1443,69 @@ int mlxcat_cache_set_token_masks(mlxcat_cache *c, int32_t k, const uint32_t *bit
 }
 
 namespace {
-// The bytes one rank hands to the others for expert parallelism.
-struct EpHandle {
-    char magic[4];              // "MXEP"
+// The bytes one rank hands to the others for expert or tensor parallelism.
+struct PeerHandle {
+    char magic[4];              // "MXPR"
     int32_t version;            // 1
+    int32_t kind;               // 1 = expert parallel, 2 = tensor parallel
     int32_t rank, ranks, cap, hidden;
+    int32_t pad;
     uint64_t bytes;             // size of the exported region
     cudaIpcMemHandle_t ipc;     // the region (its own cudaMalloc allocation)
 };
-static_assert(sizeof(EpHandle) <= MLXCAT_EP_HANDLE_BYTES, "expert-parallel handle too large");
+static_assert(sizeof(PeerHandle) <= MLXCAT_PEER_HANDLE_BYTES, "peer handle too large");
+
+int group_rank(const mlxcat_ctx *ctx) { return ctx->ep > 1 ? ctx->ep_rank : ctx->tp_rank; }
+int group_size(const mlxcat_ctx *ctx) { return ctx->ep > 1 ? ctx->ep : ctx->tp; }
 }  // namespace
 
-int mlxcat_cache_ep_handle(mlxcat_cache *c, uint8_t out[MLXCAT_EP_HANDLE_BYTES]) {
+int mlxcat_cache_peer_handle(mlxcat_cache *c, uint8_t out[MLXCAT_PEER_HANDLE_BYTES]) {
     if (!c || !out) return c ? set_err(c->ctx, MLXCAT_E_INVALID, "null handle buffer") : MLXCAT_E_INVALID;
     mlxcat_ctx *ctx = c->ctx;
-    if (ctx->ep <= 1 || !c->ep_region) return set_err(ctx, MLXCAT_E_STATE, "cache is not expert-parallel");
+    if (!c->peer_region) return set_err(ctx, MLXCAT_E_STATE, "cache is neither expert- nor tensor-parallel");
     CK(ctx, cudaSetDevice(ctx->device));
-    EpHandle h;
+    PeerHandle h;
     std::memset(&h, 0, sizeof h);
-    std::memcpy(h.magic, "MXEP", 4);
+    std::memcpy(h.magic, "MXPR", 4);
     h.version = 1;
-    h.rank = ctx->ep_rank; h.ranks = ctx->ep; h.cap = c->ep_cap; h.hidden = ctx->cfg.hidden;
-    h.bytes = c->ep_lay.total;
-    CK(ctx, cudaIpcGetMemHandle(&h.ipc, c->ep_region));
-    std::memset(out, 0, MLXCAT_EP_HANDLE_BYTES);
+    h.kind = c->peer_kind;
+    h.rank = group_rank(ctx); h.ranks = group_size(ctx); h.cap = c->peer_cap; h.hidden = ctx->cfg.hidden;
+    h.bytes = c->peer_bytes;
+    CK(ctx, cudaIpcGetMemHandle(&h.ipc, c->peer_region));
+    std::memset(out, 0, MLXCAT_PEER_HANDLE_BYTES);
     std::memcpy(out, &h, sizeof h);
     return MLXCAT_OK;
 }
 
-int mlxcat_cache_ep_connect(mlxcat_cache *c, const uint8_t *handles) {
+int mlxcat_cache_peer_connect(mlxcat_cache *c, const uint8_t *handles) {
     if (!c || !handles) return c ? set_err(c->ctx, MLXCAT_E_INVALID, "null handles") : MLXCAT_E_INVALID;
     mlxcat_ctx *ctx = c->ctx;
-    if (ctx->ep <= 1 || !c->ep_region) return set_err(ctx, MLXCAT_E_STATE, "cache is not expert-parallel");
-    if (c->ep_connected) return set_err(ctx, MLXCAT_E_STATE, "cache already connected");
+    if (!c->peer_region) return set_err(ctx, MLXCAT_E_STATE, "cache is neither expert- nor tensor-parallel");
+    if (c->peer_connected) return set_err(ctx, MLXCAT_E_STATE, "cache already connected");
     CK(ctx, cudaSetDevice(ctx->device));
-    const int N = ctx->ep;
-    std::vector<EpHandle> hs(N);
+    const int N = group_size(ctx), me = group_rank(ctx);
+    std::vector<PeerHandle> hs(N);
     for (int p = 0; p < N; ++p) {
-        std::memcpy(&hs[p], handles + (size_t)p * MLXCAT_EP_HANDLE_BYTES, sizeof(EpHandle));
-        const EpHandle &h = hs[p];
-        if (std::memcmp(h.magic, "MXEP", 4) || h.version != 1)
-            return set_err(ctx, MLXCAT_E_INVALID, "handle %d is not an expert-parallel cache handle", p);
+        std::memcpy(&hs[p], handles + (size_t)p * MLXCAT_PEER_HANDLE_BYTES, sizeof(PeerHandle));
+        const PeerHandle &h = hs[p];
+        if (std::memcmp(h.magic, "MXPR", 4) || h.version != 1 || h.kind != c->peer_kind)
+            return set_err(ctx, MLXCAT_E_INVALID, "handle %d is not a %s cache handle", p,
+                           c->peer_kind == 1 ? "expert-parallel" : "tensor-parallel");
         if (h.rank != p || h.ranks != N)
             return set_err(ctx, MLXCAT_E_INVALID, "handle %d is rank %d of %d (want rank %d of %d, in rank order)", p,
                            h.rank, h.ranks, p, N);
-        if (h.cap != c->ep_cap || h.hidden != ctx->cfg.hidden || h.bytes != c->ep_lay.total)
+        if (h.cap != c->peer_cap || h.hidden != ctx->cfg.hidden || h.bytes != c->peer_bytes)
             return set_err(ctx, MLXCAT_E_INVALID,
                            "rank %d's cache has another shape (capacity %d rows, hidden %d; this rank: %d, %d): "
                            "every rank's cache needs the same max_rows",
-                           p, h.cap, h.hidden, c->ep_cap, ctx->cfg.hidden);
+                           p, h.cap, h.hidden, c->peer_cap, ctx->cfg.hidden);
     }
+    if (c->peer_kind == 2 && ctx->cfg.hidden % (128 * N))
+        return set_err(ctx, MLXCAT_E_INVALID, "the fused allreduce needs hidden (%d) to be a multiple of 128 x %d ranks",
+                       ctx->cfg.hidden, N);
     std::vector<char *> peers(N, nullptr), opened;
     for (int p = 0; p < N; ++p) {
-        if (p == ctx->ep_rank) { peers[p] = c->ep_region; continue; }
+        if (p == me) { peers[p] = c->peer_region; continue; }
         void *q = nullptr;
         const cudaError_t e = cudaIpcOpenMemHandle(&q, hs[p].ipc, cudaIpcMemLazyEnablePeerAccess);
         if (e != cudaSuccess) {
@@ -1448,13 +1515,14 @@ int mlxcat_cache_ep_connect(mlxcat_cache *c, const uint8_t *handles) {
         peers[p] = static_cast<char *>(q);
         opened.push_back(peers[p]);
     }
-    const cudaError_t e = cudaMemcpy(c->ep_peers, peers.data(), sizeof(char *) * N, cudaMemcpyHostToDevice);
+    const cudaError_t e = cudaMemcpy(c->peer_tab, peers.data(), sizeof(char *) * N, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         for (char *o : opened) cudaIpcCloseMemHandle(o);
         return set_err(ctx, MLXCAT_E_CUDA, "peer table upload: %s", cudaGetErrorString(e));
     }
-    c->ep_opened = opened;
-    c->ep_connected = true;
+    c->peer_opened = opened;
+    c->peer_connected = true;
+    drop_graph(c);   // a captured step would still use the other allreduce
     return MLXCAT_OK;
 }
 

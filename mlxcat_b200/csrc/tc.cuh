@@ -20,6 +20,34 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
+// Flags in another GPU's memory (NVLink peer maps): a release store after the
+// payload's stores, an acquire load before the payload's loads.
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Bounded wait of one thread for *f == want (written by a peer GPU): false and
+// *err = code after limit_ns, or at once when *err is already set.
+__device__ __forceinline__ bool peer_flag_wait(const unsigned *f, unsigned want, int *err, int code,
+                                               uint64_t limit_ns) {
+    if (*reinterpret_cast<volatile int *>(err)) return false;
+    if (ld_acquire_sys(f) == want) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (ld_acquire_sys(f) == want) return true;
+        if (*reinterpret_cast<volatile int *>(err)) return false;
+        if (global_ns() - t0 > limit_ns) {
+            atomicExch(err, code);
+            return false;
+        }
+        __nanosleep(200);
+    }
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }

@@ -246,6 +246,18 @@ class Context:
         self.check(self.L.mlxcat_weights_get_bf16(self.h, tensor_id, w.ctypes.data))
         return w
 
+    NORM_FINAL = 0xFFFF0002
+
+    @staticmethod
+    def norm_id(layer: int, kind: int) -> int:
+        """id of an RMSNorm weight: kind 0 input_layernorm, 1 post_attention_layernorm,
+        2 q_norm, 3 k_norm"""
+        return layer * 16 + 8 + kind
+
+    def set_norm(self, norm_id: int, w):
+        a = np.ascontiguousarray(w, dtype=np.float32)
+        self.check(self.L.mlxcat_weights_set_norm(self.h, norm_id, a.ctypes.data))
+
     def get_q4(self, tensor_id: int, N: int, K: int):
         wq = np.zeros((N, K // 8), np.uint32)
         s = np.zeros((N, K // 64), np.uint16)
@@ -295,21 +307,21 @@ class BatchKVCache:
         self.h = h
         ctx._caches.add(self)
 
-    EP_HANDLE_BYTES = 128
+    PEER_HANDLE_BYTES = 128
 
-    def ep_handle(self) -> bytes:
-        """This rank's expert-parallel handle (mlxcat_cache_ep_handle): the
-        bytes every other rank needs to map this cache's exchange region."""
-        buf = (C.c_uint8 * self.EP_HANDLE_BYTES)()
-        self.ctx.check(self.L.mlxcat_cache_ep_handle(self.h, buf))
+    def peer_handle(self) -> bytes:
+        """This rank's expert- or tensor-parallel handle (mlxcat_cache_peer_handle):
+        the bytes every other rank needs to map this cache's exchange region."""
+        buf = (C.c_uint8 * self.PEER_HANDLE_BYTES)()
+        self.ctx.check(self.L.mlxcat_cache_peer_handle(self.h, buf))
         return bytes(buf)
 
-    def ep_connect(self, handles):
+    def peer_connect(self, handles):
         """Map every rank's region (handles: one per rank, in rank order)."""
-        if any(len(h) != self.EP_HANDLE_BYTES for h in handles):
-            raise ValueError(f"expert-parallel handles are {self.EP_HANDLE_BYTES} bytes each")
-        buf = (C.c_uint8 * (self.EP_HANDLE_BYTES * len(handles))).from_buffer_copy(b"".join(handles))
-        self.ctx.check(self.L.mlxcat_cache_ep_connect(self.h, buf))
+        if any(len(h) != self.PEER_HANDLE_BYTES for h in handles):
+            raise ValueError(f"peer handles are {self.PEER_HANDLE_BYTES} bytes each")
+        buf = (C.c_uint8 * (self.PEER_HANDLE_BYTES * len(handles))).from_buffer_copy(b"".join(handles))
+        self.ctx.check(self.L.mlxcat_cache_peer_connect(self.h, buf))
 
     def set_token_masks(self, k: int, allowed):
         """Grammar masks for the next accept(): allowed maps (row, position) to

@@ -461,7 +461,8 @@ struct orc_model {
     q4_t *lin;                   /* n_layers * 7 */
     uint16_t *router;            /* MoE: bf16 [n_layers][n_experts][hidden] */
     q4_t *experts;               /* MoE: [n_layers][n_experts][3] gate, up, down */
-    float *ones;                 /* norm weights (all ones) */
+    float *norms;                /* RMSNorm weights (ones until set): attn [L][H], mlp [L][H],
+                                    final [H], q [L][D], k [L][D] */
     float *inv_freq;
 };
 
@@ -534,9 +535,9 @@ orc_model *orc_model_empty(const orc_config *cfg) {
             q4_alloc(&m->experts[i * 3 + 2], cfg->hidden, cfg->intermediate);
         }
     }
-    int big = cfg->hidden > cfg->head_dim ? cfg->hidden : cfg->head_dim;
-    m->ones = (float *)malloc(sizeof(float) * (size_t)big);
-    for (int i = 0; i < big; ++i) m->ones[i] = 1.0f;
+    const size_t nn = (size_t)(2 * cfg->n_layers + 1) * cfg->hidden + (size_t)2 * cfg->n_layers * cfg->head_dim;
+    m->norms = (float *)malloc(sizeof(float) * nn);
+    for (size_t i = 0; i < nn; ++i) m->norms[i] = 1.0f;
     m->inv_freq = (float *)malloc(sizeof(float) * (size_t)(cfg->head_dim / 2));
     for (int i = 0; i < cfg->head_dim / 2; ++i)
         m->inv_freq[i] =
@@ -610,6 +611,32 @@ void orc_router_synth(uint64_t seed, uint32_t tensor_id, float stddev, int E, in
             const uint64_t idx = (uint64_t)e * (uint64_t)H + (uint64_t)k;
             w[(size_t)e * H + k] = orc_f32_to_bf16(orc_normal(seed, tensor_id, idx) * stddev);
         }
+}
+
+/* RMSNorm weight vectors of the model (the layer norms, the final norm, the
+ * Qwen3 per-head q/k norms); id = layer*16 + {8 input, 9 post-attention,
+ * 10 q, 11 k}, 0xFFFF0002 final. */
+static float *norm_ptr(orc_model *m, uint32_t id, int *n) {
+    const orc_config *c = &m->cfg;
+    const int L = c->n_layers, H = c->hidden, D = c->head_dim;
+    if (id == 0xFFFF0002u) { *n = H; return m->norms + (size_t)2 * L * H; }
+    const int l = (int)(id / 16u), kind = (int)(id % 16u);
+    if (id >= 0x40000000u || l >= L) return NULL;
+    switch (kind) {
+    case 8: *n = H; return m->norms + (size_t)l * H;
+    case 9: *n = H; return m->norms + (size_t)(L + l) * H;
+    case 10: *n = D; return c->qk_norm ? m->norms + (size_t)(2 * L + 1) * H + (size_t)l * D : NULL;
+    case 11: *n = D; return c->qk_norm ? m->norms + (size_t)(2 * L + 1) * H + (size_t)(L + l) * D : NULL;
+    default: return NULL;
+    }
+}
+
+int orc_model_set_norm(orc_model *m, uint32_t id, const float *w) {
+    int n = 0;
+    float *p = m->is_table ? NULL : norm_ptr(m, id, &n);
+    if (!p) return -1;
+    memcpy(p, w, sizeof(float) * (size_t)n);
+    return 0;
 }
 
 int orc_model_set_router(orc_model *m, int layer, const uint16_t *w) {
@@ -703,7 +730,7 @@ void orc_model_free(orc_model *m) {
             free(m->experts);
             free(m->router);
         }
-        free(m->ones);
+        free(m->norms);
         free(m->inv_freq);
     }
     free(m->table_next);
@@ -968,21 +995,25 @@ void orc_forward(const orc_model *m, orc_kv *kv, int M, const int32_t *tokens,
                     m->embed.b + (size_t)tokens[i] * (H / GS), H, h + (size_t)i * H);
 
     const float scale = 1.0f / sqrtf((float)D);
+    const int L = c->n_layers;
     for (int l = 0; l < c->n_layers; ++l) {
         const q4_t *W = m->lin + l * 7;
-        for (int i = 0; i < M; ++i) rmsnorm(h + (size_t)i * H, m->ones, H, c->rms_eps, x + (size_t)i * H);
+        const float *w_attn = m->norms + (size_t)l * H, *w_mlp = m->norms + (size_t)(L + l) * H;
+        const float *w_q = m->norms + (size_t)(2 * L + 1) * H + (size_t)l * D;
+        const float *w_k = m->norms + (size_t)(2 * L + 1) * H + (size_t)(L + l) * D;
+        for (int i = 0; i < M; ++i) rmsnorm(h + (size_t)i * H, w_attn, H, c->rms_eps, x + (size_t)i * H);
         lin(&W[ORC_T_Q], x, M, q);
         lin(&W[ORC_T_K], x, M, k);
         lin(&W[ORC_T_V], x, M, v);
         for (int i = 0; i < M; ++i) {
             for (int hh = 0; hh < Hq; ++hh) {
                 float *qh = q + ((size_t)i * Hq + hh) * D;
-                if (c->qk_norm) rmsnorm(qh, m->ones, D, c->rms_eps, qh);
+                if (c->qk_norm) rmsnorm(qh, w_q, D, c->rms_eps, qh);
                 rope(qh, D, pos[i], m->inv_freq);
             }
             for (int hh = 0; hh < Hkv; ++hh) {
                 float *kh = k + ((size_t)i * Hkv + hh) * D;
-                if (c->qk_norm) rmsnorm(kh, m->ones, D, c->rms_eps, kh);
+                if (c->qk_norm) rmsnorm(kh, w_k, D, c->rms_eps, kh);
                 rope(kh, D, pos[i], m->inv_freq);
                 memcpy(kv->k + kv_off(kv, rows[i], l, hh, pos[i]), kh, sizeof(float) * D);
                 memcpy(kv->v + kv_off(kv, rows[i], l, hh, pos[i]),
@@ -1017,7 +1048,7 @@ void orc_forward(const orc_model *m, orc_kv *kv, int M, const int32_t *tokens,
         }
         lin(&W[ORC_T_O], att, M, o);
         for (size_t i = 0; i < (size_t)M * H; ++i) h[i] += o[i];
-        for (int i = 0; i < M; ++i) rmsnorm(h + (size_t)i * H, m->ones, H, c->rms_eps, x + (size_t)i * H);
+        for (int i = 0; i < M; ++i) rmsnorm(h + (size_t)i * H, w_mlp, H, c->rms_eps, x + (size_t)i * H);
         if (c->n_experts) {
             moe_block(m, l, x, M, h);
             continue;
@@ -1032,7 +1063,8 @@ void orc_forward(const orc_model *m, orc_kv *kv, int M, const int32_t *tokens,
         for (size_t i = 0; i < (size_t)M * H; ++i) h[i] += o[i];
     }
     if (logits) {
-        for (int i = 0; i < M; ++i) rmsnorm(h + (size_t)i * H, m->ones, H, c->rms_eps, x + (size_t)i * H);
+        const float *w_final = m->norms + (size_t)2 * L * H;
+        for (int i = 0; i < M; ++i) rmsnorm(h + (size_t)i * H, w_final, H, c->rms_eps, x + (size_t)i * H);
         lin(c->tie_embeddings ? &m->embed : &m->lm_head, x, M, logits);
     }
     free(h); free(x); free(q); free(k); free(v); free(att); free(g); free(u); free(o);

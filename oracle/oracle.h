@@ -121,6 +121,9 @@ float orc_bf16_to_f32(uint16_t h);
 void orc_router_synth(uint64_t seed, uint32_t tensor_id, float stddev, int E, int H,
                       uint16_t *w);
 int orc_model_set_router(orc_model *m, int layer, const uint16_t *w);
+/* RMSNorm weights: id = layer*16 + {8 input, 9 post-attention, 10 q, 11 k},
+ * 0xFFFF0002 final (hidden or head_dim floats); -1 for an unknown id */
+int orc_model_set_norm(orc_model *m, uint32_t id, const float *w);
 /* MoE routing of one token (x: normalised MLP input, fp32): bf16 router
  * logits, fp32 softmax, top-k (ties to the lower expert index), optional
  * renormalisation.  Writes ids[k], weights[k]; returns the gap between the

@@ -136,6 +136,8 @@ def lib():
     L.orc_router_synth.argtypes = [C.c_uint64, C.c_uint32, C.c_float, C.c_int, C.c_int, u16p]
     L.orc_model_set_router.argtypes = [C.c_void_p, C.c_int, u16p]
     L.orc_model_set_router.restype = C.c_int
+    L.orc_model_set_norm.argtypes = [C.c_void_p, C.c_uint32, f32p]
+    L.orc_model_set_norm.restype = C.c_int
     L.orc_moe_route.argtypes = [C.c_void_p, C.c_int, f32p, i32p, f32p]
     L.orc_moe_route.restype = C.c_float
     L.orc_moe_min_margin.argtypes = [C.c_int]
@@ -368,6 +370,12 @@ class Model:
                                     _ptr(np.ascontiguousarray(b), C.c_uint16))
         if rc != 0:
             raise KeyError(tensor_id)
+
+    def set_norm(self, norm_id: int, w):
+        """RMSNorm weights (id layer*16 + {8 input, 9 post-attention, 10 q,
+        11 k}, 0xFFFF0002 final)"""
+        if lib().orc_model_set_norm(self.h, norm_id, _ptr(np.ascontiguousarray(w, np.float32), C.c_float)):
+            raise KeyError(norm_id)
 
     def set_router(self, layer: int, w):
         if lib().orc_model_set_router(self.h, layer, _ptr(np.ascontiguousarray(w, np.uint16), C.c_uint16)):

@@ -3,7 +3,7 @@ configuration) on two GPUs, one process per GPU, against the one-GPU forward.
 
 Each rank holds half of every layer's experts and runs its own rows; every MoE
 layer stores each routed operand row into the owning rank's memory over
-NVLink and the owner stores the scaled expert output back (mlxcat_cache_ep_*).
+NVLink and the owner stores the scaled expert output back (mlxcat_cache_peer_*).
 The expert kernels compute every assignment's output independently of which
 other tokens share its tile, and the results travel in fp32, so each rank's
 first tokens, drafts, per-layer routing and verify logits must equal a
@@ -65,7 +65,7 @@ def rank_main(rank, world, inbox, outboxes, results):
         spec = M.SpeculativeDecodingConfiguration(True, K, 3, 8, A.ACCEPT_PREFIX)
         ps = prompts(rank)
         cache = M.BatchKVCache(ctx, len(ps), MAX_LEN)
-        mine = cache.ep_handle()
+        mine = cache.peer_handle()
         for r in range(world):
             if r != rank:
                 outboxes[r].put((rank, mine))
@@ -73,7 +73,7 @@ def rank_main(rank, world, inbox, outboxes, results):
         while len(handles) < world:
             r, h = inbox.get(timeout=60)
             handles[r] = h
-        cache.ep_connect([handles[r] for r in range(world)])
+        cache.peer_connect([handles[r] for r in range(world)])
         out = run_rows(cache, ps, spec)
         cache.close()
         ctx.close()

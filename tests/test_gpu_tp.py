@@ -4,9 +4,12 @@ whole model.
 
 Each rank holds its slice of every linear (q/k/v heads and gate/up rows
 column-split, o/down inputs row-split), synthesised from the full tensor's
-weight stream, so the slices together are the oracle's weights; one NCCL
-allreduce follows the attention block and one the MLP block.  Both ranks must
-produce the same logits and tokens, and the logits must match the oracle
+weight stream, so the slices together are the oracle's weights; one
+allreduce follows the attention block and one the MLP block -- either NCCL
+(mlxcat_ctx_tp_connect) or the fused scatter / reduce / gather over the
+caches' peer regions (mlxcat_cache_peer_connect: the row-split projection
+writes its partial sums straight into the owning rank's memory).  Both ranks
+must produce the same logits and tokens, and the logits must match the oracle
 within the verify tolerance.  Needs two GPUs (skipped otherwise)."""
 import multiprocessing as mp
 import os
@@ -36,22 +39,33 @@ def prompts():
     return [[int(t) for t in np.random.default_rng(40 + r).integers(0, 4096, n)] for r, n in enumerate((90, 57))]
 
 
-def rank_main(rank, world, ids, results):
+def rank_main(rank, world, mode, boxes, results):
     try:
         os.environ["NCCL_NVLS_ENABLE"] = "0"
         cfg = M.ModelConfig(**TP_SMALL, name="tp-small", tp_size=world, tp_rank=rank)
         ctx = M.Context(cfg, rank)
-        if rank == 0:
-            uid = M.Context.tp_unique_id()
-            for _ in range(world - 1):
-                ids.put(uid)
-        else:
-            uid = ids.get(timeout=60)
-        ctx.tp_connect(uid)
+        if mode == "nccl":
+            if rank == 0:
+                uid = M.Context.tp_unique_id()
+                for r in range(1, world):
+                    boxes[r].put((0, uid))
+            else:
+                uid = boxes[rank].get(timeout=60)[1]
+            ctx.tp_connect(uid)
         ctx.synth_weights(SEED)
         spec = M.SpeculativeDecodingConfiguration(True, K, 3, 8, A.ACCEPT_PREFIX)
         ps = prompts()
         cache = M.BatchKVCache(ctx, len(ps), 256)
+        if mode == "peer":
+            mine = cache.peer_handle()
+            for r in range(world):
+                if r != rank:
+                    boxes[r].put((rank, mine))
+            handles = {rank: mine}
+            while len(handles) < world:
+                r, h = boxes[rank].get(timeout=60)
+                handles[r] = h
+            cache.peer_connect([handles[r] for r in range(world)])
         firsts = [cache.insert_row(r, p, 16, M.SamplingParameters()) for r, p in enumerate(ps)]
         drafts = cache.draft(spec)
         logits = cache.verify_forward(spec)
@@ -64,11 +78,12 @@ def rank_main(rank, world, ids, results):
         results.put((rank, "error", repr(e), None, None))
 
 
-def test_tensor_parallel_verify_matches_oracle():
+@pytest.mark.parametrize("mode", ["nccl", "peer"])
+def test_tensor_parallel_verify_matches_oracle(mode):
     world = 2
     ctx_mp = mp.get_context("spawn")
-    ids, results = ctx_mp.Queue(), ctx_mp.Queue()
-    procs = [ctx_mp.Process(target=rank_main, args=(r, world, ids, results)) for r in range(world)]
+    boxes, results = [ctx_mp.Queue() for _ in range(world)], ctx_mp.Queue()
+    procs = [ctx_mp.Process(target=rank_main, args=(r, world, mode, boxes, results)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
