@@ -307,6 +307,17 @@ MLXCAT_API int mlxcat_op_attention(const uint16_t *q, const uint16_t *k_cache, c
                         int32_t qg, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                         uint16_t *out, void *workspace, size_t workspace_bytes, void *stream);
 
+/* The same attention for a prompt chunk (the admission prefill,
+ * Scheduler.swift:599-668), on the tensor cores: n tokens of cache row `row`
+ * at positions s0..s0+n-1, each seeing keys 0..its position.  q [n][n_heads *
+ * head_dim], out [n][n_heads * head_dim] fp16; caches as above with `rows`
+ * rows; head_dim 128.  err: a device int the kernel sets when a pipeline wait
+ * timed out (0 otherwise).  No workspace. */
+MLXCAT_API int mlxcat_op_prefill_attention(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                                           int32_t rows, int32_t max_len, int32_t row, int32_t s0, int32_t n,
+                                           int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, uint16_t *out,
+                                           int32_t *err, void *stream);
+
 /* Sparse MoE MLP: the SwitchGLU block of mlx-swift-lm's Qwen3-MoE model
  * (un-vendored) that the verify forward (BatchGenerator.swift:900) runs in
  * every layer of a MoE model, on an already normalised input x [M][hidden]

@@ -127,6 +127,8 @@ PROTOTYPES = {
     "mlxcat_op_q4_linear_workspace": (_sz, [_i32, _i32, _i32]),
     "mlxcat_op_q4_linear": (C.c_int, [_vp, _vp, _vp, _i32, _i32, _vp, _i32, _vp, _vp, _sz, _vp]),
     "mlxcat_op_attention_workspace": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32]),
+    "mlxcat_op_prefill_attention": (C.c_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp,
+                                              _vp, _vp]),
     "mlxcat_op_attention": (C.c_int, [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
                                       _vp, _vp, _sz, _vp]),
     "mlxcat_op_attention_noalloc": (C.c_int, [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32,

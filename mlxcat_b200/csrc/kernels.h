@@ -148,11 +148,21 @@ struct KVLayer {
     int max_len = 0;
 };
 
+// ---- prefill attention on tcgen05 (fa_tc.cu) ---------------------------------
+// Causal attention of n prompt tokens of cache row `row` at positions s0..s0+n-1
+// over keys 0..s0+n-1: q [q_rows >= n][Hq * D] fp16, out [n][Hq * D] fp16.
+bool fa_prefill_supported(int head_dim);
+cudaError_t fa_prefill(const __half *q, int q_rows, const KVLayer &kv, int rows, int row, int s0, int n, int Hq,
+                       int Hkv, int D, __half *out, int *err, cudaStream_t st);
+
 // ---- dense prefill path (prefill.cu): row-major activations around gemm_tc ----
 // h[m] = dequantised embedding row of tok[m]
 cudaError_t prefill_embed(const Q4Weight &embed, const int32_t *tok, int n, float *h, cudaStream_t st);
 // x[m] = fp16(h[m] * rstd(h[m]) * w)
 cudaError_t prefill_rmsnorm(const float *h, int n, int H, const float *w, float eps, __half *x, cudaStream_t st);
+// h += y, then x = fp16(rmsnorm(h) * w) (the residual step after O and down)
+cudaError_t prefill_add_rmsnorm(float *h, const float *y, int n, int H, const float *w, float eps, __half *x,
+                                cudaStream_t st);
 // y [n][(Hq + 2 Hkv) D] fp32 -> q/k norm (optional), RoPE from the (cos, sin)
 // table; q to qbuf [n][Hq][D], k/v to the cache of `row` at tpos[m]
 cudaError_t prefill_qkv(const float *y, int n, int n_heads, int n_kv, int D, const float *q_norm,

@@ -6,8 +6,10 @@
 // by the reference's admission prefill, Scheduler.swift:670-1016): embedding,
 // pre-norm RMSNorm, q|k|v with per-head q/k RMSNorm (Qwen3) and rotate-half
 // RoPE from the cache's (cos, sin) table, K/V appended to the cache at each
-// token's position.  The residual adds and the SwiGLU are fused into the GEMM
-// epilogues.
+// token's position.  The SwiGLU is fused into the gate/up GEMM's epilogue; the
+// residual adds after the O and down projections into the RMSNorm that
+// follows them (pf_add_rmsnorm_kernel: the GEMM stores its output at full
+// rate, the add is two streamed passes over the row).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -54,6 +56,37 @@ __global__ void pf_rmsnorm_kernel(const float *__restrict__ h, int H, const floa
     ss = pf_block_sum(ss, sh);
     const float r = 1.0f / sqrtf(ss / (float)H + eps);
     for (int k = threadIdx.x; k < H; k += blockDim.x) x[(size_t)m * H + k] = __float2half_rn(hm[k] * r * nw[k]);
+}
+
+// The residual step after the O and down projections: h[m] += y[m] (the
+// projection's fp32 output), then x[m] = fp16(h[m] * rstd * w).  One CTA per
+// token, 16-byte accesses; the second pass re-reads the row just written (L1).
+__global__ void pf_add_rmsnorm_kernel(float *__restrict__ h, const float *__restrict__ y, int H,
+                                      const float *__restrict__ nw, float eps, __half *__restrict__ x) {
+    __shared__ float sh[32];
+    const int m = blockIdx.x, H4 = H / 4;
+    float4 *hm = reinterpret_cast<float4 *>(h + (size_t)m * H);
+    const float4 *ym = reinterpret_cast<const float4 *>(y + (size_t)m * H);
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < H4; k += blockDim.x) {
+        float4 a = hm[k];
+        const float4 b = ym[k];
+        a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+        hm[k] = a;
+        ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+    }
+    ss = pf_block_sum(ss, sh);
+    const float r = 1.0f / sqrtf(ss / (float)H + eps);
+    const float4 *w4 = reinterpret_cast<const float4 *>(nw);
+    uint2 *xm = reinterpret_cast<uint2 *>(x + (size_t)m * H);
+    for (int k = threadIdx.x; k < H4; k += blockDim.x) {
+        const float4 a = hm[k], w = w4[k];
+        __half2 lo = __floats2half2_rn(a.x * r * w.x, a.y * r * w.y), hi = __floats2half2_rn(a.z * r * w.z, a.w * r * w.w);
+        uint2 o;
+        o.x = *reinterpret_cast<uint32_t *>(&lo);
+        o.y = *reinterpret_cast<uint32_t *>(&hi);
+        xm[k] = o;
+    }
 }
 
 // q|k|v rows of one token: per-head q/k RMSNorm, RoPE, q -> qbuf [m][Hq][D],
@@ -135,6 +168,13 @@ cudaError_t prefill_embed(const Q4Weight &embed, const int32_t *tok, int n, floa
 
 cudaError_t prefill_rmsnorm(const float *h, int n, int H, const float *w, float eps, __half *x, cudaStream_t st) {
     pf_rmsnorm_kernel<<<n, PF_TPB, 0, st>>>(h, H, w, eps, x);
+    return cudaGetLastError();
+}
+
+cudaError_t prefill_add_rmsnorm(float *h, const float *y, int n, int H, const float *w, float eps, __half *x,
+                                cudaStream_t st) {
+    if (H % 4) return cudaErrorInvalidValue;
+    pf_add_rmsnorm_kernel<<<n, PF_TPB, 0, st>>>(h, y, H, w, eps, x);
     return cudaGetLastError();
 }
 

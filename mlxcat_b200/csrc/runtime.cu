@@ -695,7 +695,7 @@ int ensure_prefill(mlxcat_cache *c) {
     CK(ctx, dalloc(A, &pf.act, P * I));
     CK(ctx, dalloc(A, &pf.q, P * Hq * D));
     CK(ctx, dalloc(A, &pf.h, P * H));
-    CK(ctx, dalloc(A, &pf.y, P * Nqkv));
+    CK(ctx, dalloc(A, &pf.y, P * std::max(Nqkv, (size_t)H)));   // q|k|v, or the O / down output
     CK(ctx, dalloc(A, &pf.tok, P));
     CK(ctx, dalloc(A, &pf.trow, P));
     CK(ctx, dalloc(A, &pf.tpos, P));
@@ -735,18 +735,22 @@ int prefill_dense(mlxcat_cache *c, int row, const int32_t *tok, int s0, int n, b
         LK(ctx, gemm_tc(pf.wdq, Nqkv, H, pf.x, n, GEMM_STORE, pf.y, Nqkv, sm, c->err, st));
         LK(ctx, prefill_qkv(pf.y, n, Hq, Hkv, D, ctx->q_norm(l), ctx->k_norm(l), eps, c->rope, row, pf.tpos, pf.q,
                             kv, st));
-        ctx->launches++;   // attention is two kernels; its output reuses x (row-major [n][Hq*D])
-        LK(ctx, attention(pf.q, kv, pf.trow, pf.tpos, n, pf.qg, Hq, Hkv, D, pf.key_chunk, 1, pf.attn, pf.x, false,
-                          n, st, false));
+        if (fa_prefill_supported(D)) {   // tensor-core flash attention; output reuses x (row-major [n][Hq*D])
+            LK(ctx, fa_prefill(pf.q, DENSE_CHUNK, kv, c->rows, row, s0, n, Hq, Hkv, D, pf.x, c->err, st));
+        } else {
+            ctx->launches++;   // split-K attention is two kernels
+            LK(ctx, attention(pf.q, kv, pf.trow, pf.tpos, n, pf.qg, Hq, Hkv, D, pf.key_chunk, 1, pf.attn, pf.x,
+                              false, n, st, false));
+        }
         LK(ctx, dequant_q4(ctx->o[l].view(), pf.wdq, st));
-        LK(ctx, gemm_tc(pf.wdq, H, Hq * D, pf.x, n, GEMM_ADD, pf.h, H, sm, c->err, st));
-        LK(ctx, prefill_rmsnorm(pf.h, n, H, ctx->mlp_norm(l), eps, pf.x, st));
+        LK(ctx, gemm_tc(pf.wdq, H, Hq * D, pf.x, n, GEMM_STORE, pf.y, H, sm, c->err, st));
+        LK(ctx, prefill_add_rmsnorm(pf.h, pf.y, n, H, ctx->mlp_norm(l), eps, pf.x, st));
         LK(ctx, dequant_q4(ctx->gu[l].view(), pf.wdq, st));
         LK(ctx, gemm_tc(pf.wdq, 2 * I, H, pf.x, n, GEMM_SWIGLU, pf.act, I, sm, c->err, st));
         LK(ctx, dequant_q4(ctx->down[l].view(), pf.wdq, st));
-        LK(ctx, gemm_tc(pf.wdq, H, I, pf.act, n, GEMM_ADD, pf.h, H, sm, c->err, st));
-        LK(ctx, prefill_rmsnorm(pf.h, n, H, l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(), eps, pf.x,
-                                st));
+        LK(ctx, gemm_tc(pf.wdq, H, I, pf.act, n, GEMM_STORE, pf.y, H, sm, c->err, st));
+        LK(ctx, prefill_add_rmsnorm(pf.h, pf.y, n, H, l + 1 < L ? ctx->attn_norm(l + 1) : ctx->final_norm(), eps,
+                                    pf.x, st));
     }
     if (logits) {   // the last position through the q4 head (one token: the GEMV-shaped kernel)
         LK(ctx, prefill_to_blocked(pf.x + (size_t)(n - 1) * H, H, c->xn, c->m_cap, st));
@@ -2012,6 +2016,22 @@ int mlxcat_op_attention(const uint16_t *q, const uint16_t *k_cache, const uint16
                               KEY_CHUNK, splits, sc, reinterpret_cast<__half *>(out), false, M,
                               (cudaStream_t)stream);
     if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "attention: %s", cudaGetErrorString(e));
+    return MLXCAT_OK;
+}
+
+int mlxcat_op_prefill_attention(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache, int32_t rows,
+                                int32_t max_len, int32_t row, int32_t s0, int32_t n, int32_t n_heads, int32_t n_kv,
+                                int32_t D, uint16_t *out, int32_t *err, void *stream) {
+    if (!q || !k_cache || !v_cache || !out || !err || n <= 0 || n_kv <= 0 || n_heads % n_kv || rows <= 0 ||
+        row < 0 || row >= rows || s0 < 0 || s0 + n > max_len || !fa_prefill_supported(D))
+        return op_err(MLXCAT_E_INVALID, "bad prefill attention arguments (head_dim must be 128)");
+    KVLayer kv;
+    kv.k = const_cast<__half *>(reinterpret_cast<const __half *>(k_cache));
+    kv.v = const_cast<__half *>(reinterpret_cast<const __half *>(v_cache));
+    kv.max_len = max_len;
+    const cudaError_t e = fa_prefill(reinterpret_cast<const __half *>(q), n, kv, rows, row, s0, n, n_heads, n_kv, D,
+                                     reinterpret_cast<__half *>(out), err, (cudaStream_t)stream);
+    if (e != cudaSuccess) return op_err(MLXCAT_E_CUDA, "prefill attention: %s", cudaGetErrorString(e));
     return MLXCAT_OK;
 }
 

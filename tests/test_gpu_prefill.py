@@ -139,3 +139,33 @@ def test_dense_prefill_matches_oracle(cfg, lens):
         kvlen = len(prompts[r])
         ol = O.forward(om, gen.kv, toks, [r] * len(toks), list(range(kvlen, kvlen + len(toks))))
         np.testing.assert_allclose(logits[r, :len(toks)], ol, rtol=TOL, atol=TOL)
+
+
+@pytest.mark.parametrize("s0,n", [(0, 1), (0, 77), (0, 128), (300, 700), (5, 300), (1000, 129)])
+def test_prefill_attention_matches_torch(s0, n):
+    """mlxcat_op_prefill_attention (tcgen05 flash attention, head_dim 128)
+    against a torch fp32 causal softmax(q K^T / sqrt(d)) V of the same fp16
+    inputs; GQA 32 query / 8 kv heads, row 1 of a 2-row cache."""
+    rows, Hkv, Hq, D, max_len, row = 2, 8, 32, 128, 1200, 1
+    g = torch.Generator(device="cuda").manual_seed(s0 * 7 + n)
+    kc = torch.randn((rows, Hkv, max_len, D), device="cuda", generator=g).half()
+    vc = torch.randn((rows, Hkv, max_len, D), device="cuda", generator=g).half()
+    q = torch.randn((n, Hq * D), device="cuda", generator=g).half()
+    out = torch.zeros((n, Hq * D), dtype=torch.float16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    A.check(L.mlxcat_op_prefill_attention(ptr(q), ptr(kc), ptr(vc), rows, max_len, row, s0, n, Hq, Hkv, D,
+                                          ptr(out), ptr(err), None))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, "a pipeline wait timed out"
+    T = s0 + n
+    k = kc[row, :, :T].float().repeat_interleave(Hq // Hkv, dim=0)      # [Hq][T][D]
+    v = vc[row, :, :T].float().repeat_interleave(Hq // Hkv, dim=0)
+    qq = q.float().view(n, Hq, D).transpose(0, 1)                        # [Hq][n][D]
+    s = qq @ k.transpose(1, 2) / D ** 0.5                                # [Hq][n][T]
+    pos = torch.arange(s0, s0 + n, device="cuda")[:, None]
+    s = s.masked_fill(torch.arange(T, device="cuda")[None, :] > pos, float("-inf"))
+    ref = (torch.softmax(s, dim=-1) @ v).transpose(0, 1).reshape(n, Hq * D)
+    got = out.float()
+    scale = ref.abs().max().item()
+    assert torch.isfinite(got).all()
+    assert (got - ref).abs().max().item() <= 5e-3 * max(scale, 1.0), (got - ref).abs().max().item()
