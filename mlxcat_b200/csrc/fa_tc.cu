@@ -6,13 +6,15 @@
 // query token i of the chunk sits at position s0 + i and sees keys 0..s0+i of
 // the row's cache (earlier chunks included).
 //
-// CTA = (128-query tile, query head).  Keys stream in blocks of 128 through a
-// two-stage TMA ring (K and V of the head's kv head, 128-byte swizzle).  Per
-// key block j:
+// CTA = (128-query tile, query head).  Keys stream in blocks of 128 through
+// one K and one V stage (TMA, 128-byte swizzle; K_{j+1} loads once S_j is
+// computed, V_{j+1} once V_j is in TMEM, both well inside block j's softmax).
+// Per key block j:
 //   S_j  = Q K_j^T            tcgen05.mma, A = Q tile and B = K tile from shared
 //                              memory (both K-major), S in TMEM (two buffers, so
 //                              S_{j+1} is computed while S_j is in the softmax)
-//   P_j  = exp2(S_j*c - m)    four softmax warps, thread = query row (TMEM lane):
+//   P_j  = exp2(S_j*c - m)    eight softmax warps, two per query row (TMEM lane),
+//                              each taking 64 of the block's 128 keys:
 //                              the running max m moves only when a row's max
 //                              grows by more than 8 (log2 units), so P <= 256
 //                              fits fp16 and O rarely needs rescaling; P is
@@ -26,8 +28,12 @@
 // V warps scale the O^T columns of those rows by alpha before the next
 // product.  The V warps then write O^T / l as fp16 [token][head * 128 + d].
 //
-// Warps: 0 TMA producer, 1 MMA issuer, 2 TMEM allocation, 4-7 softmax,
-// 8-11 V^T / rescale / epilogue (warp w owns TMEM lanes 32 * (w % 4)..).
+// Warps: 0 TMA producer, 1 MMA issuer, 2 TMEM allocation, 4-11 softmax (keys
+// 0-63 in warps 4-7, 64-127 in warps 8-11; the two halves of a row exchange
+// their partial max through shared memory), 12-15 V^T / rescale / epilogue
+// (warp w owns TMEM lanes 32 * (w % 4)..).  The softmax is the critical path:
+// exp2 runs as ex2.approx (fp16 P), and its loops are kept small so that the
+// three roles sharing a sub-partition do not evict each other's code.
 // Every wait is bounded; a timeout sets *err and an abort flag after which
 // every role skips its work, the producer waits for its copies and the issuer
 // for its last commit, and the CTA frees TMEM.
@@ -51,24 +57,32 @@ constexpr int BQ = 128;                 // queries per CTA (MMA M of Q K^T, N of
 constexpr int BKEYS = 128;              // keys per block
 constexpr int BOX = 128 * 128;          // one [128 rows x 128 B] swizzled box
 constexpr int TILE = 2 * BOX;           // 128 rows x 256 B (head_dim 128, two boxes)
-constexpr int F_THREADS = 384;
-constexpr int SM_WARP0 = 4, VT_WARP0 = 8;
-constexpr int EPI_BAR = 1;              // softmax + V warps, before the epilogue
-constexpr uint32_t COL_S = 0, COL_O = 256, COL_VT = 384;
+constexpr int F_THREADS = 512;
+constexpr int SM_WARP0 = 4, VT_WARP0 = 12;
+constexpr int EPI_BAR = 1;              // softmax + V warps, before the epilogue (384 threads)
+constexpr int PAIR_BAR0 = 2;            // 2..5: the two softmax warps of one lane quarter
+constexpr uint32_t COL_S = 0, COL_O = 256, COL_VT = 384;   // S: 2 x 128, O^T: 128, V^T: 2 x 64 columns
 
 enum FaErr { FE_Q = 31, FE_K = 32, FE_V = 33, FE_FREE = 34, FE_SFULL = 35, FE_SFREE = 36, FE_P = 37, FE_VT = 38,
              FE_PV = 39 };
 
+// Block j uses buffer j & 1 of everything double-buffered (S, P, V^T, alpha,
+// partial maxima) and the barriers of that buffer, so a role may run one block
+// ahead of another without a barrier phase being overtaken.  The single K and
+// V stages have one full / free barrier pair each: a stage is refilled only
+// after its consumer released it, so neither side can run two phases ahead.
 struct FaBars {
-    unsigned long long q_full, k_full[2], v_full[2], kv_free[2], s_full[2], s_free[2], p_full, vt_full, pv_done;
-    float alpha[BQ];
-    float lsum[BQ];
-    int rescale[2][4];       // per block parity, per softmax warp: some row's max moved
+    unsigned long long q_full, k_full, v_full, k_free, v_free, s_full[2], s_free[2], p_full[2], vt_full[2],
+        pv_done[2];
+    float alpha[2][BQ];
+    float pmax[2][2][BQ];    // per block parity, per key half: partial row max
+    float lsum[2][BQ];       // per key half
+    int rescale[2][4];       // per buffer, per softmax warp: some row's max moved
     uint32_t tmem;
     int abort;
 };
 
-constexpr size_t SMEM_Q = 0, SMEM_K = TILE, SMEM_V = 3 * TILE, SMEM_P = 5 * TILE, SMEM_BARS = 6 * TILE;
+constexpr size_t SMEM_Q = 0, SMEM_K = TILE, SMEM_V = 2 * TILE, SMEM_P = 3 * TILE, SMEM_BARS = 5 * TILE;
 constexpr size_t FA_SMEM = 1024 + SMEM_BARS + sizeof(FaBars);
 
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
@@ -81,12 +95,40 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
         : "memory");
 }
 
+// this warp's 32 lanes, 32 consecutive 32-bit columns
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t *v) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+// try_wait with a suspend-time hint: a waiting warp sleeps in hardware until the
+// phase completes (or the hint elapses) instead of spinning on the issue slots
+// that the softmax and V warps sharing its sub-partition need
+__device__ __forceinline__ bool try_wait_sleep(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(1000000u)
+        : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ bool fwait(uint32_t bar, uint32_t parity, volatile int *abort, int *err, int code) {
     if (*abort) return false;
     if (tc::mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = tc::global_ns();
     for (;;) {
-        if (tc::mbar_try_wait(bar, parity)) return true;
+        if (try_wait_sleep(bar, parity)) return true;
         if (*abort) return false;
         if (tc::global_ns() - t0 > tc::WAIT_LIMIT_NS) {
             *abort = 1;
@@ -98,6 +140,26 @@ __device__ __forceinline__ bool fwait(uint32_t bar, uint32_t parity, volatile in
 
 __device__ __forceinline__ void named_sync(int id, int n) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// named barrier over n threads that also ORs a predicate across them
+__device__ __forceinline__ bool pair_sync_or(int id, int n, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %3, 0;\n\t"
+        "bar.red.or.pred p, %1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(r)
+        : "r"(id), "r"(n), "r"((uint32_t)pred)
+        : "memory");
+    return r != 0;
 }
 
 // byte offset of (row r, byte b) inside a 1024-aligned [rows x 128 B] box with the 128-byte swizzle
@@ -125,16 +187,17 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 
     if (threadIdx.x == 0) {
         tc::mbar_init(tc::smem_u32(&fb.q_full), 1);
+        tc::mbar_init(tc::smem_u32(&fb.k_full), 1);
+        tc::mbar_init(tc::smem_u32(&fb.v_full), 1);
+        tc::mbar_init(tc::smem_u32(&fb.k_free), 1);   // the S MMA's commit
+        tc::mbar_init(tc::smem_u32(&fb.v_free), 4);   // the four V warps
         for (int s = 0; s < 2; ++s) {
-            tc::mbar_init(tc::smem_u32(&fb.k_full[s]), 1);
-            tc::mbar_init(tc::smem_u32(&fb.v_full[s]), 1);
-            tc::mbar_init(tc::smem_u32(&fb.kv_free[s]), 1 + 4);   // the S MMA's commit + the four V warps
             tc::mbar_init(tc::smem_u32(&fb.s_full[s]), 1);
-            tc::mbar_init(tc::smem_u32(&fb.s_free[s]), 4);
+            tc::mbar_init(tc::smem_u32(&fb.s_free[s]), 8);
+            tc::mbar_init(tc::smem_u32(&fb.p_full[s]), 8);
+            tc::mbar_init(tc::smem_u32(&fb.vt_full[s]), 4);
+            tc::mbar_init(tc::smem_u32(&fb.pv_done[s]), 1);
         }
-        tc::mbar_init(tc::smem_u32(&fb.p_full), 4);
-        tc::mbar_init(tc::smem_u32(&fb.vt_full), 4);
-        tc::mbar_init(tc::smem_u32(&fb.pv_done), 1);
         fb.abort = 0;
         tc::fence_barrier_init();
         tc::prefetch_tmap(&qmap);
@@ -151,30 +214,30 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer ----------------
-            int issued = 0;
             const uint32_t qb = tc::smem_u32(&fb.q_full);
             tc::mbar_arrive_expect_tx(qb, TILE);
             tc::tma_load_2d(tc::smem_u32(sm + SMEM_Q), &qmap, h * FD, q0, qb);
             tc::tma_load_2d(tc::smem_u32(sm + SMEM_Q + BOX), &qmap, h * FD + 64, q0, qb);
+            int kissued = 0, vissued = 0;
             for (int j = 0; j < nb && !*abort; ++j) {
-                const int s = j & 1;
-                if (j >= 2 && !fwait(tc::smem_u32(&fb.kv_free[s]), ((j - 2) >> 1) & 1, abort, err, FE_FREE)) break;
                 const int y = kv_row0 + j * BKEYS;
-                const uint32_t kb = tc::smem_u32(&fb.k_full[s]), vb = tc::smem_u32(&fb.v_full[s]);
+                if (j >= 1 && !fwait(tc::smem_u32(&fb.k_free), (j - 1) & 1, abort, err, FE_FREE)) break;
+                const uint32_t kb = tc::smem_u32(&fb.k_full);
                 tc::mbar_arrive_expect_tx(kb, TILE);
-                tc::tma_load_2d(tc::smem_u32(sm + SMEM_K + s * TILE), &kmap, 0, y, kb);
-                tc::tma_load_2d(tc::smem_u32(sm + SMEM_K + s * TILE + BOX), &kmap, 64, y, kb);
+                tc::tma_load_2d(tc::smem_u32(sm + SMEM_K), &kmap, 0, y, kb);
+                tc::tma_load_2d(tc::smem_u32(sm + SMEM_K + BOX), &kmap, 64, y, kb);
+                kissued = j + 1;
+                if (j >= 1 && !fwait(tc::smem_u32(&fb.v_free), (j - 1) & 1, abort, err, FE_FREE)) break;
+                const uint32_t vb = tc::smem_u32(&fb.v_full);
                 tc::mbar_arrive_expect_tx(vb, TILE);
-                tc::tma_load_2d(tc::smem_u32(sm + SMEM_V + s * TILE), &vmap, 0, y, vb);
-                tc::tma_load_2d(tc::smem_u32(sm + SMEM_V + s * TILE + BOX), &vmap, 64, y, vb);
-                issued = j + 1;
+                tc::tma_load_2d(tc::smem_u32(sm + SMEM_V), &vmap, 0, y, vb);
+                tc::tma_load_2d(tc::smem_u32(sm + SMEM_V + BOX), &vmap, 64, y, vb);
+                vissued = j + 1;
             }
             // copies in flight must land before the CTA's shared memory is released
             tc::mbar_wait(tc::smem_u32(&fb.q_full), 0, nullptr, 0);
-            for (int j = issued - 2 > 0 ? issued - 2 : 0; j < issued; ++j) {
-                tc::mbar_wait(tc::smem_u32(&fb.k_full[j & 1]), (j >> 1) & 1, nullptr, 0);
-                tc::mbar_wait(tc::smem_u32(&fb.v_full[j & 1]), (j >> 1) & 1, nullptr, 0);
-            }
+            if (kissued) tc::mbar_wait(tc::smem_u32(&fb.k_full), (kissued - 1) & 1, nullptr, 0);
+            if (vissued) tc::mbar_wait(tc::smem_u32(&fb.v_full), (vissued - 1) & 1, nullptr, 0);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -185,11 +248,11 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             int committed = 0;   // PV products committed
             auto issue_s = [&](int j) -> bool {
                 const int s = j & 1;
-                if (!fwait(tc::smem_u32(&fb.k_full[s]), (j >> 1) & 1, abort, err, FE_K)) return false;
+                if (!fwait(tc::smem_u32(&fb.k_full), j & 1, abort, err, FE_K)) return false;
                 if (j >= 2 && !fwait(tc::smem_u32(&fb.s_free[s]), ((j - 2) >> 1) & 1, abort, err, FE_SFREE))
                     return false;
                 tc::fence_after_sync();
-                const uint32_t ka = tc::smem_u32(sm + SMEM_K + s * TILE);
+                const uint32_t ka = tc::smem_u32(sm + SMEM_K);
 #pragma unroll
                 for (int kk = 0; kk < FD / 16; ++kk) {   // 16 features per step: box kk/4, +32 B per step
                     const uint32_t off = (uint32_t)((kk >> 2) * BOX + (kk & 3) * 32);
@@ -197,104 +260,102 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                            kk ? 1u : 0u);
                 }
                 tc::mma_commit(tc::smem_u32(&fb.s_full[s]));
-                tc::mma_commit(tc::smem_u32(&fb.kv_free[s]));   // K read (the V warps arrive for V)
+                tc::mma_commit(tc::smem_u32(&fb.k_free));   // K read: the next block's K may load
                 return true;
             };
             if (ok) ok = issue_s(0);
             for (int j = 0; j < nb && ok; ++j) {
+                const int b = j & 1;
                 if (j + 1 < nb && !issue_s(j + 1)) break;
-                if (!fwait(tc::smem_u32(&fb.p_full), j & 1, abort, err, FE_P)) break;
-                if (!fwait(tc::smem_u32(&fb.vt_full), j & 1, abort, err, FE_VT)) break;
+                if (!fwait(tc::smem_u32(&fb.p_full[b]), (j >> 1) & 1, abort, err, FE_P)) break;
+                if (!fwait(tc::smem_u32(&fb.vt_full[b]), (j >> 1) & 1, abort, err, FE_VT)) break;
                 tc::fence_after_sync();
+                const uint32_t pb = pa + b * TILE;
 #pragma unroll
                 for (int kk = 0; kk < BKEYS / 16; ++kk) {   // 16 keys per step: 8 TMEM columns of V^T
                     const uint32_t off = (uint32_t)((kk >> 2) * BOX + (kk & 3) * 32);
-                    tc::mma_ts_f16(tmem + COL_O, tmem + COL_VT + kk * 8, tc::sdesc_k_sw128(pa + off), idesc,
+                    tc::mma_ts_f16(tmem + COL_O, tmem + COL_VT + b * 64 + kk * 8, tc::sdesc_k_sw128(pb + off), idesc,
                                    (j | kk) ? 1u : 0u);
                 }
-                tc::mma_commit(tc::smem_u32(&fb.pv_done));
+                tc::mma_commit(tc::smem_u32(&fb.pv_done[b]));
                 committed = j + 1;
             }
             // the MMAs issued must finish before TMEM is freed
-            if (committed > 0) tc::mbar_wait(tc::smem_u32(&fb.pv_done), (committed - 1) & 1, nullptr, 0);
+            if (committed > 0)
+                tc::mbar_wait(tc::smem_u32(&fb.pv_done[(committed - 1) & 1]), ((committed - 1) >> 1) & 1, nullptr, 0);
         }
-    } else if (warp >= SM_WARP0 && warp < SM_WARP0 + 4) {
-        // ---------------- softmax: thread = query row ----------------
-        const int q = (warp - SM_WARP0) * 32 + lane;
-        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    } else if (warp >= SM_WARP0 && warp < VT_WARP0) {
+        // ---------------- softmax: thread = (query row, key half) ----------------
+        const int quarter = warp & 3, half = (warp - SM_WARP0) >> 2;
+        const int q = quarter * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         const int qpos = qp0 + q;
         const bool qvalid = q < nq;
         float m_used = -INFINITY, l = 0.f;
-        unsigned char *prow = sm + SMEM_P;
         for (int j = 0; j < nb; ++j) {
-            const int s = j & 1;
-            bool ok = fwait(tc::smem_u32(&fb.s_full[s]), (j >> 1) & 1, abort, err, FE_SFULL);
+            const int b = j & 1;
+            // S_j computed, and P buffer b released by the product of block j - 2
+            bool ok = fwait(tc::smem_u32(&fb.s_full[b]), (j >> 1) & 1, abort, err, FE_SFULL);
+            if (ok && j >= 2) ok = fwait(tc::smem_u32(&fb.pv_done[b]), ((j - 2) >> 1) & 1, abort, err, FE_PV);
             ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
-            tc::fence_after_sync();
-            const uint32_t sc = tmem + lane_base + COL_S + s * 128;
-            const int k0 = j * BKEYS;
-            const int lim = qvalid ? qpos - k0 : -1;   // columns 0..lim are visible keys
+            // this half's 64 scores of row q, in registers for both steps
+            uint32_t v[64];
+            const int lim = qvalid ? qpos - j * BKEYS - half * 64 : -1;   // columns 0..lim visible
             float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint32_t v[16];
-                tc::tmem_ld16(sc + c * 16, v);
+            if (ok) {
+                tc::fence_after_sync();
+                tmem_ld32(tmem + lane_base + COL_S + b * 128 + half * 64, v);
+                tmem_ld32(tmem + lane_base + COL_S + b * 128 + half * 64 + 32, v + 32);
                 tc::tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    if (c * 16 + i <= lim) mx = fmaxf(mx, __uint_as_float(v[i]));
+                for (int i = 0; i < 64; ++i)
+                    if (i <= lim) mx = fmaxf(mx, __uint_as_float(v[i]));
+                fb.pmax[b][half][q] = mx;
             }
-            mx *= scale_log2;
+            // the two halves of the row meet here; both leave together on an abort
+            if (pair_sync_or(PAIR_BAR0 + quarter, 64, !ok)) break;
+            mx = fmaxf(fb.pmax[b][0][q], fb.pmax[b][1][q]) * scale_log2;
             float alpha = 1.f;
             if (mx > m_used + 8.f) {   // the row's max moved: rescale l (and O, by the V warps)
                 alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - mx);
                 m_used = mx;
             }
-            // P is single-buffered: the previous product must have read it
-            if (j >= 1) {
-                ok = fwait(tc::smem_u32(&fb.pv_done), (j - 1) & 1, abort, err, FE_PV);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) break;
-            }
+            // P = exp2(S c - m) as fp16 into P[b] row q, box `half` (128-byte swizzle)
+            unsigned char *prow = sm + SMEM_P + b * TILE + half * BOX;
+            const bool live = m_used != -INFINITY;
+            const float nm = -m_used;
             float sum = 0.f;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint32_t v[16];
-                tc::tmem_ld16(sc + c * 16, v);
-                tc::tmem_wait_ld();
-                uint32_t pk[8];
+            for (int c8 = 0; c8 < 8; ++c8) {   // 8 keys = one 16-byte chunk
+                uint32_t pk[4];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int c0 = c * 16 + 2 * i;
-                    const float p0 = (c0 <= lim && m_used != -INFINITY)
-                                         ? exp2f(__uint_as_float(v[2 * i]) * scale_log2 - m_used) : 0.f;
-                    const float p1 = (c0 + 1 <= lim && m_used != -INFINITY)
-                                         ? exp2f(__uint_as_float(v[2 * i + 1]) * scale_log2 - m_used) : 0.f;
+                for (int i = 0; i < 4; ++i) {
+                    const int c0 = c8 * 8 + 2 * i;
+                    const float p0 = (live && c0 <= lim) ? ex2(fmaf(__uint_as_float(v[c0]), scale_log2, nm)) : 0.f;
+                    const float p1 = (live && c0 + 1 <= lim) ? ex2(fmaf(__uint_as_float(v[c0 + 1]), scale_log2, nm)) : 0.f;
                     const __half2 hp = __floats2half2_rn(p0, p1);
-                    sum += __low2float(hp) + __high2float(hp);   // l sums what the product uses
+                    const float2 back = __half22float2(hp);
+                    sum += back.x + back.y;   // l sums what the product uses
                     pk[i] = *reinterpret_cast<const uint32_t *>(&hp);
                 }
-                // keys c*16 .. c*16+15 of row q: box (c/4), bytes (c%4)*32 .. +31 (two 16-byte chunks)
-                unsigned char *bx = prow + (c >> 2) * BOX;
-                const int b0 = (c & 3) * 32;
-                *reinterpret_cast<uint4 *>(bx + sw128(q, b0)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                *reinterpret_cast<uint4 *>(bx + sw128(q, b0 + 16)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                *reinterpret_cast<uint4 *>(prow + sw128(q, c8 * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
             l = l * alpha + sum;
-            fb.alpha[q] = alpha;
-            const int moved = __any_sync(0xffffffffu, alpha != 1.f && j > 0);
-            if (lane == 0) fb.rescale[s][warp - SM_WARP0] = moved;
+            if (half == 0) {
+                fb.alpha[b][q] = alpha;
+                const int moved = __any_sync(0xffffffffu, alpha != 1.f && j > 0);
+                if (lane == 0) fb.rescale[b][quarter] = moved;
+            }
             tc::fence_before_sync();
             tc::fence_proxy_async_smem();   // P (generic stores) visible to the tensor core
             __syncwarp();
             if (lane == 0) {
-                tc::mbar_arrive(tc::smem_u32(&fb.s_free[s]));
-                tc::mbar_arrive(tc::smem_u32(&fb.p_full));
+                tc::mbar_arrive(tc::smem_u32(&fb.s_free[b]));
+                tc::mbar_arrive(tc::smem_u32(&fb.p_full[b]));
             }
         }
-        fb.lsum[q] = l;
-        named_sync(EPI_BAR, 256);
+        fb.lsum[half][q] = l;
+        named_sync(EPI_BAR, 384);
     } else if (warp >= VT_WARP0) {
         // ---------------- V^T into TMEM, O rescale, epilogue: thread = feature d ----------------
         const int d = (warp - VT_WARP0) * 32 + lane;
@@ -302,62 +363,69 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         const int vbox = d >> 6, vb = (d & 63) * 2;   // V[key][d]: box, byte within the 128-byte row
         bool ok = true;
         for (int j = 0; j < nb && ok; ++j) {
-            const int s = j & 1;
-            ok = fwait(tc::smem_u32(&fb.v_full[s]), (j >> 1) & 1, abort, err, FE_V);
-            if (ok && j >= 1) ok = fwait(tc::smem_u32(&fb.pv_done), (j - 1) & 1, abort, err, FE_PV);
+            const int b = j & 1;
+            ok = fwait(tc::smem_u32(&fb.v_full), j & 1, abort, err, FE_V);
+            // V^T buffer b was last read by the product of block j - 2
+            if (ok && j >= 2) ok = fwait(tc::smem_u32(&fb.pv_done[b]), ((j - 2) >> 1) & 1, abort, err, FE_PV);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc::fence_after_sync();
-            const unsigned char *vt = sm + SMEM_V + s * TILE + vbox * BOX;
-#pragma unroll
+            const unsigned char *vt = sm + SMEM_V + vbox * BOX;
+#pragma unroll 1
             for (int cp = 0; cp < 4; ++cp) {   // 32 keys -> 16 TMEM columns of key pairs
                 uint32_t r[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int key = cp * 32 + 2 * i;
                     const uint16_t a = *reinterpret_cast<const uint16_t *>(vt + sw128(key, vb));
-                    const uint16_t b = *reinterpret_cast<const uint16_t *>(vt + sw128(key + 1, vb));
-                    r[i] = (uint32_t)a | ((uint32_t)b << 16);
+                    const uint16_t c = *reinterpret_cast<const uint16_t *>(vt + sw128(key + 1, vb));
+                    r[i] = (uint32_t)a | ((uint32_t)c << 16);
                 }
-                tc::tmem_st16(tmem + lane_base + COL_VT + cp * 16, r);
+                tc::tmem_st16(tmem + lane_base + COL_VT + b * 64 + cp * 16, r);
             }
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&fb.kv_free[s]));   // V read
+            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&fb.v_free));   // V read: the next block's V may load
             // the softmax of block j decides whether O^T must be rescaled first
-            ok = fwait(tc::smem_u32(&fb.p_full), j & 1, abort, err, FE_P);
+            ok = fwait(tc::smem_u32(&fb.p_full[b]), (j >> 1) & 1, abort, err, FE_P);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
-            if (fb.rescale[s][0] | fb.rescale[s][1] | fb.rescale[s][2] | fb.rescale[s][3]) {
+            if (fb.rescale[b][0] | fb.rescale[b][1] | fb.rescale[b][2] | fb.rescale[b][3]) {
+                // O^T must hold the product of block j - 1 before it is scaled
+                ok = fwait(tc::smem_u32(&fb.pv_done[b ^ 1]), ((j - 1) >> 1) & 1, abort, err, FE_PV);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                tc::fence_after_sync();
 #pragma unroll 1
                 for (int c = 0; c < 8; ++c) {
                     uint32_t v[16];
                     tc::tmem_ld16(tmem + lane_base + COL_O + c * 16, v);
                     tc::tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * fb.alpha[c * 16 + i]);
+                    for (int i = 0; i < 16; ++i)
+                        v[i] = __float_as_uint(__uint_as_float(v[i]) * fb.alpha[b][c * 16 + i]);
                     tc::tmem_st16(tmem + lane_base + COL_O + c * 16, v);
                 }
             }
             tc::tmem_wait_st();
             tc::fence_before_sync();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&fb.vt_full));
+            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&fb.vt_full[b]));
         }
-        if (ok && nb > 0) ok = fwait(tc::smem_u32(&fb.pv_done), (nb - 1) & 1, abort, err, FE_PV);
-        named_sync(EPI_BAR, 256);
+        if (ok && nb > 0) ok = fwait(tc::smem_u32(&fb.pv_done[(nb - 1) & 1]), ((nb - 1) >> 1) & 1, abort, err, FE_PV);
+        named_sync(EPI_BAR, 384);
         ok = __shfl_sync(0xffffffffu, ok, 0) && !*abort;
         if (ok) {
             tc::fence_after_sync();
             __half *o = out + (size_t)q0 * Hq * FD + h * FD + d;
 #pragma unroll 1
-            for (int c = 0; c < 8; ++c) {
-                uint32_t v[16];
-                tc::tmem_ld16(tmem + lane_base + COL_O + c * 16, v);
+            for (int c = 0; c < 4; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_base + COL_O + c * 32, v);
                 tc::tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int q = c * 16 + i;
-                    const float lq = fb.lsum[q];
+                for (int i = 0; i < 32; ++i) {
+                    const int q = c * 32 + i;
+                    const float lq = fb.lsum[0][q] + fb.lsum[1][q];
                     if (q < nq) o[(size_t)q * Hq * FD] = __float2half_rn(lq > 0.f ? __uint_as_float(v[i]) / lq : 0.f);
                 }
             }
