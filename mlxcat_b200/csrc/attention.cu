@@ -64,9 +64,13 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
     constexpr int PITCH = D + 8;               // halves
     constexpr int NTHREADS = QT * 64;
     extern __shared__ __align__(16) unsigned char smem[];
-    __half *qs = reinterpret_cast<__half *>(smem);                 // [QROWS][PITCH]
-    __half *ks = qs + QROWS * PITCH;                                // [KSTAGES][KB][PITCH]
-    __half *vs = ks + KSTAGES * KB * PITCH;                         // [KSTAGES][KB][PITCH]
+    // The query tile is read into registers once, before the last V stage is
+    // first filled, so when it fits that stage it lives there (52 KB instead of
+    // 61 KB per CTA at 32 query rows: four CTAs per SM instead of three).
+    constexpr bool QALIAS = QROWS <= KB;
+    __half *ks = reinterpret_cast<__half *>(smem) + (QALIAS ? 0 : QROWS * PITCH);   // [KSTAGES][KB][PITCH]
+    __half *vs = ks + KSTAGES * KB * PITCH;                                       // [KSTAGES][KB][PITCH]
+    __half *qs = QALIAS ? vs + (KSTAGES - 1) * KB * PITCH : reinterpret_cast<__half *>(smem);   // [QROWS][PITCH]
     constexpr int KPW = KB / 2;                                     // keys per warp per block
     constexpr int NU = KPW / 16, NN = KPW / 8;
 
@@ -152,6 +156,20 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
     }
 
     uint32_t qf[D / 16][4];
+    auto load_q = [&]() {
+#pragma unroll
+        for (int ks16 = 0; ks16 < D / 16; ++ks16) {
+            const int mi = lane >> 3, rr = lane & 7;
+            const int qr = mt * 16 + (mi & 1) * 8 + rr;
+            ldsm_x4(qf[ks16], qs_a + (uint32_t)(qr * PITCH + ks16 * 16 + (mi >> 1) * 8) * 2);
+        }
+    };
+    if (QALIAS) {   // Q (first cp.async group) into registers before its stage is reused
+        cp_wait<KSTAGES - 2>();
+        __syncthreads();
+        load_q();
+        __syncthreads();
+    }
     float o[D / 8][4];
 #pragma unroll
     for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
@@ -166,14 +184,7 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
         cp_commit();
         cp_wait<KSTAGES - 1>();
         __syncthreads();
-        if (b == 0) {
-#pragma unroll
-            for (int ks16 = 0; ks16 < D / 16; ++ks16) {
-                const int mi = lane >> 3, rr = lane & 7;
-                const int qr = mt * 16 + (mi & 1) * 8 + rr;
-                ldsm_x4(qf[ks16], qs_a + (uint32_t)(qr * PITCH + ks16 * 16 + (mi >> 1) * 8) * 2);
-            }
-        }
+        if (!QALIAS && b == 0) load_q();
         const int buf = b % KSTAGES;
         const int key_base = kb + b * KB + kh * KPW;
         // S = Q K^T over this warp's KPW keys (NN n8 tiles)
@@ -403,8 +414,8 @@ cudaError_t launch_attn(const __half *qbuf, KVLayer kv, const int32_t *trow, con
                         int M, int qg, int Hq, int Hkv, int key_chunk, int splits,
                         AttnScratch sc, __half *out, bool permuted, int out_rows, bool early_kv, cudaStream_t st) {
     constexpr int PITCH = D + 8;
-    const size_t smem = std::max((size_t)(QT * 16 + 2 * KSTAGES * KB) * PITCH * 2,
-                                 (size_t)QT * 16 * (D + 2) * 4);   // K/V ring, then the split merge
+    const size_t smem = std::max((size_t)((QT * 16 <= KB ? 0 : QT * 16) + 2 * KSTAGES * KB) * PITCH * 2,
+                                 (size_t)QT * 16 * (D + 2) * 4);   // K/V ring (+ Q), then the split merge
     static bool attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
