@@ -256,7 +256,8 @@ def roofline_of(prof, verify_ms, cfg, rows, k1, lens_before, wbytes, hbm, tflops
     M = rows * k1
     weights = wbytes / 0.5625                      # q4: 0.5 B per weight + 4 B per 64-group
     q4_flops = 2.0 * M * weights
-    kv_tok = 2 * cfg.n_kv_heads * cfg.head_dim * 2 * cfg.n_layers
+    # K and V bytes per cached token on this rank (a tensor-parallel rank holds n_kv_heads / tp of them)
+    kv_tok = 2 * (cfg.n_kv_heads // max(1, cfg.tp_size)) * cfg.head_dim * 2 * cfg.n_layers
     at_bytes = statistics.mean(sum(l + k1 for l in lb) * kv_tok for lb in lens_before)
     tensor_bound = q4_flops / (tflops * 1e12) > wbytes / (hbm * 1e9)
     kern = {

@@ -177,8 +177,15 @@ __device__ uint32_t top_p_threshold(const float *l, int V, float m, uint64_t S1,
             if (in) {
                 const int b = (int)((key >> sh) & (uint32_t)(nb - 1));
                 const uint32_t P = fix24(det_exp_neg(__fadd_rn(l[i], -m)));
-                if (P) atomicAdd(&sm.mass[b], (unsigned long long)P);
-                atomicAdd(&sm.cnt[b], 1u);
+                // Logits cluster in a few buckets, so the lanes of a warp that
+                // share a bucket add their masses first (integer sums: the same
+                // totals in any order) and one of them updates the histogram.
+                const unsigned grp = __match_any_sync(__activemask(), b);
+                const unsigned sum = __reduce_add_sync(grp, P);   // < 32 * 2^24: no overflow
+                if ((int)(__ffs(grp) - 1) == (threadIdx.x & 31)) {
+                    if (sum) atomicAdd(&sm.mass[b], (unsigned long long)sum);
+                    atomicAdd(&sm.cnt[b], (unsigned)__popc(grp));
+                }
             }
         }
         __syncthreads();

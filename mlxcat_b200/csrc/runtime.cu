@@ -30,7 +30,21 @@ constexpr int PREFILL_CHUNK = 128;   // prompt tokens per prefill forward (q4 ke
 constexpr int PREFILL_QG = 8;        // prompt tokens per attention group
 constexpr int DENSE_CHUNK = 4096;    // prompt tokens per dense prefill forward (fp16 GEMMs)
 constexpr int DENSE_MIN = 256;       // prompts at least this long take the dense prefill
-constexpr int KEY_CHUNK = 384;       // keys per attention split (3-deep ring, one wave at the verify shape)
+constexpr int KEY_CHUNK = 384;       // keys per attention split of the operator entry points
+constexpr int KEY_CHUNK_MAX = 1024;  // longest split a cache's verify attention uses
+
+// Keys per split of a cache's verify attention: about 2.5 waves of split CTAs
+// (four per SM) over the cache's (row, kv head) pairs at its full length, at
+// least KEY_CHUNK.  Long contexts over many rows take longer splits (fewer
+// partials to merge, less per-split overhead): at 32 rows x 8 kv heads x 4.4k
+// keys, 768 keys per split ran 135 us per layer against 152 at 384; a few rows
+// keep 384 (8 x 8 x 2.8k: 29.6 us at 384, 43.6 at 768).
+int cache_key_chunk(int rows, int n_kv, int max_len, int sm_count) {
+    const double pairs = (double)rows * n_kv, slots = 4.0 * sm_count;
+    int kc = (int)(max_len * pairs / (2.5 * slots));
+    kc = (kc + 31) / 32 * 32;
+    return std::min(KEY_CHUNK_MAX, std::max(KEY_CHUNK, kc));
+}
 
 thread_local std::string g_op_err;
 
@@ -166,7 +180,7 @@ struct mlxcat_cache {
     int *err = nullptr;               // device-side wait timeouts
     int32_t *h_err = nullptr;
     AttnScratch attn;
-    int attn_splits = 1;
+    int attn_splits = 1, key_chunk = KEY_CHUNK;
     SampleScratch samp{};
     // dense prefill: fp16 weights of one linear, row-major activations of one
     // chunk of DENSE_CHUNK prompt tokens, attention scratch (one key split)
@@ -472,7 +486,7 @@ int forward(mlxcat_cache *c, int M, int qg, const int32_t *tok, const int32_t *t
         }
         ctx->launches++;  // attention is two kernels
         { ProfScope ps(c, 1);
-          LK(ctx, attention(c->qbuf, kv, trow, tpos, M, qg, Hq, Hkv, D, KEY_CHUNK, c->attn_splits,
+          LK(ctx, attention(c->qbuf, kv, trow, tpos, M, qg, Hq, Hkv, D, c->key_chunk, c->attn_splits,
                             c->attn, c->xn, true, R, st, true)); }
         if (ctx->tp > 1) {   // row-split output projection: partial sums, allreduce, residual
             int rc = tp_residual(c, ctx->o[l], c->xn, M, ctx->mlp_norm(l), c->r_attn, c->xg, 2 * l);
@@ -1354,7 +1368,8 @@ int mlxcat_cache_create(mlxcat_ctx *ctx, int32_t max_rows, int32_t max_len, mlxc
         chk(dalloc(A, &c->counters, nc));
         if (rc == MLXCAT_OK) chk(cudaMemset(c->counters, 0, nc * sizeof(unsigned)));
         // attention scratch
-        c->attn_splits = attention_max_splits(max_len, KEY_CHUNK);
+        c->key_chunk = cache_key_chunk(R, Hkv, max_len, ctx->sm_count);
+        c->attn_splits = attention_max_splits(max_len, c->key_chunk);
         int groups = std::max(R, (PREFILL_CHUNK + PREFILL_QG - 1) / PREFILL_QG);
         int qrows = 16;
         for (int k = 0; k <= MLXCAT_MAX_PROPOSAL; ++k) qrows = std::max(qrows, attention_qrows(k + 1, Hq, Hkv));
