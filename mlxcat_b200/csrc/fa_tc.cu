@@ -307,9 +307,14 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 tmem_ld32(tmem + lane_base + COL_S + b * 128 + half * 64, v);
                 tmem_ld32(tmem + lane_base + COL_S + b * 128 + half * 64 + 32, v + 32);
                 tc::tmem_wait_ld();
+                if (lim >= 63) {
 #pragma unroll
-                for (int i = 0; i < 64; ++i)
-                    if (i <= lim) mx = fmaxf(mx, __uint_as_float(v[i]));
+                    for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i)
+                        if (i <= lim) mx = fmaxf(mx, __uint_as_float(v[i]));
+                }
                 fb.pmax[b][half][q] = mx;
             }
             // the two halves of the row meet here; both leave together on an abort
@@ -320,25 +325,43 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - mx);
                 m_used = mx;
             }
-            // P = exp2(S c - m) as fp16 into P[b] row q, box `half` (128-byte swizzle)
+            // P = exp2(S c - m) as fp16 into P[b] row q, box `half` (128-byte swizzle).
+            // A half with every key visible (all but the diagonal blocks) skips the mask;
+            // l sums the fp32 values (their fp16 rounding errors average out in l).
             unsigned char *prow = sm + SMEM_P + b * TILE + half * BOX;
             const bool live = m_used != -INFINITY;
             const float nm = -m_used;
             float sum = 0.f;
+            if (live && lim >= 63) {
 #pragma unroll
-            for (int c8 = 0; c8 < 8; ++c8) {   // 8 keys = one 16-byte chunk
-                uint32_t pk[4];
+                for (int c8 = 0; c8 < 8; ++c8) {   // 8 keys = one 16-byte chunk
+                    uint32_t pk[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int c0 = c8 * 8 + 2 * i;
-                    const float p0 = (live && c0 <= lim) ? ex2(fmaf(__uint_as_float(v[c0]), scale_log2, nm)) : 0.f;
-                    const float p1 = (live && c0 + 1 <= lim) ? ex2(fmaf(__uint_as_float(v[c0 + 1]), scale_log2, nm)) : 0.f;
-                    const __half2 hp = __floats2half2_rn(p0, p1);
-                    const float2 back = __half22float2(hp);
-                    sum += back.x + back.y;   // l sums what the product uses
-                    pk[i] = *reinterpret_cast<const uint32_t *>(&hp);
+                    for (int i = 0; i < 4; ++i) {
+                        const int c0 = c8 * 8 + 2 * i;
+                        const float p0 = ex2(fmaf(__uint_as_float(v[c0]), scale_log2, nm));
+                        const float p1 = ex2(fmaf(__uint_as_float(v[c0 + 1]), scale_log2, nm));
+                        sum += p0 + p1;
+                        const __half2 hp = __floats2half2_rn(p0, p1);
+                        pk[i] = *reinterpret_cast<const uint32_t *>(&hp);
+                    }
+                    *reinterpret_cast<uint4 *>(prow + sw128(q, c8 * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
-                *reinterpret_cast<uint4 *>(prow + sw128(q, c8 * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            } else {
+#pragma unroll
+                for (int c8 = 0; c8 < 8; ++c8) {
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int c0 = c8 * 8 + 2 * i;
+                        const float p0 = (live && c0 <= lim) ? ex2(fmaf(__uint_as_float(v[c0]), scale_log2, nm)) : 0.f;
+                        const float p1 = (live && c0 + 1 <= lim) ? ex2(fmaf(__uint_as_float(v[c0 + 1]), scale_log2, nm)) : 0.f;
+                        sum += p0 + p1;
+                        const __half2 hp = __floats2half2_rn(p0, p1);
+                        pk[i] = *reinterpret_cast<const uint32_t *>(&hp);
+                    }
+                    *reinterpret_cast<uint4 *>(prow + sw128(q, c8 * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
             }
             l = l * alpha + sum;
             if (half == 0) {
