@@ -23,6 +23,7 @@ a quantized router is dequantised to bf16 (the router is kept bf16).
 from __future__ import annotations
 
 import json
+import mmap
 import os
 import struct
 from typing import Dict, Tuple
@@ -52,16 +53,19 @@ def tensor_expert(layer: int, expert: int, kind: int) -> int:
 # safetensors container
 # --------------------------------------------------------------------------- #
 def read_safetensors(path: str) -> Tuple[Dict[str, np.ndarray], Dict[str, str], Dict[str, str]]:
-    """(tensors, metadata, dtypes) of one file: numpy views of one read (BF16
-    as uint16 bits), the header's __metadata__, and each tensor's dtype name."""
+    """(tensors, metadata, dtypes) of one file: numpy views of the mapped file
+    (BF16 as uint16 bits), the header's __metadata__, and each tensor's dtype name."""
+    # mapped, not read: a 70B checkpoint's shards are tens of GB, and each tensor
+    # is a view of the mapping until it is copied to the device
     with open(path, "rb") as f:
-        data = f.read()
+        size = os.fstat(f.fileno()).st_size
+        data = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ) if size else b""
     if len(data) < 8:
         raise ValueError(f"{path}: not a safetensors file")
     (n,) = struct.unpack("<Q", data[:8])
     if 8 + n > len(data):
         raise ValueError(f"{path}: header length {n} past the end of the file")
-    header = json.loads(data[8:8 + n].decode("utf-8"))
+    header = json.loads(bytes(data[8:8 + n]).decode("utf-8"))
     meta = header.pop("__metadata__", {}) or {}
     base = 8 + n
     out = {}

@@ -295,6 +295,8 @@ bool valid_config(const mlxcat_model_config *c, std::string &why) {
     }
     if (c->n_heads % c->n_kv_heads) { why = "n_heads must be a multiple of n_kv_heads"; return false; }
     if (c->head_dim != 64 && c->head_dim != 128) { why = "head_dim must be 64 or 128"; return false; }
+    // the exchange's flag waits run one thread per peer in a single warp
+    if (c->tp_size > 32 || c->ep_size > 32) { why = "tp_size and ep_size are at most 32"; return false; }
     if (c->tp_size > 1) {
         const int T = c->tp_size;
         if (c->tp_rank < 0 || c->tp_rank >= T) { why = "tp_rank must be in [0, tp_size)"; return false; }
