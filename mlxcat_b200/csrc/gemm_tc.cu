@@ -12,7 +12,8 @@
 // TMA, 128-byte swizzled.
 //
 // Tile: 128 weight rows (the MMA's M) x BN tokens (its N, 256), k in steps of
-// 64 (one 128-byte row per operand row and stage).  Persistent CTAs walk the
+// 64 (one 128-byte row per operand row and stage); the plain-store GEMMs take
+// two 128-row blocks per tile (see GTile).  Persistent CTAs walk the
 // tiles with the token tile fastest, so CTAs running at the same time share a
 // weight block and each weight byte comes from HBM about once; the
 // activations stay in L2.
@@ -52,14 +53,24 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
 
 namespace {
 
-constexpr int GM = 128;        // weight rows per tile
+constexpr int GM = 128;        // weight rows per row block (the MMA's M)
 constexpr int GBN = 256;       // tokens per tile
 constexpr int GK = 64;         // k per stage
-constexpr int GSTAGES = 4;
+constexpr int GSTAGES = 4;     // stages of a one-block tile (3 of a two-block tile)
 constexpr int G_THREADS = 192;
-constexpr int A_BYTES = GM * GK * 2;           // 16 KB
+constexpr int A_BYTES = GM * GK * 2;           // 16 KB per row block
 constexpr int B_BYTES = GBN * GK * 2;          // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+
+// Tiles of RB row blocks (RB = 1: 128 x 256, two accumulator sets so a tile's
+// epilogue overlaps the next tile's MMAs; RB = 2: 256 x 256, the two blocks'
+// MMAs share each token stage -- a third fewer operand bytes per FLOP -- with
+// one accumulator set of 2 x 256 TMEM columns).
+template <int RB> struct GTile {
+    static constexpr int ROWS = GM * RB;
+    static constexpr int STAGES = RB == 1 ? 4 : 3;
+    static constexpr int STAGE = RB * A_BYTES + B_BYTES;
+    static constexpr int SETS = 2 / RB;
+};
 constexpr int EPI_BAR = 1;                     // named barrier of the 4 epilogue warps
 constexpr int SWG_COLS = 16;                   // token columns per epilogue step
 
@@ -116,28 +127,30 @@ __device__ __forceinline__ bool named_sync_or(int id, int n, bool pred) {
     return r != 0;
 }
 
-template <int EPI>
+template <int EPI, int RB>
 __global__ void __launch_bounds__(G_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, int N, int M,
                int K, void *out, int ldo, int *err) {
+    using T = GTile<RB>;
+    constexpr int NS = T::STAGES, STAGE_BYTES = T::STAGE, SETS = T::SETS;
     // token rows of one B box: the whole 256-row tile, or M when the operand is
     // shorter (the stage's remaining rows then hold stale data, which only
     // feeds accumulator columns >= M that are never stored)
-    const uint32_t stage_tx = A_BYTES + (uint32_t)(M < GBN ? M : GBN) * GK * 2;
+    const uint32_t stage_tx = RB * A_BYTES + (uint32_t)(M < GBN ? M : GBN) * GK * 2;
     extern __shared__ __align__(1024) unsigned char gsm_raw[];
     unsigned char *ring = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~(uintptr_t)1023);
-    GemmBars &gb = *reinterpret_cast<GemmBars *>(ring + GSTAGES * STAGE_BYTES);
+    GemmBars &gb = *reinterpret_cast<GemmBars *>(ring + NS * STAGE_BYTES);
     volatile int *abort = &gb.abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int mt = (M + GBN - 1) / GBN, tiles = (N / GM) * mt, nk = K / GK;
+    const int mt = (M + GBN - 1) / GBN, tiles = (N / T::ROWS) * mt, nk = K / GK;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < GSTAGES; ++s) {
+        for (int s = 0; s < NS; ++s) {
             tc::mbar_init(tc::smem_u32(&gb.full[s]), 1);
             tc::mbar_init(tc::smem_u32(&gb.empty[s]), 1);
         }
-        for (int a = 0; a < 2; ++a) {
+        for (int a = 0; a < SETS; ++a) {
             tc::mbar_init(tc::smem_u32(&gb.dfull[a]), 1);
             tc::mbar_init(tc::smem_u32(&gb.dempty[a]), 4);
         }
@@ -157,20 +170,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
             // ---------------- TMA producer ----------------
             int it = 0;
             for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
-                const int n0 = (t / mt) * GM, m0 = (t % mt) * GBN;
+                const int n0 = (t / mt) * T::ROWS, m0 = (t % mt) * GBN;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % GSTAGES;
-                    if (!gwait(tc::smem_u32(&gb.empty[s]), ((it / GSTAGES) & 1) ^ 1, abort, err, GE_EMPTY)) break;
+                    const int s = it % NS;
+                    if (!gwait(tc::smem_u32(&gb.empty[s]), ((it / NS) & 1) ^ 1, abort, err, GE_EMPTY)) break;
                     const uint32_t bar = tc::smem_u32(&gb.full[s]);
                     unsigned char *st = ring + (size_t)s * STAGE_BYTES;
                     tc::mbar_arrive_expect_tx(bar, stage_tx);
-                    tc::tma_load_2d(tc::smem_u32(st), &wmap, kb * GK, n0, bar);
-                    tc::tma_load_2d(tc::smem_u32(st + A_BYTES), &xmap, kb * GK, m0, bar);
+#pragma unroll
+                    for (int rb = 0; rb < RB; ++rb)
+                        tc::tma_load_2d(tc::smem_u32(st + rb * A_BYTES), &wmap, kb * GK, n0 + rb * GM, bar);
+                    tc::tma_load_2d(tc::smem_u32(st + RB * A_BYTES), &xmap, kb * GK, m0, bar);
                 }
             }
             if (*abort)   // copies issued must land before the CTA's shared memory is released
-                for (int j = it - GSTAGES > 0 ? it - GSTAGES : 0; j < it; ++j)
-                    tc::mbar_wait(tc::smem_u32(&gb.full[j % GSTAGES]), (j / GSTAGES) & 1, nullptr, 0);
+                for (int j = it - NS > 0 ? it - NS : 0; j < it; ++j)
+                    tc::mbar_wait(tc::smem_u32(&gb.full[j % NS]), (j / NS) & 1, nullptr, 0);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -178,20 +193,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
             constexpr uint32_t idesc = tc::idesc_f16_f32(GM, GBN);
             int it = 0, lt = 0, last = -1;
             for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x, ++lt) {
-                const int a = lt & 1;
-                if (!gwait(tc::smem_u32(&gb.dempty[a]), ((lt >> 1) & 1) ^ 1, abort, err, GE_DEMPTY)) break;
+                const int a = lt % SETS;
+                if (!gwait(tc::smem_u32(&gb.dempty[a]), ((lt / SETS) & 1) ^ 1, abort, err, GE_DEMPTY)) break;
                 tc::fence_after_sync();
-                const uint32_t dcol = tmem + a * GBN;
+                const uint32_t dcol = tmem + a * RB * GBN;   // row block rb accumulates at dcol + rb * GBN
                 bool ok = true;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % GSTAGES;
-                    if (!gwait(tc::smem_u32(&gb.full[s]), (it / GSTAGES) & 1, abort, err, GE_FULL)) { ok = false; break; }
+                    const int s = it % NS;
+                    if (!gwait(tc::smem_u32(&gb.full[s]), (it / NS) & 1, abort, err, GE_FULL)) { ok = false; break; }
                     tc::fence_after_sync();
                     const uint32_t sa = tc::smem_u32(ring + (size_t)s * STAGE_BYTES);
-                    const uint64_t ad = tc::sdesc_k_sw128(sa), bd = tc::sdesc_k_sw128(sa + A_BYTES);
+                    const uint64_t bd = tc::sdesc_k_sw128(sa + RB * A_BYTES);
 #pragma unroll
                     for (int q = 0; q < GK / 16; ++q)   // +32 bytes per 16-element k step
-                        mma_ss_f16(dcol, ad + 2 * q, bd + 2 * q, idesc, (kb | q) ? 1u : 0u);
+#pragma unroll
+                        for (int rb = 0; rb < RB; ++rb)
+                            mma_ss_f16(dcol + rb * GBN, tc::sdesc_k_sw128(sa + rb * A_BYTES) + 2 * q, bd + 2 * q, idesc,
+                                       (kb | q) ? 1u : 0u);
                     tc::mma_commit(tc::smem_u32(&gb.empty[s]));   // stage free once these MMAs finish
                     last = it;
                 }
@@ -199,7 +217,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
                 tc::mma_commit(tc::smem_u32(&gb.dfull[a]));       // tile complete
             }
             if (*abort && last >= 0)   // MMAs in flight read shared memory and write TMEM
-                tc::mbar_wait(tc::smem_u32(&gb.empty[last % GSTAGES]), (last / GSTAGES) & 1, nullptr, 0);
+                tc::mbar_wait(tc::smem_u32(&gb.empty[last % NS]), (last / NS) & 1, nullptr, 0);
         }
     } else {
         // ---------------- epilogue: warps 2..5, TMEM lane quarter warp % 4 ----------------
@@ -207,15 +225,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
         const int row = q * 32 + lane;   // weight row inside the tile
         int lt = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
-            const int a = lt & 1;
-            const int n0 = (t / mt) * GM, m0 = (t % mt) * GBN;
-            bool failed = !gwait(tc::smem_u32(&gb.dfull[a]), (lt >> 1) & 1, abort, err, GE_DFULL);
+            const int a = lt % SETS;
+            const int m0 = (t % mt) * GBN;
+            bool failed = !gwait(tc::smem_u32(&gb.dfull[a]), (lt / SETS) & 1, abort, err, GE_DFULL);
             // the SwiGLU steps pair warps through named barriers: all four leave together
             if (EPI == GEMM_SWIGLU) failed = named_sync_or(EPI_BAR, 128, failed);
             if (failed) break;
             tc::fence_after_sync();
-            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + a * GBN;
             const int ncols = min(GBN, M - m0);
+            for (int rb = 0; rb < RB; ++rb) {
+            const int n0 = (t / mt) * T::ROWS + rb * GM;
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (a * RB + rb) * GBN;
             for (int c = 0; c < GBN / SWG_COLS; ++c) {
                 if (c * SWG_COLS >= ncols) break;
                 uint32_t v[16];
@@ -252,6 +272,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
                     }
                     named_sync(EPI_BAR, 128);
                 }
+            }
             }
             tc::fence_before_sync();
             __syncwarp();
@@ -293,7 +314,8 @@ bool make_map_2d(CUtensorMap *map, const __half *p, int inner, int outer, int bo
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-size_t gemm_smem() { return 1024 + (size_t)GSTAGES * STAGE_BYTES + sizeof(GemmBars); }
+template <int RB>
+size_t gemm_smem() { return 1024 + (size_t)GTile<RB>::STAGES * GTile<RB>::STAGE + sizeof(GemmBars); }
 
 }  // namespace
 
@@ -313,19 +335,25 @@ cudaError_t gemm_tc(const __half *w, int N, int K, const __half *x, int M, int e
     CUtensorMap wmap, xmap;
     if (!make_map_2d(&wmap, w, K, N, GM) || !make_map_2d(&xmap, x, K, M, M < GBN ? M : GBN))
         return cudaErrorInvalidValue;
-    const int tiles = (N / GM) * ((M + GBN - 1) / GBN);
+    // Two-block tiles for the plain store, where the rows allow them and the token
+    // tiles are full: 1.18 -> 1.36 PFLOP/s on the prefill's QKV / O / down shapes.
+    // The SwiGLU epilogue (exchange through shared memory, exponentials) is too
+    // long to run unoverlapped after every tile (0.81 -> 1.13 ms per gate/up
+    // launch at 4096 tokens), so it keeps the double-buffered one-block tiles.
+    const bool two = epi == GEMM_STORE && N % (2 * GM) == 0 && M >= GBN;
+    const int tiles = (N / (two ? 2 * GM : GM)) * ((M + GBN - 1) / GBN);
     const int grid = tiles < sm_count ? tiles : sm_count;
-    const size_t smem = gemm_smem();
-    auto launch = [&](auto kern) -> cudaError_t {
+    auto launch = [&](auto kern, size_t smem) -> cudaError_t {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         kern<<<grid, G_THREADS, smem, st>>>(wmap, xmap, N, M, K, out, ldo, err);
         return cudaGetLastError();
     };
+    if (two) return launch(gemm_tc_kernel<GEMM_STORE, 2>, gemm_smem<2>());
     switch (epi) {
-    case GEMM_STORE: return launch(gemm_tc_kernel<GEMM_STORE>);
-    case GEMM_ADD: return launch(gemm_tc_kernel<GEMM_ADD>);
-    case GEMM_SWIGLU: return launch(gemm_tc_kernel<GEMM_SWIGLU>);
+    case GEMM_STORE: return launch(gemm_tc_kernel<GEMM_STORE, 1>, gemm_smem<1>());
+    case GEMM_ADD: return launch(gemm_tc_kernel<GEMM_ADD, 1>, gemm_smem<1>());
+    case GEMM_SWIGLU: return launch(gemm_tc_kernel<GEMM_SWIGLU, 1>, gemm_smem<1>());
     default: return cudaErrorInvalidValue;
     }
 }
