@@ -774,11 +774,8 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
             const uint4 w0 = *reinterpret_cast<const uint4 *>(wt + sw_off);
             const uint4 w1 = *reinterpret_cast<const uint4 *>(wt + sw_off1);
             const uint32_t sbv = reinterpret_cast<const uint32_t *>(wst + 2 * WBOX)[(h * 4 + g) * ROWS + r];
-            if (h == 1) {
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.w_free[s]));   // both boxes of the stage read
-                if (++s == sw) { s = 0; wpar ^= 1; }
-            }
+            const int s_read = s;           // released after its second box is in TMEM
+            if (h == 1 && ++s == sw) { s = 0; wpar ^= 1; }
             if (j >= R) {   // the MMAs that last read this A buffer have completed
                 if (lane == 0)
                     ok = ok && wait_or_abort(tc::smem_u32(&cs.mma_done[as]), (mpar >> as) & 1, abort_flag, ep.err,
@@ -796,6 +793,13 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                 dequant16(w1, kc, a);
                 tc::tmem_st16(ta + 16, a);
                 tc::tmem_wait_st();
+            }
+            if (h == 1) {
+                // the stage goes back to the producer only once the values read
+                // from it are in TMEM: handing it back right after the loads were
+                // issued let the next TMA write race them
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(tc::smem_u32(&cs.w_free[s_read]));
             }
             tc::fence_before_sync();
             named_bar_arrive(1 + is * MAX_AST + as, C::BAR_COUNT);

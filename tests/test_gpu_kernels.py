@@ -40,7 +40,7 @@ def test_synth_q4_bit_exact(N, K, tid):
 # --------------------------------------------------------------------------- #
 # q4 linear
 # --------------------------------------------------------------------------- #
-@pytest.mark.parametrize("M", [1, 5, 16, 17, 48, 64, 100, 200])
+@pytest.mark.parametrize("M", [1, 5, 16, 17, 48, 64, 100, 144, 150, 160, 200, 300])   # 129..160: one wide tile
 @pytest.mark.parametrize("N,K", [(256, 512), (384, 1408), (1024, 2560), (128, 9728), (128, 128)])
 def test_q4_linear_matches_oracle(M, N, K):
     rng = np.random.default_rng(M * 7 + N)
