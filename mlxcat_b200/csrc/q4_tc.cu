@@ -203,7 +203,7 @@ struct Smem {
     int abort_flag;
     int last_flag;
     float wsum[4][16];          // [row quarter][token of the piece]
-    float xch[ROWS * 16];       // epilogue exchange: [row][token of the piece]
+    float xch[128];             // epilogue warps: folded-norm scales; QKV tail: token rows / positions
     // the tail epilogue of the dequant warps (may overlap the epilogue warps)
     int last_flag2;
     float wsum2[4][4][16];      // [token group][row quarter][token]
@@ -979,79 +979,6 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                                 ep.norm_part[(size_t)blk * ep.norm_rows + m0 + etid] =
                                     cs.wsum[0][etid] + cs.wsum[1][etid] + cs.wsum[2][etid] + cs.wsum[3][etid];
                             named_bar_sync(EPI_BAR, EP_THREADS);
-                        }
-                    } else if constexpr (OP == Q4Epilogue::SWIGLU) {
-                        // rows [0,64) gate, [64,128) up of the same 64 outputs
-                        if (r >= 64) {
-#pragma unroll
-                            for (int q = 0; q < 16; ++q) cs.xch[(r - 64) * 16 + q] = y[q];
-                        }
-                        named_bar_sync(EPI_BAR, EP_THREADS);
-                        if (r < 64) {
-                            const int oi = blk * 64 + r;
-#pragma unroll
-                            for (int q = 0; q < 16; ++q) {
-                                if (q >= mlim) break;
-                                const float gv = y[q], uv = cs.xch[r * 16 + q];
-                                const float av = gv / (1.0f + expf(-gv)) * uv;
-                                ep.xout[xblk(m0 + q, oi, ep.ldx_rows)] = __float2half_rn(av);
-                            }
-                        }
-                        named_bar_sync(EPI_BAR, EP_THREADS);
-                    } else {   // QKV
-                        const int D = ep.head_dim;
-                        const int hh = f / D;      // head index in q|k|v order
-                        const int d = f % D;
-                        const bool is_q = hh < ep.n_heads, is_k = !is_q && hh < ep.n_heads + ep.n_kv;
-                        const float *nw = is_q ? ep.q_norm : (is_k ? ep.k_norm : nullptr);
-                        if (nw) {
-                            // per-head sum of squares for each token: warp shuffles + smem
-#pragma unroll
-                            for (int q = 0; q < 16; ++q) {
-                                const float t2 = warp_sum(y[q] * y[q]);
-                                if (lane == q) cs.wsum[quarter][q] = t2;
-                            }
-                        }
-                        named_bar_sync(EPI_BAR, EP_THREADS);
-                        if (nw) {
-                            const int wpk = D / 32, w0 = (quarter / wpk) * wpk;
-#pragma unroll
-                            for (int q = 0; q < 16; ++q) {
-                                float ss = 0.f;
-                                for (int ww = w0; ww < w0 + wpk; ++ww) ss += cs.wsum[ww][q];
-                                y[q] = y[q] * (1.0f / sqrtf(ss / (float)D + ep.eps)) * nw[d];
-                            }
-                        }
-                        // rotate-half RoPE on q and k: partner row r +- D/2
-#pragma unroll
-                        for (int q = 0; q < 16; ++q) cs.xch[r * 16 + q] = y[q];
-                        named_bar_sync(EPI_BAR, EP_THREADS);
-                        if (is_q || is_k) {
-                            const int half = D / 2;
-                            const int pr = d < half ? r + half : r - half;
-#pragma unroll
-                            for (int q = 0; q < 16; ++q) {
-                                if (q >= mlim) break;
-                                const float2 csn = ep.rope[(size_t)ep.tpos[m0 + q] * half + d % half];
-                                const float sn = csn.y, cn = csn.x;
-                                const float pv = cs.xch[pr * 16 + q];
-                                y[q] = d < half ? y[q] * cn - pv * sn : pv * sn + y[q] * cn;
-                            }
-                        }
-                        named_bar_sync(EPI_BAR, EP_THREADS);
-#pragma unroll
-                        for (int q = 0; q < 16; ++q) {
-                            if (q >= mlim) break;
-                            const int m = m0 + q;
-                            __half *dst;
-                            if (is_q) {
-                                dst = ep.qbuf + ((size_t)m * ep.n_heads + hh) * D;
-                            } else {
-                                const int kvh = is_k ? hh - ep.n_heads : hh - ep.n_heads - ep.n_kv;
-                                dst = (is_k ? ep.kc : ep.vc) +
-                                      (((size_t)ep.trow[m] * ep.n_kv + kvh) * ep.max_len + ep.tpos[m]) * D;
-                            }
-                            dst[d] = __float2half_rn(y[q]);
                         }
                     }
                 }
