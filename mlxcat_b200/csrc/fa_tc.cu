@@ -7,8 +7,10 @@
 // the row's cache (earlier chunks included).
 //
 // CTA = (128-query tile, query head).  Keys stream in blocks of 128 through
-// one K and one V stage (TMA, 128-byte swizzle; K_{j+1} loads once S_j is
-// computed, V_{j+1} once V_j is in TMEM, both well inside block j's softmax).
+// one K stage and two V stages (TMA, 128-byte swizzle; K_{j+1} loads once S_j
+// is computed, V_{j+1} while V_j is moved into TMEM), each from its own
+// producer thread.  With one V stage the next V load waited for the previous
+// transpose, and load plus transpose set the pace of every key block.
 // Per key block j:
 //   S_j  = Q K_j^T            tcgen05.mma, A = Q tile and B = K tile from shared
 //                              memory (both K-major), S in TMEM (two buffers, so
@@ -28,7 +30,8 @@
 // V warps scale the O^T columns of those rows by alpha before the next
 // product.  The V warps then write O^T / l as fp16 [token][head * 128 + d].
 //
-// Warps: 0 TMA producer, 1 MMA issuer, 2 TMEM allocation, 4-11 softmax (keys
+// Warps: 0 TMA producer (Q, K), 1 MMA issuer, 2 TMEM allocation, 3 TMA
+// producer (V), 4-11 softmax (keys
 // 0-63 in warps 4-7, 64-127 in warps 8-11; the two halves of a row exchange
 // their partial max through shared memory), 12-15 V^T / rescale / epilogue
 // (warp w owns TMEM lanes 32 * (w % 4)..).  The softmax is the critical path:
@@ -66,13 +69,13 @@ constexpr uint32_t COL_S = 0, COL_O = 256, COL_VT = 384;   // S: 2 x 128, O^T: 1
 enum FaErr { FE_Q = 31, FE_K = 32, FE_V = 33, FE_FREE = 34, FE_SFULL = 35, FE_SFREE = 36, FE_P = 37, FE_VT = 38,
              FE_PV = 39 };
 
-// Block j uses buffer j & 1 of everything double-buffered (S, P, V^T, alpha,
-// partial maxima) and the barriers of that buffer, so a role may run one block
-// ahead of another without a barrier phase being overtaken.  The single K and
-// V stages have one full / free barrier pair each: a stage is refilled only
-// after its consumer released it, so neither side can run two phases ahead.
+// Block j uses buffer j & 1 of everything double-buffered (S, P, V, V^T,
+// alpha, partial maxima) and the barriers of that buffer, so a role may run one
+// block ahead of another without a barrier phase being overtaken.  The single K
+// stage has one full / free barrier pair: it is refilled only after its
+// consumer released it, so neither side can run two phases ahead.
 struct FaBars {
-    unsigned long long q_full, k_full, v_full, k_free, v_free, s_full[2], s_free[2], p_full[2], vt_full[2],
+    unsigned long long q_full, k_full, k_free, v_full[2], v_free[2], s_full[2], s_free[2], p_full[2], vt_full[2],
         pv_done[2];
     float alpha[2][BQ];
     float pmax[2][2][BQ];    // per block parity, per key half: partial row max
@@ -82,8 +85,9 @@ struct FaBars {
     int abort;
 };
 
-constexpr size_t SMEM_Q = 0, SMEM_K = TILE, SMEM_V = 2 * TILE, SMEM_P = 3 * TILE, SMEM_BARS = 5 * TILE;
+constexpr size_t SMEM_Q = 0, SMEM_K = TILE, SMEM_V = 2 * TILE, SMEM_P = 4 * TILE, SMEM_BARS = 6 * TILE;
 constexpr size_t FA_SMEM = 1024 + SMEM_BARS + sizeof(FaBars);
+static_assert(FA_SMEM <= 227 * 1024, "Q, K, two V and two P tiles must fit one CTA");
 
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
@@ -188,10 +192,10 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     if (threadIdx.x == 0) {
         tc::mbar_init(tc::smem_u32(&fb.q_full), 1);
         tc::mbar_init(tc::smem_u32(&fb.k_full), 1);
-        tc::mbar_init(tc::smem_u32(&fb.v_full), 1);
         tc::mbar_init(tc::smem_u32(&fb.k_free), 1);   // the S MMA's commit
-        tc::mbar_init(tc::smem_u32(&fb.v_free), 4);   // the four V warps
         for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(tc::smem_u32(&fb.v_full[s]), 1);
+            tc::mbar_init(tc::smem_u32(&fb.v_free[s]), 4);   // the four V warps
             tc::mbar_init(tc::smem_u32(&fb.s_full[s]), 1);
             tc::mbar_init(tc::smem_u32(&fb.s_free[s]), 8);
             tc::mbar_init(tc::smem_u32(&fb.p_full[s]), 8);
@@ -213,12 +217,12 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---------------- TMA producer ----------------
+            // ---------------- TMA producer: Q, then K ----------------
             const uint32_t qb = tc::smem_u32(&fb.q_full);
             tc::mbar_arrive_expect_tx(qb, TILE);
             tc::tma_load_2d(tc::smem_u32(sm + SMEM_Q), &qmap, h * FD, q0, qb);
             tc::tma_load_2d(tc::smem_u32(sm + SMEM_Q + BOX), &qmap, h * FD + 64, q0, qb);
-            int kissued = 0, vissued = 0;
+            int kissued = 0;
             for (int j = 0; j < nb && !*abort; ++j) {
                 const int y = kv_row0 + j * BKEYS;
                 if (j >= 1 && !fwait(tc::smem_u32(&fb.k_free), (j - 1) & 1, abort, err, FE_FREE)) break;
@@ -227,17 +231,28 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 tc::tma_load_2d(tc::smem_u32(sm + SMEM_K), &kmap, 0, y, kb);
                 tc::tma_load_2d(tc::smem_u32(sm + SMEM_K + BOX), &kmap, 64, y, kb);
                 kissued = j + 1;
-                if (j >= 1 && !fwait(tc::smem_u32(&fb.v_free), (j - 1) & 1, abort, err, FE_FREE)) break;
-                const uint32_t vb = tc::smem_u32(&fb.v_full);
-                tc::mbar_arrive_expect_tx(vb, TILE);
-                tc::tma_load_2d(tc::smem_u32(sm + SMEM_V), &vmap, 0, y, vb);
-                tc::tma_load_2d(tc::smem_u32(sm + SMEM_V + BOX), &vmap, 64, y, vb);
-                vissued = j + 1;
             }
             // copies in flight must land before the CTA's shared memory is released
             tc::mbar_wait(tc::smem_u32(&fb.q_full), 0, nullptr, 0);
             if (kissued) tc::mbar_wait(tc::smem_u32(&fb.k_full), (kissued - 1) & 1, nullptr, 0);
-            if (vissued) tc::mbar_wait(tc::smem_u32(&fb.v_full), (vissued - 1) & 1, nullptr, 0);
+        }
+    } else if (warp == 3) {
+        if (lane == 0) {
+            // ---------------- TMA producer: V, two stages ----------------
+            int vissued = 0;
+            for (int j = 0; j < nb && !*abort; ++j) {
+                const int y = kv_row0 + j * BKEYS, b = j & 1;
+                // stage b was last read (moved into TMEM) for block j - 2
+                if (j >= 2 && !fwait(tc::smem_u32(&fb.v_free[b]), ((j - 2) >> 1) & 1, abort, err, FE_FREE)) break;
+                const uint32_t vb = tc::smem_u32(&fb.v_full[b]);
+                const uint32_t vs = tc::smem_u32(sm + SMEM_V + b * TILE);
+                tc::mbar_arrive_expect_tx(vb, TILE);
+                tc::tma_load_2d(vs, &vmap, 0, y, vb);
+                tc::tma_load_2d(vs + BOX, &vmap, 64, y, vb);
+                vissued = j + 1;
+            }
+            for (int i = vissued >= 2 ? vissued - 2 : 0; i < vissued; ++i)
+                tc::mbar_wait(tc::smem_u32(&fb.v_full[i & 1]), (i >> 1) & 1, nullptr, 0);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -387,13 +402,13 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         bool ok = true;
         for (int j = 0; j < nb && ok; ++j) {
             const int b = j & 1;
-            ok = fwait(tc::smem_u32(&fb.v_full), j & 1, abort, err, FE_V);
+            ok = fwait(tc::smem_u32(&fb.v_full[b]), (j >> 1) & 1, abort, err, FE_V);
             // V^T buffer b was last read by the product of block j - 2
             if (ok && j >= 2) ok = fwait(tc::smem_u32(&fb.pv_done[b]), ((j - 2) >> 1) & 1, abort, err, FE_PV);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc::fence_after_sync();
-            const unsigned char *vt = sm + SMEM_V + vbox * BOX;
+            const unsigned char *vt = sm + SMEM_V + b * TILE + vbox * BOX;
 #pragma unroll 1
             for (int cp = 0; cp < 4; ++cp) {   // 32 keys -> 16 TMEM columns of key pairs
                 uint32_t r[16];
@@ -407,7 +422,7 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 tc::tmem_st16(tmem + lane_base + COL_VT + b * 64 + cp * 16, r);
             }
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&fb.v_free));   // V read: the next block's V may load
+            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&fb.v_free[b]));   // V stage b read: block j + 2 may load
             // the softmax of block j decides whether O^T must be rescaled first
             ok = fwait(tc::smem_u32(&fb.p_full[b]), (j >> 1) & 1, abort, err, FE_P);
             ok = __shfl_sync(0xffffffffu, ok, 0);
