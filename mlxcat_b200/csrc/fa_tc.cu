@@ -6,40 +6,35 @@
 // query token i of the chunk sits at position s0 + i and sees keys 0..s0+i of
 // the row's cache (earlier chunks included).
 //
-// CTA = (128-query tile, query head).  Keys stream in blocks of 128 through
-// one K stage and two V stages (TMA, 128-byte swizzle; K_{j+1} loads once S_j
-// is computed, V_{j+1} while V_j is moved into TMEM), each from its own
-// producer thread.  With one V stage the next V load waited for the previous
-// transpose, and load plus transpose set the pace of every key block.
-// Per key block j:
-//   S_j  = Q K_j^T            tcgen05.mma, A = Q tile and B = K tile from shared
-//                              memory (both K-major), S in TMEM (two buffers, so
-//                              S_{j+1} is computed while S_j is in the softmax)
+// CTA = (128-query tile, query head).  Keys stream in blocks of 128 through two
+// K and two V stages (TMA, 128-byte swizzle), each fed by its own producer
+// thread.  Per key block j (buffer b = j & 1):
+//   S_j  = Q K_j^T            tcgen05.mma, A = Q and B = K_j from shared memory
+//                              (both K-major), S into TMEM buffer b
 //   P_j  = exp2(S_j*c - m)    eight softmax warps, two per query row (TMEM lane),
-//                              each taking 64 of the block's 128 keys:
-//                              the running max m moves only when a row's max
-//                              grows by more than 8 (log2 units), so P <= 256
-//                              fits fp16 and O rarely needs rescaling; P is
-//                              stored row-major into shared memory with the
-//                              128-byte swizzle (the MMA's K-major B operand)
-//   O^T += V_j^T P_j^T         tcgen05.mma with A = V_j^T in TMEM: four warps,
-//                              thread = feature d (TMEM lane), read V_j column d
-//                              out of the swizzled tile and store it as fp16
-//                              key pairs; O^T [d][query] accumulates in TMEM
-// so every shared-memory operand is K-major.  When some row's max moved, the
-// V warps scale the O^T columns of those rows by alpha before the next
-// product.  The V warps then write O^T / l as fp16 [token][head * 128 + d].
+//                              each taking 64 of the block's 128 keys; the
+//                              running max m moves only when a row's max grows
+//                              by more than 8 (log2 units), so P <= 256 fits
+//                              fp16 and O rarely needs rescaling.  P goes back
+//                              into TMEM as fp16 key pairs over the first 64
+//                              columns of S buffer b.
+//   O   += P_j V_j            tcgen05.mma with A = P_j from TMEM and B = V_j
+//                              read in place from its TMA tile as an MN-major
+//                              operand (keys along K, features along N); O
+//                              [query][feature] accumulates in TMEM.
+// When a row's max moved, its two softmax threads scale that row of O (once
+// the product of block j - 1 is in) before P_j is handed to the issuer; they
+// finally write O / l as fp16 [token][head * 128 + d].  (An earlier layout
+// computed O^T = V^T P^T with V^T copied into TMEM by four more warps; that copy
+// set the pace of every key block.)
 //
 // Warps: 0 TMA producer (Q, K), 1 MMA issuer, 2 TMEM allocation, 3 TMA
-// producer (V), 4-11 softmax (keys
-// 0-63 in warps 4-7, 64-127 in warps 8-11; the two halves of a row exchange
-// their partial max through shared memory), 12-15 V^T / rescale / epilogue
-// (warp w owns TMEM lanes 32 * (w % 4)..).  The softmax is the critical path:
-// exp2 runs as ex2.approx (fp16 P), and its loops are kept small so that the
-// three roles sharing a sub-partition do not evict each other's code.
-// Every wait is bounded; a timeout sets *err and an abort flag after which
-// every role skips its work, the producer waits for its copies and the issuer
-// for its last commit, and the CTA frees TMEM.
+// producer (V), 4-11 softmax and epilogue (keys 0-63 in warps 4-7, 64-127 in
+// warps 8-11; the two halves of a row exchange their partial max through
+// shared memory).  The softmax is the critical path: exp2 runs as ex2.approx
+// (fp16 P).  Every wait is bounded; a timeout sets *err and an abort flag after
+// which every role skips its work, the producers wait for their copies and the
+// issuer for everything it committed, and the CTA frees TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -56,38 +51,31 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
 namespace {
 
 constexpr int FD = 128;                 // head_dim
-constexpr int BQ = 128;                 // queries per CTA (MMA M of Q K^T, N of V^T P^T)
+constexpr int BQ = 128;                 // queries per CTA (MMA M of both products)
 constexpr int BKEYS = 128;              // keys per block
 constexpr int BOX = 128 * 128;          // one [128 rows x 128 B] swizzled box
 constexpr int TILE = 2 * BOX;           // 128 rows x 256 B (head_dim 128, two boxes)
-constexpr int F_THREADS = 512;
-constexpr int SM_WARP0 = 4, VT_WARP0 = 12;
-constexpr int EPI_BAR = 1;              // softmax + V warps, before the epilogue (384 threads)
-constexpr int PAIR_BAR0 = 2;            // 2..5: the two softmax warps of one lane quarter
-constexpr uint32_t COL_S = 0, COL_O = 256, COL_VT = 384;   // S: 2 x 128, O^T: 128, V^T: 2 x 64 columns
+constexpr int F_THREADS = 384;
+constexpr int SM_WARP0 = 4;
+constexpr int PAIR_BAR0 = 1;            // 1..4: the two softmax warps of one lane quarter
+constexpr uint32_t COL_S = 0, COL_O = 256;   // S (and P over it): 2 x 128 columns, O: 128 columns
 
-enum FaErr { FE_Q = 31, FE_K = 32, FE_V = 33, FE_FREE = 34, FE_SFULL = 35, FE_SFREE = 36, FE_P = 37, FE_VT = 38,
-             FE_PV = 39 };
+enum FaErr { FE_Q = 31, FE_K = 32, FE_V = 33, FE_FREE = 34, FE_SFULL = 35, FE_P = 37, FE_PV = 39 };
 
-// Block j uses buffer j & 1 of everything double-buffered (S, P, V, V^T,
-// alpha, partial maxima) and the barriers of that buffer, so a role may run one
-// block ahead of another without a barrier phase being overtaken.  The single K
-// stage has one full / free barrier pair: it is refilled only after its
-// consumer released it, so neither side can run two phases ahead.
+// Block j uses buffer j & 1 of every double-buffered resource (K and V stages,
+// S / P in TMEM, partial maxima) and the barriers of that buffer, so a role may
+// run one block ahead of another without a barrier phase being overtaken.
 struct FaBars {
-    unsigned long long q_full, k_full, k_free, v_full[2], v_free[2], s_full[2], s_free[2], p_full[2], vt_full[2],
-        pv_done[2];
-    float alpha[2][BQ];
+    unsigned long long q_full, k_full[2], k_free[2], v_full[2], v_free[2], s_full[2], p_full[2], pv_done[2], fin;
     float pmax[2][2][BQ];    // per block parity, per key half: partial row max
     float lsum[2][BQ];       // per key half
-    int rescale[2][4];       // per buffer, per softmax warp: some row's max moved
     uint32_t tmem;
     int abort;
 };
 
-constexpr size_t SMEM_Q = 0, SMEM_K = TILE, SMEM_V = 2 * TILE, SMEM_P = 4 * TILE, SMEM_BARS = 6 * TILE;
+constexpr size_t SMEM_Q = 0, SMEM_K = TILE, SMEM_V = 3 * TILE, SMEM_BARS = 5 * TILE;
 constexpr size_t FA_SMEM = 1024 + SMEM_BARS + sizeof(FaBars);
-static_assert(FA_SMEM <= 227 * 1024, "Q, K, two V and two P tiles must fit one CTA");
+static_assert(FA_SMEM <= 227 * 1024, "Q and two K and two V tiles must fit one CTA");
 
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
@@ -96,6 +84,32 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
         ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// A V tile as the MN-major B operand of O += P V: keys (the K dimension) are
+// the tile's 128-byte rows, features (N) run along a row; groups of 8 keys are
+// 1024 bytes apart (stride byte offset) and the two 64-feature boxes BOX bytes
+// apart (leading byte offset); 128-byte swizzle, as the TMA wrote it.
+__device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);            // start address
+    d |= (uint64_t)((BOX >> 4) & 0x3FFFu) << 16;        // leading byte offset: next 64 features
+    d |= (uint64_t)((1024 >> 4) & 0x3FFFu) << 32;       // stride byte offset: next 8 keys
+    d |= (uint64_t)1u << 46;                            // descriptor version (sm100)
+    d |= (uint64_t)2u << 61;                            // layout: SWIZZLE_128B
+    return d;
+}
+
+// this warp's 32 lanes, 32 consecutive 32-bit columns
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+          "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+          "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+          "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
 }
 
@@ -142,10 +156,6 @@ __device__ __forceinline__ bool fwait(uint32_t bar, uint32_t parity, volatile in
     }
 }
 
-__device__ __forceinline__ void named_sync(int id, int n) {
-    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory");
-}
-
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -164,11 +174,6 @@ __device__ __forceinline__ bool pair_sync_or(int id, int n, bool pred) {
         : "r"(id), "r"(n), "r"((uint32_t)pred)
         : "memory");
     return r != 0;
-}
-
-// byte offset of (row r, byte b) inside a 1024-aligned [rows x 128 B] box with the 128-byte swizzle
-__device__ __forceinline__ uint32_t sw128(int r, int b) {
-    return (uint32_t)(r * 128 + ((((b >> 4) ^ (r & 7)) << 4) | (b & 15)));
 }
 
 // Q: [tokens][Hq * 128] fp16 (the prefill's query buffer); K, V: one layer's
@@ -191,17 +196,16 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 
     if (threadIdx.x == 0) {
         tc::mbar_init(tc::smem_u32(&fb.q_full), 1);
-        tc::mbar_init(tc::smem_u32(&fb.k_full), 1);
-        tc::mbar_init(tc::smem_u32(&fb.k_free), 1);   // the S MMA's commit
         for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(tc::smem_u32(&fb.k_full[s]), 1);
+            tc::mbar_init(tc::smem_u32(&fb.k_free[s]), 1);    // the S product's commit
             tc::mbar_init(tc::smem_u32(&fb.v_full[s]), 1);
-            tc::mbar_init(tc::smem_u32(&fb.v_free[s]), 4);   // the four V warps
+            tc::mbar_init(tc::smem_u32(&fb.v_free[s]), 1);    // the O product's commit
             tc::mbar_init(tc::smem_u32(&fb.s_full[s]), 1);
-            tc::mbar_init(tc::smem_u32(&fb.s_free[s]), 8);
-            tc::mbar_init(tc::smem_u32(&fb.p_full[s]), 8);
-            tc::mbar_init(tc::smem_u32(&fb.vt_full[s]), 4);
+            tc::mbar_init(tc::smem_u32(&fb.p_full[s]), 8);    // the eight softmax warps
             tc::mbar_init(tc::smem_u32(&fb.pv_done[s]), 1);
         }
+        tc::mbar_init(tc::smem_u32(&fb.fin), 1);
         fb.abort = 0;
         tc::fence_barrier_init();
         tc::prefetch_tmap(&qmap);
@@ -215,67 +219,58 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     const uint32_t tmem = fb.tmem;
     griddep_wait();   // the queries and the chunk's keys come from the previous kernel
 
-    if (warp == 0) {
+    if (warp == 0 || warp == 3) {
         if (lane == 0) {
-            // ---------------- TMA producer: Q, then K ----------------
-            const uint32_t qb = tc::smem_u32(&fb.q_full);
-            tc::mbar_arrive_expect_tx(qb, TILE);
-            tc::tma_load_2d(tc::smem_u32(sm + SMEM_Q), &qmap, h * FD, q0, qb);
-            tc::tma_load_2d(tc::smem_u32(sm + SMEM_Q + BOX), &qmap, h * FD + 64, q0, qb);
-            int kissued = 0;
-            for (int j = 0; j < nb && !*abort; ++j) {
-                const int y = kv_row0 + j * BKEYS;
-                if (j >= 1 && !fwait(tc::smem_u32(&fb.k_free), (j - 1) & 1, abort, err, FE_FREE)) break;
-                const uint32_t kb = tc::smem_u32(&fb.k_full);
-                tc::mbar_arrive_expect_tx(kb, TILE);
-                tc::tma_load_2d(tc::smem_u32(sm + SMEM_K), &kmap, 0, y, kb);
-                tc::tma_load_2d(tc::smem_u32(sm + SMEM_K + BOX), &kmap, 64, y, kb);
-                kissued = j + 1;
+            // ---------------- TMA producers: warp 0 Q and K, warp 3 V ----------------
+            const bool kp = warp == 0;
+            if (kp) {
+                const uint32_t qb = tc::smem_u32(&fb.q_full);
+                tc::mbar_arrive_expect_tx(qb, TILE);
+                tc::tma_load_2d(tc::smem_u32(sm + SMEM_Q), &qmap, h * FD, q0, qb);
+                tc::tma_load_2d(tc::smem_u32(sm + SMEM_Q + BOX), &qmap, h * FD + 64, q0, qb);
             }
-            // copies in flight must land before the CTA's shared memory is released
-            tc::mbar_wait(tc::smem_u32(&fb.q_full), 0, nullptr, 0);
-            if (kissued) tc::mbar_wait(tc::smem_u32(&fb.k_full), (kissued - 1) & 1, nullptr, 0);
-        }
-    } else if (warp == 3) {
-        if (lane == 0) {
-            // ---------------- TMA producer: V, two stages ----------------
-            int vissued = 0;
+            const CUtensorMap *map = kp ? &kmap : &vmap;
+            unsigned long long *full = kp ? fb.k_full : fb.v_full, *freed = kp ? fb.k_free : fb.v_free;
+            unsigned char *stage0 = sm + (kp ? SMEM_K : SMEM_V);
+            int issued = 0;
             for (int j = 0; j < nb && !*abort; ++j) {
                 const int y = kv_row0 + j * BKEYS, b = j & 1;
-                // stage b was last read (moved into TMEM) for block j - 2
-                if (j >= 2 && !fwait(tc::smem_u32(&fb.v_free[b]), ((j - 2) >> 1) & 1, abort, err, FE_FREE)) break;
-                const uint32_t vb = tc::smem_u32(&fb.v_full[b]);
-                const uint32_t vs = tc::smem_u32(sm + SMEM_V + b * TILE);
-                tc::mbar_arrive_expect_tx(vb, TILE);
-                tc::tma_load_2d(vs, &vmap, 0, y, vb);
-                tc::tma_load_2d(vs + BOX, &vmap, 64, y, vb);
-                vissued = j + 1;
+                // stage b was last read by the product of block j - 2
+                if (j >= 2 && !fwait(tc::smem_u32(&freed[b]), ((j - 2) >> 1) & 1, abort, err, FE_FREE)) break;
+                const uint32_t bar = tc::smem_u32(&full[b]), st = tc::smem_u32(stage0 + b * TILE);
+                tc::mbar_arrive_expect_tx(bar, TILE);
+                tc::tma_load_2d(st, map, 0, y, bar);
+                tc::tma_load_2d(st + BOX, map, 64, y, bar);
+                issued = j + 1;
             }
-            for (int i = vissued >= 2 ? vissued - 2 : 0; i < vissued; ++i)
-                tc::mbar_wait(tc::smem_u32(&fb.v_full[i & 1]), (i >> 1) & 1, nullptr, 0);
+            // copies in flight must land before the CTA's shared memory is released
+            if (kp) tc::mbar_wait(tc::smem_u32(&fb.q_full), 0, nullptr, 0);
+            for (int i = issued >= 2 ? issued - 2 : 0; i < issued; ++i)
+                tc::mbar_wait(tc::smem_u32(&full[i & 1]), (i >> 1) & 1, nullptr, 0);
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
-            constexpr uint32_t idesc = tc::idesc_f16_f32(128, 128);
-            const uint32_t qa = tc::smem_u32(sm + SMEM_Q), pa = tc::smem_u32(sm + SMEM_P);
+            constexpr uint32_t idesc_s = tc::idesc_f16_f32(128, 128);
+            constexpr uint32_t idesc_pv = tc::idesc_f16_f32(128, 128) | (1u << 16);   // B (V) MN-major
+            const uint32_t qa = tc::smem_u32(sm + SMEM_Q);
             bool ok = fwait(tc::smem_u32(&fb.q_full), 0, abort, err, FE_Q);
-            int committed = 0;   // PV products committed
             auto issue_s = [&](int j) -> bool {
-                const int s = j & 1;
-                if (!fwait(tc::smem_u32(&fb.k_full), j & 1, abort, err, FE_K)) return false;
-                if (j >= 2 && !fwait(tc::smem_u32(&fb.s_free[s]), ((j - 2) >> 1) & 1, abort, err, FE_SFREE))
+                const int b = j & 1;
+                if (!fwait(tc::smem_u32(&fb.k_full[b]), (j >> 1) & 1, abort, err, FE_K)) return false;
+                // S buffer b holds P_{j-2} until the product of block j - 2 has read it
+                if (j >= 2 && !fwait(tc::smem_u32(&fb.pv_done[b]), ((j - 2) >> 1) & 1, abort, err, FE_PV))
                     return false;
                 tc::fence_after_sync();
-                const uint32_t ka = tc::smem_u32(sm + SMEM_K);
+                const uint32_t ka = tc::smem_u32(sm + SMEM_K + b * TILE);
 #pragma unroll
                 for (int kk = 0; kk < FD / 16; ++kk) {   // 16 features per step: box kk/4, +32 B per step
                     const uint32_t off = (uint32_t)((kk >> 2) * BOX + (kk & 3) * 32);
-                    mma_ss(tmem + COL_S + s * 128, tc::sdesc_k_sw128(qa + off), tc::sdesc_k_sw128(ka + off), idesc,
+                    mma_ss(tmem + COL_S + b * 128, tc::sdesc_k_sw128(qa + off), tc::sdesc_k_sw128(ka + off), idesc_s,
                            kk ? 1u : 0u);
                 }
-                tc::mma_commit(tc::smem_u32(&fb.s_full[s]));
-                tc::mma_commit(tc::smem_u32(&fb.k_free));   // K read: the next block's K may load
+                tc::mma_commit(tc::smem_u32(&fb.s_full[b]));
+                tc::mma_commit(tc::smem_u32(&fb.k_free[b]));   // K stage b read
                 return true;
             };
             if (ok) ok = issue_s(0);
@@ -283,37 +278,34 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 const int b = j & 1;
                 if (j + 1 < nb && !issue_s(j + 1)) break;
                 if (!fwait(tc::smem_u32(&fb.p_full[b]), (j >> 1) & 1, abort, err, FE_P)) break;
-                if (!fwait(tc::smem_u32(&fb.vt_full[b]), (j >> 1) & 1, abort, err, FE_VT)) break;
+                if (!fwait(tc::smem_u32(&fb.v_full[b]), (j >> 1) & 1, abort, err, FE_V)) break;
                 tc::fence_after_sync();
-                const uint32_t pb = pa + b * TILE;
+                const uint32_t va = tc::smem_u32(sm + SMEM_V + b * TILE);
 #pragma unroll
-                for (int kk = 0; kk < BKEYS / 16; ++kk) {   // 16 keys per step: 8 TMEM columns of V^T
-                    const uint32_t off = (uint32_t)((kk >> 2) * BOX + (kk & 3) * 32);
-                    tc::mma_ts_f16(tmem + COL_O, tmem + COL_VT + b * 64 + kk * 8, tc::sdesc_k_sw128(pb + off), idesc,
-                                   (j | kk) ? 1u : 0u);
-                }
+                for (int kk = 0; kk < BKEYS / 16; ++kk)   // 16 keys per step: 8 TMEM columns of P, 2048 B of V
+                    tc::mma_ts_f16(tmem + COL_O, tmem + COL_S + b * 128 + kk * 8, sdesc_mn_sw128(va + kk * 2048),
+                                   idesc_pv, (j | kk) ? 1u : 0u);
                 tc::mma_commit(tc::smem_u32(&fb.pv_done[b]));
-                committed = j + 1;
+                tc::mma_commit(tc::smem_u32(&fb.v_free[b]));   // V stage b read
             }
-            // the MMAs issued must finish before TMEM is freed
-            if (committed > 0)
-                tc::mbar_wait(tc::smem_u32(&fb.pv_done[(committed - 1) & 1]), ((committed - 1) >> 1) & 1, nullptr, 0);
+            // every product issued must finish before TMEM is freed
+            tc::mma_commit(tc::smem_u32(&fb.fin));
+            tc::mbar_wait(tc::smem_u32(&fb.fin), 0, nullptr, 0);
         }
-    } else if (warp >= SM_WARP0 && warp < VT_WARP0) {
-        // ---------------- softmax: thread = (query row, key half) ----------------
+    } else if (warp >= SM_WARP0) {
+        // ---------------- softmax and epilogue: thread = (query row, key half) ----------------
         const int quarter = warp & 3, half = (warp - SM_WARP0) >> 2;
         const int q = quarter * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         const int qpos = qp0 + q;
         const bool qvalid = q < nq;
         float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
         for (int j = 0; j < nb; ++j) {
             const int b = j & 1;
-            // S_j computed, and P buffer b released by the product of block j - 2
-            bool ok = fwait(tc::smem_u32(&fb.s_full[b]), (j >> 1) & 1, abort, err, FE_SFULL);
-            if (ok && j >= 2) ok = fwait(tc::smem_u32(&fb.pv_done[b]), ((j - 2) >> 1) & 1, abort, err, FE_PV);
+            ok = fwait(tc::smem_u32(&fb.s_full[b]), (j >> 1) & 1, abort, err, FE_SFULL);
             ok = __shfl_sync(0xffffffffu, ok, 0);
-            // this half's 64 scores of row q, in registers for both steps
+            // this half's 64 scores of row q
             uint32_t v[64];
             const int lim = qvalid ? qpos - j * BKEYS - half * 64 : -1;   // columns 0..lim visible
             float mx = -INFINITY;
@@ -332,139 +324,97 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 }
                 fb.pmax[b][half][q] = mx;
             }
-            // the two halves of the row meet here; both leave together on an abort
-            if (pair_sync_or(PAIR_BAR0 + quarter, 64, !ok)) break;
+            // the two halves of the row meet here (both have read their scores before
+            // either writes P over them); both leave together on an abort
+            tc::fence_before_sync();
+            ok = !pair_sync_or(PAIR_BAR0 + quarter, 64, !ok);
+            if (!ok) break;
+            tc::fence_after_sync();
             mx = fmaxf(fb.pmax[b][0][q], fb.pmax[b][1][q]) * scale_log2;
             float alpha = 1.f;
-            if (mx > m_used + 8.f) {   // the row's max moved: rescale l (and O, by the V warps)
+            if (mx > m_used + 8.f) {   // the row's max moved: rescale l and O
                 alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - mx);
                 m_used = mx;
             }
-            // P = exp2(S c - m) as fp16 into P[b] row q, box `half` (128-byte swizzle).
+            // P = exp2(S c - m) as fp16 key pairs into columns half*32.. of S buffer b.
             // A half with every key visible (all but the diagonal blocks) skips the mask;
             // l sums the fp32 values (their fp16 rounding errors average out in l).
-            unsigned char *prow = sm + SMEM_P + b * TILE + half * BOX;
             const bool live = m_used != -INFINITY;
             const float nm = -m_used;
             float sum = 0.f;
+            uint32_t pk[32];
             if (live && lim >= 63) {
 #pragma unroll
-                for (int c8 = 0; c8 < 8; ++c8) {   // 8 keys = one 16-byte chunk
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int c0 = c8 * 8 + 2 * i;
-                        const float p0 = ex2(fmaf(__uint_as_float(v[c0]), scale_log2, nm));
-                        const float p1 = ex2(fmaf(__uint_as_float(v[c0 + 1]), scale_log2, nm));
-                        sum += p0 + p1;
-                        const __half2 hp = __floats2half2_rn(p0, p1);
-                        pk[i] = *reinterpret_cast<const uint32_t *>(&hp);
-                    }
-                    *reinterpret_cast<uint4 *>(prow + sw128(q, c8 * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                for (int i = 0; i < 32; ++i) {
+                    const float p0 = ex2(fmaf(__uint_as_float(v[2 * i]), scale_log2, nm));
+                    const float p1 = ex2(fmaf(__uint_as_float(v[2 * i + 1]), scale_log2, nm));
+                    sum += p0 + p1;
+                    const __half2 hp = __floats2half2_rn(p0, p1);
+                    pk[i] = *reinterpret_cast<const uint32_t *>(&hp);
                 }
             } else {
 #pragma unroll
-                for (int c8 = 0; c8 < 8; ++c8) {
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int c0 = c8 * 8 + 2 * i;
-                        const float p0 = (live && c0 <= lim) ? ex2(fmaf(__uint_as_float(v[c0]), scale_log2, nm)) : 0.f;
-                        const float p1 = (live && c0 + 1 <= lim) ? ex2(fmaf(__uint_as_float(v[c0 + 1]), scale_log2, nm)) : 0.f;
-                        sum += p0 + p1;
-                        const __half2 hp = __floats2half2_rn(p0, p1);
-                        pk[i] = *reinterpret_cast<const uint32_t *>(&hp);
-                    }
-                    *reinterpret_cast<uint4 *>(prow + sw128(q, c8 * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                for (int i = 0; i < 32; ++i) {
+                    const int c0 = 2 * i;
+                    const float p0 = (live && c0 <= lim) ? ex2(fmaf(__uint_as_float(v[c0]), scale_log2, nm)) : 0.f;
+                    const float p1 = (live && c0 + 1 <= lim) ? ex2(fmaf(__uint_as_float(v[c0 + 1]), scale_log2, nm)) : 0.f;
+                    sum += p0 + p1;
+                    const __half2 hp = __floats2half2_rn(p0, p1);
+                    pk[i] = *reinterpret_cast<const uint32_t *>(&hp);
                 }
             }
+            tmem_st32(tmem + lane_base + COL_S + b * 128 + half * 32, pk);
             l = l * alpha + sum;
-            if (half == 0) {
-                fb.alpha[b][q] = alpha;
-                const int moved = __any_sync(0xffffffffu, alpha != 1.f && j > 0);
-                if (lane == 0) fb.rescale[b][quarter] = moved;
-            }
-            tc::fence_before_sync();
-            tc::fence_proxy_async_smem();   // P (generic stores) visible to the tensor core
-            __syncwarp();
-            if (lane == 0) {
-                tc::mbar_arrive(tc::smem_u32(&fb.s_free[b]));
-                tc::mbar_arrive(tc::smem_u32(&fb.p_full[b]));
-            }
-        }
-        fb.lsum[half][q] = l;
-        named_sync(EPI_BAR, 384);
-    } else if (warp >= VT_WARP0) {
-        // ---------------- V^T into TMEM, O rescale, epilogue: thread = feature d ----------------
-        const int d = (warp - VT_WARP0) * 32 + lane;
-        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const int vbox = d >> 6, vb = (d & 63) * 2;   // V[key][d]: box, byte within the 128-byte row
-        bool ok = true;
-        for (int j = 0; j < nb && ok; ++j) {
-            const int b = j & 1;
-            ok = fwait(tc::smem_u32(&fb.v_full[b]), (j >> 1) & 1, abort, err, FE_V);
-            // V^T buffer b was last read by the product of block j - 2
-            if (ok && j >= 2) ok = fwait(tc::smem_u32(&fb.pv_done[b]), ((j - 2) >> 1) & 1, abort, err, FE_PV);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
-            tc::fence_after_sync();
-            const unsigned char *vt = sm + SMEM_V + b * TILE + vbox * BOX;
+            // a row whose max moved scales its O (this half's 64 features) once the
+            // product of block j - 1 is in; the product of block j waits for p_full
+            if (__any_sync(0xffffffffu, alpha != 1.f && j > 0)) {
+                bool okp = true;
+                if (lane == 0) okp = fwait(tc::smem_u32(&fb.pv_done[b ^ 1]), ((j - 1) >> 1) & 1, abort, err, FE_PV);
+                okp = __shfl_sync(0xffffffffu, okp, 0);
+                if (okp) {
+                    tc::fence_after_sync();
 #pragma unroll 1
-            for (int cp = 0; cp < 4; ++cp) {   // 32 keys -> 16 TMEM columns of key pairs
-                uint32_t r[16];
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t o[16];
+                        tc::tmem_ld16(tmem + lane_base + COL_O + half * 64 + c * 16, o);
+                        tc::tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int key = cp * 32 + 2 * i;
-                    const uint16_t a = *reinterpret_cast<const uint16_t *>(vt + sw128(key, vb));
-                    const uint16_t c = *reinterpret_cast<const uint16_t *>(vt + sw128(key + 1, vb));
-                    r[i] = (uint32_t)a | ((uint32_t)c << 16);
-                }
-                tc::tmem_st16(tmem + lane_base + COL_VT + b * 64 + cp * 16, r);
-            }
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&fb.v_free[b]));   // V stage b read: block j + 2 may load
-            // the softmax of block j decides whether O^T must be rescaled first
-            ok = fwait(tc::smem_u32(&fb.p_full[b]), (j >> 1) & 1, abort, err, FE_P);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
-            if (fb.rescale[b][0] | fb.rescale[b][1] | fb.rescale[b][2] | fb.rescale[b][3]) {
-                // O^T must hold the product of block j - 1 before it is scaled
-                ok = fwait(tc::smem_u32(&fb.pv_done[b ^ 1]), ((j - 1) >> 1) & 1, abort, err, FE_PV);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) break;
-                tc::fence_after_sync();
-#pragma unroll 1
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t v[16];
-                    tc::tmem_ld16(tmem + lane_base + COL_O + c * 16, v);
-                    tc::tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                        v[i] = __float_as_uint(__uint_as_float(v[i]) * fb.alpha[b][c * 16 + i]);
-                    tc::tmem_st16(tmem + lane_base + COL_O + c * 16, v);
+                        for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tc::tmem_st16(tmem + lane_base + COL_O + half * 64 + c * 16, o);
+                    }
                 }
             }
             tc::tmem_wait_st();
             tc::fence_before_sync();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&fb.vt_full[b]));
+            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&fb.p_full[b]));
         }
-        if (ok && nb > 0) ok = fwait(tc::smem_u32(&fb.pv_done[(nb - 1) & 1]), ((nb - 1) >> 1) & 1, abort, err, FE_PV);
-        named_sync(EPI_BAR, 384);
-        ok = __shfl_sync(0xffffffffu, ok, 0) && !*abort;
+        // epilogue: O / l of row q, this half's 64 features, once the last product is in
+        fb.lsum[half][q] = l;
+        if (ok && lane == 0) ok = fwait(tc::smem_u32(&fb.pv_done[(nb - 1) & 1]), ((nb - 1) >> 1) & 1, abort, err, FE_PV);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        ok = !pair_sync_or(PAIR_BAR0 + quarter, 64, !ok) && !*abort;
         if (ok) {
             tc::fence_after_sync();
-            __half *o = out + (size_t)q0 * Hq * FD + h * FD + d;
+            const float lq = fb.lsum[0][q] + fb.lsum[1][q];
+            const float inv = lq > 0.f ? 1.f / lq : 0.f;
+            __half *o = out + (size_t)(q0 + q) * Hq * FD + h * FD + half * 64;
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                uint32_t v[32];
-                tmem_ld32(tmem + lane_base + COL_O + c * 32, v);
+            for (int c = 0; c < 2; ++c) {
+                uint32_t acc[32];
+                tmem_ld32(tmem + lane_base + COL_O + half * 64 + c * 32, acc);
                 tc::tmem_wait_ld();
+                uint32_t hv[16];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int q = c * 32 + i;
-                    const float lq = fb.lsum[0][q] + fb.lsum[1][q];
-                    if (q < nq) o[(size_t)q * Hq * FD] = __float2half_rn(lq > 0.f ? __uint_as_float(v[i]) / lq : 0.f);
+                for (int i = 0; i < 16; ++i) {
+                    const __half2 h2 = __floats2half2_rn(__uint_as_float(acc[2 * i]) * inv,
+                                                         __uint_as_float(acc[2 * i + 1]) * inv);
+                    hv[i] = *reinterpret_cast<const uint32_t *>(&h2);
+                }
+                if (qvalid) {
+                    uint4 *dst = reinterpret_cast<uint4 *>(o + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) dst[i] = make_uint4(hv[4 * i], hv[4 * i + 1], hv[4 * i + 2], hv[4 * i + 3]);
                 }
             }
         }
