@@ -4,6 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config llama3-8b]
     python bench.py --impl reference ...      # CPU restatement arm
     python bench.py --config qwen3-4b --kernel-case q4_linear|attention|moe
+    python bench.py --kernel-case prefill|prefill_attention|gemm
 
 Default workload (``llama3-8b``): the Llama-3-8B-shape serving configuration,
 32 rows per GPU of 4096-token segment-pool prompts; requests arrive Poisson(4)
@@ -667,6 +668,35 @@ def run_kernel_case(args):
     if args.kernel_case == "prefill":
         run_prefill_case(args, wl, cfg)
         return
+    if args.kernel_case == "prefill_attention":
+        # the admission's causal attention over one 4096-token prompt chunk
+        # (mlxcat_op_prefill_attention, one layer); a few tens of MB on the device
+        n, Hq, Hkv, D = 4096, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        q = (torch.randn((n, Hq * D), device="cuda") * 0.5).half()
+        kc = (torch.randn((1, Hkv, n, D), device="cuda") * 0.5).half()
+        vc = torch.randn((1, Hkv, n, D), device="cuda").half()
+        out = torch.empty((n, Hq * D), dtype=torch.float16, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        flops = 4.0 * Hq * D * n * (n + 1) / 2
+
+        def launch():
+            A.check(L.mlxcat_op_prefill_attention(p(q), p(kc), p(vc), 1, n, 0, 0, n, Hq, Hkv, D, p(out), p(err),
+                                                  None))
+        for i in range(args.warmup):
+            launch()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            launch()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        print(json.dumps({"kernel_case": "prefill_attention", "config": args.config,
+                          "shape": {"tokens": n, "Hq": Hq, "Hkv": Hkv, "D": D, "causal": True},
+                          "us_per_launch": ms * 1e3, "tflops": flops / (ms / 1e3) / 1e12,
+                          "timeout_flag": int(err.item())}))
+        return
     if args.kernel_case == "gemm":
         # the prefill's fused gate/up GEMM on one 2048-token chunk (fp16 weights, tcgen05)
         N, K, Mt = 2 * cfg.intermediate, cfg.hidden, 2048
@@ -819,7 +849,8 @@ def main():
     ap.add_argument("--config", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="mlxcat", choices=["mlxcat", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-case", choices=["q4_linear", "attention", "moe", "gemm", "prefill"])
+    ap.add_argument("--kernel-case", choices=["q4_linear", "attention", "moe", "gemm", "prefill",
+                                              "prefill_attention"])
     ap.add_argument("--kernel-reps", type=int, default=50)
     ap.add_argument("--tp-allreduce", default="peer", choices=["peer", "nccl"],
                     help="tensor-parallel allreduce: fused over peer memory, or one NCCL call per block")
