@@ -77,105 +77,6 @@ constexpr size_t SMEM_Q = 0, SMEM_K = TILE, SMEM_V = 3 * TILE, SMEM_BARS = 5 * T
 constexpr size_t FA_SMEM = 1024 + SMEM_BARS + sizeof(FaBars);
 static_assert(FA_SMEM <= 227 * 1024, "Q and two K and two V tiles must fit one CTA");
 
-__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
-        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-// A V tile as the MN-major B operand of O += P V: keys (the K dimension) are
-// the tile's 128-byte rows, features (N) run along a row; groups of 8 keys are
-// 1024 bytes apart (stride byte offset) and the two 64-feature boxes BOX bytes
-// apart (leading byte offset); 128-byte swizzle, as the TMA wrote it.
-__device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);            // start address
-    d |= (uint64_t)((BOX >> 4) & 0x3FFFu) << 16;        // leading byte offset: next 64 features
-    d |= (uint64_t)((1024 >> 4) & 0x3FFFu) << 32;       // stride byte offset: next 8 keys
-    d |= (uint64_t)1u << 46;                            // descriptor version (sm100)
-    d |= (uint64_t)2u << 61;                            // layout: SWIZZLE_128B
-    return d;
-}
-
-// this warp's 32 lanes, 32 consecutive 32-bit columns
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n"
-        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-          "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
-          "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
-          "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-        : "memory");
-}
-
-// this warp's 32 lanes, 32 consecutive 32-bit columns
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t *v) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
-          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-        : "r"(taddr)
-        : "memory");
-}
-
-// try_wait with a suspend-time hint: a waiting warp sleeps in hardware until the
-// phase completes (or the hint elapses) instead of spinning on the issue slots
-// that the softmax and V warps sharing its sub-partition need
-__device__ __forceinline__ bool try_wait_sleep(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(1000000u)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ bool fwait(uint32_t bar, uint32_t parity, volatile int *abort, int *err, int code) {
-    if (*abort) return false;
-    if (tc::mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = tc::global_ns();
-    for (;;) {
-        if (try_wait_sleep(bar, parity)) return true;
-        if (*abort) return false;
-        if (tc::global_ns() - t0 > tc::WAIT_LIMIT_NS) {
-            *abort = 1;
-            if (err) atomicExch(err, code);
-            return false;
-        }
-    }
-}
-
-__device__ __forceinline__ float ex2(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
-// named barrier over n threads that also ORs a predicate across them
-__device__ __forceinline__ bool pair_sync_or(int id, int n, bool pred) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 q, %3, 0;\n\t"
-        "bar.red.or.pred p, %1, %2, q;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(r)
-        : "r"(id), "r"(n), "r"((uint32_t)pred)
-        : "memory");
-    return r != 0;
-}
-
 // Q: [tokens][Hq * 128] fp16 (the prefill's query buffer); K, V: one layer's
 // cache viewed as [(row * Hkv + kvh) * max_len + key][128]; out: [tokens][Hq * 128].
 __global__ void __launch_bounds__(F_THREADS, 1)
@@ -236,7 +137,7 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             for (int j = 0; j < nb && !*abort; ++j) {
                 const int y = kv_row0 + j * BKEYS, b = j & 1;
                 // stage b was last read by the product of block j - 2
-                if (j >= 2 && !fwait(tc::smem_u32(&freed[b]), ((j - 2) >> 1) & 1, abort, err, FE_FREE)) break;
+                if (j >= 2 && !tc::mbar_wait_abort(tc::smem_u32(&freed[b]), ((j - 2) >> 1) & 1, abort, err, FE_FREE)) break;
                 const uint32_t bar = tc::smem_u32(&full[b]), st = tc::smem_u32(stage0 + b * TILE);
                 tc::mbar_arrive_expect_tx(bar, TILE);
                 tc::tma_load_2d(st, map, 0, y, bar);
@@ -254,19 +155,19 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             constexpr uint32_t idesc_s = tc::idesc_f16_f32(128, 128);
             constexpr uint32_t idesc_pv = tc::idesc_f16_f32(128, 128) | (1u << 16);   // B (V) MN-major
             const uint32_t qa = tc::smem_u32(sm + SMEM_Q);
-            bool ok = fwait(tc::smem_u32(&fb.q_full), 0, abort, err, FE_Q);
+            bool ok = tc::mbar_wait_abort(tc::smem_u32(&fb.q_full), 0, abort, err, FE_Q);
             auto issue_s = [&](int j) -> bool {
                 const int b = j & 1;
-                if (!fwait(tc::smem_u32(&fb.k_full[b]), (j >> 1) & 1, abort, err, FE_K)) return false;
+                if (!tc::mbar_wait_abort(tc::smem_u32(&fb.k_full[b]), (j >> 1) & 1, abort, err, FE_K)) return false;
                 // S buffer b holds P_{j-2} until the product of block j - 2 has read it
-                if (j >= 2 && !fwait(tc::smem_u32(&fb.pv_done[b]), ((j - 2) >> 1) & 1, abort, err, FE_PV))
+                if (j >= 2 && !tc::mbar_wait_abort(tc::smem_u32(&fb.pv_done[b]), ((j - 2) >> 1) & 1, abort, err, FE_PV))
                     return false;
                 tc::fence_after_sync();
                 const uint32_t ka = tc::smem_u32(sm + SMEM_K + b * TILE);
 #pragma unroll
                 for (int kk = 0; kk < FD / 16; ++kk) {   // 16 features per step: box kk/4, +32 B per step
                     const uint32_t off = (uint32_t)((kk >> 2) * BOX + (kk & 3) * 32);
-                    mma_ss(tmem + COL_S + b * 128, tc::sdesc_k_sw128(qa + off), tc::sdesc_k_sw128(ka + off), idesc_s,
+                    tc::mma_ss_f16(tmem + COL_S + b * 128, tc::sdesc_k_sw128(qa + off), tc::sdesc_k_sw128(ka + off), idesc_s,
                            kk ? 1u : 0u);
                 }
                 tc::mma_commit(tc::smem_u32(&fb.s_full[b]));
@@ -277,13 +178,13 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             for (int j = 0; j < nb && ok; ++j) {
                 const int b = j & 1;
                 if (j + 1 < nb && !issue_s(j + 1)) break;
-                if (!fwait(tc::smem_u32(&fb.p_full[b]), (j >> 1) & 1, abort, err, FE_P)) break;
-                if (!fwait(tc::smem_u32(&fb.v_full[b]), (j >> 1) & 1, abort, err, FE_V)) break;
+                if (!tc::mbar_wait_abort(tc::smem_u32(&fb.p_full[b]), (j >> 1) & 1, abort, err, FE_P)) break;
+                if (!tc::mbar_wait_abort(tc::smem_u32(&fb.v_full[b]), (j >> 1) & 1, abort, err, FE_V)) break;
                 tc::fence_after_sync();
                 const uint32_t va = tc::smem_u32(sm + SMEM_V + b * TILE);
 #pragma unroll
                 for (int kk = 0; kk < BKEYS / 16; ++kk)   // 16 keys per step: 8 TMEM columns of P, 2048 B of V
-                    tc::mma_ts_f16(tmem + COL_O, tmem + COL_S + b * 128 + kk * 8, sdesc_mn_sw128(va + kk * 2048),
+                    tc::mma_ts_f16(tmem + COL_O, tmem + COL_S + b * 128 + kk * 8, tc::sdesc_mn_sw128(va + kk * 2048, BOX),
                                    idesc_pv, (j | kk) ? 1u : 0u);
                 tc::mma_commit(tc::smem_u32(&fb.pv_done[b]));
                 tc::mma_commit(tc::smem_u32(&fb.v_free[b]));   // V stage b read
@@ -303,7 +204,7 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         bool ok = true;
         for (int j = 0; j < nb; ++j) {
             const int b = j & 1;
-            ok = fwait(tc::smem_u32(&fb.s_full[b]), (j >> 1) & 1, abort, err, FE_SFULL);
+            ok = tc::mbar_wait_abort(tc::smem_u32(&fb.s_full[b]), (j >> 1) & 1, abort, err, FE_SFULL);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             // this half's 64 scores of row q
             uint32_t v[64];
@@ -311,8 +212,8 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             float mx = -INFINITY;
             if (ok) {
                 tc::fence_after_sync();
-                tmem_ld32(tmem + lane_base + COL_S + b * 128 + half * 64, v);
-                tmem_ld32(tmem + lane_base + COL_S + b * 128 + half * 64 + 32, v + 32);
+                tc::tmem_ld32(tmem + lane_base + COL_S + b * 128 + half * 64, v);
+                tc::tmem_ld32(tmem + lane_base + COL_S + b * 128 + half * 64 + 32, v + 32);
                 tc::tmem_wait_ld();
                 if (lim >= 63) {
 #pragma unroll
@@ -327,7 +228,7 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             // the two halves of the row meet here (both have read their scores before
             // either writes P over them); both leave together on an abort
             tc::fence_before_sync();
-            ok = !pair_sync_or(PAIR_BAR0 + quarter, 64, !ok);
+            ok = !tc::bar_sync_or(PAIR_BAR0 + quarter, 64, !ok);
             if (!ok) break;
             tc::fence_after_sync();
             mx = fmaxf(fb.pmax[b][0][q], fb.pmax[b][1][q]) * scale_log2;
@@ -346,8 +247,8 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             if (live && lim >= 63) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    const float p0 = ex2(fmaf(__uint_as_float(v[2 * i]), scale_log2, nm));
-                    const float p1 = ex2(fmaf(__uint_as_float(v[2 * i + 1]), scale_log2, nm));
+                    const float p0 = tc::ex2_approx(fmaf(__uint_as_float(v[2 * i]), scale_log2, nm));
+                    const float p1 = tc::ex2_approx(fmaf(__uint_as_float(v[2 * i + 1]), scale_log2, nm));
                     sum += p0 + p1;
                     const __half2 hp = __floats2half2_rn(p0, p1);
                     pk[i] = *reinterpret_cast<const uint32_t *>(&hp);
@@ -356,20 +257,20 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int c0 = 2 * i;
-                    const float p0 = (live && c0 <= lim) ? ex2(fmaf(__uint_as_float(v[c0]), scale_log2, nm)) : 0.f;
-                    const float p1 = (live && c0 + 1 <= lim) ? ex2(fmaf(__uint_as_float(v[c0 + 1]), scale_log2, nm)) : 0.f;
+                    const float p0 = (live && c0 <= lim) ? tc::ex2_approx(fmaf(__uint_as_float(v[c0]), scale_log2, nm)) : 0.f;
+                    const float p1 = (live && c0 + 1 <= lim) ? tc::ex2_approx(fmaf(__uint_as_float(v[c0 + 1]), scale_log2, nm)) : 0.f;
                     sum += p0 + p1;
                     const __half2 hp = __floats2half2_rn(p0, p1);
                     pk[i] = *reinterpret_cast<const uint32_t *>(&hp);
                 }
             }
-            tmem_st32(tmem + lane_base + COL_S + b * 128 + half * 32, pk);
+            tc::tmem_st32(tmem + lane_base + COL_S + b * 128 + half * 32, pk);
             l = l * alpha + sum;
             // a row whose max moved scales its O (this half's 64 features) once the
             // product of block j - 1 is in; the product of block j waits for p_full
             if (__any_sync(0xffffffffu, alpha != 1.f && j > 0)) {
                 bool okp = true;
-                if (lane == 0) okp = fwait(tc::smem_u32(&fb.pv_done[b ^ 1]), ((j - 1) >> 1) & 1, abort, err, FE_PV);
+                if (lane == 0) okp = tc::mbar_wait_abort(tc::smem_u32(&fb.pv_done[b ^ 1]), ((j - 1) >> 1) & 1, abort, err, FE_PV);
                 okp = __shfl_sync(0xffffffffu, okp, 0);
                 if (okp) {
                     tc::fence_after_sync();
@@ -391,9 +292,9 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         }
         // epilogue: O / l of row q, this half's 64 features, once the last product is in
         fb.lsum[half][q] = l;
-        if (ok && lane == 0) ok = fwait(tc::smem_u32(&fb.pv_done[(nb - 1) & 1]), ((nb - 1) >> 1) & 1, abort, err, FE_PV);
+        if (ok && lane == 0) ok = tc::mbar_wait_abort(tc::smem_u32(&fb.pv_done[(nb - 1) & 1]), ((nb - 1) >> 1) & 1, abort, err, FE_PV);
         ok = __shfl_sync(0xffffffffu, ok, 0);
-        ok = !pair_sync_or(PAIR_BAR0 + quarter, 64, !ok) && !*abort;
+        ok = !tc::bar_sync_or(PAIR_BAR0 + quarter, 64, !ok) && !*abort;
         if (ok) {
             tc::fence_after_sync();
             const float lq = fb.lsum[0][q] + fb.lsum[1][q];
@@ -402,7 +303,7 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 #pragma unroll 1
             for (int c = 0; c < 2; ++c) {
                 uint32_t acc[32];
-                tmem_ld32(tmem + lane_base + COL_O + half * 64 + c * 32, acc);
+                tc::tmem_ld32(tmem + lane_base + COL_O + half * 64 + c * 32, acc);
                 tc::tmem_wait_ld();
                 uint32_t hv[16];
 #pragma unroll

@@ -181,5 +181,108 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t saddr) {
     return d;
 }
 
+
+// D[tmem] (+)= A[smem desc] . B[smem desc]^T ; kind::f16 (fp16 inputs, fp32 accumulate)
+__device__ __forceinline__ void mma_ss_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor, MN-major, 128-byte swizzle: the K dimension
+// runs down 128-byte rows (8-row groups 1024 bytes apart: stride byte offset),
+// the MN dimension along a row, 64 16-bit elements per row; the next 64 MN
+// elements start `lbo` bytes on (leading byte offset).  This is the layout a
+// [rows][64-element] TMA box with the 128-byte swizzle writes, read with the
+// rows as K (e.g. the V tile of O += P V).
+__device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t saddr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);            // start address
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;        // leading byte offset: next 64 MN elements
+    d |= (uint64_t)((1024u >> 4) & 0x3FFFu) << 32;      // stride byte offset: next 8 K rows
+    d |= (uint64_t)1u << 46;                            // descriptor version (sm100)
+    d |= (uint64_t)2u << 61;                            // layout: SWIZZLE_128B
+    return d;
+}
+
+// this warp's 32 lanes, 32 consecutive 32-bit columns
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+          "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+          "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+          "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t *v) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+// try_wait with a suspend-time hint: a waiting warp sleeps in hardware until the
+// phase completes (or the hint elapses) instead of spinning on issue slots that
+// the warps sharing its sub-partition need
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(1000000u)
+        : "memory");
+    return ok != 0;
+}
+
+// bounded wait that also gives up once *abort is set; a timeout sets *abort and *err
+__device__ __forceinline__ bool mbar_wait_abort(uint32_t bar, uint32_t parity, volatile int *abort, int *err,
+                                                int code) {
+    if (*abort) return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity)) return true;
+        if (*abort) return false;
+        if (global_ns() - t0 > WAIT_LIMIT_NS) {
+            *abort = 1;
+            if (err) atomicExch(err, code);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// named barrier over n threads that also ORs a predicate across them
+__device__ __forceinline__ bool bar_sync_or(int id, int n, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %3, 0;\n\t"
+        "bar.red.or.pred p, %1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(r)
+        : "r"(id), "r"(n), "r"((uint32_t)pred)
+        : "memory");
+    return r != 0;
+}
+
 }  // namespace tc
 }  // namespace mlxcat
