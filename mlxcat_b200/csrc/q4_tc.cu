@@ -11,7 +11,11 @@
 // 4 KB of them next to its weight tile (pack_q4_sb below).
 //
 // Swap-AB: the 128 weight rows of a block are the MMA's M dimension, the
-// tokens of the verify batch (16..128) its N dimension.
+// tokens of the verify batch (a tile of 16..128, or 144..160 for the gate/up
+// projection) its N dimension.  One tcgen05.mma of M=128, K=16 holds the
+// tensor pipe for about 120 cycles whatever its N up to 128 (measured on
+// B200), so 129..160 tokens of the gate/up projection run as one tile instead
+// of two (the other projections keep two: measured slower as one).
 //
 // Schedule: persistent, one CTA per SM, stream-K over units of (128-row block
 // x 512-wide k chunk); a block whose chunks span several CTAs is finished by
@@ -21,8 +25,10 @@
 // Warp roles (20 warps):
 //   warp 18 (one lane)  W producer: per unit one W stage = two TMA boxes of
 //                       [128 rows x 128 B] (128B swizzle) + the unit's packed
-//                       scale/bias (bulk copy).  A W stage is released as soon
-//                       as the dequant warps have read it.
+//                       scale/bias (bulk copy); per 256-k half (one box) for
+//                       tiles above 128 tokens, whose 80 KB x stages leave
+//                       less room.  A W stage is released once the dequant
+//                       warps have put its values into TMEM.
 //   warp 19 (one lane)  x producer: per sub-chunk one x stage = the token tile
 //                       [4 x NT x 64] fp16 (3-D box, 128B swizzle), released
 //                       when the MMAs reading it have completed.  x stages and
@@ -39,9 +45,9 @@
 //   warps 16-17         MMA issuers (lane 0): issuer i waits on its named
 //                       barrier, then issues tcgen05.mma (M=128, N=NT, K=16,
 //                       A from TMEM, B from shared memory) for groups 2i, 2i+1
-//                       into its own fp32 accumulator in TMEM (one issuing
-//                       thread sustains about one MMA per 50 cycles; two keep
-//                       up with the dequantisers).
+//                       into its own fp32 accumulator in TMEM.  Tiles above
+//                       128 tokens have one issuer (one accumulator of NT
+//                       columns: the TMEM holds no second one).
 //
 // Inside each 8-wide k block the unpack order is (0,4,1,5,2,6,3,7); the token
 // operand is stored in that order and blocked by 64 features ([K/64][rows][64],
@@ -60,6 +66,8 @@
 // the CTA drains its in-flight copies and MMAs (bounded) before freeing TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -96,10 +104,10 @@ constexpr int EP_WARP0 = XP_WARP + 1;  // epilogue warps 20..23 (TMEM lane quart
 constexpr int EP_THREADS = 128;
 constexpr int THREADS = (EP_WARP0 + 4) * 32;
 constexpr int A_COLS = KS / 2;         // TMEM columns of one A buffer (fp16 pairs)
-constexpr int WBOX = ROWS * 128;       // one [128 rows x 128 B] weight box
+constexpr int WBOX = ROWS * 128;       // one [128 rows x 128 B] weight box (256 k)
 constexpr int SB_BYTES = 8 * ROWS * 4; // packed (scale, bias) of one unit
-constexpr int WSTAGE = 2 * WBOX + SB_BYTES;
 constexpr int MAX_SW = 4, MAX_AST = 3;
+constexpr int MAX_NT = 160;            // widest token tile (gate/up projection)
 constexpr int EPI_BAR = 9;             // named barrier of the epilogue warps (1..6: issuers)
 constexpr int TAIL_BAR = 10;           // named barrier of the dequant warps' tail epilogue
 constexpr int TAIL_THREADS = DQ_WARPS * 32;
@@ -108,19 +116,25 @@ enum ErrCode { ERR_WFULL = 1, ERR_XFULL = 2, ERR_MDONE = 3, ERR_XFREE = 4, ERR_W
 
 template <int NT>
 struct Cfg {
-    static constexpr int NI = 2;                             // MMA issuers
+    static constexpr bool WIDE = NT > 128;                   // one accumulator of up to 160 columns
+    static constexpr int NI = WIDE ? 1 : 2;                  // MMA issuers (one accumulator each)
     static constexpr int GPI = 4 / NI;                       // 64-k groups per issuer
     static constexpr int BAR_COUNT = 32 + 128 * GPI;         // issuer warp + its dequant warps
     // TMEM: ring of A buffers, then DSETS sets of NI fp32 accumulators.  With
     // two sets the MMAs of the next block segment run while the epilogue warps
     // read the previous one.
-    static constexpr int DCOLS = NT <= 32 ? 32 : (NT <= 64 ? 64 : 128);
+    static constexpr int DCOLS = NT <= 32 ? 32 : (NT <= 64 ? 64 : (NT <= 128 ? 128 : 256));
     static constexpr int DSETS = NT <= 64 ? 2 : 1;
     static constexpr int AST = NT <= 32 ? 3 : 2;             // ring slots: A buffers in TMEM = x stages
     static constexpr int D_COL = AST * A_COLS;
     static constexpr int XSTAGE = 4 * NT * 128;              // 256 k of NT tokens
     static constexpr int PIECES = NT / 16;                   // 16-token pieces of the epilogue
+    // W: one stage per unit (two boxes + the unit's scale/bias), or per 256-k
+    // half (one box + half of them) for the wide tile; two sub-chunks or one
+    // read each
+    static constexpr int WSTAGE = WIDE ? WBOX + SB_BYTES / 2 : 2 * WBOX + SB_BYTES;
     static_assert(D_COL + DSETS * NI * DCOLS <= 512, "TMEM budget");
+    static_assert(NT % 16 == 0 && NT <= MAX_NT, "token tile");
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
@@ -203,12 +217,12 @@ struct Smem {
     int abort_flag;
     int last_flag;
     float wsum[4][16];          // [row quarter][token of the piece]
-    float xch[128];             // epilogue warps: folded-norm scales; QKV tail: token rows / positions
+    float xch[MAX_NT];          // epilogue warps: folded-norm scales; QKV tail: token rows / positions
     // the tail epilogue of the dequant warps (may overlap the epilogue warps)
     int last_flag2;
     float wsum2[4][4][16];      // [token group][row quarter][token]
     float xch2[2][ROWS * 16];   // [token group pair][row][token]
-    float cscale[128];          // folded RMSNorm: per-token column scale of the tail epilogue
+    float cscale[MAX_NT];       // folded RMSNorm: per-token column scale of the tail epilogue
     int cscale_tile;            // token tile whose scales the idle epilogue warps put in cscale
 };
 
@@ -226,31 +240,33 @@ __device__ __forceinline__ int unit_owner(int u, int U, int G) {
 // Folded RMSNorm, consumer side: the token operand rows are fp16(h * w * s[m])
 // with a pre-scale s (an earlier rstd of the same row); the accumulators of row m
 // are multiplied by rstd(m) / s[m], rstd from the producer's per-block sums of
-// squares (summed in block order).  Threads 0..NT-1 fill dst[] for x rows
-// xrow0..xrow0+NT-1 (rows past the operand give 0).
-__device__ __forceinline__ void fold_scale(const Q4Epilogue &ep, int K, int xrow0, int nrows, int t, float *dst,
-                                           int NT) {
-    if (t >= NT) return;
-    const int m = xrow0 + t;
-    float c = 0.f;
-    if (t < nrows) {
-        // 16 loads in flight per batch; summed in block order
-        const float prev = __ldcg(ep.col_prev + m);
-        const int nb = K / 128;
-        float ss = 0.f;
-        for (int b0 = 0; b0 < nb; b0 += 16) {
-            float v[16];
+// squares (summed in block order).  Thread t0 of `stride` threads fills dst[t]
+// for t = t0, t0 + stride, .. < NT, the x rows xrow0 + t (rows past the operand
+// give 0).
+__device__ __forceinline__ void fold_scale(const Q4Epilogue &ep, int K, int xrow0, int nrows, int t0, int stride,
+                                           float *dst, int NT) {
+    for (int t = t0; t < NT; t += stride) {
+        const int m = xrow0 + t;
+        float c = 0.f;
+        if (t < nrows) {
+            // 16 loads in flight per batch; summed in block order
+            const float prev = __ldcg(ep.col_prev + m);
+            const int nb = K / 128;
+            float ss = 0.f;
+            for (int b0 = 0; b0 < nb; b0 += 16) {
+                float v[16];
 #pragma unroll
-            for (int k = 0; k < 16; ++k)
-                v[k] = b0 + k < nb ? __ldcg(ep.col_part + (size_t)(b0 + k) * ep.norm_rows + m) : 0.f;
+                for (int k = 0; k < 16; ++k)
+                    v[k] = b0 + k < nb ? __ldcg(ep.col_part + (size_t)(b0 + k) * ep.norm_rows + m) : 0.f;
 #pragma unroll
-            for (int k = 0; k < 16; ++k) ss += v[k];
+                for (int k = 0; k < 16; ++k) ss += v[k];
+            }
+            const float r = 1.0f / sqrtf(ss / (float)K + ep.col_eps);
+            if (ep.col_rstd) ep.col_rstd[m] = r;
+            c = r / prev;
         }
-        const float r = 1.0f / sqrtf(ss / (float)K + ep.col_eps);
-        if (ep.col_rstd) ep.col_rstd[m] = r;
-        c = r / prev;
+        dst[t] = c;
     }
-    dst[t] = c;
 }
 
 // Sums over the warp of sixteen per-lane values (one per token of a piece) in
@@ -313,7 +329,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *wring = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    unsigned char *xring = wring + (size_t)sw * WSTAGE;
+    unsigned char *xring = wring + (size_t)sw * C::WSTAGE;
     constexpr int R = C::AST;
     Smem &cs = *reinterpret_cast<Smem *>(xring + (size_t)R * C::XSTAGE);
 
@@ -356,23 +372,30 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
 
     if (warp == WP_WARP) {
         if (lane == 0) {
-            // ---------------- W producer: one stage per unit ----------------
+            // ------- W producer: one stage per unit (per 256-k half: wide tile) -------
+            constexpr int HALVES = C::WIDE ? 2 : 1;      // W stages per unit
             int issued = 0;
             int b = u0 / nc, c = u0 - b * nc;
-            for (int i = 0; i < n && !*abort_flag; ++i) {
-                const int blk = b % nblk;
+            for (int i = 0; i < n * HALVES && !*abort_flag; ++i) {
+                const int hh = HALVES == 2 ? (i & 1) : 0, blk = b % nblk;
                 const int s = i % sw;
                 if (i >= sw && !wait_or_abort(tc::smem_u32(&cs.w_free[s]), ((i - sw) / sw) & 1, abort_flag, ep.err,
                                               ERR_WFREE))
                     break;
-                const uint32_t st = tc::smem_u32(wring + (size_t)s * WSTAGE);
+                const uint32_t st = tc::smem_u32(wring + (size_t)s * C::WSTAGE);
                 const uint32_t bar = tc::smem_u32(&cs.full_w[s]);
-                tc::mbar_arrive_expect_tx(bar, WSTAGE);
-                tc::tma_load_2d(st, &wmap, c * (KU / 2), blk * ROWS, bar);
-                tc::tma_load_2d(st + WBOX, &wmap, c * (KU / 2) + KS / 2, blk * ROWS, bar);
-                bulk_load(st + 2 * WBOX, sbp + (size_t)(blk * nc + c) * (8 * ROWS), SB_BYTES, bar);
+                const uint32_t *sbu = sbp + (size_t)(blk * nc + c) * (8 * ROWS);
+                tc::mbar_arrive_expect_tx(bar, C::WSTAGE);
+                if constexpr (C::WIDE) {
+                    tc::tma_load_2d(st, &wmap, c * (KU / 2) + hh * (KS / 2), blk * ROWS, bar);
+                    bulk_load(st + WBOX, sbu + hh * (4 * ROWS), SB_BYTES / 2, bar);
+                } else {
+                    tc::tma_load_2d(st, &wmap, c * (KU / 2), blk * ROWS, bar);
+                    tc::tma_load_2d(st + WBOX, &wmap, c * (KU / 2) + KS / 2, blk * ROWS, bar);
+                    bulk_load(st + 2 * WBOX, sbu, SB_BYTES, bar);
+                }
                 issued = i + 1;
-                if (++c == nc) { c = 0; ++b; }
+                if (hh == HALVES - 1 && ++c == nc) { c = 0; ++b; }
             }
             if (*abort_flag)   // let every issued copy land before the CTA can exit
                 for (int i = max(0, issued - sw); i < issued; ++i)
@@ -458,7 +481,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
         int ctile = -1;                          // token tile whose folded-norm scales are in cs.cscale
         // epilogue of one block segment by the sixteen dequantising warps
         auto seg_epilogue = [&](const int ub, const int lseg, const bool release) {
-            constexpr int PIECES = NT <= 64 ? 1 : 2;      // 16-token pieces per token group
+            constexpr int PIECES = NT <= 64 ? 1 : (NT <= 128 ? 2 : 3);   // 16-token pieces per token group
             const int tg = g;                             // token group of this warp
             const int ldset = lseg % C::DSETS;
             const int seg_first_unit = max(u0, ub * nc), seg_last_unit = min(u1 - 1, ub * nc + nc - 1);
@@ -588,7 +611,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                 }
                 if (!have) {
                     griddep_wait();
-                    fold_scale(ep, K, tok_base + tile * NT, max(0, min(NT, M - tile * NT)), tid, cs.cscale, NT);
+                    fold_scale(ep, K, tok_base + tile * NT, max(0, min(NT, M - tile * NT)), tid, TAIL_THREADS, cs.cscale, NT);
                     named_bar_sync(TAIL_BAR, TAIL_THREADS);
                 }
                 ctile = tile;
@@ -764,18 +787,22 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
         const int sw_off = (((2 * g) ^ sw8) << 4), sw_off1 = (((2 * g + 1) ^ sw8) << 4);
         for (int j = 0; j < nsub; ++j) {
             const int h = j & 1;
-            const unsigned char *wst = wring + (size_t)s * WSTAGE;
+            // the W stage of this sub-chunk: half h of the unit's stage, or a stage of
+            // its own for the wide tile
+            const bool stage_first = C::WIDE || h == 0, stage_last = C::WIDE || h == 1;
+            const unsigned char *wst = wring + (size_t)s * C::WSTAGE;
             bool ok = true;
-            if (h == 0) {
+            if (stage_first) {
                 if (lane == 0) ok = wait_or_abort(tc::smem_u32(&cs.full_w[s]), wpar, abort_flag, ep.err, ERR_WFULL);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
             }
-            const unsigned char *wt = wst + h * WBOX + r * 128;
+            const unsigned char *wt = wst + (C::WIDE ? 0 : h * WBOX) + r * 128;
             const uint4 w0 = *reinterpret_cast<const uint4 *>(wt + sw_off);
             const uint4 w1 = *reinterpret_cast<const uint4 *>(wt + sw_off1);
-            const uint32_t sbv = reinterpret_cast<const uint32_t *>(wst + 2 * WBOX)[(h * 4 + g) * ROWS + r];
-            const int s_read = s;           // released after its second box is in TMEM
-            if (h == 1 && ++s == sw) { s = 0; wpar ^= 1; }
+            const uint32_t *sbs = reinterpret_cast<const uint32_t *>(wst + (C::WIDE ? WBOX : 2 * WBOX));
+            const uint32_t sbv = sbs[((C::WIDE ? 0 : h * 4) + g) * ROWS + r];
+            const int s_read = s;           // released once its values are in TMEM
+            if (stage_last && ++s == sw) { s = 0; wpar ^= 1; }
             if (j >= R) {   // the MMAs that last read this A buffer have completed
                 if (lane == 0)
                     ok = ok && wait_or_abort(tc::smem_u32(&cs.mma_done[as]), (mpar >> as) & 1, abort_flag, ep.err,
@@ -794,7 +821,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
                 tc::tmem_st16(ta + 16, a);
                 tc::tmem_wait_st();
             }
-            if (h == 1) {
+            if (stage_last) {
                 // the stage goes back to the producer only once the values read
                 // from it are in TMEM: handing it back right after the loads were
                 // issued let the next TMA write race them
@@ -821,7 +848,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
             const int et = tid - EP_WARP0 * 32;
             const int tile0 = u0 / (nblk * nc);
             griddep_wait();   // the sums of squares come from the previous kernel
-            fold_scale(ep, K, tok_base + tile0 * NT, max(0, min(NT, M - tile0 * NT)), et, cs.cscale, NT);
+            fold_scale(ep, K, tok_base + tile0 * NT, max(0, min(NT, M - tile0 * NT)), et, EP_THREADS, cs.cscale, NT);
             named_bar_sync(EPI_BAR, EP_THREADS);
             if (et == 0) {
                 __threadfence_block();
@@ -905,7 +932,7 @@ q4_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ C
             if (!skip && last) {
                 if (ep.col_part && ctile != tile) {   // folded RMSNorm of the token operand (STORE only)
                     griddep_wait();
-                    fold_scale(ep, K, tok_base + tile * NT, max(0, min(NT, M - tile * NT)), etid, cs.xch, NT);
+                    fold_scale(ep, K, tok_base + tile * NT, max(0, min(NT, M - tile * NT)), etid, EP_THREADS, cs.xch, NT);
                     named_bar_sync(EPI_BAR, EP_THREADS);
                     ctile = tile;
                 }
@@ -1036,7 +1063,7 @@ constexpr size_t SMEM_LIMIT = 227 * 1024;
 
 template <int NT>
 size_t smem_for(int sw) {
-    return 1024 + (size_t)sw * WSTAGE + (size_t)Cfg<NT>::AST * Cfg<NT>::XSTAGE + sizeof(Smem);
+    return 1024 + (size_t)sw * Cfg<NT>::WSTAGE + (size_t)Cfg<NT>::AST * Cfg<NT>::XSTAGE + sizeof(Smem);
 }
 
 // deepest W ring that fits the shared memory of one CTA
@@ -1053,6 +1080,8 @@ cudaError_t launch_op(const Q4WeightTC &w, const CUtensorMap &xmap, int M, int t
     static bool attr[64] = {};   // per instantiation
     int dev = 0;
     cudaGetDevice(&dev);
+    static_assert(1024 + 2 * Cfg<NT>::WSTAGE + Cfg<NT>::AST * Cfg<NT>::XSTAGE + sizeof(Smem) <= SMEM_LIMIT,
+                  "two W stages, the x ring and the CTA state must fit one CTA's shared memory");
     const int sw = stages_for<NT>();
     const size_t sm = smem_for<NT>(sw);
     if (sm > SMEM_LIMIT) return cudaErrorInvalidConfiguration;
@@ -1134,6 +1163,15 @@ int q4_tc_tile(int M) {
     return ((per + 15) / 16) * 16;
 }
 
+// token tile of one launch: the gate/up projection (SWIGLU epilogue) runs
+// 129..160 tokens as one tile (one pass of its 117 M weights instead of two;
+// its kernel span 75 -> 60 us at the Llama-3-8B verify shape), the other
+// projections as two (one wide tile measured slower for them)
+int q4_tc_launch_tile(int M, int op) {
+    if (op == Q4Epilogue::SWIGLU && M > 128 && M <= MAX_NT) return ((M + 15) / 16) * 16;
+    return q4_tc_tile(M);
+}
+
 // most CTAs that share one row block (stream-K contributors)
 int q4_tc_pmax(int U, int G, int nc) {
     // a CTA covers floor(U/G) or ceil(U/G) units; a block of nc units meets at most
@@ -1142,16 +1180,20 @@ int q4_tc_pmax(int U, int G, int nc) {
     return (nc - 1 + per - 1) / per + 1;
 }
 
+// split-K partials / tickets of a launch: enough for either tiling of M
 size_t q4_tc_partial_floats(int N, int K, int M, int sm_count) {
-    const int nt = q4_tc_tile(M);
-    const int tiles = (M + nt - 1) / nt;
-    const int nblk = N / ROWS, nc = (K + KU - 1) / KU;
-    const int U = tiles * nblk * nc, G = U < sm_count ? U : sm_count;
-    return (size_t)tiles * nblk * q4_tc_pmax(U, G, nc) * ROWS * nt;
+    size_t most = 0;
+    for (const int nt : {q4_tc_tile(M), q4_tc_launch_tile(M, Q4Epilogue::SWIGLU)}) {
+        const int tiles = (M + nt - 1) / nt;
+        const int nblk = N / ROWS, nc = (K + KU - 1) / KU;
+        const int U = tiles * nblk * nc, G = U < sm_count ? U : sm_count;
+        most = std::max(most, (size_t)tiles * nblk * q4_tc_pmax(U, G, nc) * ROWS * nt);
+    }
+    return most;
 }
 
 size_t q4_tc_counters(int N, int M) {
-    const int nt = q4_tc_tile(M);
+    const int nt = q4_tc_tile(M);   // the one-tile launch has fewer blocks to count
     return (size_t)((M + nt - 1) / nt) * (N / ROWS);
 }
 
@@ -1160,7 +1202,7 @@ cudaError_t q4_tc(const Q4WeightTC &w, const __half *x_blk, int ldx_rows, int to
     if (w.N % ROWS || w.K % 128 || M <= 0 || tok_base + M > ldx_rows || !w.sbp) return cudaErrorInvalidValue;
     auto fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
-    const int nt = q4_tc_tile(M);
+    const int nt = q4_tc_launch_tile(M, ep.op);
     const int tiles = (M + nt - 1) / nt;
     // token operand [K/64][ldx_rows][64] fp16 -> 3-D map (64, rows, K/64)
     CUtensorMap xmap;
@@ -1180,7 +1222,10 @@ cudaError_t q4_tc(const Q4WeightTC &w, const __half *x_blk, int ldx_rows, int to
     case 80: return launch_nt<80>(w, xmap, M, tok_base, tiles, sm_count, ep, st);
     case 96: return launch_nt<96>(w, xmap, M, tok_base, tiles, sm_count, ep, st);
     case 112: return launch_nt<112>(w, xmap, M, tok_base, tiles, sm_count, ep, st);
-    default: return launch_nt<128>(w, xmap, M, tok_base, tiles, sm_count, ep, st);
+    case 128: return launch_nt<128>(w, xmap, M, tok_base, tiles, sm_count, ep, st);
+    case 144: return launch_op<144, Q4Epilogue::SWIGLU>(w, xmap, M, tok_base, tiles, sm_count, ep, st);
+    case 160: return launch_op<160, Q4Epilogue::SWIGLU>(w, xmap, M, tok_base, tiles, sm_count, ep, st);
+    default: return cudaErrorInvalidValue;
     }
 }
 
