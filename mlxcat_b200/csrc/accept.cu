@@ -159,11 +159,13 @@ __device__ unsigned long long block_excl_scan_u64(unsigned long long v, DistSmem
 }
 
 // top-p threshold: lowest key whose strictly-higher mass A satisfies
-// (A << 20) < S1 * tp, found MSB-first over 11/11/10-bit buckets.
-__device__ uint32_t top_p_threshold(const float *l, int V, float m, uint64_t S1, uint64_t tp,
-                                    DistSmem &sm) {
+// (A << 20) < S1 * tp, found MSB-first over 11/11/10-bit buckets.  S1, the
+// total fixed-point mass of the row, is the sum of the first pass's histogram
+// (integer sums: the same value as a separate pass over the row, without its
+// exponentials).
+__device__ uint32_t top_p_threshold(const float *l, int V, float m, uint64_t tp, DistSmem &sm) {
     uint32_t prefix = 0;
-    unsigned long long base = 0;
+    unsigned long long base = 0, S1 = 0;
     const int shifts[3] = {21, 10, 0};
     const int widths[3] = {11, 11, 10};
     for (int pass = 0; pass < 3; ++pass) {
@@ -192,6 +194,7 @@ __device__ uint32_t top_p_threshold(const float *l, int V, float m, uint64_t S1,
         // thread j owns buckets 2047-2j, 2046-2j (descending)
         const int b_hi = NB - 1 - 2 * threadIdx.x, b_lo = b_hi - 1;
         const unsigned long long mh = sm.mass[b_hi], ml = sm.mass[b_lo];
+        if (pass == 0) S1 = block_sum_u64(mh + ml, sm);
         const unsigned long long ex = block_excl_scan_u64(mh + ml, sm);
         const unsigned long long above_hi = base + ex, above_lo = base + ex + mh;
         int cand = NB;
@@ -227,12 +230,9 @@ __device__ void dist_stats(const float *l, int V, float T, float top_p, int d, D
     const float m = block_max_f(mx, sm);
     uint32_t thr = 0;
     if (top_p > 0.0f && top_p < 1.0f) {
-        unsigned long long s1 = 0;
-        for (int i = threadIdx.x; i < V; i += STPB) s1 += fix24(det_exp_neg(__fadd_rn(l[i], -m)));
-        const unsigned long long S1 = block_sum_u64(s1, sm);
         long long tp = (long long)rintf(__fmul_rn(top_p, 1048576.0f));
         tp = tp < 1 ? 1 : (tp > 1048576 ? 1048576 : tp);
-        thr = top_p_threshold(l, V, m, S1, (uint64_t)tp, sm);
+        thr = top_p_threshold(l, V, m, (uint64_t)tp, sm);
     }
     unsigned long long s = 0;
     for (int i = threadIdx.x; i < V; i += STPB) s += tempered_p(l[i], m, T, thr);
