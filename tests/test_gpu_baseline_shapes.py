@@ -12,6 +12,9 @@
   rtol/atol 2e-2 of the oracle, acceptance bit-exact on the device's logits,
   greedy tokens equal to the oracle's except at top-2 gaps under 1e-2, the
   appended KV within 2e-2.
+* A ragged token count: 29 rows x 5 verify tokens = 145, which the gate/up
+  projection runs as one 160-column tile with 15 padding columns and the
+  other projections as two 80-token tiles (reduced widths, greedy).
 * The q4 linear operator at every (N, K, M) the benchmarks launch, against the
   oracle's fp32 restatement on three 128-row blocks of each output (the first,
   a middle and the last block), so the stream-K split, token tiles and the
@@ -38,6 +41,8 @@ TIE = 1e-2
 QWEN3_4B_2L = M.ModelConfig(2, 2560, 32, 8, 128, 9728, 151936, True, True, 1e-6, 1e6, name="qwen3-4b-2l")
 LLAMA3_8B_2L = M.ModelConfig(2, 4096, 32, 8, 128, 14336, 128256, False, False, 1e-5, 500000.0,
                              name="llama3-8b-2l")
+RAGGED_SMALL = M.ModelConfig(2, 1024, 16, 4, 128, 2816, 8192, False, False, 1e-5, 500000.0,
+                             name="llama-small-ragged")
 
 
 def segment_prompt(vocab, n_seg, seg_len, length, seed):
@@ -121,6 +126,11 @@ def verify_at_shape(cfg, rows, ctx_len, k, n, temperature, top_p, seed):
         np.testing.assert_allclose(kk[:, lo:].astype(np.float32), ok, rtol=TOL, atol=TOL)
         np.testing.assert_allclose(vv[:, lo:].astype(np.float32), ovv, rtol=TOL, atol=TOL)
     return drafts
+
+
+def test_ragged_token_count_verify_matches_oracle():
+    """145 verify tokens (29 rows x 5): the one-tile gate/up launch with padding columns."""
+    verify_at_shape(RAGGED_SMALL, 29, 600, 4, 3, 0.0, 0.0, 43)
 
 
 def test_qwen3_4b_shape_verify_matches_oracle():
