@@ -350,7 +350,9 @@ attn_kernel(const __half *__restrict__ qbuf, const __half *__restrict__ kc,
     }
 }
 
-// merge the split partials of one (group, kv head, query row); thread = d
+// merge the split partials of one (group, kv head): thread = 8 consecutive
+// features of one query row (16-byte loads of each split, one 16-byte store);
+// per feature the same two-level merge as a plain loop over the splits
 template <int QT>
 __global__ void attn_combine_kernel(const float *__restrict__ o_part, const float *__restrict__ ml_part,
                                     int M, int qg, int Hq, int Hkv, int D, int splits,
@@ -358,30 +360,37 @@ __global__ void attn_combine_kernel(const float *__restrict__ o_part, const floa
     constexpr int QROWS = QT * 16;
     griddep_launch_dependents();   // the output projection may start prefetching its weights
     griddep_wait();                // the split partials come from the split pass
-    const int grp = blockIdx.x, h = blockIdx.y, qi = blockIdx.z;
+    const int grp = blockIdx.x, h = blockIdx.y;
     const int G = Hq / Hkv;
     const int t0 = grp * qg;
     const int ntok = min(qg, M - t0);
     const int NQ = ntok * G;
-    if (qi >= NQ) return;
-    const int P = splits;
+    const int P = splits, DC = D / 8;
     const size_t it0 = ((size_t)grp * Hkv + h) * P;
     const int KO = Hq * D;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    for (int w = threadIdx.x; w < NQ * DC; w += blockDim.x) {
+        const int qi = w / DC, d0 = (w - qi * DC) * 8;
         // splits in batches of PB whose loads are all issued before any is used
         // (one L2 round trip per batch); a running max rescales across batches,
         // and with P <= PB the sums are exactly the two-pass ones
         constexpr int PB = 8;
-        float num = 0.f, den = 0.f, mrun = -INFINITY;
+        float num[8], den = 0.f, mrun = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) num[i] = 0.f;
         for (int p0 = 0; p0 < P; p0 += PB) {
-            float m[PB], l[PB], v[PB];
+            float m[PB], l[PB];
+            float4 va[PB], vb[PB];
 #pragma unroll
             for (int k = 0; k < PB; ++k) {
-                m[k] = -INFINITY; l[k] = 0.f; v[k] = 0.f;
+                m[k] = -INFINITY; l[k] = 0.f;
+                va[k] = vb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (p0 + k < P) {
-                    const float2 ml = *reinterpret_cast<const float2 *>(ml_part + ((it0 + p0 + k) * QROWS + qi) * 2);
+                    const size_t item = it0 + p0 + k;
+                    const float2 ml = *reinterpret_cast<const float2 *>(ml_part + (item * QROWS + qi) * 2);
                     m[k] = ml.x; l[k] = ml.y;
-                    v[k] = o_part[((it0 + p0 + k) * QROWS + qi) * D + d];
+                    const float4 *src = reinterpret_cast<const float4 *>(o_part + (item * QROWS + qi) * D + d0);
+                    va[k] = src[0];
+                    vb[k] = src[1];
                 }
             }
             float mb = mrun;
@@ -390,22 +399,30 @@ __global__ void attn_combine_kernel(const float *__restrict__ o_part, const floa
             if (mb == -INFINITY) continue;
             if (mrun != -INFINITY && mrun != mb) {
                 const float a = exp2f(mrun - mb);
-                num *= a;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) num[i] *= a;
                 den *= a;
             }
 #pragma unroll
             for (int k = 0; k < PB; ++k) {
                 if (m[k] == -INFINITY) continue;
-                const float w = exp2f(m[k] - mb);
-                den += w * l[k];
-                num += w * v[k];
+                const float wk = exp2f(m[k] - mb);
+                den += wk * l[k];
+                num[0] += wk * va[k].x; num[1] += wk * va[k].y; num[2] += wk * va[k].z; num[3] += wk * va[k].w;
+                num[4] += wk * vb[k].x; num[5] += wk * vb[k].y; num[6] += wk * vb[k].z; num[7] += wk * vb[k].w;
             }
             mrun = mb;
         }
-        const float r = den > 0.f ? num / den : 0.f;
+        // 8 features inside one 64-feature block; the blocked operand layout keeps
+        // them in perm8 order, so feature i goes to slot perm8(i) of the 16 bytes
+        __align__(16) __half r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            r[permuted ? perm8(i) : i] = __float2half_rn(den > 0.f ? num[i] / den : 0.f);
         const int j = qi / G, gh = qi - j * G;
-        const int k = (h * G + gh) * D + d;
-        out[permuted ? xblk(t0 + j, k, out_rows) : (size_t)(t0 + j) * KO + k] = __float2half_rn(r);
+        const int k0 = (h * G + gh) * D + d0;
+        __half *dst = permuted ? out + xblk(t0 + j, k0, out_rows) : out + (size_t)(t0 + j) * KO + k0;
+        *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(r);
     }
 }
 
@@ -435,9 +452,10 @@ cudaError_t launch_attn(const __half *qbuf, KVLayer kv, const int32_t *trow, con
                                trow, tpos, M, qg, Hq, Hkv, key_chunk, splits, scale_log2, sc.o, sc.ml,
                                early_kv ? 1 : 0, direct);
     if (e != cudaSuccess || direct) return e;
-    dim3 g2(groups, Hkv, QT * 16);
-    return launch_pdl(attn_combine_kernel<QT>, g2, dim3(D), 0, st, (const float *)sc.o, (const float *)sc.ml, M, qg,
-                      Hq, Hkv, D, splits, out, permuted ? 1 : 0, out_rows);
+    dim3 g2(groups, Hkv);
+    const int cthreads = std::min(512, QT * 16 * (D / 8));
+    return launch_pdl(attn_combine_kernel<QT>, g2, dim3(cthreads), 0, st, (const float *)sc.o, (const float *)sc.ml,
+                      M, qg, Hq, Hkv, D, splits, out, permuted ? 1 : 0, out_rows);
 }
 
 }  // namespace
