@@ -1154,9 +1154,9 @@ cudaError_t pack_q4_sb(const __half *scales, const __half *biases, int N, int K,
     return cudaGetLastError();
 }
 
-// token tile: the fewest tiles of at most 128 tokens, split evenly (M = 160 ->
-// two tiles of 80, not 128 + 32 padded to 128: the MMAs of a sub-chunk and its
-// token-operand loads scale with the tile width)
+// token tile of the two-issuer launches: the fewest tiles of at most 128
+// tokens, split evenly (M = 160 -> two tiles of 80, not 128 + 32 padded to
+// 128: the token-operand loads and the epilogue scale with the tile width)
 int q4_tc_tile(int M) {
     const int tiles = (M + 127) / 128;
     const int per = (M + tiles - 1) / tiles;
